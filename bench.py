@@ -1,0 +1,376 @@
+"""Benchmark of the gpt-oss-20b MXFP4 MoE path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload moe-decode] [--impl ours|reference]
+
+Workload "moe-decode" (BASELINE configs[0] stacked as in configs[1]): bs=1 decode through the 24 MoE layers of a
+20b-shaped random-init model: per step, one token x goes x <- x + MoE(RMSNorm(x)) through 24 distinct layers
+(router 2880->32, top-4, MXFP4 gate/up + clamped SwiGLU, MXFP4 down, weighted combine). 24 x 423 MB of expert
+weights are resident, far above the 126 MB L2, and each step reads 24 x 53,130,240 algorithmic bytes.
+
+Timed region: W untimed steps, then exactly K steps between a barrier + synchronize on both sides, CUDA events on
+the launching stream, max over ranks. With N > 1 every rank runs an independent replica (bs=1 decode does not
+shard): value = N * K * bytes / max time ("replicas only", scaling "weak").
+
+--impl reference times the reference's own CPU algorithm for this path (the fp32 Reference.moe of
+openvang/gptoss-infer, restated in oracle/moe.py, dequantizing each selected expert per call as the reference does)
+on the host cores, on a bounded sample per step, and prints the same metric.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "gptoss-infer_b200")]
+
+H, I, E, K_TOP, LAYERS = 2880, 2880, 32, 4, 24
+EXPERT_BYTES = 8_294_400 + 518_400 + 4_147_200 + 259_200            # blocks + scales, gate/up and down
+LAYER_BYTES = K_TOP * EXPERT_BYTES + 184_320 + K_TOP * (5760 + 2880) * 2   # + router + bf16 biases = 53,130,240
+GATEUP_BYTES = K_TOP * (8_294_400 + 518_400 + 5760 * 4) + H * 4 + K_TOP * I * 4   # per launch, fp32 bias/in/out
+METRIC = "bs=1 decode MoE-layer HBM GB/s (20b-shaped, 24 layers)"
+UNIT = "GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--moe-impl", type=int, default=None, help="0 = SIMT, 1 = tensor cores (default: library's)")
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.t.join(timeout=5)
+
+    def summary(self):
+        import statistics
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) >= 9:
+                for n, v in zip(names, r[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------------- setup
+def dist_init():
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def make_layers(n_layers, dev):
+    """Layer 0 from synth seed 0 (the config-0 layer); the others drawn on the device with the same distributions."""
+    import torch
+    from gptoss_b200 import synth
+    layers = []
+    t0 = synth.moe_layer(seed=0)
+    p = "model.layers.0."
+    g = torch.Generator(device=dev).manual_seed(1234)
+    for l in range(n_layers):
+        if l == 0:
+            d = {k[len(p):]: v.to(dev) for k, v in t0.items()}
+        else:
+            d = {}
+            d["post_attention_layernorm.weight"] = (1 + torch.randn(H, device=dev, generator=g) * 0.02).bfloat16()
+            d["mlp.router.weight"] = (torch.randn(E, H, device=dev, generator=g) * 0.02).bfloat16()
+            d["mlp.router.bias"] = (torch.randn(E, device=dev, generator=g) * 0.01).bfloat16()
+            for name, rows, k in (("gate_up_proj", 2 * I, H), ("down_proj", H, I)):
+                q = "mlp.experts." + name
+                d[q + "_blocks"] = torch.randint(0, 256, (E, rows, k // 32, 16), device=dev, generator=g,
+                                                 dtype=torch.uint8)
+                d[q + "_scales"] = torch.randint(120, 127, (E, rows, k // 32), device=dev, generator=g,
+                                                 dtype=torch.uint8)
+                d[q + "_bias"] = (torch.randn(E, rows, device=dev, generator=g) * 0.01).bfloat16()
+        L = {
+            "ln": d["post_attention_layernorm.weight"].float(),
+            "W": d["mlp.router.weight"].contiguous(),
+            "b": d["mlp.router.bias"].float(),
+            "ex": [d["mlp.experts.gate_up_proj_blocks"], d["mlp.experts.gate_up_proj_scales"],
+                   d["mlp.experts.gate_up_proj_bias"].float(), d["mlp.experts.down_proj_blocks"],
+                   d["mlp.experts.down_proj_scales"], d["mlp.experts.down_proj_bias"].float()],
+        }
+        layers.append(L)
+    return layers, t0
+
+
+# ------------------------------------------------------------------------------------------------------- cpu
+def cpu_moe_sample(t0, budget_s, token_seed=99):
+    """The reference's CPU algorithm (Reference.moe, fp32, per-call dequant) on one token of layer 0, repeated until
+    about budget_s seconds have passed. Returns (bytes_per_s, n_tokens, threads)."""
+    import numpy as np
+    from gptoss_b200 import synth
+    from oracle import moe as omoe
+    tn = synth.to_numpy(t0)
+    p = "model.layers.0."
+    x = synth.tokens(64, seed=token_seed).numpy()
+    h = omoe.rms_norm(x, tn[p + "post_attention_layernorm.weight"])
+    omoe.moe(tn, p, h[:1])                                        # cold run
+    n, t_start = 0, time.perf_counter()
+    while True:
+        omoe.moe(tn, p, h[n % 64: n % 64 + 1])
+        n += 1
+        el = time.perf_counter() - t_start
+        if el >= budget_s or n >= 64:
+            break
+    return LAYER_BYTES * n / el, n, os.cpu_count()
+
+
+# ------------------------------------------------------------------------------------------------------- main
+def run_reference(args):
+    """Reference arm: the reference's CPU implementation of this path, bounded sample per step."""
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    from gptoss_b200 import synth
+    from oracle import moe as omoe
+    t0 = synth.moe_layer(seed=0)
+    tn = synth.to_numpy(t0)
+    p = "model.layers.0."
+    x = synth.tokens(64, seed=99).numpy()
+    h = omoe.rms_norm(x, tn[p + "post_attention_layernorm.weight"])
+    # A step is one token through one MoE layer, scaled down to a row slice of the selected experts when K is large,
+    # so the whole run stays within about two minutes. GB/s is per byte actually processed.
+    budget = 120.0
+    probe_t = time.perf_counter()
+    omoe.moe(tn, p, h[:1])
+    per_layer = time.perf_counter() - probe_t
+    frac = min(1.0, budget / max(1, args.steps + args.warmup) / max(per_layer, 1e-3))
+    _, ids, gate = omoe.router(h, tn[p + "mlp.router.weight"], tn[p + "mlp.router.bias"], K_TOP)
+    pe = p + "mlp.experts."
+
+    def step(i):
+        r = i % 64
+        out = np.zeros(H, np.float32)
+        nbytes = 0
+        for slot, e in enumerate(ids[r].tolist()):
+            rows_gu = max(2, int(2 * I * frac) // 2 * 2)
+            rows_dn = max(1, int(H * frac))
+            from oracle import mxfp4
+            w1 = mxfp4.dequant(tn[pe + "gate_up_proj_blocks"][e][:rows_gu], tn[pe + "gate_up_proj_scales"][e][:rows_gu])
+            a = omoe.swiglu(w1 @ h[r] + tn[pe + "gate_up_proj_bias"][e][:rows_gu])
+            w2 = mxfp4.dequant(tn[pe + "down_proj_blocks"][e][:rows_dn], tn[pe + "down_proj_scales"][e][:rows_dn])
+            out[:rows_dn] += gate[r, slot] * (w2[:, :a.shape[0]] @ a + tn[pe + "down_proj_bias"][e][:rows_dn])
+            nbytes += rows_gu * 90 * 17 + rows_dn * 90 * 17
+        return nbytes + int(184_320 * frac)
+
+    for i in range(args.warmup):
+        step(i)
+    t = time.perf_counter()
+    nbytes = sum(step(i) for i in range(args.steps))
+    el = time.perf_counter() - t
+    value = nbytes / el / 1e9
+    sample = (f"one token through one MoE layer per step, rows sliced to {frac:.4f} of each selected expert "
+              f"(numpy fp32, per-call MXFP4 dequant)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "moe-decode (configs[0] stacked x24, bs=1)", "layers": LAYERS},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    from gptoss_b200 import capi
+    ws, rank, local = dist_init()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = capi.load()
+    if args.moe_impl is not None and lib.gptoss_set_moe_impl(args.moe_impl) < 0:
+        raise RuntimeError(lib.gptoss_last_error().decode())
+    P = capi.ptr
+    layers, t0 = make_layers(args.layers, dev)
+    n_tok = args.steps + args.warmup
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    X = torch.randn(n_tok, H, device=dev, generator=g)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step(x, events=None):
+        for L in layers:
+            rc = lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
+                                            P(x), E, K_TOP, H, I, 1.702, 7.0, sp, events)
+            if rc != 0:
+                raise RuntimeError(lib.gptoss_last_error().decode())
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        step(X[args.steps + i])
+    barrier()
+
+    # ---- timed region: exactly K steps
+    with ClockSampler(local) as clocks:
+        barrier()
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0e.record(stream)
+        for i in range(args.steps):
+            step(X[i])
+        t1e.record(stream)
+        barrier()
+    ms = t0e.elapsed_time(t1e)
+    if ws > 1:
+        tt = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+    value = ws * args.steps * args.layers * LAYER_BYTES / (ms / 1e3) / 1e9
+    gpu_launches = args.steps * args.layers * 4           # rmsnorm, router, gate/up, down per layer
+
+    # ---- per-kernel durations: the same K steps again, with events between the kernels of every layer
+    n_prof = min(args.steps, 200)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_prof * args.layers)]
+    for quad in ev:                                       # torch creates the CUDA event at its first record
+        for e in quad:
+            e.record(stream)
+    handles = [ctypes_array(e) for e in ev]
+    barrier()
+    for i in range(n_prof):
+        x = X[i]
+        for li, L in enumerate(layers):
+            rc = lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
+                                            P(x), E, K_TOP, H, I, 1.702, 7.0, sp, handles[i * args.layers + li])
+            assert rc == 0, lib.gptoss_last_error().decode()
+    barrier()
+    router_us = sum(e[0].elapsed_time(e[1]) for e in ev) / len(ev) * 1e3
+    gateup_us = sum(e[1].elapsed_time(e[2]) for e in ev) / len(ev) * 1e3
+    down_us = sum(e[2].elapsed_time(e[3]) for e in ev) / len(ev) * 1e3
+    del handles
+
+    # ---- end to end through the public API: host x in, host x out, every step
+    xh = torch.randn(args.steps, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
+    yh = torch.empty(H).pin_memory()
+    xd = torch.empty(H, device=dev)
+    barrier()
+    te0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        xd.copy_(xh[i], non_blocking=True)
+        step(xd)
+        yh.copy_(xd, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    if ws > 1:
+        tt = torch.tensor([ms_e2e], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(tt.item())
+    e2e = ws * args.steps * args.layers * LAYER_BYTES / (ms_e2e / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        bps, n, cores = cpu_moe_sample(t0, budget_s=15.0)
+        cpu = {"value": bps / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{n} tokens x 1 MoE layer of the same workload (numpy fp32, per-call MXFP4 dequant, "
+                         f"{cores} host threads)"}
+
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    achieved = GATEUP_BYTES / (gateup_us * 1e-6) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("moe_gateup")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init 20b-shaped MoE layers)",
+            "config": {"workload": "moe-decode (configs[0] stacked x24, bs=1)", "layers": args.layers,
+                       "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
+                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                       "l2": "inputs larger than L2: 24 distinct layers, 10.2 GB of experts"},
+            "tok_per_s": ws * args.steps / (ms / 1e3),
+            "us_per_moe_layer": ms / args.steps / args.layers * 1e3,
+            "kernel_us": {"router+rmsnorm": router_us, "gate_up": gateup_us, "down+combine": down_us},
+            "roofline": {"bound": "hbm", "kernel": "moe gate/up GEMV", "achieved": achieved, "peak": hbm,
+                         "peak_source": peak_src, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
+                         "frac_of_8TBs_nominal": achieved / 8000.0,
+                         "algorithmic_bytes_per_launch": GATEUP_BYTES},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
+                    "api": "gptoss_moe_block_async x24 per token, host x copied in and out every step"},
+            "gpu_launches": gpu_launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def ctypes_array(events):
+    import ctypes
+    arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+    return arr
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,91 @@
+// Shared device helpers for the gpt-oss MXFP4 MoE path on B200 (sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace gpt {
+
+#define GPT_CHECK(x)                                                                                    \
+    do {                                                                                                \
+        cudaError_t e_ = (x);                                                                           \
+        if (e_ != cudaSuccess) throw std::runtime_error(std::string(#x) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+inline void check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+inline void require(bool ok, const char* what) {
+    if (!ok) throw std::runtime_error(what);
+}
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+// E8M0 byte -> 2^(s-127) built from the bit pattern; s == 0 is the fp32 subnormal 2^-127. (0xFF is rejected by the
+// callers that can see it.) Exact on every input, unlike exp2f.
+__device__ __forceinline__ float e8m0_to_f32(uint32_t s) {
+    return s == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(s << 23);
+}
+
+// One byte of two e2m1 codes (low nibble = even element) -> two floats, via the sm_100 e2m1x2 converter. Every e2m1
+// value is exact in f16 and in f32, so this is lossless.
+__device__ __forceinline__ void e2m1x4_to_f32(uint32_t word16, float* out4) {
+    uint32_t h01, h23;
+    asm("{\n\t.reg .b8 b0, b1;\n\t"
+        "mov.b16 {b0, b1}, %2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t}"
+        : "=r"(h01), "=r"(h23)
+        : "h"((unsigned short)word16));
+    const float2 a = __half22float2(*reinterpret_cast<__half2*>(&h01));
+    const float2 b = __half22float2(*reinterpret_cast<__half2*>(&h23));
+    out4[0] = a.x; out4[1] = a.y; out4[2] = b.x; out4[3] = b.y;
+}
+
+// Packed fp32x2 FMA (sm_100): d = a * b + c, two lanes at once.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// 16-byte read-only global load that does not allocate in L1 (weights are streamed once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its prologue, and wait for the previous
+// kernel's memory to be visible. Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+}  // namespace gpt

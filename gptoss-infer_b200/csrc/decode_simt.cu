@@ -1,0 +1,425 @@
+// Decode-path kernels that run on the CUDA cores: RMSNorm, the MXFP4 decoder, the router, and the SIMT MXFP4
+// GEMV pair (gate/up + clamped SwiGLU, down + weighted combine). The tensor-core decode path lives in
+// decode_tc.cu; this one is the correctness baseline and handles every shape the C ABI accepts.
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace gpt {
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        GPT_CHECK(cudaGetDevice(&dev));
+        GPT_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    }
+    return n;
+}
+
+namespace {
+
+// ---------------------------------------------------------------------------------------------------------------
+// RMSNorm: one CTA per row.
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                       float* __restrict__ y, int n, float eps) {
+    __shared__ float red[32];
+    const float* xr = x + size_t(blockIdx.x) * n;
+    float* yr = y + size_t(blockIdx.x) * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float r = 1.0f / sqrtf(red[0] / float(n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * r * w[i];
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// MXFP4 decode: one thread per block. value = e2m1 * 2^(s-127) is one IEEE multiply of two exact values, so the
+// result is bit-identical to the CPU decoder (subnormal 2^-127 for s == 0, inf for 6 * 2^127).
+__global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks, const uint8_t* __restrict__ scales,
+                                     float* __restrict__ out, long long n_blocks, int* bad) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= n_blocks) return;
+    const uint32_t s = scales[i];
+    if (s == 0xFFu) atomicExch(bad, 1);
+    const float sc = e8m0_to_f32(s);
+    const uint4 u = *reinterpret_cast<const uint4*>(blocks + i * 16);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float4* o = reinterpret_cast<float4*>(out + i * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float v[8];
+        e2m1x4_to_f32(w[q] & 0xffffu, v);
+        e2m1x4_to_f32(w[q] >> 16, v + 4);
+        o[2 * q] = make_float4(v[0] * sc, v[1] * sc, v[2] * sc, v[3] * sc);
+        o[2 * q + 1] = make_float4(v[4] * sc, v[5] * sc, v[6] * sc, v[7] * sc);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Router for one token. A cluster of 8 CTAs splits the experts (CTA r owns experts r, r+8, r+16, r+24); each CTA
+// reduces its logits and stores them straight into CTA 0's shared memory over DSMEM, then one warp of CTA 0 picks
+// the top k. Products bf16 x fp32 are exact in fp64 and the sum is kept in fp64, so the selected ids are the exact
+// ranking of the true logits: they agree with any float64 reference except for exact ties, which go to the lower
+// id (runtime/src/kernels.cu:307-324 states the same rule).
+constexpr int kRouterCluster = 8, kRouterThreads = 256, kRouterPerCta = 4;
+
+__device__ __forceinline__ void dsmem_store_f64(double* local_ptr, unsigned cta, double v) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local_ptr));
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(cta));
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(ra), "d"(v) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ double bf16_lo_d(uint32_t w) { return double(__uint_as_float(w << 16)); }
+__device__ __forceinline__ double bf16_hi_d(uint32_t w) { return double(__uint_as_float(w & 0xffff0000u)); }
+
+__global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouterThreads)
+    router_decode_kernel(const __nv_bfloat16* __restrict__ W, const float* __restrict__ b,
+                         const float* __restrict__ x, int E, int H, int k, int* __restrict__ ids,
+                         float* __restrict__ weights) {
+    __shared__ double red[kRouterThreads / 32][kRouterPerCta];
+    __shared__ double logits[32];
+    const unsigned r = cluster_rank();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H8 = H >> 3;
+    const uint4* Wv = reinterpret_cast<const uint4*>(W);
+    const float4* xv = reinterpret_cast<const float4*>(x);
+    double acc[kRouterPerCta] = {0.0, 0.0, 0.0, 0.0};
+    for (int c = tid; c < H8; c += kRouterThreads) {
+        const float4 xa = __ldg(xv + 2 * c), xb = __ldg(xv + 2 * c + 1);
+#pragma unroll
+        for (int q = 0; q < kRouterPerCta; ++q) {
+            const int e = int(r) + kRouterCluster * q;
+            if (e < E) {
+                const uint4 u = __ldg(Wv + size_t(e) * H8 + c);
+                double s = bf16_lo_d(u.x) * double(xa.x);
+                s = fma(bf16_hi_d(u.x), double(xa.y), s);
+                s = fma(bf16_lo_d(u.y), double(xa.z), s);
+                s = fma(bf16_hi_d(u.y), double(xa.w), s);
+                s = fma(bf16_lo_d(u.z), double(xb.x), s);
+                s = fma(bf16_hi_d(u.z), double(xb.y), s);
+                s = fma(bf16_lo_d(u.w), double(xb.z), s);
+                s = fma(bf16_hi_d(u.w), double(xb.w), s);
+                acc[q] += s;
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < kRouterPerCta; ++q) {
+        const double v = warp_sum(acc[q]);
+        if (lane == 0) red[warp][q] = v;
+    }
+    __syncthreads();
+    if (tid < kRouterPerCta) {
+        const int e = int(r) + kRouterCluster * tid;
+        if (e < E) {
+            double t = 0.0;
+            for (int w = 0; w < kRouterThreads / 32; ++w) t += red[w][tid];
+            dsmem_store_f64(&logits[e], 0, t + double(b[e]));
+        }
+    }
+    cluster_sync_all();
+    if (r != 0 || warp != 0) return;
+
+    // Lane i holds expert i; lanes >= E and already-picked experts carry -inf and an id >= 32, so real experts win
+    // ties against them. NaN never wins.
+    double v = lane < E ? logits[lane] : -INFINITY;
+    if (v != v) v = -INFINITY;
+    int id = lane < E ? lane : 32 + lane;
+    float sel = -INFINITY;
+    int sel_id = 0;
+    for (int j = 0; j < k; ++j) {
+        double best = v;
+        int besti = id;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const double ob = __shfl_xor_sync(kFull, best, o);
+            const int oi = __shfl_xor_sync(kFull, besti, o);
+            if (ob > best || (ob == best && oi < besti)) { best = ob; besti = oi; }
+        }
+        if (lane == j) { sel = float(best); sel_id = besti; }
+        if (id == besti) { v = -INFINITY; id = 32 + lane; }
+    }
+    const float top = __shfl_sync(kFull, sel, 0);
+    const float p = lane < k ? expf(sel - top) : 0.f;
+    const float sum = warp_sum(p);
+    if (lane < k) { ids[lane] = sel_id; weights[lane] = p / sum; }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// SIMT MXFP4 GEMV. Lane l of a warp owns blocks g = l, l+32, ... of every row it touches; the activation vector is
+// staged in shared memory transposed (element e of block g at [e][g]) so the 32 lanes read 32 consecutive words,
+// and each activation read is reused across the rows a warp processes together.
+constexpr int kSimtThreads = 256;
+
+template <int NB>
+__device__ __forceinline__ void stage_transposed(float* xs, const float* __restrict__ x, int n) {
+    constexpr int Gp = 32 * NB;
+    for (int i = threadIdx.x; i < 32 * Gp; i += blockDim.x) {
+        const int e = i / Gp, g = i % Gp;
+        const int src = g * 32 + e;
+        xs[i] = src < n ? x[src] : 0.f;
+    }
+}
+
+// Dot of one 16-byte MXFP4 block with 32 activations held in registers, unscaled.
+__device__ __forceinline__ float block_dot(const uint4 u, const float* xr) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float v[8];
+        e2m1x4_to_f32(w[q] & 0xffffu, v);
+        e2m1x4_to_f32(w[q] >> 16, v + 4);
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            acc = ffma2(make_float2(v[2 * t], v[2 * t + 1]), make_float2(xr[q * 8 + 2 * t], xr[q * 8 + 2 * t + 1]), acc);
+    }
+    return acc.x + acc.y;
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kSimtThreads) gateup_simt_kernel(const uint8_t* __restrict__ blocks,
+                                                                   const uint8_t* __restrict__ scales,
+                                                                   const float* __restrict__ bias,
+                                                                   const float* __restrict__ x,
+                                                                   const int* __restrict__ ids, float* __restrict__ a,
+                                                                   int k, int H, int I, float alpha, float limit) {
+    constexpr int Gp = 32 * NB;
+    extern __shared__ float xs[];                       // [32][Gp]
+    stage_transposed<NB>(xs, x, H);
+    __syncthreads();
+    const int G = H >> 5, lane = threadIdx.x & 31;
+    const int warp_g = blockIdx.x * (kSimtThreads / 32) + (threadIdx.x >> 5);
+    const int warp_n = gridDim.x * (kSimtThreads / 32);
+    const int half = I >> 1;                            // units of two outputs j = 2u, 2u+1 (four rows)
+    for (int u = warp_g; u < k * half; u += warp_n) {
+        const int slot = u / half, jp = u % half;
+        const int e = ids[slot];
+        const size_t row0 = size_t(e) * 2 * I + 4 * size_t(jp);
+        uint4 wv[4][NB];
+        uint32_t sv[4][NB];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int i = 0; i < NB; ++i) {
+                const int g = lane + 32 * i;
+                if (g < G) {
+                    wv[r][i] = ldg_stream(blocks + ((row0 + r) * G + g) * 16);
+                    sv[r][i] = scales[(row0 + r) * G + g];
+                }
+            }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+            const int g = lane + 32 * i;
+            if (g < G) {
+                float xr[32];
+#pragma unroll
+                for (int q = 0; q < 32; ++q) xr[q] = xs[q * Gp + g];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[r] = fmaf(block_dot(wv[r][i], xr), e8m0_to_f32(sv[r][i]), acc[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r] = warp_sum(acc[r]);
+        if (lane == 0) {
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                float gv = acc[2 * p] + bias[row0 + 2 * p], lv = acc[2 * p + 1] + bias[row0 + 2 * p + 1];
+                gv = fminf(gv, limit);                                   // glu: clamped from above only
+                lv = fminf(fmaxf(lv, -limit), limit);
+                a[size_t(slot) * I + 2 * jp + p] = gv / (1.f + expf(-alpha * gv)) * (lv + 1.f);
+            }
+        }
+    }
+    pdl_launch_dependents();
+}
+
+template <int NB, int KC>
+__global__ void __launch_bounds__(kSimtThreads) down_simt_kernel(const uint8_t* __restrict__ blocks,
+                                                                 const uint8_t* __restrict__ scales,
+                                                                 const float* __restrict__ bias,
+                                                                 const float* __restrict__ a,
+                                                                 const int* __restrict__ ids,
+                                                                 const float* __restrict__ weights,
+                                                                 float* __restrict__ x_resid, int k, int H, int I) {
+    constexpr int Gp = 32 * NB;
+    extern __shared__ float as[];                       // [k][32][Gp]
+    pdl_wait();                                         // a[] comes from the gate/up kernel
+    for (int s = 0; s < k; ++s) stage_transposed<NB>(as + size_t(s) * 32 * Gp, a + size_t(s) * I, I);
+    __syncthreads();
+    const int G = I >> 5, lane = threadIdx.x & 31;
+    const int warp_g = blockIdx.x * (kSimtThreads / 32) + (threadIdx.x >> 5);
+    const int warp_n = gridDim.x * (kSimtThreads / 32);
+    for (int rp = warp_g; rp < (H >> 1); rp += warp_n) {
+        float add[2] = {0.f, 0.f};
+        for (int s0 = 0; s0 < k; s0 += KC) {
+            uint4 wv[KC][2][NB];
+            uint32_t sv[KC][2][NB];
+#pragma unroll
+            for (int c = 0; c < KC; ++c) {
+                if (s0 + c < k) {
+                    const size_t row0 = size_t(ids[s0 + c]) * H + 2 * size_t(rp);
+#pragma unroll
+                    for (int r = 0; r < 2; ++r)
+#pragma unroll
+                        for (int i = 0; i < NB; ++i) {
+                            const int g = lane + 32 * i;
+                            if (g < G) {
+                                wv[c][r][i] = ldg_stream(blocks + ((row0 + r) * G + g) * 16);
+                                sv[c][r][i] = scales[(row0 + r) * G + g];
+                            }
+                        }
+                }
+            }
+            float acc[KC][2];
+#pragma unroll
+            for (int c = 0; c < KC; ++c) acc[c][0] = acc[c][1] = 0.f;
+#pragma unroll
+            for (int c = 0; c < KC; ++c) {
+                if (s0 + c < k) {
+                    const float* asl = as + size_t(s0 + c) * 32 * Gp;
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) {
+                        const int g = lane + 32 * i;
+                        if (g < G) {
+                            float xr[32];
+#pragma unroll
+                            for (int q = 0; q < 32; ++q) xr[q] = asl[q * Gp + g];
+#pragma unroll
+                            for (int r = 0; r < 2; ++r)
+                                acc[c][r] = fmaf(block_dot(wv[c][r][i], xr), e8m0_to_f32(sv[c][r][i]), acc[c][r]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < KC; ++c) {
+                const float y0 = warp_sum(acc[c][0]), y1 = warp_sum(acc[c][1]);
+                if (s0 + c < k && lane == 0) {
+                    const size_t rb = size_t(ids[s0 + c]) * H + 2 * size_t(rp);
+                    const float w = weights[s0 + c];
+                    add[0] += w * (y0 + bias[rb]);                       // slot order, as the reference combines
+                    add[1] += w * (y1 + bias[rb + 1]);
+                }
+            }
+        }
+        if (lane == 0) {
+            x_resid[2 * rp] += add[0];
+            x_resid[2 * rp + 1] += add[1];
+        }
+    }
+}
+
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    GPT_CHECK(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
+template <int NB>
+void moe_simt_nb(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias, const uint8_t* dn_blocks,
+                 const uint8_t* dn_scales, const float* dn_bias, const float* x_norm, const int* ids,
+                 const float* weights, float* x_resid, int k, int H, int I, float alpha, float limit, float* a,
+                 cudaStream_t s, void* mid_event) {
+    constexpr int Gp = 32 * NB;
+    const int sms = num_sms();
+    const size_t smem_gu = size_t(32) * Gp * sizeof(float);
+    const int units = k * (I / 2);
+    const int grid_gu = std::max(1, std::min(sms * 4, (units + 7) / 8));
+    gateup_simt_kernel<NB><<<grid_gu, kSimtThreads, smem_gu, s>>>(gu_blocks, gu_scales, gu_bias, x_norm, ids, a, k,
+                                                                   H, I, alpha, limit);
+    check_launch("moe gate/up (simt)");
+    if (mid_event) GPT_CHECK(cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s));
+    const size_t smem_dn = size_t(k) * 32 * Gp * sizeof(float);
+    const int grid_dn = std::max(1, std::min(sms * 2, (H / 2 + 7) / 8));
+    auto kern = down_simt_kernel<NB, 4>;
+    GPT_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_dn)));
+    launch_pdl(kern, dim3(grid_dn), dim3(kSimtThreads), smem_dn, s, true, dn_blocks, dn_scales, dn_bias,
+               (const float*)a, ids, weights, x_resid, k, H, I);
+    check_launch("moe down (simt)");
+}
+
+}  // namespace
+
+void launch_rmsnorm(const float* x, const float* w, float* y, int T, int n, float eps, cudaStream_t s) {
+    require(T >= 1 && n >= 1, "rmsnorm: T and n must be positive");
+    rmsnorm_kernel<<<T, 1024, 0, s>>>(x, w, y, n, eps);
+    check_launch("rmsnorm");
+}
+
+void launch_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, float* out, long long n_blocks, int* bad,
+                          cudaStream_t s) {
+    require(n_blocks >= 0, "mxfp4_dequant: n_blocks must be >= 0");
+    if (n_blocks == 0) return;
+    const long long grid = (n_blocks + 255) / 256;
+    require(grid < (1LL << 31), "mxfp4_dequant: too many blocks");
+    mxfp4_dequant_kernel<<<unsigned(grid), 256, 0, s>>>(blocks, scales, out, n_blocks, bad);
+    check_launch("mxfp4_dequant");
+}
+
+void launch_router_decode(const __nv_bfloat16* W, const float* b, const float* x, int E, int H, int k, int* ids,
+                          float* weights, cudaStream_t s) {
+    if (E < 1 || E > 32 || k < 1 || k > 8 || k > E || H % 8 || H < 8)
+        throw std::runtime_error("router: unsupported shape (need 1 <= k <= 8, k <= E <= 32, H % 8 == 0)");
+    router_decode_kernel<<<kRouterCluster, kRouterThreads, 0, s>>>(W, b, x, E, H, k, ids, weights);
+    check_launch("router");
+}
+
+size_t moe_decode_scratch_bytes(int k, int I) { return size_t(k) * size_t(I) * sizeof(float); }
+
+void launch_moe_decode_simt(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                            const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                            const float* x_norm, const int* ids, const float* weights, float* x_resid, int k,
+                            int H, int I, float alpha, float limit, void* scratch, cudaStream_t s,
+                            void* mid_event) {
+    if (k < 1 || k > 8) throw std::runtime_error("moe: k must be in 1..8");
+    if (H % 32 || I % 32 || H < 32 || I < 32) throw std::runtime_error("moe: H and I must be positive multiples of 32");
+    const int G = std::max(H, I) / 32;
+    float* a = static_cast<float*>(scratch);
+    if (G <= 32)
+        moe_simt_nb<1>(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
+                       H, I, alpha, limit, a, s, mid_event);
+    else if (G <= 64)
+        moe_simt_nb<2>(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
+                       H, I, alpha, limit, a, s, mid_event);
+    else if (G <= 96)
+        moe_simt_nb<3>(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
+                       H, I, alpha, limit, a, s, mid_event);
+    else
+        throw std::runtime_error("moe: H and I must be at most 3072");
+}
+
+}  // namespace gpt

@@ -1,0 +1,95 @@
+/* C ABI of the B200-native gpt-oss MXFP4 MoE path.
+ *
+ * Drop-in for openvang/gptoss-infer's runtime/include/gptoss/gptoss.h: every function of that header is declared
+ * here with the same signature, the same argument meaning and the same error convention (0 on success, -1 on
+ * failure with the message in gptoss_last_error(), a thread-local string; exceptions never cross the ABI). Kernel
+ * entry points take caller-owned DEVICE pointers and synchronize the device before returning, as the reference's
+ * do (reference capi.cpp:34-37). Not thread-safe: use one engine per thread.
+ *
+ * Functions marked [extension] do not exist in the reference; they are additive.
+ */
+#ifndef GPTOSS_H
+#define GPTOSS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct gptoss_engine gptoss_engine;
+
+/* ---- Engine lifecycle and decode (reference gptoss.h:14-42) ------------------------------------------------ */
+
+/* Loads the checkpoint in model_dir onto the current CUDA device; returns NULL on failure (reference gptoss.h:14-17).
+ * vram_budget_bytes > 0 caps the engine's own device allocations. */
+gptoss_engine* gptoss_create(const char* model_dir, int max_ctx, long long vram_budget_bytes);
+void gptoss_destroy(gptoss_engine* e);                                   /* reference gptoss.h:18 */
+const char* gptoss_last_error(void);                                     /* reference gptoss.h:19 */
+int gptoss_vocab(const gptoss_engine* e);                                /* reference gptoss.h:21 */
+int gptoss_position(const gptoss_engine* e);                             /* reference gptoss.h:22 */
+long long gptoss_device_bytes(const gptoss_engine* e);                   /* reference gptoss.h:23 */
+int gptoss_reset(gptoss_engine* e);                                      /* reference gptoss.h:25 */
+int gptoss_use_graph(gptoss_engine* e, int on);                          /* reference gptoss.h:26 */
+int gptoss_step(gptoss_engine* e, int token);                            /* reference gptoss.h:27-28 */
+int gptoss_logits(gptoss_engine* e, float* out);                         /* reference gptoss.h:29 */
+int gptoss_prefill(gptoss_engine* e, const int32_t* tokens, int n, const int32_t* ids, int k, float* lp,
+                   int32_t* argmax, float* target_lp);                   /* reference gptoss.h:30-35 */
+int gptoss_score(gptoss_engine* e, const int32_t* ids, int k, int target, float* lp, int32_t* argmax,
+                 float* target_lp, float* lse);                          /* reference gptoss.h:36-38 */
+int gptoss_set_position(gptoss_engine* e, int pos);                      /* reference gptoss.h:40-41 */
+int gptoss_bench_steps(gptoss_engine* e, int token, int n);              /* reference gptoss.h:42 */
+
+/* ---- Kernel entry points (reference gptoss.h:44-58). Device pointers; each call synchronizes. ------------- */
+
+int gptoss_kernel_gemv_bf16(const void* W, const float* x, const float* bias, const float* resid, float* y, int N,
+                            int K);                                      /* reference gptoss.h:45-46 */
+/* y = x * rsqrt(mean(x^2) + eps) * w over n floats (reference gptoss.h:47). */
+int gptoss_kernel_rmsnorm(const float* x, const float* w, float* y, int n, float eps);
+int gptoss_kernel_rope_append(float* qkv, const float* cos_t, const float* sin_t, int pos, void* k_cache,
+                              void* v_cache, int window);                /* reference gptoss.h:48-49 */
+int gptoss_kernel_attention(const float* q, const void* k_cache, const void* v_cache, const float* sinks, int pos,
+                            int window, int max_ctx, float* out);        /* reference gptoss.h:50-51 */
+/* Router for one token (reference gptoss.h:52-53): logits = W[E,H] (bf16) x + b; ids = top-k sorted by logit
+ * descending, ties to the lower expert id; weights = softmax over the k selected logits. 1 <= k <= 8, k <= E <= 32,
+ * H % 8 == 0; anything else returns -1 (k > E included). */
+int gptoss_kernel_router(const void* W, const float* b, const float* x, int E, int H, int k, int32_t* ids,
+                         float* weights);
+/* x_resid += sum_e w[e] * (W2[ids[e]] swiglu(W1[ids[e]] x_norm + b1) + b2)   (reference gptoss.h:54-58)
+ * gu_blocks uint8 [E, 2I, H/32, 16], gu_scales uint8 [E, 2I, H/32], gu_bias fp32 [E, 2I],
+ * dn_blocks uint8 [E, H, I/32, 16], dn_scales uint8 [E, H, I/32], dn_bias fp32 [E, H]; gate/up rows interleaved
+ * (even = glu, clamped above at limit; odd = linear, clamped to [-limit, limit]). */
+int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                      const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias, const float* x_norm,
+                      const int32_t* ids, const float* weights, float* x_resid, int k, int H, int I, float alpha,
+                      float limit);
+
+/* ---- [extension] MoE-path entry points with no counterpart in the reference ------------------------------- */
+
+/* [extension] Bit-exact MXFP4 decode of n_blocks blocks (16 bytes + 1 E8M0 scale each) into out[n_blocks * 32]
+ * fp32, element 2j from the low nibble of byte j. Restates reference/gptoss_ref/mxfp4.py:17-31 on the GPU: returns
+ * -1 if any scale is 0xFF (NaN in the OCP MX spec), as the reference's dequant raises. */
+int gptoss_kernel_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, float* out, long long n_blocks);
+
+/* [extension] One MoE block for one token, asynchronous: h = RMSNorm(x; norm_w, eps), router (W bf16 [E,H],
+ * b fp32 [E]) as gptoss_kernel_router, then x_resid += MoE(h) as gptoss_kernel_moe. x_resid may alias x (the
+ * residual stream). Runs on `stream` (a cudaStream_t; NULL = legacy default stream) and returns without
+ * synchronizing; launch errors are reported, device faults surface at the caller's next synchronization.
+ * `events`, if not NULL, points to 4 cudaEvent_t recorded before the router, before the gate/up GEMV, before the
+ * down GEMV and after it (for per-kernel timing). Uses the calling thread's workspace: calls from one thread on
+ * different streams must not overlap. Same expert layouts as gptoss_kernel_moe. */
+int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const void* router_w,
+                           const float* router_b, const uint8_t* gu_blocks, const uint8_t* gu_scales,
+                           const float* gu_bias, const uint8_t* dn_blocks, const uint8_t* dn_scales,
+                           const float* dn_bias, float* x_resid, int E, int k, int H, int I, float alpha, float limit,
+                           void* stream, void* const* events);
+
+/* [extension] Which decode MoE implementation gptoss_kernel_moe uses: 0 = SIMT (CUDA cores), 1 = tensor cores
+ * (tcgen05 block-scaled MMA) where the shape allows it. Returns the previous setting, or -1. */
+int gptoss_set_moe_impl(int impl);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPTOSS_H */

@@ -1,0 +1,216 @@
+"""GPU parity tests through the C ABI (ctypes, device pointers), against the CPU oracle and the reference-made golden
+vectors. Mirrors openvang/gptoss-infer runtime/tests/test_kernels.py:129-174 (router, real-shape MoE) and adds the
+bit-exact MXFP4 decode, the config-0 block, and the tensor-core path.
+
+Tolerances (stated here, used below):
+  * MXFP4 decode, expert ids: bit-exact.
+  * router weights: rtol 1e-5, atol 1e-6 vs float64 (the reference test's bound).
+  * gptoss_kernel_moe vs float64: rtol 1e-4, atol 1e-3 (runtime/tests/test_kernels.py:174), and additionally
+    max-abs <= 2e-5 * max|ref| and rel-L2 <= 2e-5 (fp32 accumulation-order noise only).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, tiny_tensors
+from gptoss_b200 import capi, synth
+from oracle import moe as omoe
+from oracle import mxfp4
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+P = capi.ptr
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return capi.load()
+
+
+def ok(lib, rc):
+    assert rc == 0, lib.gptoss_last_error().decode()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def rel_err(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return np.abs(got - want).max() / max(np.abs(want).max(), 1e-30), \
+        np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+
+
+# ---------------------------------------------------------------------------------------------------- dequant
+def test_mxfp4_dequant_bitexact(lib):
+    g = torch.Generator().manual_seed(5)
+    n = 4096
+    blocks = torch.randint(0, 256, (n, 16), generator=g, dtype=torch.uint8).numpy()
+    scales = torch.randint(0, 255, (n,), generator=g, dtype=torch.uint8).numpy()
+    scales[:255] = np.arange(255, dtype=np.uint8)                     # every valid scale, 0 and 254 included
+    blocks[:16] = (np.arange(256, dtype=np.uint8).reshape(16, 16))    # every byte value
+    db, ds = dev(blocks), dev(scales)
+    out = torch.empty(n * 32, device=DEV)
+    ok(lib, lib.gptoss_kernel_mxfp4_dequant(P(db), P(ds), P(out), n))
+    want = mxfp4.dequant(blocks.reshape(n, 1, 16), scales.reshape(n, 1)).reshape(-1)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_mxfp4_dequant_golden_and_nan_rejection(lib):
+    g = load_golden("mxfp4_kat.npz")
+    b, s = g["rand_blocks"].reshape(-1, 16), g["rand_scales"].reshape(-1)
+    out = torch.empty(b.shape[0] * 32, device=DEV)
+    ok(lib, lib.gptoss_kernel_mxfp4_dequant(P(dev(b)), P(dev(s)), P(out), b.shape[0]))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), g["rand_out"].reshape(-1).view(np.uint32))
+    bad = dev(np.array([127, 255], np.uint8))
+    assert lib.gptoss_kernel_mxfp4_dequant(P(dev(b[:2])), P(bad), P(out), 2) == -1
+    assert b"0xFF" in lib.gptoss_last_error()
+
+
+# ---------------------------------------------------------------------------------------------------- rmsnorm
+def test_rmsnorm(lib):
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    x, w = torch.randn(2880, device=DEV, generator=gen) * 3, torch.randn(2880, device=DEV, generator=gen)
+    y = torch.empty_like(x)
+    ok(lib, lib.gptoss_kernel_rmsnorm(P(x), P(w), P(y), 2880, 1e-5))
+    xd = x.double()
+    torch.testing.assert_close(y.double(), xd * torch.rsqrt(xd.pow(2).mean() + 1e-5) * w.double(), rtol=1e-5,
+                               atol=1e-6)
+
+
+# ---------------------------------------------------------------------------------------------------- router
+@pytest.mark.parametrize("E,k", [(32, 4), (32, 8), (6, 4), (1, 1), (17, 3)])
+def test_router(lib, E, k):
+    """runtime/tests/test_kernels.py:263-279, with the engineered tie: experts 1 and E-1 tie, the lower id wins."""
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    W = (torch.randn(E, 2880, device=DEV, generator=gen) * 0.05).to(torch.bfloat16)
+    b, x = torch.randn(E, device=DEV, generator=gen) * 0.1, torch.randn(2880, device=DEV, generator=gen)
+    if E > 2:
+        b[1] += 10
+        W[E - 1], b[E - 1] = W[1], b[1]
+    ids = torch.empty(k, device=DEV, dtype=torch.int32)
+    w = torch.empty(k, device=DEV)
+    ok(lib, lib.gptoss_kernel_router(P(W), P(b), P(x), E, 2880, k, P(ids), P(w)))
+    logits = (W.double() @ x.double() + b.double()).tolist()
+    want = sorted(range(E), key=lambda e: (-logits[e], e))[:k]
+    assert ids.tolist() == want
+    v = torch.tensor([logits[e] for e in want], dtype=torch.float64)
+    torch.testing.assert_close(w.double().cpu(), torch.softmax(v, 0), rtol=1e-5, atol=1e-6)
+    assert lib.gptoss_kernel_router(P(W), P(b), P(x), E, 2880, E + 1, P(ids), P(w)) != 0   # k > E is rejected
+
+
+def test_router_many_tokens_exact_ids(lib):
+    """512 random tokens at config-0 router statistics: ids equal the float64 ranking on every token."""
+    t = synth.moe_layer(seed=21, E=32)
+    Wt = t["model.layers.0.mlp.router.weight"]
+    bt = t["model.layers.0.mlp.router.bias"].float()
+    W, b = Wt.to(DEV), bt.to(DEV)
+    X = synth.tokens(512, seed=22)
+    ids = torch.empty(4, device=DEV, dtype=torch.int32)
+    w = torch.empty(4, device=DEV)
+    got = []
+    for r in range(X.shape[0]):
+        x = X[r].to(DEV)
+        ok(lib, lib.gptoss_kernel_router(P(W), P(b), P(x), 32, 2880, 4, P(ids), P(w)))
+        got.append(ids.cpu().numpy().copy())
+    logits = X.double().numpy() @ Wt.double().numpy().T + bt.double().numpy()
+    want = omoe.topk_ids(logits, 4)
+    assert np.array_equal(np.stack(got), want)
+
+
+# ---------------------------------------------------------------------------------------------------- moe
+def real_shape_case(E=6, seed=4):
+    """runtime/tests/test_kernels.py:282-294: real H = I = 2880, E experts, ids [5, 0, 3, 2]."""
+    g = torch.Generator().manual_seed(seed)
+    H = I = 2880
+    k = 4
+    gu_b = torch.randint(0, 256, (E, 2 * I, H // 32, 16), generator=g, dtype=torch.uint8)
+    gu_s = torch.randint(118, 124, (E, 2 * I, H // 32), generator=g, dtype=torch.uint8)
+    dn_b = torch.randint(0, 256, (E, H, I // 32, 16), generator=g, dtype=torch.uint8)
+    dn_s = torch.randint(118, 124, (E, H, I // 32), generator=g, dtype=torch.uint8)
+    gu_bias, dn_bias = torch.randn(E, 2 * I, generator=g) * 0.1, torch.randn(E, H, generator=g) * 0.1
+    x = torch.randn(H, generator=g)
+    resid = torch.randn(H, generator=g)
+    ids = torch.tensor([5, 0, 3, 2], dtype=torch.int32)
+    weights = torch.softmax(torch.randn(k, generator=g), 0)
+    return [gu_b, gu_s, gu_bias, dn_b, dn_s, dn_bias, x, ids, weights], resid, H, I, k
+
+
+@pytest.mark.parametrize("impl", [0, 1])
+def test_moe_real_shape(lib, impl):
+    args, resid, H, I, k = real_shape_case()
+    want = omoe.kernel_moe_f64(*[a.numpy() for a in args[:6]], args[6].numpy(), args[7].numpy(), args[8].numpy(),
+                               resid.numpy())
+    d = [t.to(DEV).contiguous() for t in args]
+    out = resid.to(DEV).clone()
+    prev = lib.gptoss_set_moe_impl(impl)
+    try:
+        ok(lib, lib.gptoss_kernel_moe(*(P(t) for t in d), P(out), k, H, I, 1.702, 7.0))
+    finally:
+        lib.gptoss_set_moe_impl(prev)
+    got = out.cpu().double().numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
+    mx, l2 = rel_err(got - resid.double().numpy(), want - resid.double().numpy())
+    assert mx <= 2e-5 and l2 <= 2e-5, (mx, l2)
+
+
+def test_moe_tiny_golden(lib):
+    """Reference.moe on the tiny layer (H=64, I=32, 8 experts), one token at a time through the two ABI calls."""
+    g = load_golden("tiny_moe.npz")
+    t = tiny_tensors(g)
+    p = "model.layers.0.mlp."
+    W = torch.from_numpy(t[p + "router.weight"]).to(torch.bfloat16).to(DEV)
+    b = dev(t[p + "router.bias"])
+    ex = [dev(t[p + "experts." + n]) for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias",
+                                               "down_proj_blocks", "down_proj_scales", "down_proj_bias")]
+    ids = torch.empty(4, device=DEV, dtype=torch.int32)
+    w = torch.empty(4, device=DEV)
+    for r in range(g["h"].shape[0]):
+        h = dev(g["h"][r])
+        ok(lib, lib.gptoss_kernel_router(P(W), P(b), P(h), 8, 64, 4, P(ids), P(w)))
+        assert ids.cpu().numpy().tolist() == g["top_idx"][r].tolist()
+        out = torch.zeros(64, device=DEV)
+        ok(lib, lib.gptoss_kernel_moe(*(P(e) for e in ex), P(h), P(ids), P(w), P(out), 4, 64, 32, 1.702, 7.0))
+        mx, l2 = rel_err(out.cpu().numpy(), g["out"][r])
+        assert mx <= 2e-5 and l2 <= 2e-5, (r, mx, l2)
+
+
+@pytest.fixture(scope="module")
+def config0():
+    t = synth.moe_layer(seed=0)
+    g = load_golden("config0_moe.npz")
+    assert synth.digest(t) == str(g["weights_sha256"])
+    p = "model.layers.0."
+    d = {
+        "ln": t[p + "post_attention_layernorm.weight"].float().to(DEV),
+        "W": t[p + "mlp.router.weight"].to(DEV), "b": t[p + "mlp.router.bias"].float().to(DEV),
+        "ex": [t[p + "mlp.experts." + n].to(DEV).float() if n.endswith("bias") else t[p + "mlp.experts." + n].to(DEV)
+               for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias",
+                         "down_proj_blocks", "down_proj_scales", "down_proj_bias")],
+    }
+    return d, g
+
+
+@pytest.mark.parametrize("impl", [0, 1])
+def test_config0_block_vs_reference_golden(lib, config0, impl):
+    """RMSNorm -> router -> MoE for each of the 4 golden tokens, against Reference.moe's own output."""
+    d, g = config0
+    ids = torch.empty(4, device=DEV, dtype=torch.int32)
+    w = torch.empty(4, device=DEV)
+    prev = lib.gptoss_set_moe_impl(impl)
+    try:
+        for r in range(g["x"].shape[0]):
+            x = dev(g["x"][r])
+            h = torch.empty_like(x)
+            ok(lib, lib.gptoss_kernel_rmsnorm(P(x), P(d["ln"]), P(h), 2880, 1e-5))
+            np.testing.assert_allclose(h.cpu().numpy(), g["h"][r], rtol=1e-5, atol=1e-6)
+            hg = dev(g["h"][r])                              # feed the golden h so routing sees the same input
+            ok(lib, lib.gptoss_kernel_router(P(d["W"]), P(d["b"]), P(hg), 32, 2880, 4, P(ids), P(w)))
+            assert ids.cpu().numpy().tolist() == g["top_idx"][r].tolist()
+            out = torch.zeros(2880, device=DEV)
+            ok(lib, lib.gptoss_kernel_moe(*(P(e) for e in d["ex"]), P(hg), P(ids), P(w), P(out), 4, 2880, 2880,
+                                          1.702, 7.0))
+            mx, l2 = rel_err(out.cpu().numpy(), g["out"][r])
+            assert mx <= 2e-5 and l2 <= 2e-5, (r, mx, l2)
+    finally:
+        lib.gptoss_set_moe_impl(prev)

@@ -45,19 +45,33 @@ __device__ __forceinline__ float e8m0_to_f32(uint32_t s) {
     return s == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(s << 23);
 }
 
-// One byte of two e2m1 codes (low nibble = even element) -> two floats, via the sm_100 e2m1x2 converter. Every e2m1
-// value is exact in f16 and in f32, so this is lossless.
-__device__ __forceinline__ void e2m1x4_to_f32(uint32_t word16, float* out4) {
-    uint32_t h01, h23;
-    asm("{\n\t.reg .b8 b0, b1;\n\t"
-        "mov.b16 {b0, b1}, %2;\n\t"
+// One 32-bit word of eight e2m1 codes (byte j: low nibble = element 2j) -> eight floats, via the sm_100 e2m1x2
+// converter. The word is unpacked inside the asm from a full 32-bit register: feeding a 16-bit view of a wider
+// register (e.g. (unsigned short)(w >> 16)) was miscompiled into reading the wrong byte. Every e2m1 value is exact in
+// f16 and f32, so this is lossless.
+__device__ __forceinline__ void e2m1x8_to_f32(uint32_t word, float* out8) {
+    uint32_t h[4];
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
         "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t}"
-        : "=r"(h01), "=r"(h23)
-        : "h"((unsigned short)word16));
-    const float2 a = __half22float2(*reinterpret_cast<__half2*>(&h01));
-    const float2 b = __half22float2(*reinterpret_cast<__half2*>(&h23));
-    out4[0] = a.x; out4[1] = a.y; out4[2] = b.x; out4[3] = b.y;
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+        : "r"(word));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
+        out8[2 * i] = f.x;
+        out8[2 * i + 1] = f.y;
+    }
+}
+
+// Exact e2m1 decode by bit construction, no converter involved: the 3 magnitude bits placed at fp32 bits 22-24 give
+// 2^-126 * value (code 1 lands on the subnormal 2^-127 = 2^-126 * 0.5), the sign bit goes to bit 31, and one multiply
+// by 2^126 rescales exactly. Needs IEEE subnormals (no flush-to-zero), which this build keeps.
+__device__ __forceinline__ float e2m1_exact(uint32_t nib) {
+    return __uint_as_float(((nib & 7u) << 22) | ((nib & 8u) << 28)) * 0x1p126f;
 }
 
 // Packed fp32x2 FMA (sm_100): d = a * b + c, two lanes at once.

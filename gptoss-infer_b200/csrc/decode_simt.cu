@@ -60,10 +60,10 @@ __global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks, const u
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         float v[8];
-        e2m1x4_to_f32(w[q] & 0xffffu, v);
-        e2m1x4_to_f32(w[q] >> 16, v + 4);
-        o[2 * q] = make_float4(v[0] * sc, v[1] * sc, v[2] * sc, v[3] * sc);
-        o[2 * q + 1] = make_float4(v[4] * sc, v[5] * sc, v[6] * sc, v[7] * sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = e2m1_exact(w[q] >> (4 * j)) * sc;
+        o[2 * q] = make_float4(v[0], v[1], v[2], v[3]);
+        o[2 * q + 1] = make_float4(v[4], v[5], v[6], v[7]);
     }
 }
 
@@ -190,8 +190,7 @@ __device__ __forceinline__ float block_dot(const uint4 u, const float* xr) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         float v[8];
-        e2m1x4_to_f32(w[q] & 0xffffu, v);
-        e2m1x4_to_f32(w[q] >> 16, v + 4);
+        e2m1x8_to_f32(w[q], v);
 #pragma unroll
         for (int t = 0; t < 4; ++t)
             acc = ffma2(make_float2(v[2 * t], v[2 * t + 1]), make_float2(xr[q * 8 + 2 * t], xr[q * 8 + 2 * t + 1]), acc);

@@ -62,6 +62,10 @@ def load(path=None):
     lib.gptoss_last_error.restype = ctypes.c_char_p
     lib.gptoss_last_error.argtypes = []
     for name, (args, res) in SIGNATURES.items():
+        if not hasattr(lib, name):
+            if path == DEFAULT_LIB:
+                raise AttributeError(f"{path} does not export {name}")
+            continue                      # another library of the same ABI (e.g. the reference's) may lack extensions
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = res

@@ -169,6 +169,15 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
     });
 }
 
+int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
+                              const uint8_t* b_scales, float* d, int N, int K) {
+    return guard([&] {
+        const size_t bytes = size_t(1) << 22;
+        void* scratch = g_scratch.get(bytes);
+        gpt::selftest_mxf4_gemm(a_blocks, a_scales, b_blocks, b_scales, d, N, K, scratch, bytes, nullptr);
+    });
+}
+
 int gptoss_set_moe_impl(int impl) {
     if (impl != 0 && impl != 1) {
         g_error = "gptoss_set_moe_impl: impl must be 0 (SIMT) or 1 (tensor cores)";

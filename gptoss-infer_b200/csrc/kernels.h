@@ -33,4 +33,15 @@ void launch_moe_decode_simt(const uint8_t* gu_blocks, const uint8_t* gu_scales, 
                             int H, int I, float alpha, float limit, void* scratch, cudaStream_t s,
                             void* mid_event = nullptr);
 
+// Scale-factor repack: raw E8M0 bytes [mats][rows][G] -> tcgen05 chunks [mats][ceil(rows/128)][ceil(G/4)][512],
+// chunk byte (r % 32) * 16 + (r / 32) * 4 + kb for row r and k-block kb of the chunk; zero padded.
+size_t sf_repacked_bytes(long long mats, int rows, int G);
+void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s);
+
+// Single-CTA tcgen05 kind::mxf4 GEMM, D[128][N] = dequant(A)[128][K] . dequant(B)[N][K]^T, from raw MXFP4 arrays
+// (checkpoint layout). Pins the layout conventions of the tensor-core kernels. Synchronizes.
+void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
+                        const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
+                        cudaStream_t s);
+
 }  // namespace gpt

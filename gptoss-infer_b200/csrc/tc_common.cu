@@ -1,0 +1,230 @@
+// Tensor-core support shared by the decode and prefill paths: TMA tensor maps, the scale-factor repack into the
+// tcgen05 chunk layout, and a single-CTA block-scaled GEMM self-test that pins every layout convention the real
+// kernels rely on (operand swizzle, descriptor fields, scale-factor placement, accumulator readback).
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+#include "tma.h"
+
+namespace gpt {
+
+// ---------------------------------------------------------------------------------------------------- TMA maps
+namespace {
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+}  // namespace
+
+CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                               uint32_t box_rows) {
+    require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+    require(row_bytes % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+    require(box_bytes <= 128 && box_bytes % 16 == 0 && box_rows >= 1 && box_rows <= 256, "bad TMA box");
+    CUtensorMap m;
+    std::memset(&m, 0, sizeof(m));
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_bytes, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+    return m;
+}
+
+// ---------------------------------------------------------------------------------------------------- SF repack
+namespace {
+// raw [mats][rows][G] E8M0 bytes -> [mats][RT][KT][512] tcgen05 chunks (RT = ceil(rows/128), KT = ceil(G/4)), zero
+// padded. One thread per output word of 4 bytes (one row's 4 k-blocks).
+__global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, long long mats, int rows,
+                                 int G, int RT, int KT) {
+    const long long words = mats * RT * KT * 128;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int w = int(i % 128);                  // word within the chunk: (row % 32) * 4 + row / 32
+        long long c = i / 128;
+        const int kt = int(c % KT);
+        c /= KT;
+        const int rt = int(c % RT);
+        const long long mat = c / RT;
+        const int row = rt * 128 + (w & 3) * 32 + (w >> 2);
+        uint32_t v = 0;
+        if (row < rows) {
+            const uint8_t* src = raw + (mat * rows + row) * G;
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+                const int g = kt * 4 + kb;
+                if (g < G) v |= uint32_t(src[g]) << (8 * kb);
+            }
+        }
+        reinterpret_cast<uint32_t*>(out)[i] = v;
+    }
+}
+}  // namespace
+
+size_t sf_repacked_bytes(long long mats, int rows, int G) {
+    return size_t(mats) * size_t((rows + 127) / 128) * size_t((G + 3) / 4) * 512;
+}
+
+void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s) {
+    const int RT = (rows + 127) / 128, KT = (G + 3) / 4;
+    const long long words = mats * RT * KT * 128;
+    const int grid = int(std::min<long long>((words + 255) / 256, num_sms() * 8LL));
+    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT);
+    check_launch("repack_sf");
+}
+
+// ---------------------------------------------------------------------------------------------------- self-test
+namespace {
+__global__ void __launch_bounds__(128) mxf4_selftest_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                            const uint8_t* __restrict__ sfa,
+                                                            const uint8_t* __restrict__ bimg,
+                                                            const uint8_t* __restrict__ sfb, float* __restrict__ out,
+                                                            int N, int K, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = (K + 255) / 256, KT = (K + 127) / 128, nB = N > 128 ? 2 : 1;
+    uint8_t* sA = smem;                                      // S x 16384
+    uint8_t* sB = sA + S * 16384;                            // S x N*128
+    uint8_t* sSFA = sB + S * N * 128;                        // KT x 512
+    uint8_t* sSFB = sSFA + KT * 512;                         // KT x nB x 512
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + KT * nB * 512);   // S full + 1 done
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + S + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+
+    if (tid == 0) {
+        for (int s = 0; s <= S; ++s) tc::mbar_init(&bars[s], 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(holder, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tm = *holder;
+    const uint32_t tm_d = tm, tm_sfa = tm + 256, tm_sfb = tm + 256 + 4 * KT;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            const int kt0 = 2 * s, nkt = min(2, KT - kt0);
+            const uint32_t bytes = 16384 + N * 128 + nkt * 512 + nkt * nB * 512;
+            tc::mbar_arrive_expect_tx(&bars[s], bytes);
+            tc::tma_load_2d(sA + s * 16384, &tmA, s * 128, 0, &bars[s]);
+            tc::bulk_g2s(sB + s * N * 128, bimg + size_t(s) * N * 128, N * 128, &bars[s]);
+            tc::bulk_g2s(sSFA + kt0 * 512, sfa + size_t(kt0) * 512, nkt * 512, &bars[s]);
+            tc::bulk_g2s(sSFB + kt0 * nB * 512, sfb + size_t(kt0) * nB * 512, nkt * nB * 512, &bars[s]);
+        }
+        bool ok = true;
+        for (int s = 0; s < S && ok; ++s) {
+            ok = tc::mbar_wait(&bars[s], 0, err, 1);
+            if (!ok) break;
+            tc::tc_fence_after();
+            for (int kt2 = 0; kt2 < 2; ++kt2) {
+                const int kt = 2 * s + kt2;
+                if (kt >= KT) break;
+                tc::tmem_cp_sf(tm_sfa + 4 * kt, tc::desc_sf_chunk(tc::smem_u32(sSFA + kt * 512)));
+                for (int b = 0; b < nB; ++b)
+                    tc::tmem_cp_sf(tm_sfb + 4 * (kt * nB + b), tc::desc_sf_chunk(tc::smem_u32(sSFB + (kt * nB + b) * 512)));
+                for (int j = 0; j < 2; ++j) {
+                    const int kk = kt * 128 + j * 64;
+                    if (kk >= K) break;
+                    const uint64_t ad = tc::desc_sw128(tc::smem_u32(sA + s * 16384 + (kt2 * 2 + j) * 32));
+                    const uint64_t bd = tc::desc_sw128(tc::smem_u32(sB + s * N * 128 + (kt2 * 2 + j) * 32));
+                    const uint32_t sf_id = 2u * j;
+                    tc::mma_mxf4(tm_d, ad, bd, tc::idesc_mxf4(128, N, sf_id, sf_id), (tm_sfa + 4 * kt) | (sf_id << 30),
+                                 (tm_sfb + 4 * kt * nB) | (sf_id << 30), kk > 0);
+                }
+            }
+        }
+        tc::mma_commit(&bars[S]);                // arrives once all issued MMAs (possibly none) completed
+    }
+    __syncwarp();
+    const bool done = __all_sync(kFull, tc::mbar_wait(&bars[S], 0, err, 2));   // warp-uniform for tcgen05.ld
+    tc::tc_fence_after();
+    if (done) {
+        const int row = warp * 32 + (tid & 31);
+        for (int c = 0; c < N; c += 8) {
+            float v[8];
+            tc::tmem_ld_32x32b_x8(tm_d + (uint32_t(warp * 32) << 16) + c, v);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) out[size_t(row) * N + c + i] = v[i];
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tm, 512);
+}
+}  // namespace
+
+void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
+                        const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
+                        cudaStream_t s) {
+    require(N % 8 == 0 && N >= 8 && N <= 256, "selftest: N must be a multiple of 8 in 8..256");
+    require(K % 64 == 0 && K >= 64 && K <= 1024, "selftest: K must be a multiple of 64 in 64..1024");
+    const int S = (K + 255) / 256, KT = (K + 127) / 128, nB = N > 128 ? 2 : 1, G = K / 32;
+    // B operand images (swizzled, zero beyond K) and SFB chunks, built on the host from the raw device arrays.
+    std::vector<uint8_t> hb(size_t(N) * K / 2), hs(size_t(N) * G);
+    GPT_CHECK(cudaMemcpy(hb.data(), b_blocks, hb.size(), cudaMemcpyDeviceToHost));
+    GPT_CHECK(cudaMemcpy(hs.data(), b_scales, hs.size(), cudaMemcpyDeviceToHost));
+    std::vector<uint8_t> img(size_t(S) * N * 128, 0), sfb(size_t(KT) * nB * 512, 0);
+    for (int st = 0; st < S; ++st)
+        for (int n = 0; n < N; ++n)
+            for (int kb = 0; kb < 128; ++kb) {
+                const int src = st * 128 + kb;
+                if (src < K / 2) img[size_t(st) * N * 128 + tc::sw128_offset(n, kb)] = hb[size_t(n) * K / 2 + src];
+            }
+    for (int kt = 0; kt < KT; ++kt)
+        for (int n = 0; n < N; ++n)
+            for (int kb = 0; kb < 4; ++kb) {
+                const int g = kt * 4 + kb;
+                if (g < G) sfb[(size_t(kt) * nB + n / 128) * 512 + tc::sf_offset(n % 128, kb)] = hs[size_t(n) * G + g];
+            }
+    const size_t sfa_bytes = sf_repacked_bytes(1, 128, G);
+    const size_t need = img.size() + sfb.size() + sfa_bytes + 64;
+    require(scratch_bytes >= need, "selftest: scratch too small");
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    uint8_t* d_img = base;
+    uint8_t* d_sfb = d_img + ((img.size() + 1023) & ~size_t(1023));
+    uint8_t* d_sfa = d_sfb + ((sfb.size() + 1023) & ~size_t(1023));
+    int* d_err = reinterpret_cast<int*>(d_sfa + ((sfa_bytes + 1023) & ~size_t(1023)));
+    GPT_CHECK(cudaMemcpy(d_img, img.data(), img.size(), cudaMemcpyHostToDevice));
+    GPT_CHECK(cudaMemcpy(d_sfb, sfb.data(), sfb.size(), cudaMemcpyHostToDevice));
+    GPT_CHECK(cudaMemset(d_err, 0, sizeof(int)));
+    launch_repack_sf(a_scales, d_sfa, 1, 128, G, s);
+    const CUtensorMap tmA = make_tmap_u8_sw128(a_blocks, K / 2, 128, 128, 128);
+    const size_t smem = 1024 + size_t(S) * 16384 + size_t(S) * N * 128 + KT * 512 + KT * nB * 512 + (S + 1) * 8 + 16;
+    GPT_CHECK(cudaFuncSetAttribute(mxf4_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    mxf4_selftest_kernel<<<1, 128, smem, s>>>(tmA, d_sfa, d_img, d_sfb, d, N, K, d_err);
+    check_launch("mxf4 selftest");
+    GPT_CHECK(cudaStreamSynchronize(s));
+    int herr = 0;
+    GPT_CHECK(cudaMemcpy(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) throw std::runtime_error("mxf4 selftest: a bounded wait timed out at site " + std::to_string(herr));
+}
+
+}  // namespace gpt

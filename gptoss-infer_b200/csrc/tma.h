@@ -1,0 +1,16 @@
+// Host-side TMA tensor-map construction (driver entry point resolved through the runtime, no -lcuda needed at
+// link time) with a small cache keyed by (pointer, shape), so repeated calls on the same weights reuse the map.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace gpt {
+
+// 2-D uint8 tensor [rows][row_bytes] (row pitch = row_bytes, a multiple of 16), box [box_rows][box_bytes] with the
+// 128-byte swizzle (box_bytes <= 128). Out-of-range box parts read as zero.
+CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                               uint32_t box_rows);
+
+}  // namespace gpt

@@ -84,6 +84,13 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
                            const float* dn_bias, float* x_resid, int E, int k, int H, int I, float alpha, float limit,
                            void* stream, void* const* events);
 
+/* [extension] Self-test of the tensor-core block-scaled MMA path: D[128, N] (fp32, row-major) =
+ * dequant(a_blocks [128, K/32, 16], a_scales [128, K/32]) . dequant(b_blocks [N, K/32, 16], b_scales [N, K/32])^T
+ * computed by one CTA with TMA, tcgen05.cp scale factors and tcgen05.mma kind::mxf4. N % 8 == 0, 8 <= N <= 256,
+ * K % 64 == 0, 64 <= K <= 1024. Device pointers; synchronizes. */
+int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
+                              const uint8_t* b_scales, float* d, int N, int K);
+
 /* [extension] Which decode MoE implementation gptoss_kernel_moe uses: 0 = SIMT (CUDA cores), 1 = tensor cores
  * (tcgen05 block-scaled MMA) where the shape allows it. Returns the previous setting, or -1. */
 int gptoss_set_moe_impl(int impl);

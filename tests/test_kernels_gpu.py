@@ -60,10 +60,11 @@ def test_mxfp4_dequant_golden_and_nan_rejection(lib):
     g = load_golden("mxfp4_kat.npz")
     b, s = g["rand_blocks"].reshape(-1, 16), g["rand_scales"].reshape(-1)
     out = torch.empty(b.shape[0] * 32, device=DEV)
-    ok(lib, lib.gptoss_kernel_mxfp4_dequant(P(dev(b)), P(dev(s)), P(out), b.shape[0]))
+    db, ds = dev(b), dev(s)          # keep the device tensors alive for the duration of the call
+    ok(lib, lib.gptoss_kernel_mxfp4_dequant(P(db), P(ds), P(out), b.shape[0]))
     assert np.array_equal(out.cpu().numpy().view(np.uint32), g["rand_out"].reshape(-1).view(np.uint32))
     bad = dev(np.array([127, 255], np.uint8))
-    assert lib.gptoss_kernel_mxfp4_dequant(P(dev(b[:2])), P(bad), P(out), 2) == -1
+    assert lib.gptoss_kernel_mxfp4_dequant(P(db), P(bad), P(out), 2) == -1
     assert b"0xFF" in lib.gptoss_last_error()
 
 

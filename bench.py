@@ -239,17 +239,31 @@ def main():
         raise RuntimeError(lib.gptoss_last_error().decode())
     P = capi.ptr
     layers, t0 = make_layers(args.layers, dev)
+    impl = args.moe_impl if args.moe_impl is not None else 1
+    handles = []
+    if impl == 1:
+        for L in layers:
+            hdl = lib.gptoss_moe_layer_create(P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]), E,
+                                              K_TOP, H, I, 1.702, 7.0)
+            if not hdl:
+                raise RuntimeError(lib.gptoss_last_error().decode())
+            handles.append(hdl)
     n_tok = args.steps + args.warmup
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     X = torch.randn(n_tok, H, device=dev, generator=g)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
+    def layer_call(li, x, events):
+        if handles:
+            return lib.gptoss_moe_layer_forward(handles[li], P(x), P(x), sp, events)
+        L = layers[li]
+        return lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
+                                          P(x), E, K_TOP, H, I, 1.702, 7.0, sp, events)
+
     def step(x, events=None):
-        for L in layers:
-            rc = lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
-                                            P(x), E, K_TOP, H, I, 1.702, 7.0, sp, events)
-            if rc != 0:
+        for li in range(len(layers)):
+            if layer_call(li, x, events) != 0:
                 raise RuntimeError(lib.gptoss_last_error().decode())
 
     def barrier():
@@ -276,7 +290,8 @@ def main():
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         ms = float(tt.item())
     value = ws * args.steps * args.layers * LAYER_BYTES / (ms / 1e3) / 1e9
-    gpu_launches = args.steps * args.layers * 4           # rmsnorm, router, gate/up, down per layer
+    # per layer: tensor cores = fused router + gate/up + down; SIMT = rmsnorm + router + gate/up + down
+    gpu_launches = args.steps * args.layers * (3 if handles else 4)
 
     # ---- per-kernel durations: the same K steps again, with events between the kernels of every layer
     n_prof = min(args.steps, 200)
@@ -284,19 +299,18 @@ def main():
     for quad in ev:                                       # torch creates the CUDA event at its first record
         for e in quad:
             e.record(stream)
-    handles = [ctypes_array(e) for e in ev]
+    evh = [ctypes_array(e) for e in ev]
     barrier()
     for i in range(n_prof):
         x = X[i]
-        for li, L in enumerate(layers):
-            rc = lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
-                                            P(x), E, K_TOP, H, I, 1.702, 7.0, sp, handles[i * args.layers + li])
+        for li in range(len(layers)):
+            rc = layer_call(li, x, evh[i * args.layers + li])
             assert rc == 0, lib.gptoss_last_error().decode()
     barrier()
     router_us = sum(e[0].elapsed_time(e[1]) for e in ev) / len(ev) * 1e3
     gateup_us = sum(e[1].elapsed_time(e[2]) for e in ev) / len(ev) * 1e3
     down_us = sum(e[2].elapsed_time(e[3]) for e in ev) / len(ev) * 1e3
-    del handles
+    del evh
 
     # ---- end to end through the public API: host x in, host x out, every step
     xh = torch.randn(args.steps, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
@@ -350,6 +364,7 @@ def main():
                        "l2": "inputs larger than L2: 24 distinct layers, 10.2 GB of experts"},
             "tok_per_s": ws * args.steps / (ms / 1e3),
             "us_per_moe_layer": ms / args.steps / args.layers * 1e3,
+            "moe_impl": "tensor cores (tcgen05 kind::mxf4)" if handles else "SIMT",
             "kernel_us": {"router+rmsnorm": router_us, "gate_up": gateup_us, "down+combine": down_us},
             "roofline": {"bound": "hbm", "kernel": "moe gate/up GEMV", "achieved": achieved, "peak": hbm,
                          "peak_source": peak_src, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
@@ -357,11 +372,14 @@ def main():
                          "algorithmic_bytes_per_launch": GATEUP_BYTES},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
-                    "api": "gptoss_moe_block_async x24 per token, host x copied in and out every step"},
+                    "api": ("gptoss_moe_layer_forward" if handles else "gptoss_moe_block_async") +
+                           " x24 per token, host x copied in and out every step"},
             "gpu_launches": gpu_launches,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line))
+    for hdl in handles:
+        lib.gptoss_moe_layer_destroy(hdl)
     if ws > 1:
         torch.distributed.destroy_process_group()
 

@@ -9,6 +9,7 @@
 #include "common.cuh"
 #include "gptoss.h"
 #include "kernels.h"
+#include "tma.h"
 
 namespace {
 
@@ -57,6 +58,84 @@ struct Scratch {
 };
 thread_local Scratch g_scratch;
 
+// Workspace of the tensor-core decode path (B terms, partial sums, tile counters, gathered scales), owned by the
+// calling thread, one per device. Zero-filled whenever it is (re)allocated: the tile counters must start at zero
+// and reset themselves after every launch.
+struct DecodeWs {
+    void* p[64] = {};
+    size_t n[64] = {};
+    ~DecodeWs() {
+        for (int d = 0; d < 64; ++d)
+            if (p[d]) cudaFree(p[d]);
+    }
+    void* get(size_t bytes) {
+        int dev = 0;
+        GPT_CHECK(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= 64) throw std::runtime_error("device index out of range");
+        if (n[dev] < bytes) {
+            if (p[dev]) GPT_CHECK(cudaFree(p[dev]));
+            p[dev] = nullptr;
+            n[dev] = 0;
+            GPT_CHECK(cudaMalloc(&p[dev], bytes));
+            GPT_CHECK(cudaMemset(p[dev], 0, bytes));
+            n[dev] = bytes;
+        }
+        return p[dev];
+    }
+};
+thread_local DecodeWs g_dws;
+
+bool tc_shape_ok(int k, int H, int I) { return k >= 1 && k <= 8 && H % 64 == 0 && I % 64 == 0 && H >= 64 && I >= 64; }
+
+// Reads the device-side error word of the tensor-core kernels after a synchronization; on error the workspace's
+// counters are cleared so the next call starts clean.
+void check_tc_error(void* ws, const gpt::DecodeTcLayout& L) {
+    int h = 0;
+    GPT_CHECK(cudaMemcpy(&h, static_cast<char*>(ws) + L.off_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) {
+        GPT_CHECK(cudaMemset(static_cast<char*>(ws) + L.zero_bytes_from, 0, L.zero_bytes_to - L.zero_bytes_from));
+        throw std::runtime_error("moe (tensor cores): a bounded wait gave up (site " + std::to_string(h) + ")");
+    }
+}
+
+// Tensor-core MoE on raw checkpoint-layout experts whose count is unknown: the scales of the k selected experts
+// are gathered and repacked per call, x is split into residual terms, then gate/up and down run.
+void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias, const uint8_t* dn_blocks,
+                const uint8_t* dn_scales, const float* dn_bias, const float* x_norm, const int* ids,
+                const float* weights, float* x_resid, int k, int H, int I, float alpha, float limit, void* ws,
+                const gpt::DecodeTcLayout& L, bool x_terms_ready, cudaStream_t s, void* mid_event) {
+    char* w = static_cast<char*>(ws);
+    gpt::launch_repack_sf(gu_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_gu), k, 2 * I, H / 32, s, ids);
+    gpt::launch_repack_sf(dn_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_dn), k, H, I / 32, s, ids);
+    if (!x_terms_ready)
+        gpt::launch_quantize_terms(x_norm, H, reinterpret_cast<uint8_t*>(w + L.off_xq_img),
+                                   reinterpret_cast<uint8_t*>(w + L.off_xq_sf), s);
+    // The expert count is not part of this ABI: the maps span the 32 experts the format allows; only the selected
+    // experts' rows are ever read.
+    const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, 32, 128, 128);
+    const CUtensorMap td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, 32, 128, 128);
+    gpt::DecodeTcArgs a{};
+    a.tmap_gu = &tg;
+    a.tmap_dn = &td;
+    a.sfa_gu = reinterpret_cast<uint8_t*>(w + L.off_sfa_gu);
+    a.sfa_dn = reinterpret_cast<uint8_t*>(w + L.off_sfa_dn);
+    a.sfa_by_slot = 1;
+    a.gu_bias = gu_bias;
+    a.dn_bias = dn_bias;
+    a.ids = ids;
+    a.weights = weights;
+    a.x_resid = x_resid;
+    a.k = k;
+    a.H = H;
+    a.I = I;
+    a.alpha = alpha;
+    a.limit = limit;
+    a.workspace = ws;
+    a.pdl_gateup = true;
+    a.mid_event = mid_event;
+    gpt::launch_moe_decode_tc(a, s);
+}
+
 int g_moe_impl = 1;
 
 [[noreturn]] void not_built(const char* what) {
@@ -64,6 +143,24 @@ int g_moe_impl = 1;
 }
 
 }  // namespace
+
+struct gptoss_moe_layer {
+    const float* norm_w;
+    float eps;
+    const void* router_w;
+    const float* router_b;
+    const float* gu_bias;
+    const float* dn_bias;
+    int E, k, H, I;
+    float alpha, limit;
+    uint8_t* sfa_gu = nullptr;
+    uint8_t* sfa_dn = nullptr;
+    CUtensorMap tg, td;
+    ~gptoss_moe_layer() {
+        if (sfa_gu) cudaFree(sfa_gu);
+        if (sfa_dn) cudaFree(sfa_dn);
+    }
+};
 
 extern "C" {
 
@@ -122,6 +219,15 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
                       float limit) {
     return guard([&] {
         if (k < 1 || k > 8) throw std::runtime_error("moe: k must be in 1..8");
+        if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
+            const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
+            void* ws = g_dws.get(L.bytes);
+            moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
+                       H, I, alpha, limit, ws, L, false, nullptr, nullptr);
+            sync_check("moe");
+            check_tc_error(ws, L);
+            return;
+        }
         void* scratch = g_scratch.get(gpt::moe_decode_scratch_bytes(k, I));
         gpt::launch_moe_decode_simt(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids,
                                     weights, x_resid, k, H, I, alpha, limit, scratch, nullptr);
@@ -159,6 +265,22 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
         auto rec = [&](int i) {
             if (events) GPT_CHECK(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s));
         };
+        if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
+            const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
+            char* tw = static_cast<char*>(g_dws.get(L.bytes));
+            float* th = reinterpret_cast<float*>(tw + L.off_misc);
+            int* tids = reinterpret_cast<int*>(tw + L.off_misc + ((size_t(H) * 4 + 127) & ~size_t(127)));
+            float* tgw = reinterpret_cast<float*>(tids + 32);
+            rec(0);
+            gpt::launch_router_decode(static_cast<const __nv_bfloat16*>(router_w), router_b, x, E, H, k, tids, tgw, s,
+                                      reinterpret_cast<uint8_t*>(tw + L.off_xq_img),
+                                      reinterpret_cast<uint8_t*>(tw + L.off_xq_sf), norm_w, eps, th);
+            rec(1);
+            moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, th, tids, tgw, x_resid, k, H, I,
+                       alpha, limit, tw, L, true, s, events ? events[2] : nullptr);
+            rec(3);
+            return;
+        }
         gpt::launch_rmsnorm(x, norm_w, h, 1, H, eps, s);
         rec(0);
         gpt::launch_router_decode(static_cast<const __nv_bfloat16*>(router_w), router_b, h, E, H, k, ids, w, s);
@@ -175,6 +297,74 @@ int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, 
         const size_t bytes = size_t(1) << 22;
         void* scratch = g_scratch.get(bytes);
         gpt::selftest_mxf4_gemm(a_blocks, a_scales, b_blocks, b_scales, d, N, K, scratch, bytes, nullptr);
+    });
+}
+
+gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const void* router_w, const float* router_b,
+                                          const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                                          const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                                          int E, int k, int H, int I, float alpha, float limit) {
+    gptoss_moe_layer* L = nullptr;
+    guard([&] {
+        if (!tc_shape_ok(k, H, I) || E < k || E > 32)
+            throw std::runtime_error("moe_layer_create: need 1 <= k <= 8, k <= E <= 32, H % 64 == 0, I % 64 == 0");
+        auto* l = new gptoss_moe_layer{norm_w, eps, router_w, router_b, gu_bias, dn_bias, E, k, H, I, alpha, limit};
+        try {
+            GPT_CHECK(cudaMalloc(&l->sfa_gu, gpt::sf_repacked_bytes(E, 2 * I, H / 32)));
+            GPT_CHECK(cudaMalloc(&l->sfa_dn, gpt::sf_repacked_bytes(E, H, I / 32)));
+            gpt::launch_repack_sf(gu_scales, l->sfa_gu, E, 2 * I, H / 32, nullptr);
+            gpt::launch_repack_sf(dn_scales, l->sfa_dn, E, H, I / 32, nullptr);
+            l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, 128);
+            l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, 128);
+            sync_check("moe_layer_create");
+        } catch (...) {
+            delete l;
+            throw;
+        }
+        L = l;
+    });
+    return L;
+}
+
+void gptoss_moe_layer_destroy(gptoss_moe_layer* layer) { delete layer; }
+
+int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid, void* stream, void* const* events) {
+    return guard([&] {
+        if (!l) throw std::runtime_error("moe_layer_forward: null layer");
+        const gpt::DecodeTcLayout L = gpt::decode_tc_layout(l->k, l->H, l->I);
+        char* w = static_cast<char*>(g_dws.get(L.bytes));
+        int* ids = reinterpret_cast<int*>(w + L.off_misc + ((size_t(l->H) * 4 + 127) & ~size_t(127)));
+        float* gw = reinterpret_cast<float*>(ids + 32);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        auto rec = [&](int i) {
+            if (events) GPT_CHECK(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s));
+        };
+        rec(0);
+        gpt::launch_router_decode(static_cast<const __nv_bfloat16*>(l->router_w), l->router_b, x, l->E, l->H, l->k,
+                                  ids, gw, s, reinterpret_cast<uint8_t*>(w + L.off_xq_img),
+                                  reinterpret_cast<uint8_t*>(w + L.off_xq_sf), l->norm_w, l->eps, nullptr);
+        rec(1);
+        gpt::DecodeTcArgs a{};
+        a.tmap_gu = &l->tg;
+        a.tmap_dn = &l->td;
+        a.sfa_gu = l->sfa_gu;
+        a.sfa_dn = l->sfa_dn;
+        a.sfa_by_slot = 0;
+        a.gu_bias = l->gu_bias;
+        a.dn_bias = l->dn_bias;
+        a.ids = ids;
+        a.weights = gw;
+        a.x_resid = x_resid;
+        a.k = l->k;
+        a.H = l->H;
+        a.I = l->I;
+        a.alpha = l->alpha;
+        a.limit = l->limit;
+        a.workspace = w;
+        a.pdl_gateup = events == nullptr;
+        a.mid_event = events ? events[2] : nullptr;
+        gpt::launch_moe_decode_tc(a, s);
+        rec(3);
     });
 }
 

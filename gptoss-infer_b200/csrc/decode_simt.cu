@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "terms.cuh"
 
 namespace gpt {
 
@@ -97,17 +98,40 @@ __device__ __forceinline__ double bf16_hi_d(uint32_t w) { return double(__uint_a
 
 __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouterThreads)
     router_decode_kernel(const __nv_bfloat16* __restrict__ W, const float* __restrict__ b,
-                         const float* __restrict__ x, int E, int H, int k, int* __restrict__ ids,
-                         float* __restrict__ weights) {
+                         const float* __restrict__ x_in, int E, int H, int k, int* __restrict__ ids,
+                         float* __restrict__ weights, uint8_t* xq_img, uint8_t* xq_sf,
+                         const float* __restrict__ norm_w, float eps, float* h_out) {
     __shared__ double red[kRouterThreads / 32][kRouterPerCta];
     __shared__ double logits[32];
+    __shared__ float ssum[kRouterThreads / 32];
+    extern __shared__ float hs[];                          // [H] when norm_w is given
     const unsigned r = cluster_rank();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H8 = H >> 3;
+    pdl_launch_dependents();                               // let the tensor-core gate/up CTAs become resident
+    const float* x = x_in;
+    if (norm_w) {
+        // Fused RMSNorm (every CTA of the cluster normalizes the whole row into its shared memory).
+        float ss = 0.f;
+        for (int i = tid; i < H; i += kRouterThreads) ss = fmaf(x_in[i], x_in[i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) ssum[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int w = 0; w < kRouterThreads / 32; ++w) tot += ssum[w];
+        const float rn = 1.0f / sqrtf(tot / float(H) + eps);
+        for (int i = tid; i < H; i += kRouterThreads) {
+            const float v = x_in[i] * rn * norm_w[i];
+            hs[i] = v;
+            if (h_out && r == 0) h_out[i] = v;
+        }
+        __syncthreads();
+        x = hs;
+    }
     const uint4* Wv = reinterpret_cast<const uint4*>(W);
     const float4* xv = reinterpret_cast<const float4*>(x);
     double acc[kRouterPerCta] = {0.0, 0.0, 0.0, 0.0};
     for (int c = tid; c < H8; c += kRouterThreads) {
-        const float4 xa = __ldg(xv + 2 * c), xb = __ldg(xv + 2 * c + 1);
+        const float4 xa = xv[2 * c], xb = xv[2 * c + 1];
 #pragma unroll
         for (int q = 0; q < kRouterPerCta; ++q) {
             const int e = int(r) + kRouterCluster * q;
@@ -139,6 +163,9 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
             dsmem_store_f64(&logits[e], 0, t + double(b[e]));
         }
     }
+    // Fused for the tensor-core path: the cluster's 64 warps split x into e2m1 residual terms (gate/up's B operand).
+    if (xq_img) quantize_vector_terms_warp(x, H, xq_img, xq_sf, int(r) * (kRouterThreads / 32) + warp,
+                                           kRouterCluster * (kRouterThreads / 32));
     cluster_sync_all();
     if (r != 0 || warp != 0) return;
 
@@ -390,10 +417,16 @@ void launch_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, float* o
 }
 
 void launch_router_decode(const __nv_bfloat16* W, const float* b, const float* x, int E, int H, int k, int* ids,
-                          float* weights, cudaStream_t s) {
+                          float* weights, cudaStream_t s, uint8_t* xq_img, uint8_t* xq_sf, const float* norm_w,
+                          float eps, float* h_out) {
     if (E < 1 || E > 32 || k < 1 || k > 8 || k > E || H % 8 || H < 8)
         throw std::runtime_error("router: unsupported shape (need 1 <= k <= 8, k <= E <= 32, H % 8 == 0)");
-    router_decode_kernel<<<kRouterCluster, kRouterThreads, 0, s>>>(W, b, x, E, H, k, ids, weights);
+    if (xq_img && H % 32) throw std::runtime_error("router: fused quantization needs H % 32 == 0");
+    const size_t smem = norm_w ? size_t(H) * sizeof(float) : 0;
+    if (smem > 48 * 1024)
+        GPT_CHECK(cudaFuncSetAttribute(router_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    router_decode_kernel<<<kRouterCluster, kRouterThreads, smem, s>>>(W, b, x, E, H, k, ids, weights, xq_img, xq_sf,
+                                                                       norm_w, eps, h_out);
     check_launch("router");
 }
 

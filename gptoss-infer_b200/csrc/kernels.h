@@ -1,6 +1,7 @@
 // Host-side launchers of the MoE-path kernels. Every launcher takes the stream to run on and throws
 // std::runtime_error on invalid shapes or launch failure; the C ABI (capi.cu) turns that into -1.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -9,6 +10,9 @@
 namespace gpt {
 
 int num_sms();
+
+// Residual e2m1 terms per activation value in the tensor-core decode path (the MMA's N).
+constexpr int kDecodeTerms = 16;
 
 // y[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w for T rows of n.
 void launch_rmsnorm(const float* x, const float* w, float* y, int T, int n, float eps, cudaStream_t s);
@@ -20,8 +24,12 @@ void launch_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, float* o
 
 // Decode router for one token: logits = W[E,H] x + b accumulated exactly in fp64, top-k by (logit desc, id asc)
 // with NaN never selected ahead of a number, softmax over the k selected fp32 logits.
+// With xq_img != nullptr the router also writes its input as e2m1 residual terms (the tensor-core gate/up's B
+// operand). With norm_w != nullptr the input is RMSNorm(x; norm_w, eps) computed in the kernel (and stored to h_out
+// if given) instead of x itself.
 void launch_router_decode(const __nv_bfloat16* W, const float* b, const float* x, int E, int H, int k, int* ids,
-                          float* weights, cudaStream_t s);
+                          float* weights, cudaStream_t s, uint8_t* xq_img = nullptr, uint8_t* xq_sf = nullptr,
+                          const float* norm_w = nullptr, float eps = 0.f, float* h_out = nullptr);
 
 // Decode MoE for one token on raw checkpoint-layout MXFP4 experts (SIMT path).
 //   a[slot][j] = swiglu(W1[ids[slot]] x + b1)          gate/up rows interleaved (even glu, odd linear)
@@ -36,7 +44,39 @@ void launch_moe_decode_simt(const uint8_t* gu_blocks, const uint8_t* gu_scales, 
 // Scale-factor repack: raw E8M0 bytes [mats][rows][G] -> tcgen05 chunks [mats][ceil(rows/128)][ceil(G/4)][512],
 // chunk byte (r % 32) * 16 + (r / 32) * 4 + kb for row r and k-block kb of the chunk; zero padded.
 size_t sf_repacked_bytes(long long mats, int rows, int G);
-void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s);
+// With ids != nullptr, output matrix m is gathered from raw matrix ids[m] (m < mats).
+void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
+                      const int* ids = nullptr);
+
+// Tensor-core decode MoE (decode_tc.cu). The workspace layout depends only on (k, H, I); the byte range
+// [zero_bytes_from, zero_bytes_to) must be zero before the first launch (counters reset themselves afterwards).
+struct DecodeTcLayout {
+    int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
+    size_t off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu, off_cnt_dn, off_err;
+    size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
+};
+DecodeTcLayout decode_tc_layout(int k, int H, int I);
+
+struct DecodeTcArgs {
+    const CUtensorMap* tmap_gu;   // gate/up blocks viewed as [E][2I][H/2] bytes
+    const CUtensorMap* tmap_dn;   // down blocks viewed as [E][H][I/2] bytes
+    const uint8_t* sfa_gu;        // repacked scales, [mat][RT_gu][KT_gu][512]
+    const uint8_t* sfa_dn;        // repacked scales, [mat][RT_dn][KT_dn][512]
+    int sfa_by_slot;              // 1: mat = slot (scales gathered for the selected experts); 0: mat = expert id
+    const float* gu_bias;
+    const float* dn_bias;
+    const int* ids;
+    const float* weights;
+    float* x_resid;
+    int k, H, I;
+    float alpha, limit;
+    void* workspace;              // decode_tc_layout(k, H, I).bytes; B terms of x already in place
+    bool pdl_gateup;              // launch gate/up as a programmatic dependent of the previous kernel
+    void* mid_event;              // if set: recorded between the two GEMVs (disables their overlap)
+};
+void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
+// x [n] -> kDecodeTerms e2m1 residual terms in the B-operand image layout (img [n/256][terms*128], sf [n/128][512]).
+void launch_quantize_terms(const float* x, int n, uint8_t* img, uint8_t* sf, cudaStream_t s);
 
 // Single-CTA tcgen05 kind::mxf4 GEMM, D[128][N] = dequant(A)[128][K] . dequant(B)[N][K]^T, from raw MXFP4 arrays
 // (checkpoint layout). Pins the layout conventions of the tensor-core kernels. Synchronizes.

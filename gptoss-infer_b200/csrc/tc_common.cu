@@ -54,12 +54,30 @@ CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t ro
     return m;
 }
 
+CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
+                                  uint32_t box_bytes, uint32_t box_rows) {
+    require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+    require(row_bytes % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+    require(box_bytes <= 128 && box_bytes % 16 == 0 && box_rows >= 1 && box_rows <= 256, "bad TMA box");
+    CUtensorMap m;
+    std::memset(&m, 0, sizeof(m));
+    const cuuint64_t dims[3] = {row_bytes, rows, mats};
+    const cuuint64_t strides[2] = {row_bytes, row_bytes * rows};
+    const cuuint32_t box[3] = {box_bytes, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3d) failed: " + std::to_string(int(r)));
+    return m;
+}
+
 // ---------------------------------------------------------------------------------------------------- SF repack
 namespace {
 // raw [mats][rows][G] E8M0 bytes -> [mats][RT][KT][512] tcgen05 chunks (RT = ceil(rows/128), KT = ceil(G/4)), zero
 // padded. One thread per output word of 4 bytes (one row's 4 k-blocks).
 __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, long long mats, int rows,
-                                 int G, int RT, int KT) {
+                                 int G, int RT, int KT, const int* __restrict__ ids) {
     const long long words = mats * RT * KT * 128;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
          i += (long long)gridDim.x * blockDim.x) {
@@ -68,7 +86,7 @@ __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __res
         const int kt = int(c % KT);
         c /= KT;
         const int rt = int(c % RT);
-        const long long mat = c / RT;
+        const long long mat = ids ? (long long)ids[c / RT] : c / RT;
         const int row = rt * 128 + (w & 3) * 32 + (w >> 2);
         uint32_t v = 0;
         if (row < rows) {
@@ -88,11 +106,12 @@ size_t sf_repacked_bytes(long long mats, int rows, int G) {
     return size_t(mats) * size_t((rows + 127) / 128) * size_t((G + 3) / 4) * 512;
 }
 
-void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s) {
+void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
+                      const int* ids) {
     const int RT = (rows + 127) / 128, KT = (G + 3) / 4;
     const long long words = mats * RT * KT * 128;
     const int grid = int(std::min<long long>((words + 255) / 256, num_sms() * 8LL));
-    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT);
+    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, ids);
     check_launch("repack_sf");
 }
 

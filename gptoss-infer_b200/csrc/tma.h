@@ -13,4 +13,9 @@ namespace gpt {
 CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
                                uint32_t box_rows);
 
+// 3-D uint8 tensor [mats][rows][row_bytes], box [1][box_rows][box_bytes], 128-byte swizzle. Rows past `rows`
+// within a matrix read as zero (no spill into the next matrix).
+CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
+                                  uint32_t box_bytes, uint32_t box_rows);
+
 }  // namespace gpt

@@ -27,6 +27,9 @@ SIGNATURES = {
     "gptoss_kernel_mxfp4_dequant": ([P, P, P, I64], I32),
     "gptoss_set_moe_impl": ([I32], I32),
     "gptoss_selftest_mxf4_gemm": ([P, P, P, P, P, I32, I32], I32),
+    "gptoss_moe_layer_create": ([P, F32, P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32], P),
+    "gptoss_moe_layer_destroy": ([P], None),
+    "gptoss_moe_layer_forward": ([P, P, P, P, P], I32),
     "gptoss_moe_block_async": ([P, P, F32, P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32, P, P], I32),
     "gptoss_create": ([ctypes.c_char_p, I32, I64], P),
     "gptoss_destroy": ([P], None),

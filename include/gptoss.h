@@ -84,6 +84,25 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
                            const float* dn_bias, float* x_resid, int E, int k, int H, int I, float alpha, float limit,
                            void* stream, void* const* events);
 
+/* [extension] A prepared MoE layer for the tensor-core decode path. Creation keeps the caller's device pointers
+ * (they must stay valid for the handle's lifetime), repacks the E8M0 scales once into the tcgen05 scale-factor
+ * layout (device memory owned by the handle, 24.9 MB for gpt-oss-20b's 32 experts) and builds the TMA descriptors;
+ * returns NULL on failure (gptoss_last_error). Needs H % 64 == 0, I % 64 == 0, 1 <= k <= 8, k <= E <= 32.
+ * norm_w fp32 [H]; router_w bf16 [E,H]; router_b fp32 [E]; expert layouts as gptoss_kernel_moe. Synchronizes. */
+typedef struct gptoss_moe_layer gptoss_moe_layer;
+gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const void* router_w, const float* router_b,
+                                          const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                                          const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                                          int E, int k, int H, int I, float alpha, float limit);
+void gptoss_moe_layer_destroy(gptoss_moe_layer* layer);
+/* [extension] x_resid += MoE(RMSNorm(x)) for one token with a prepared layer, asynchronous on `stream` (a
+ * cudaStream_t; NULL = legacy default stream): one cluster kernel (RMSNorm, router, top-k, softmax, x split into
+ * e2m1 residual terms) and the two tensor-core GEMV kernels, chained with programmatic dependent launch. x_resid may
+ * alias x. `events` as in gptoss_moe_block_async (recording them disables the kernels' overlap). Calls from one
+ * thread share its workspace and must not overlap on the GPU. */
+int gptoss_moe_layer_forward(gptoss_moe_layer* layer, const float* x, float* x_resid, void* stream,
+                             void* const* events);
+
 /* [extension] Self-test of the tensor-core block-scaled MMA path: D[128, N] (fp32, row-major) =
  * dequant(a_blocks [128, K/32, 16], a_scales [128, K/32]) . dequant(b_blocks [N, K/32, 16], b_scales [N, K/32])^T
  * computed by one CTA with TMA, tcgen05.cp scale factors and tcgen05.mma kind::mxf4. N % 8 == 0, 8 <= N <= 256,

@@ -215,3 +215,49 @@ def test_config0_block_vs_reference_golden(lib, config0, impl):
             assert mx <= 2e-5 and l2 <= 2e-5, (r, mx, l2)
     finally:
         lib.gptoss_set_moe_impl(prev)
+
+
+def make_layer(lib, d, E=32, k=4):
+    L = lib.gptoss_moe_layer_create(P(d["ln"]), 1e-5, P(d["W"]), P(d["b"]), *(P(e) for e in d["ex"]), E, k, 2880, 2880,
+                                    1.702, 7.0)
+    assert L, lib.gptoss_last_error().decode()
+    return L
+
+
+def test_layer_forward_config0_vs_reference_golden(lib, config0):
+    """Prepared layer (fused RMSNorm + router + tensor-core GEMVs) on the 4 golden tokens: x + Reference.moe(h)."""
+    d, g = config0
+    L = make_layer(lib, d)
+    try:
+        for r in range(g["x"].shape[0]):
+            x = dev(g["x"][r])
+            out = x.clone()
+            ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(out), None, None))
+            torch.cuda.synchronize()
+            mx, l2 = rel_err((out - x).cpu().numpy(), g["out"][r])
+            assert mx <= 2e-5 and l2 <= 2e-5, (r, mx, l2)
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+
+
+def test_layer_forward_is_deterministic_and_in_place(lib, config0):
+    d, g = config0
+    L = make_layer(lib, d)
+    try:
+        x = dev(g["x"][1])
+        a, b = x.clone(), x.clone()
+        ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(a), None, None))
+        ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(b), None, None))
+        c = x.clone()
+        ok(lib, lib.gptoss_moe_layer_forward(L, P(c), P(c), None, None))     # x_resid aliases x
+        torch.cuda.synchronize()
+        assert torch.equal(a, b) and torch.equal(a, c)
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+
+
+def test_layer_create_rejects_bad_shapes(lib, config0):
+    d, _ = config0
+    L = lib.gptoss_moe_layer_create(P(d["ln"]), 1e-5, P(d["W"]), P(d["b"]), *(P(e) for e in d["ex"]), 32, 9, 2880,
+                                    2880, 1.702, 7.0)
+    assert not L and b"k <= 8" in lib.gptoss_last_error()

@@ -271,8 +271,28 @@ def main():
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    for i in range(args.warmup):
-        step(X[args.steps + i])
+    # One decode step (24 MoE layers) is captured once as a CUDA graph and replayed, as the reference engine does
+    # with its decode step (runtime/src/engine.cu:264-279): the host issues two operations per step, not 72
+    # launches. The programmatic-dependent-launch edges between a layer's kernels are kept in the graph.
+    x_static = torch.empty(H, device=dev)
+    for i in range(args.warmup):                          # eager warm-up also sizes the library's workspaces
+        x_static.copy_(X[args.steps + i])
+        step(x_static)
+    barrier()
+    cap = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    x_static.copy_(X[0])
+    with torch.cuda.graph(graph, stream=cap):
+        sp_cap = cap.cuda_stream
+        for li in range(len(layers)):
+            rc = (lib.gptoss_moe_layer_forward(handles[li], P(x_static), P(x_static), sp_cap, None) if handles else
+                  lib.gptoss_moe_block_async(P(x_static), P(layers[li]["ln"]), 1e-5, P(layers[li]["W"]),
+                                             P(layers[li]["b"]), *(P(e) for e in layers[li]["ex"]), P(x_static), E,
+                                             K_TOP, H, I, 1.702, 7.0, sp_cap, None))
+            assert rc == 0, lib.gptoss_last_error().decode()
+    for i in range(3):
+        x_static.copy_(X[args.steps + (i % max(1, args.warmup))])
+        graph.replay()
     barrier()
 
     # ---- timed region: exactly K steps
@@ -281,7 +301,8 @@ def main():
         t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0e.record(stream)
         for i in range(args.steps):
-            step(X[i])
+            x_static.copy_(X[i])
+            graph.replay()
         t1e.record(stream)
         barrier()
     ms = t0e.elapsed_time(t1e)
@@ -293,37 +314,48 @@ def main():
     # per layer: tensor cores = fused router + gate/up + down; SIMT = rmsnorm + router + gate/up + down
     gpu_launches = args.steps * args.layers * (3 if handles else 4)
 
-    # ---- per-kernel durations: the same K steps again, with events between the kernels of every layer
-    n_prof = min(args.steps, 200)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_prof * args.layers)]
+    # ---- per-kernel durations: a second graph of the same step with events between the kernels of every layer
+    # (the events serialize the kernels, so these are upper bounds of the overlapped kernels' own durations)
+    n_prof = min(args.steps, 100)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.layers)]
     for quad in ev:                                       # torch creates the CUDA event at its first record
         for e in quad:
             e.record(stream)
+    torch.cuda.synchronize()
     evh = [ctypes_array(e) for e in ev]
+    pgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(pgraph, stream=cap):
+        for li in range(len(layers)):
+            rc = (lib.gptoss_moe_layer_forward(handles[li], P(x_static), P(x_static), cap.cuda_stream, evh[li])
+                  if handles else
+                  lib.gptoss_moe_block_async(P(x_static), P(layers[li]["ln"]), 1e-5, P(layers[li]["W"]),
+                                             P(layers[li]["b"]), *(P(e) for e in layers[li]["ex"]), P(x_static), E,
+                                             K_TOP, H, I, 1.702, 7.0, cap.cuda_stream, evh[li]))
+            assert rc == 0, lib.gptoss_last_error().decode()
+    sums = [0.0, 0.0, 0.0]
     barrier()
     for i in range(n_prof):
-        x = X[i]
-        for li in range(len(layers)):
-            rc = layer_call(li, x, evh[i * args.layers + li])
-            assert rc == 0, lib.gptoss_last_error().decode()
-    barrier()
-    router_us = sum(e[0].elapsed_time(e[1]) for e in ev) / len(ev) * 1e3
-    gateup_us = sum(e[1].elapsed_time(e[2]) for e in ev) / len(ev) * 1e3
-    down_us = sum(e[2].elapsed_time(e[3]) for e in ev) / len(ev) * 1e3
+        x_static.copy_(X[i])
+        pgraph.replay()
+        torch.cuda.synchronize()
+        for q in ev:
+            sums[0] += q[0].elapsed_time(q[1])
+            sums[1] += q[1].elapsed_time(q[2])
+            sums[2] += q[2].elapsed_time(q[3])
+    nl = n_prof * args.layers
+    router_us, gateup_us, down_us = (v / nl * 1e3 for v in sums)
     del evh
 
     # ---- end to end through the public API: host x in, host x out, every step
     xh = torch.randn(args.steps, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
     yh = torch.empty(H).pin_memory()
-    xd = torch.empty(H, device=dev)
     barrier()
-    te0 = time.perf_counter()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        xd.copy_(xh[i], non_blocking=True)
-        step(xd)
-        yh.copy_(xd, non_blocking=True)
+        x_static.copy_(xh[i], non_blocking=True)
+        graph.replay()
+        yh.copy_(x_static, non_blocking=True)
         stream.synchronize()
     e1.record(stream)
     barrier()
@@ -333,6 +365,7 @@ def main():
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         ms_e2e = float(tt.item())
     e2e = ws * args.steps * args.layers * LAYER_BYTES / (ms_e2e / 1e3) / 1e9
+    del graph, pgraph
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -373,7 +406,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
                     "api": ("gptoss_moe_layer_forward" if handles else "gptoss_moe_block_async") +
-                           " x24 per token, host x copied in and out every step"},
+                           " x24 per token captured in one CUDA graph; host x copied in and out every step"},
             "gpu_launches": gpu_launches,
             "clocks": clocks.summary(),
         }

@@ -99,17 +99,14 @@ void check_tc_error(void* ws, const gpt::DecodeTcLayout& L) {
 }
 
 // Tensor-core MoE on raw checkpoint-layout experts whose count is unknown: the scales of the k selected experts
-// are gathered and repacked per call, x is split into residual terms, then gate/up and down run.
+// are gathered and repacked per call, then the fused kernel runs with the given ids (router off).
 void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias, const uint8_t* dn_blocks,
                 const uint8_t* dn_scales, const float* dn_bias, const float* x_norm, const int* ids,
                 const float* weights, float* x_resid, int k, int H, int I, float alpha, float limit, void* ws,
-                const gpt::DecodeTcLayout& L, bool x_terms_ready, cudaStream_t s, void* mid_event) {
+                const gpt::DecodeTcLayout& L, cudaStream_t s) {
     char* w = static_cast<char*>(ws);
     gpt::launch_repack_sf(gu_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_gu), k, 2 * I, H / 32, s, ids);
     gpt::launch_repack_sf(dn_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_dn), k, H, I / 32, s, ids);
-    if (!x_terms_ready)
-        gpt::launch_quantize_terms(x_norm, H, reinterpret_cast<uint8_t*>(w + L.off_xq_img),
-                                   reinterpret_cast<uint8_t*>(w + L.off_xq_sf), s);
     // The expert count is not part of this ABI: the maps span the 32 experts the format allows; only the selected
     // experts' rows are ever read.
     const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, 32, 128, 128);
@@ -122,6 +119,7 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
     a.sfa_by_slot = 1;
     a.gu_bias = gu_bias;
     a.dn_bias = dn_bias;
+    a.x = x_norm;
     a.ids = ids;
     a.weights = weights;
     a.x_resid = x_resid;
@@ -131,12 +129,11 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
     a.alpha = alpha;
     a.limit = limit;
     a.workspace = ws;
-    a.pdl_gateup = true;
-    a.mid_event = mid_event;
     gpt::launch_moe_decode_tc(a, s);
 }
 
-int g_moe_impl = 1;
+int g_moe_impl = 1;                   // 0: SIMT decode MoE, 1: tensor cores where the shape allows
+long long* g_trace = nullptr;          // device buffer for pipeline traces, installed by gptoss_trace_enable
 
 [[noreturn]] void not_built(const char* what) {
     throw std::runtime_error(std::string(what) + ": not part of this build (the B200 MoE path); see gptoss.h");
@@ -223,7 +220,7 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
             void* ws = g_dws.get(L.bytes);
             moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
-                       H, I, alpha, limit, ws, L, false, nullptr, nullptr);
+                       H, I, alpha, limit, ws, L, nullptr);
             sync_check("moe");
             check_tc_error(ws, L);
             return;
@@ -263,9 +260,10 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
         void* a = ws + h_bytes + 256;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         auto rec = [&](int i) {
-            if (events) GPT_CHECK(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s));
+            if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
         };
         if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
+            // raw scales: the router runs first (its ids select which scales to repack), then the fused kernel
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
             char* tw = static_cast<char*>(g_dws.get(L.bytes));
             float* th = reinterpret_cast<float*>(tw + L.off_misc);
@@ -273,11 +271,11 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
             float* tgw = reinterpret_cast<float*>(tids + 32);
             rec(0);
             gpt::launch_router_decode(static_cast<const __nv_bfloat16*>(router_w), router_b, x, E, H, k, tids, tgw, s,
-                                      reinterpret_cast<uint8_t*>(tw + L.off_xq_img),
-                                      reinterpret_cast<uint8_t*>(tw + L.off_xq_sf), norm_w, eps, th);
+                                      nullptr, nullptr, norm_w, eps, th);
             rec(1);
+            rec(2);
             moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, th, tids, tgw, x_resid, k, H, I,
-                       alpha, limit, tw, L, true, s, events ? events[2] : nullptr);
+                       alpha, limit, tw, L, s);
             rec(3);
             return;
         }
@@ -337,13 +335,11 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
         float* gw = reinterpret_cast<float*>(ids + 32);
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         auto rec = [&](int i) {
-            if (events) GPT_CHECK(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s));
+            if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
         };
         rec(0);
-        gpt::launch_router_decode(static_cast<const __nv_bfloat16*>(l->router_w), l->router_b, x, l->E, l->H, l->k,
-                                  ids, gw, s, reinterpret_cast<uint8_t*>(w + L.off_xq_img),
-                                  reinterpret_cast<uint8_t*>(w + L.off_xq_sf), l->norm_w, l->eps, nullptr);
         rec(1);
+        rec(2);
         gpt::DecodeTcArgs a{};
         a.tmap_gu = &l->tg;
         a.tmap_dn = &l->td;
@@ -352,8 +348,14 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
         a.sfa_by_slot = 0;
         a.gu_bias = l->gu_bias;
         a.dn_bias = l->dn_bias;
-        a.ids = ids;
-        a.weights = gw;
+        a.router_w = l->router_w;
+        a.router_b = l->router_b;
+        a.norm_w = l->norm_w;
+        a.eps = l->eps;
+        a.E = l->E;
+        a.x = x;
+        a.ids_out = ids;
+        a.w_out = gw;
         a.x_resid = x_resid;
         a.k = l->k;
         a.H = l->H;
@@ -361,10 +363,24 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
         a.alpha = l->alpha;
         a.limit = l->limit;
         a.workspace = w;
-        a.pdl_gateup = events == nullptr;
-        a.mid_event = events ? events[2] : nullptr;
+        a.trace = g_trace;
         gpt::launch_moe_decode_tc(a, s);
         rec(3);
+    });
+}
+
+int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, int which) {
+    return guard([&] {
+        const size_t bytes = size_t(n / 256 + 1) * gpt::kDecodeTerms * 128 + size_t(n / 128 + 1) * 512;
+        gpt::selftest_terms(x, n, out, per_term, which, g_scratch.get(bytes), bytes, nullptr);
+    });
+}
+
+int gptoss_trace_enable(void* device_buffer, long long bytes) {
+    return guard([&] {
+        if (device_buffer && bytes < 160LL * 160 * 8)
+            throw std::runtime_error("trace buffer too small: need 160 * 160 * 8 bytes");
+        g_trace = static_cast<long long*>(device_buffer);
     });
 }
 

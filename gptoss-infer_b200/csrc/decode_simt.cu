@@ -388,11 +388,15 @@ void moe_simt_nb(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float
     gateup_simt_kernel<NB><<<grid_gu, kSimtThreads, smem_gu, s>>>(gu_blocks, gu_scales, gu_bias, x_norm, ids, a, k,
                                                                    H, I, alpha, limit);
     check_launch("moe gate/up (simt)");
-    if (mid_event) GPT_CHECK(cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s));
+    if (mid_event) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(mid_event), s, cudaEventRecordExternal));
     const size_t smem_dn = size_t(k) * 32 * Gp * sizeof(float);
     const int grid_dn = std::max(1, std::min(sms * 2, (H / 2 + 7) / 8));
     auto kern = down_simt_kernel<NB, 4>;
-    GPT_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_dn)));
+    static int smem_set = 0;                              // attribute calls stay out of CUDA-graph captures
+    if (int(smem_dn) > smem_set) {
+        GPT_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_dn)));
+        smem_set = int(smem_dn);
+    }
     launch_pdl(kern, dim3(grid_dn), dim3(kSimtThreads), smem_dn, s, true, dn_blocks, dn_scales, dn_bias,
                (const float*)a, ids, weights, x_resid, k, H, I);
     check_launch("moe down (simt)");

@@ -48,11 +48,13 @@ size_t sf_repacked_bytes(long long mats, int rows, int G);
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
                       const int* ids = nullptr);
 
-// Tensor-core decode MoE (decode_tc.cu). The workspace layout depends only on (k, H, I); the byte range
-// [zero_bytes_from, zero_bytes_to) must be zero before the first launch (counters reset themselves afterwards).
+// Tensor-core decode MoE (decode_tc.cu): one persistent cooperative kernel per MoE layer. The workspace layout
+// depends only on (k, H, I); the byte range [zero_bytes_from, zero_bytes_to) must be zero before the first launch
+// (tile counters and the grid barrier reset themselves afterwards).
 struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
-    size_t off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu, off_cnt_dn, off_err;
+    size_t off_xq_img, off_xq_sf, off_partials, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu,
+        off_cnt_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
 };
 DecodeTcLayout decode_tc_layout(int k, int H, int I);
@@ -65,23 +67,33 @@ struct DecodeTcArgs {
     int sfa_by_slot;              // 1: mat = slot (scales gathered for the selected experts); 0: mat = expert id
     const float* gu_bias;
     const float* dn_bias;
-    const int* ids;
-    const float* weights;
+    const void* router_w;         // bf16 [E][H]; null: ids/weights below give the experts
+    const float* router_b;
+    const float* norm_w;          // null: x is already normalized
+    float eps;
+    int E;
+    const float* x;               // [H]
+    const int* ids;               // [k] when router_w is null
+    const float* weights;         // [k] when router_w is null
+    int* ids_out;                 // optional: the router's choice
+    float* w_out;
     float* x_resid;
     int k, H, I;
     float alpha, limit;
-    void* workspace;              // decode_tc_layout(k, H, I).bytes; B terms of x already in place
-    bool pdl_gateup;              // launch gate/up as a programmatic dependent of the previous kernel
-    void* mid_event;              // if set: recorded between the two GEMVs (disables their overlap)
+    void* workspace;              // decode_tc_layout(k, H, I).bytes
+    long long* trace = nullptr;   // optional pipeline trace: [num_sms][96] clock64 stamps
 };
 void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
-// x [n] -> kDecodeTerms e2m1 residual terms in the B-operand image layout (img [n/256][terms*128], sf [n/128][512]).
-void launch_quantize_terms(const float* x, int n, uint8_t* img, uint8_t* sf, cudaStream_t s);
 
 // Single-CTA tcgen05 kind::mxf4 GEMM, D[128][N] = dequant(A)[128][K] . dequant(B)[N][K]^T, from raw MXFP4 arrays
 // (checkpoint layout). Pins the layout conventions of the tensor-core kernels. Synchronizes.
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                         const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
                         cudaStream_t s);
+
+// Quantizes x [n] into kDecodeTerms e2m1 residual terms (which = 0: comparison quantizer, 1: converter quantizer)
+// and decodes them back into out [n]; per_term (optional, [2][n]) receives the first two terms. Synchronizes.
+void selftest_terms(const float* x, int n, float* out, float* per_term, int which, void* scratch, size_t bytes,
+                    cudaStream_t s);
 
 }  // namespace gpt

@@ -22,6 +22,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// One lane of a converged warp (the warp must be converged at the call).
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+    return pred != 0;
+}
+
 // ---------------------------------------------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -55,14 +62,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Every wait is bounded: after kSpinLimit failed polls (seconds of wall time with the back-off) the wait gives up,
-// records `where` in *err (first error wins) and returns false; callers then skip the dependent work, drain and exit.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Every wait is bounded: mbarrier.try_wait suspends the thread in hardware until the phase completes or a short
+// system-defined window passes, so the loop needs no sleep of its own (one would only delay the wake-up); after
+// kSpinLimit unsuccessful tries (well over a second) the wait gives up, records `where` in *err (first error wins)
+// and returns false; callers then skip the dependent work, drain and exit.
+constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int where) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) __nanosleep(i > 4096 ? 256 : 32);
+    if (err) atomicCAS(err, 0, where);
+    return false;
+}
+
+// Bounded wait with a sleep between tries, for threads whose wake-up latency does not matter (they would otherwise
+// take issue slots from the producer and MMA threads of their own and co-resident CTAs while they wait).
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, int* err, int where, uint32_t ns) {
+    for (uint32_t i = 0; i < kSpinLimit / 16; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(ns);
     }
     if (err) atomicCAS(err, 0, where);
     return false;

@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
+#include "terms.cuh"
 #include "tma.h"
 
 namespace gpt {
@@ -244,6 +245,58 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
     int herr = 0;
     GPT_CHECK(cudaMemcpy(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (herr) throw std::runtime_error("mxf4 selftest: a bounded wait timed out at site " + std::to_string(herr));
+}
+
+namespace {
+// One warp per 8 blocks: quantize x into residual terms with the chosen quantizer (0 = comparisons, 1 = converters).
+__global__ void terms_quantize_kernel(const float* x, int n, uint8_t* img, uint8_t* sf, int which) {
+    const int lane = threadIdx.x & 31, sub = lane & 3;
+    const int g = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 8 + (lane >> 2);
+    const bool active = g < n / 32;
+    const int gg = active ? g : 0;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = active ? x[gg * 32 + sub * 8 + i] : 0.f;
+    uint8_t* im = img + (gg / 8) * (kDecodeTerms * 128);
+    uint8_t* sc = sf + (gg / 4) * 512;
+    if (which) quantize_block_terms_cvt(v, im, gg % 8, sc, gg % 4, sub, active);
+    else quantize_block_terms(v, im, gg % 8, sc, gg % 4, sub, active);
+}
+
+// Reference decoder of the term images: out[i] = sum_t e2m1(code_t[i]) * 2^(scale_t - 127), in fp64 then rounded.
+__global__ void terms_decode_kernel(const uint8_t* img, const uint8_t* sf, int n, float* out, float* per_term) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int g = i / 32, e = i % 32;
+    double acc = 0.0;
+    for (int t = 0; t < kDecodeTerms; ++t) {
+        const uint8_t* row = img + (g / 8) * (kDecodeTerms * 128) + t * 128;
+        const int q = g % 8;
+        const uint8_t byte = row[((q ^ (t & 7)) << 4) + e / 2];
+        const uint32_t code = (e & 1) ? (byte >> 4) : (byte & 15);
+        const uint32_t s = sf[(g / 4) * 512 + (t & 31) * 16 + (t >> 5) * 4 + (g % 4)];
+        const double v = double(e2m1_exact(code)) * ldexp(1.0, int(s) - 127);
+        if (per_term && t < 2) per_term[size_t(t) * n + i] = float(v);
+        acc += v;
+    }
+    out[i] = float(acc);
+}
+}  // namespace
+
+void selftest_terms(const float* x, int n, float* out, float* per_term, int which, void* scratch, size_t bytes,
+                    cudaStream_t s) {
+    require(n % 256 == 0 && n > 0, "selftest_terms: n must be a positive multiple of 256");
+    const size_t img_bytes = size_t(n / 256) * kDecodeTerms * 128, sf_bytes = size_t(n / 128) * 512;
+    require(bytes >= img_bytes + sf_bytes, "selftest_terms: scratch too small");
+    uint8_t* img = static_cast<uint8_t*>(scratch);
+    uint8_t* sf = img + img_bytes;
+    GPT_CHECK(cudaMemsetAsync(scratch, 0, img_bytes + sf_bytes, s));
+    const int warps = (n / 32 + 7) / 8;
+    terms_quantize_kernel<<<(warps + 3) / 4, 128, 0, s>>>(x, n, img, sf, which);
+    check_launch("terms quantize");
+    terms_decode_kernel<<<(n + 255) / 256, 256, 0, s>>>(img, sf, n, out, per_term);
+    check_launch("terms decode");
+    GPT_CHECK(cudaStreamSynchronize(s));
 }
 
 }  // namespace gpt

@@ -11,20 +11,23 @@ __device__ __forceinline__ float exp2i_exact(int n) {         // exact 2^n for n
     return n <= -127 ? __uint_as_float(0x00400000u) : __uint_as_float(uint32_t(n + 127) << 23);
 }
 
-// Warp-cooperative: lane i holds element i of one 32-element block. Writes kDecodeTerms e2m1 residual terms of the
-// block: term t's 16 code bytes at img_stage + t*128 + ((q ^ (t & 7)) << 4) (q = the block's 16-byte chunk within
-// the 128-byte stage row, pre-swizzled) and its E8M0 scale at sf_chunk[(t % 32) * 16 + (t / 32) * 4 + kb].
-// Each term's scale is the smallest power of two keeping the remaining block maximum within 6; codes round to
-// nearest, ties to even; the subtraction of each term is exact, so the terms sum to the input up to the last
-// term's rounding.
-__device__ __forceinline__ void quantize_block_terms(float v, uint8_t* img_stage, int q, uint8_t* sf_chunk, int kb) {
-    const int lane = threadIdx.x & 31;
-    float r = v;
+// Quantization of 32-element blocks into kDecodeTerms e2m1 residual terms, four lanes per block: lane `sub` (0..3)
+// of a 4-lane group holds elements 8*sub .. 8*sub+7 in v[], which become one 32-bit word (bytes 4*sub..4*sub+3) of
+// the block's 16 code bytes. Term t's codes go to img_stage + t*128 + ((q ^ (t & 7)) << 4) + 4*sub (the B-operand
+// image, pre-swizzled; q = the block's 16-byte chunk within its 128-byte stage row) and its E8M0 scale to
+// sf_chunk[(t % 32) * 16 + (t / 32) * 4 + kb]. Each term's scale is the smallest power of two keeping the remaining
+// block maximum within 6; codes round to nearest, ties to even; each term's subtraction is exact, so the terms sum
+// to the input up to the last term's rounding. All 32 lanes must call (the group max uses shuffles); `active`
+// false only suppresses a group's stores.
+__device__ __forceinline__ void quantize_block_terms(float (&v)[8], uint8_t* img_stage, int q, uint8_t* sf_chunk, int kb,
+                                                     int sub, bool active) {
 #pragma unroll 1
     for (int t = 0; t < kDecodeTerms; ++t) {
-        float amax = fabsf(r);
+        float amax = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
         int k = -127;
         const uint32_t bits = __float_as_uint(amax);
         const int e = int((bits >> 23) & 0xFF);
@@ -33,31 +36,176 @@ __device__ __forceinline__ void quantize_block_terms(float v, uint8_t* img_stage
             k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
             k = max(-127, min(127, k));
         }
-        const float y = fabsf(r) * exp2i_exact(-k);
-        uint32_t c = (y > 0.25f) + (y >= 0.75f) + (y > 1.25f) + (y >= 1.75f) + (y > 2.5f) + (y >= 3.5f) + (y > 5.0f);
-        const float mag = e2m1_exact(c) * exp2i_exact(k);
-        if (signbit(r)) {
-            c |= 8u;
-            r += mag;
-        } else {
-            r -= mag;
+        const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float y = fabsf(v[i]) * inv;
+            uint32_t c = (y > 0.25f) + (y >= 0.75f) + (y > 1.25f) + (y >= 1.75f) + (y > 2.5f) + (y >= 3.5f) + (y > 5.0f);
+            const float mag = e2m1_exact(c) * sc;
+            if (signbit(v[i])) {
+                c |= 8u;
+                v[i] += mag;
+            } else {
+                v[i] -= mag;
+            }
+            word |= c << (4 * i);
         }
-        uint32_t w = c << (4 * (lane & 7));
-        w |= __shfl_xor_sync(kFull, w, 1);
-        w |= __shfl_xor_sync(kFull, w, 2);
-        w |= __shfl_xor_sync(kFull, w, 4);
-        if ((lane & 7) == 0)
-            *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | ((lane >> 3) * 4))) = w;
-        if (lane == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(k + 127);
+        if (active) {
+            *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | (sub * 4))) = word;
+            if (sub == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(k + 127);
+        }
     }
 }
 
-// Quantize a whole vector (n elements, n % 32 == 0) into B terms: img [n/256 stages][R*128], sf [n/128 chunks][512].
-__device__ __forceinline__ void quantize_vector_terms_warp(const float* x, int n, uint8_t* img, uint8_t* sf, int warp_id, int n_warps) {
-    const int lane = threadIdx.x & 31;
-    for (int g = warp_id; g < n / 32; g += n_warps) {
-        const float v = x[g * 32 + lane];
-        quantize_block_terms(v, img + (g / 8) * (kDecodeTerms * 128), g % 8, sf + (g / 4) * 512, g % 4);
+// Same contract as quantize_block_terms, computed with the sm_100 converters: cvt.rn.satfinite.e2m1x2.f32 rounds
+// pairs to e2m1 (nearest, ties to even) and cvt.rn.f16x2.e2m1x2 decodes them back exactly for the residual. About a
+// quarter of the instructions of the comparison form. The bytes are packed from and unpacked to whole 32-bit
+// registers inside the asm (16-bit views of wider registers were miscompiled into wrong bytes).
+__device__ __forceinline__ void quantize_block_terms_cvt(float (&v)[8], uint8_t* img_stage, int q, uint8_t* sf_chunk,
+                                                         int kb, int sub, bool active) {
+#pragma unroll 1
+    for (int t = 0; t < kDecodeTerms; ++t) {
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+        int k = -127;
+        const uint32_t bits = __float_as_uint(amax);
+        const int e = int((bits >> 23) & 0xFF);
+        if (e != 0) {
+            const int k0 = e - 127;
+            k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
+            k = max(-127, min(127, k));
+        }
+        const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = v[i] * inv;
+        // each pair is rounded to e2m1 and decoded back from the same 8-bit register; the four bytes are packed
+        // into the output word once at the end
+        uint32_t word, h[4];
+        asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b0, %6, %5;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b1, %8, %7;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b2, %10, %9;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b3, %12, %11;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %1, b0;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %2, b1;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %3, b2;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %4, b3;\n\t"
+            "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+            : "=r"(word), "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+            : "f"(y[0]), "f"(y[1]), "f"(y[2]), "f"(y[3]), "f"(y[4]), "f"(y[5]), "f"(y[6]), "f"(y[7]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
+            v[2 * i] = fmaf(-f.x, sc, v[2 * i]);
+            v[2 * i + 1] = fmaf(-f.y, sc, v[2 * i + 1]);
+        }
+        if (active) {
+            *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | (sub * 4))) = word;
+            if (sub == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(k + 127);
+        }
+    }
+}
+
+// Quantize a whole vector (n elements, n % 32 == 0) into B terms: img [n/256 stages][terms*128],
+// sf [n/128 chunks][512]. Each warp handles 8 blocks at a time; warp_id/n_warps enumerate the participating warps.
+__device__ __forceinline__ void quantize_vector_terms_warp(const float* x, int n, uint8_t* img, uint8_t* sf,
+                                                           int warp_id, int n_warps) {
+    const int lane = threadIdx.x & 31, sub = lane & 3;
+    const int nb = n / 32;
+    for (int g0 = warp_id * 8; g0 < nb; g0 += n_warps * 8) {
+        const int g = g0 + (lane >> 2);
+        const bool active = g < nb;
+        float v[8];
+        if (active) {
+            const float4 a = *reinterpret_cast<const float4*>(x + g * 32 + sub * 8);
+            const float4 b = *reinterpret_cast<const float4*>(x + g * 32 + sub * 8 + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        }
+        const int gg = active ? g : 0;
+        quantize_block_terms_cvt(v, img + (gg / 8) * (kDecodeTerms * 128), gg % 8, sf + (gg / 4) * 512, gg % 4,
+                                 sub, active);
+    }
+}
+
+// Quantize a vector (n % 32 == 0, n <= 32 * 8 * n_warps * 3) into B terms like quantize_vector_terms_warp, with
+// each warp working on up to three groups of 8 blocks at once: the three independent dependency chains (group
+// maximum, scale, rounding, residual per term) overlap, so the warp takes about as long as for one group.
+__device__ __forceinline__ void quantize_vector_terms_multi(const float* x, int n, uint8_t* img, uint8_t* sf,
+                                                            int warp_id, int n_warps) {
+    const int lane = threadIdx.x & 31, sub = lane & 3;
+    const int nb = n / 32;
+    float v[3][8];
+    int gg[3];
+    bool act[3];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        const int g = (warp_id + r * n_warps) * 8 + (lane >> 2);
+        act[r] = g < nb;
+        gg[r] = act[r] ? g : 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[r][i] = act[r] ? x[gg[r] * 32 + sub * 8 + i] : 0.f;
+    }
+#pragma unroll 1
+    for (int t = 0; t < kDecodeTerms; ++t) {
+        float amax[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            amax[r] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax[r] = fmaxf(amax[r], fabsf(v[r][i]));
+        }
+#pragma unroll
+        for (int r = 0; r < 3; ++r) amax[r] = fmaxf(amax[r], __shfl_xor_sync(kFull, amax[r], 1));
+#pragma unroll
+        for (int r = 0; r < 3; ++r) amax[r] = fmaxf(amax[r], __shfl_xor_sync(kFull, amax[r], 2));
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            int k = -127;
+            const uint32_t bits = __float_as_uint(amax[r]);
+            const int e = int((bits >> 23) & 0xFF);
+            if (e != 0) {
+                const int k0 = e - 127;
+                k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
+                k = max(-127, min(127, k));
+            }
+            const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = v[r][i] * inv;
+            uint32_t word, h[4];
+            asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 b0, %6, %5;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 b1, %8, %7;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 b2, %10, %9;\n\t"
+                "cvt.rn.satfinite.e2m1x2.f32 b3, %12, %11;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %1, b0;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %2, b1;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %3, b2;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %4, b3;\n\t"
+                "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+                : "=r"(word), "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+                : "f"(y[0]), "f"(y[1]), "f"(y[2]), "f"(y[3]), "f"(y[4]), "f"(y[5]), "f"(y[6]), "f"(y[7]));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
+                v[r][2 * i] = fmaf(-f.x, sc, v[r][2 * i]);
+                v[r][2 * i + 1] = fmaf(-f.y, sc, v[r][2 * i + 1]);
+            }
+            if (act[r]) {
+                const int g = gg[r];
+                uint8_t* im = img + (g / 8) * (kDecodeTerms * 128);
+                *reinterpret_cast<uint32_t*>(im + t * 128 + ((((g % 8) ^ (t & 7)) << 4) | (sub * 4))) = word;
+                if (sub == 0) sf[(g / 4) * 512 + (t & 31) * 16 + (t >> 5) * 4 + (g % 4)] = uint8_t(k + 127);
+            }
+        }
     }
 }
 

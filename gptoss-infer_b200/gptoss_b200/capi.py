@@ -26,6 +26,8 @@ SIGNATURES = {
     "gptoss_kernel_moe": ([P, P, P, P, P, P, P, P, P, P, I32, I32, I32, F32, F32], I32),
     "gptoss_kernel_mxfp4_dequant": ([P, P, P, I64], I32),
     "gptoss_set_moe_impl": ([I32], I32),
+    "gptoss_trace_enable": ([P, I64], I32),
+    "gptoss_selftest_terms": ([P, I32, P, P, I32], I32),
     "gptoss_selftest_mxf4_gemm": ([P, P, P, P, P, I32, I32], I32),
     "gptoss_moe_layer_create": ([P, F32, P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32], P),
     "gptoss_moe_layer_destroy": ([P], None),

@@ -96,9 +96,9 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
                                           int E, int k, int H, int I, float alpha, float limit);
 void gptoss_moe_layer_destroy(gptoss_moe_layer* layer);
 /* [extension] x_resid += MoE(RMSNorm(x)) for one token with a prepared layer, asynchronous on `stream` (a
- * cudaStream_t; NULL = legacy default stream): one cluster kernel (RMSNorm, router, top-k, softmax, x split into
- * e2m1 residual terms) and the two tensor-core GEMV kernels, chained with programmatic dependent launch. x_resid may
- * alias x. `events` as in gptoss_moe_block_async (recording them disables the kernels' overlap). Calls from one
+ * cudaStream_t; NULL = legacy default stream): one persistent cooperative kernel (RMSNorm, router, top-k, softmax,
+ * gate/up with SwiGLU, down with the weighted combine, all on tensor cores). x_resid may alias x. `events`, if not
+ * NULL, points to 4 cudaEvent_t: [0], [1], [2] are recorded before the kernel and [3] after it. Calls from one
  * thread share its workspace and must not overlap on the GPU. */
 int gptoss_moe_layer_forward(gptoss_moe_layer* layer, const float* x, float* x_resid, void* stream,
                              void* const* events);
@@ -109,6 +109,20 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* layer, const float* x, float* x_r
  * K % 64 == 0, 64 <= K <= 1024. Device pointers; synchronizes. */
 int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                               const uint8_t* b_scales, float* d, int N, int K);
+
+/* [extension] Pipeline tracing of the tensor-core decode kernel (profiling aid). With a device buffer of at least
+ * 160 * 160 int64 installed, every later gptoss_moe_layer_forward stores, per CTA, 160 clock64 stamps: [0] start,
+ * [1] expert ids known, [2+i] producer issues stage i, [34+i] MMA warp sees stage i landed, [66+g] epilogue finished
+ * segment g, [81] grid barrier passed, [82] end, [84..93] phase-0 and producer set-up steps, [96+i] MMA warp done
+ * issuing stage i (unused slots keep their old contents). NULL turns tracing off. A process-wide setting; not for
+ * concurrent use. */
+int gptoss_trace_enable(void* device_buffer, long long bytes);
+
+/* [extension] Self-test of the activation quantizer of the tensor-core path: splits x[n] (n % 256 == 0) into e2m1
+ * residual terms with per-32 E8M0 scales (which = 0: comparison rounding, 1: the hardware converters), decodes the
+ * terms back into out[n], and, if per_term is not NULL, stores the first two terms into per_term[2][n]. Device
+ * pointers; synchronizes. */
+int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, int which);
 
 /* [extension] Which decode MoE implementation gptoss_kernel_moe uses: 0 = SIMT (CUDA cores), 1 = tensor cores
  * (tcgen05 block-scaled MMA) where the shape allows it. Returns the previous setting, or -1. */

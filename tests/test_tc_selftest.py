@@ -37,3 +37,36 @@ def test_mxf4_gemm_selftest(N, K):
     err = np.abs(got - want)
     assert err.max() <= 1e-5 * np.abs(want).max(), err.max() / np.abs(want).max()
     assert np.linalg.norm(got - want) <= 1e-6 * np.linalg.norm(want)
+
+
+@pytest.mark.parametrize("which", [0, 1])
+def test_activation_terms_roundtrip(which):
+    """x -> 16 e2m1 residual terms -> decoded sum: within 2^-22 of each 32-block's maximum (fp32 rounding of the sum
+    included), and the first term equals the reference quantizer's rounding of x (oracle/mxfp4.quantize: the same
+    power-of-two scale), except at exact midpoints between e2m1 values, which round to even here and to the lower
+    value there."""
+    lib = capi.load()
+    g = torch.Generator().manual_seed(9 + which)
+    n = 3072
+    x = torch.randn(n, generator=g) * torch.exp(torch.randn(n, generator=g))    # widely varying magnitudes
+    x[:32] = 0.0
+    x[32:64] = torch.tensor([6.0, -6.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.25] + [1e-3] * 22)
+    dx = x.to(DEV)
+    out = torch.empty_like(dx)
+    per = torch.empty(2, n, device=DEV)
+    assert lib.gptoss_selftest_terms(P(dx), n, P(out), P(per), which) == 0, lib.gptoss_last_error().decode()
+    xb = x.view(-1, 32).double()
+    err = (out.cpu().double().view(-1, 32) - xb).abs().max(dim=1).values
+    amax = xb.abs().max(dim=1).values
+    assert (err <= amax * 2.0 ** -22).all(), (err / amax.clamp_min(1e-30)).max()
+    qb, qs = mxfp4.quantize(x.numpy().reshape(-1, 32)[None])
+    first = mxfp4.dequant(qb, qs).reshape(-1)
+    scale = np.repeat(mxfp4.e8m0_to_float(qs.reshape(-1)), 32)
+    y = np.abs(x.numpy()) / scale
+    tie = np.isin(y, np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32))
+    got = per[0].cpu().numpy()
+    assert tie.sum() >= 6
+    assert np.array_equal(got[~tie], first[~tie])
+    even = {0.25: 0.0, 0.75: 1.0, 1.25: 1.0, 1.75: 2.0, 2.5: 2.0, 3.5: 4.0, 5.0: 4.0}
+    want_tie = np.sign(x.numpy()[tie]) * np.array([even[float(v)] for v in y[tie]]) * scale[tie]
+    assert np.array_equal(got[tie], want_tie.astype(np.float32))

@@ -53,7 +53,7 @@ void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows
 // (tile counters and the grid barrier reset themselves afterwards).
 struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
-    size_t off_xq_img, off_xq_sf, off_partials, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu,
+    size_t off_partials, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu,
         off_cnt_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
 };
@@ -81,7 +81,7 @@ struct DecodeTcArgs {
     int k, H, I;
     float alpha, limit;
     void* workspace;              // decode_tc_layout(k, H, I).bytes
-    long long* trace = nullptr;   // optional pipeline trace: [num_sms][96] clock64 stamps
+    long long* trace = nullptr;   // optional pipeline trace: [num_sms][160] clock64 stamps
 };
 void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
 
@@ -91,7 +91,8 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
                         const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
                         cudaStream_t s);
 
-// Quantizes x [n] into kDecodeTerms e2m1 residual terms (which = 0: comparison quantizer, 1: converter quantizer)
+// Quantizes x [n] into kDecodeTerms e2m1 residual terms (which = 0: comparison quantizer, 1: converter quantizer,
+// 2: fixed scale schedule with fp32 rounding)
 // and decodes them back into out [n]; per_term (optional, [2][n]) receives the first two terms. Synchronizes.
 void selftest_terms(const float* x, int n, float* out, float* per_term, int which, void* scratch, size_t bytes,
                     cudaStream_t s);

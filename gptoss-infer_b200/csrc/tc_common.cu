@@ -248,7 +248,8 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
 }
 
 namespace {
-// One warp per 8 blocks: quantize x into residual terms with the chosen quantizer (0 = comparisons, 1 = converters).
+// One warp per 8 blocks: quantize x into residual terms with the chosen quantizer (0 = comparisons, 1 = converters,
+// 2 = fixed scale schedule with fp32 rounding, the decode kernel's quantizer).
 __global__ void terms_quantize_kernel(const float* x, int n, uint8_t* img, uint8_t* sf, int which) {
     const int lane = threadIdx.x & 31, sub = lane & 3;
     const int g = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 8 + (lane >> 2);
@@ -259,7 +260,8 @@ __global__ void terms_quantize_kernel(const float* x, int n, uint8_t* img, uint8
     for (int i = 0; i < 8; ++i) v[i] = active ? x[gg * 32 + sub * 8 + i] : 0.f;
     uint8_t* im = img + (gg / 8) * (kDecodeTerms * 128);
     uint8_t* sc = sf + (gg / 4) * 512;
-    if (which) quantize_block_terms_cvt(v, im, gg % 8, sc, gg % 4, sub, active);
+    if (which == 2) quantize_block_terms_fixed(v, im, gg % 8, sc, gg % 4, sub, active);
+    else if (which == 1) quantize_block_terms_cvt(v, im, gg % 8, sc, gg % 4, sub, active);
     else quantize_block_terms(v, im, gg % 8, sc, gg % 4, sub, active);
 }
 

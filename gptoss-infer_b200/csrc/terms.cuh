@@ -62,8 +62,10 @@ __device__ __forceinline__ void quantize_block_terms(float (&v)[8], uint8_t* img
 // pairs to e2m1 (nearest, ties to even) and cvt.rn.f16x2.e2m1x2 decodes them back exactly for the residual. About a
 // quarter of the instructions of the comparison form. The bytes are packed from and unpacked to whole 32-bit
 // registers inside the asm (16-bit views of wider registers were miscompiled into wrong bytes).
+// `reps` copies of the output are written, the r-th at img_stage + r * img_rs and sf_chunk + r * sf_rs.
 __device__ __forceinline__ void quantize_block_terms_cvt(float (&v)[8], uint8_t* img_stage, int q, uint8_t* sf_chunk,
-                                                         int kb, int sub, bool active) {
+                                                         int kb, int sub, bool active, int reps = 1,
+                                                         size_t img_rs = 0, size_t sf_rs = 0) {
 #pragma unroll 1
     for (int t = 0; t < kDecodeTerms; ++t) {
         float amax = 0.f;
@@ -105,8 +107,79 @@ __device__ __forceinline__ void quantize_block_terms_cvt(float (&v)[8], uint8_t*
             v[2 * i + 1] = fmaf(-f.y, sc, v[2 * i + 1]);
         }
         if (active) {
+            for (int r = 0; r < reps; ++r) {
+                *reinterpret_cast<uint32_t*>(img_stage + r * img_rs + t * 128 + (((q ^ (t & 7)) << 4) | (sub * 4))) =
+                    word;
+                if (sub == 0) sf_chunk[r * sf_rs + (t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(k + 127);
+            }
+        }
+    }
+}
+
+// Nearest e2m1 value of y for |y| <= 6, ties to even, in plain fp32 arithmetic: adding and subtracting 1.5 * 2^23 *
+// step rounds y to a multiple of the grid step (0.5 below 2, 1 below 4, 2 up to 6) with the hardware's
+// round-to-nearest-even, and an even multiple of the step is exactly an e2m1 value with an even mantissa bit. Short
+// latency (two adds after a select), unlike the converter instructions.
+__device__ __forceinline__ float round_e2m1(float y) {
+    const float a = fabsf(y);
+    const float c = a < 2.f ? 0x1.8p22f : (a < 4.f ? 0x1.8p23f : 0x1.8p24f);   // 1.5 * 2^23 * (0.5, 1, 2)
+    return __fsub_rn(__fadd_rn(y, c), c);
+}
+
+// e2m1 code (sign in bit 3) of a value q that is exactly an e2m1 value (other inputs give some code, never more
+// than 4 bits).
+__device__ __forceinline__ uint32_t e2m1_code(float q) {
+    const uint32_t u = __float_as_uint(q);
+    const float a = fabsf(q);
+    const uint32_t mag = a < 1.f ? (a > 0.f ? 1u : 0u) : ((((u & 0x7FFFFFFFu) >> 22) - 252u) & 7u);
+    return mag | ((u >> 28) & 8u);
+}
+
+constexpr int kActiveTerms = 10;              // terms quantize_block_terms_fixed computes; the rest are zero
+
+// Same image format and first term as quantize_block_terms_cvt, with the later terms' scales fixed instead of
+// taken from each residual's maximum: term 0 keeps the block's maximum within 6 * 2^k0, so its rounding error is at
+// most 2^k0 (the e2m1 grid step is 2 between 4 and 6); term 1 uses k0 - 2 (|y| <= 4), and from then on every
+// rounding error is at most half a grid step of 1, i.e. 2^(k-1), so k drops by 3 per term and |y| stays <= 4.
+// After kActiveTerms = 10 terms the remainder is below 2^-27 of the block's maximum scale (the subtractions are
+// exact); the remaining terms are written as zeros. There is no per-term maximum (no lane shuffles), and the rounding
+// is round_e2m1: each term is a short chain of full-rate fp32 operations per element. Scales below 2^-127 are clamped
+// there (the terms of such tiny remainders are then merely close, never NaN).
+__device__ __forceinline__ void quantize_block_terms_fixed(float (&v)[8], uint8_t* img_stage, int q, uint8_t* sf_chunk,
+                                                           int kb, int sub, bool active) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+    int k = -127;
+    {
+        const uint32_t bits = __float_as_uint(amax);
+        const int e = int((bits >> 23) & 0xFF);
+        if (e != 0) {
+            const int k0 = e - 127;
+            k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
+            k = max(-127, min(127, k));
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kDecodeTerms; ++t) {
+        uint32_t word = 0, scale = 0;
+        if (t < kActiveTerms) {
+            const int kc = max(-127, k);
+            const float inv = exp2i_exact(-kc), sc = exp2i_exact(kc);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float qv = round_e2m1(v[i] * inv);
+                v[i] = fmaf(-qv, sc, v[i]);
+                word |= e2m1_code(qv) << (4 * i);
+            }
+            scale = uint32_t(kc + 127);
+            k -= t == 0 ? 2 : 3;
+        }
+        if (active) {
             *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | (sub * 4))) = word;
-            if (sub == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(k + 127);
+            if (sub == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(scale);
         }
     }
 }

@@ -111,11 +111,9 @@ int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, 
                               const uint8_t* b_scales, float* d, int N, int K);
 
 /* [extension] Pipeline tracing of the tensor-core decode kernel (profiling aid). With a device buffer of at least
- * 160 * 160 int64 installed, every later gptoss_moe_layer_forward stores, per CTA, 160 clock64 stamps: [0] start,
- * [1] expert ids known, [2+i] producer issues stage i, [34+i] MMA warp sees stage i landed, [66+g] epilogue finished
- * segment g, [81] grid barrier passed, [82] end, [84..93] phase-0 and producer set-up steps, [96+i] MMA warp done
- * issuing stage i (unused slots keep their old contents). NULL turns tracing off. A process-wide setting; not for
- * concurrent use. */
+ * 160 * 160 int64 installed, every later gptoss_moe_layer_forward stores, per CTA, up to 160 clock64 stamps of its
+ * phases (the slot list is at the trace stamp helper in decode_tc.cu; unused slots keep their old contents). NULL
+ * turns tracing off. A process-wide setting; not for concurrent use. */
 int gptoss_trace_enable(void* device_buffer, long long bytes);
 
 /* [extension] Self-test of the activation quantizer of the tensor-core path: splits x[n] (n % 256 == 0) into e2m1

@@ -3,6 +3,7 @@
 // returning (runtime/src/capi.cpp:34-37).
 #include <cuda_runtime.h>
 
+#include <mutex>
 #include <stdexcept>
 #include <string>
 
@@ -229,6 +230,54 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
         gpt::launch_moe_decode_simt(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids,
                                     weights, x_resid, k, H, I, alpha, limit, scratch, nullptr);
         sync_check("moe");
+    });
+}
+
+// ---- gptoss_kernel_moe_static_scratch: the CUDA-core MoE with its scratch in a fixed device array
+//
+// The only scratch of the CUDA-core path is the SwiGLU output a[k][I] (fp32), written in full by the gate/up kernel
+// before the down kernel reads it, so it needs no zeroing between calls. Here it lives in one file-scope device
+// array per device (kStaticScratchFloats floats = 96 KiB: k <= 8 experts of I <= 3072) instead of memory obtained
+// from cudaMalloc. Its device address comes from cudaGetSymbolAddress, looked up once per device on the first call
+// made with that device current, and is then passed to the kernels like any scratch pointer.
+constexpr size_t kStaticScratchFloats = size_t(8) * 3072;
+static __device__ __align__(256) float g_moe_static_scratch[kStaticScratchFloats];
+
+namespace {
+std::mutex g_static_mu;
+void* g_static_addr[64] = {};
+
+void* static_scratch_address() {
+    int dev = 0;
+    GPT_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("moe_static_scratch: device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_moe_static_scratch);
+        if (e != cudaSuccess || !p)
+            throw std::runtime_error(std::string("moe_static_scratch: cudaGetSymbolAddress failed: ") +
+                                     cudaGetErrorString(e));
+        g_static_addr[dev] = p;
+    }
+    return g_static_addr[dev];
+}
+}  // namespace
+
+int gptoss_kernel_moe_static_scratch(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                                     const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                                     const float* x_norm, const int32_t* ids, const float* weights, float* x_resid,
+                                     int k, int H, int I, float alpha, float limit) {
+    return guard([&] {
+        if (k < 1 || k > 8) throw std::runtime_error("moe_static_scratch: k must be in 1..8");
+        if (I < 1 || size_t(k) * size_t(I) > kStaticScratchFloats)
+            throw std::runtime_error("moe_static_scratch: k * I = " + std::to_string(size_t(k) * size_t(I)) +
+                                     " exceeds the fixed scratch of " + std::to_string(kStaticScratchFloats) +
+                                     " floats (k <= 8 with I <= 3072)");
+        void* scratch = static_scratch_address();
+        gpt::launch_moe_decode_simt(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids,
+                                    weights, x_resid, k, H, I, alpha, limit, scratch, nullptr);
+        sync_check("moe_static_scratch");
     });
 }
 

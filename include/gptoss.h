@@ -66,6 +66,20 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
 
 /* ---- [extension] MoE-path entry points with no counterpart in the reference ------------------------------- */
 
+/* [extension] No counterpart in the reference. gptoss_kernel_moe for callers that must not allocate device memory
+ * during the call: for example an engine whose device memory is all handed to its own budgeted allocator, or a
+ * decode loop where an allocation (and the device synchronization cudaMalloc may imply) is not acceptable. Same
+ * arguments, semantics, layouts and synchronization as gptoss_kernel_moe, always on the CUDA-core path. Its only
+ * scratch (the SwiGLU output, k * I floats) lives in a fixed device array of 8 * 3072 floats (96 KiB) per device, so
+ * k * I must be at most 24576 (k <= 8 with I <= 3072); larger shapes return -1 with a message. Nothing in that array
+ * needs to start at zero. The first call on each device looks up the array's address (with that device current)
+ * and should come before any stream capture on that device. Calls that overlap on the same device (several host
+ * threads) share the one array and race: serialize them. */
+int gptoss_kernel_moe_static_scratch(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                                     const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                                     const float* x_norm, const int32_t* ids, const float* weights, float* x_resid,
+                                     int k, int H, int I, float alpha, float limit);
+
 /* [extension] Bit-exact MXFP4 decode of n_blocks blocks (16 bytes + 1 E8M0 scale each) into out[n_blocks * 32]
  * fp32, element 2j from the low nibble of byte j. Restates reference/gptoss_ref/mxfp4.py:17-31 on the GPU: returns
  * -1 if any scale is 0xFF (NaN in the OCP MX spec), as the reference's dequant raises. */

@@ -106,12 +106,14 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
                 const float* weights, float* x_resid, int k, int H, int I, float alpha, float limit, void* ws,
                 const gpt::DecodeTcLayout& L, cudaStream_t s) {
     char* w = static_cast<char*>(ws);
-    gpt::launch_repack_sf(gu_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_gu), k, 2 * I, H / 32, s, ids);
-    gpt::launch_repack_sf(dn_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_dn), k, H, I / 32, s, ids);
+    gpt::launch_repack_sf(gu_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_gu), k, 2 * I, H / 32, s, ids,
+                          gpt::kDecodeTileRows);
+    gpt::launch_repack_sf(dn_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_dn), k, H, I / 32, s, ids,
+                          gpt::kDecodeTileRows);
     // The expert count is not part of this ABI: the maps span the 32 experts the format allows; only the selected
     // experts' rows are ever read.
-    const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, 32, 128, 128);
-    const CUtensorMap td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, 32, 128, 128);
+    const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, 32, 128, gpt::kDecodeTileRows);
+    const CUtensorMap td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, 32, 128, gpt::kDecodeTileRows);
     gpt::DecodeTcArgs a{};
     a.tmap_gu = &tg;
     a.tmap_dn = &td;
@@ -357,12 +359,12 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
             throw std::runtime_error("moe_layer_create: need 1 <= k <= 8, k <= E <= 32, H % 64 == 0, I % 64 == 0");
         auto* l = new gptoss_moe_layer{norm_w, eps, router_w, router_b, gu_bias, dn_bias, E, k, H, I, alpha, limit};
         try {
-            GPT_CHECK(cudaMalloc(&l->sfa_gu, gpt::sf_repacked_bytes(E, 2 * I, H / 32)));
-            GPT_CHECK(cudaMalloc(&l->sfa_dn, gpt::sf_repacked_bytes(E, H, I / 32)));
-            gpt::launch_repack_sf(gu_scales, l->sfa_gu, E, 2 * I, H / 32, nullptr);
-            gpt::launch_repack_sf(dn_scales, l->sfa_dn, E, H, I / 32, nullptr);
-            l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, 128);
-            l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, 128);
+            GPT_CHECK(cudaMalloc(&l->sfa_gu, gpt::sf_repacked_bytes(E, 2 * I, H / 32, gpt::kDecodeTileRows)));
+            GPT_CHECK(cudaMalloc(&l->sfa_dn, gpt::sf_repacked_bytes(E, H, I / 32, gpt::kDecodeTileRows)));
+            gpt::launch_repack_sf(gu_scales, l->sfa_gu, E, 2 * I, H / 32, nullptr, nullptr, gpt::kDecodeTileRows);
+            gpt::launch_repack_sf(dn_scales, l->sfa_dn, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows);
+            l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
+            l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
             sync_check("moe_layer_create");
         } catch (...) {
             delete l;

@@ -1,29 +1,31 @@
 // Tensor-core decode MoE for one token: one persistent, cooperatively launched kernel per MoE layer.
 //
-// Operands. A = expert weights straight from the checkpoint layout (TMA boxes of 128 rows x 128 bytes of K, 128-byte
-// swizzle); their E8M0 scales repacked into 512-byte tcgen05 chunks. B = the activation vector split into R = 16
-// e2m1 residual terms, each with its own E8M0 scale per 32 elements, so x equals the sum of the terms to about
-// 2^-30 of each block's maximum: the MMA's N = 16 columns hold the terms, the tensor core performs the MXFP4
-// dequantization (tcgen05.mma kind::mxf4 block32) and the epilogue adds the 16 columns.
+// Operands. B = expert weights straight from the checkpoint layout: TMA boxes of 256 rows x 128 bytes of K (256
+// e2m1 values) with the 128-byte swizzle, one 32 KB box per pipeline stage; their E8M0 scales repacked once into
+// 512-byte tcgen05 chunks ([tile][K chunk][half]). A = the activation vector split into NT = 8 e2m1 residual terms,
+// each with its own E8M0 scale per 32 elements (x equals their sum to 2^-24 of each block's maximum): 8 rows of
+// 128 bytes per 256 values of K, read as M = 128 rows through a descriptor whose 8-row groups all start at the same
+// address. One tcgen05.mma kind::mxf4 (M = 128, N = 256, K = 64) therefore consumes 8 KB of weights; the tensor core
+// performs the MXFP4 dequantization, accumulator rows 0..7 hold the 8 terms' dot products and the epilogue adds them.
 //
 // Phases of every CTA (all 148 resident, one per SM):
 //   0. RMSNorm of x (every CTA, into shared memory) and the router split over the grid: each CTA computes the
 //      router's partial dot products over its slice of K (fp64, exact products) and publishes them; after a
 //      counting barrier every CTA adds all partial sums in the same fixed order (so all CTAs pick the same experts),
 //      takes the top k (ties to the lower id) and the softmax over the k.
-//   1. Gate/up stream-K GEMV; the CTA finishing a 128-row tile applies bias, the clamped SwiGLU (rows 2j glu, 2j+1
-//      linear) and the slot's gate weight, and writes the result as down's B terms (global memory).
-//   2. Down stream-K GEMV over K' = k * I: the k experts' rows form one long GEMV because B carries the gate
+//   1. Gate/up stream-K GEMV; the CTA finishing a 256-row tile applies bias, the clamped SwiGLU (rows 2j glu, 2j+1
+//      linear) and the slot's gate weight, and writes the tile's 128 activations as down's A terms (global memory).
+//   2. Down stream-K GEMV over K' = k * I: the k experts' rows form one long GEMV because A carries the gate
 //      weights; the CTA finishing a tile adds sum_slot w b2 and the residual.
-// Roles: warp 0 streams the weights (TMA, one 16 KB box per stage, gate/up and down through one ring, so down's
-// weights arrive while the grid finishes gate/up); warp 1 issues the MMAs (every scale factor is copied into TMEM
-// once, up front, and one commit releases two ring slots: a tcgen05.commit costs about ten MMAs to issue); warps
-// 2-5 split h into x's terms in shared memory and load the weight scale chunks with asynchronous 16-byte copies,
-// run the tile epilogues, and after the grid barrier (all gate/up epilogues done) load down's B terms. Every wait is bounded:
-// the launch is cooperative, so all CTAs are resident and every barrier completes; a timeout records an error
-// instead of hanging. Split tiles are reduced by their last contributor (deterministic order), never by spinning.
-// The per-CTA stage lists are computed on the host once per shape (stream-K partition, segment boundaries and
-// which CTAs share each tile) and read by each CTA at start.
+// Roles: warp 0 streams the weights (TMA, gate/up and down through one ring, so down's weights arrive while the grid
+// finishes gate/up); warp 1 issues the tcgen05 operations (per stage: the weight scales into a ring of TMEM columns,
+// x's scales the first time they are needed, 4 MMAs, one commit); warps 2-5 split h into x's terms in shared memory
+// and load the weight scale chunks with asynchronous 16-byte copies, run the tile epilogues (the accumulator is read
+// out by the warp that owns TMEM lanes 0-31), and after the grid barrier (all gate/up epilogues done) load down's A
+// terms. Every wait is bounded: the launch is cooperative, so all CTAs are resident and every barrier completes; a
+// timeout records an error instead of hanging. Split tiles are reduced by their last contributor (deterministic
+// order), never by spinning. The per-CTA stage lists are computed on the host once per shape (stream-K partition,
+// segment boundaries and which CTAs share each tile) and read by each CTA at start.
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -44,18 +46,25 @@ namespace fz {
 using sk::Part;
 using sk::Stage;
 static_assert(sizeof(Stage) % 4 == 0, "stage entries are copied as 32-bit words");
-constexpr int R = kDecodeTerms;
+constexpr int NT = 8;                         // activation terms (A rows)
+constexpr int kRows = kDecodeTileRows;        // weight rows per tile (the MMA's N)
 constexpr int kThreads = 192;                 // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue
-constexpr int kA = 16384, kB = R * 128;       // one weight stage (128 rows x 128 bytes of K), one B stage
+constexpr int kB = kRows * 128;               // one weight stage: 256 rows x 128 bytes of K (32 KB)
+constexpr int kA = NT * 128;                  // one activation stage: 8 terms x 128 bytes (1 KB)
+constexpr int kSFB = 2 * 1024;                // a stage's weight scales: 2 K chunks x 2 halves x 512 bytes
+constexpr int kSlot = kB + kSFB;              // ring slot: the weight box, then its scales
+constexpr int kSF8 = 128;                     // an activation scale chunk: rows 0-7 of a 512-byte chunk
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColSF = 2 * R;            // accumulators in columns [0, 2R), scale factors from 2R on
+constexpr uint32_t kColX = kRows;             // accumulator in columns [0, 256); x's scale chunks from 256 on
 constexpr int kTraceSlots = 160;
 constexpr int kMaxK = 8;
 constexpr int kMaxX4 = 8;                     // x is held as kMaxX4 float4 per thread: H <= 4 * kThreads * kMaxX4
+constexpr int kEpiWarpLane0 = 4;              // the epilogue warp that may read TMEM lanes 0-31 (warp % 4 == 0)
 
 struct Layout {
-    int NS, cap;                              // weight ring depth (even), stage-list capacity
-    int ringA, regBgu, regSFBgu, regSFA, regBdn, regSFBdn, hs, bars, misc, bytes;
+    int NS, NSF, cap;                         // weight ring depth, TMEM scale ring depth, stage-list capacity
+    uint32_t colSFB, colDSF;                  // TMEM columns of the weight-scale ring and of down's A-scale ring
+    int ring, xA, xSF, dA, dSF, hs, red, bars, misc, bytes;
 };
 
 struct Job {
@@ -67,32 +76,34 @@ struct Job {
     const float* x;
     const int* ids_in;
     const float* w_in;
-    int* ids_out;                             // written by the publishing CTA when not null
+    int* ids_out;                             // written by CTA 0 when not null
     float* w_out;
-    const uint8_t* sfa_gu;                    // [mat][RT][KT][512]
-    const uint8_t* sfa_dn;
-    int sfa_by_slot;                          // mat = slot (1) or expert id (0)
+    const uint8_t* sf_gu;                     // [mat][RT][KT][2][512]
+    const uint8_t* sf_dn;
+    int sf_by_slot;                           // mat = slot (1) or expert id (0)
     const float* gu_bias;                     // [E][2I]
     const float* dn_bias;                     // [E][H]
     float alpha, limit;
     Part gu, dn;
     const Stage* stab;                        // host-built stage lists of all CTAs
     const int* shdr;                          // [grid][4]: first entry, entries, gate/up entries
-    int sf_upfront;                           // 1: every scale chunk of the CTA fits in TMEM at once
-    uint8_t* aq_img;                          // down's B terms [k][SPS_dn][R*128]
-    uint8_t* aq_sf;                           // down's B scales [k][KT_dn][512]
+    uint8_t* xq_img;                          // x's A terms [SPS_gu][NT*128] (written by all CTAs in phase 0)
+    uint8_t* xq_sf;                           // their scales [KT_gu][128] (rows 0-7 of each chunk)
+    uint8_t* aq_img;                          // down's A terms [k][SPS_dn][NT*128]
+    uint8_t* aq_sf;                           // down's A scales [k][KT_dn][128]
     float* x_resid;
-    unsigned* gbar;                           // [3]: gate/up done, exits, router partials published
+    unsigned* gbar;                           // [3]: gate/up done, exits, router partials and x blocks published
     double* partials;                         // [grid][32] router partial sums
     int* err;
     long long* trace;                         // optional [grid][kTraceSlots] clock64 stamps
     Layout L;
 };
 
-// Trace slots per CTA: 0 start, 84 h in shared memory, 85 router partials published, 86 all partials published, 87
-// logits, 88 ids known, 1 phase 0 done, 89 producer start, 2+i producer issues stage i, 80 small operands in shared memory, 90 scale
-// factors in TMEM, 34+i MMA warp sees stage i landed, 96+i its MMAs issued, 66+g epilogue finished segment g, 81 grid
-// barrier passed, 83 down's B terms in shared memory, 82 end.
+// Trace slots per CTA: 0 start, 123 stage list copied, 124/125 sum of squares, 84 h in shared memory, 85 router
+// partials published, 86 all partials published, 87 partial sums added, 120 logits, 121 top k, 122 softmax, 88 ids
+// known, 1 phase 0 done, 89 producer start, 2+i producer issues stage i, 126 scale copies issued, 127+p x terms pass
+// p, 80 small operands in shared memory, 34+i MMA warp sees stage i landed, 96+i its MMAs issued, 66+g epilogue
+// finished segment g, 81 grid barrier passed, 83 down's A terms in shared memory, 82 end.
 __device__ __forceinline__ void stamp(const Job& j, int slot) {
     if (j.trace) j.trace[size_t(blockIdx.x) * kTraceSlots + slot] = clock64();
 }
@@ -113,34 +124,61 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     return v;
 }
 
+// Atomic add with acquire-release semantics at GPU scope: the CTA's stores before a bar.sync are released with it,
+// and the returning thread acquires the other contributors' (other threads read after the next bar.sync).
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ double bf16lo(uint32_t w) { return double(__uint_as_float(w << 16)); }
 __device__ __forceinline__ double bf16hi(uint32_t w) { return double(__uint_as_float(w & 0xffff0000u)); }
+
+// Warp reads 32 lanes (its quadrant) x 32 consecutive fp32 columns: thread t gets lane (quadrant * 32 + t).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
 
 __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_constant__ CUtensorMap tm_gu,
                                                                 const __grid_constant__ CUtensorMap tm_dn,
                                                                 const __grid_constant__ Job j) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int NS = j.L.NS, cap = j.L.cap, NP = NS / 2;
-    uint8_t* ringA = smem + j.L.ringA;
-    uint8_t* regBgu = smem + j.L.regBgu;
-    uint8_t* regSFBgu = smem + j.L.regSFBgu;
-    uint8_t* regSFA = smem + j.L.regSFA;
-    uint8_t* regBdn = smem + j.L.regBdn;
-    uint8_t* regSFBdn = smem + j.L.regSFBdn;
-    uint64_t* fullA = reinterpret_cast<uint64_t*>(smem + j.L.bars);   // [NS] weight stage landed
-    uint64_t* emptyP = fullA + NS;            // [NS/2] both slots of a pair consumed by the MMAs
-    uint64_t* fullS = emptyP + NP;            // [0] gate/up's small operands, [1] down's B terms and scales
-    uint64_t* accF = fullS + 2;               // [2] accumulator buffer complete
-    uint64_t* accE = accF + 2;                // [2] accumulator buffer read out
+    const int NS = j.L.NS, NSF = j.L.NSF, cap = j.L.cap;
+    uint8_t* ring = smem + j.L.ring;          // [NS][kSlot] weight stages and their scales
+    uint8_t* xA = smem + j.L.xA;              // [SPS_gu][kA] x's terms
+    uint8_t* xSF = smem + j.L.xSF;            // [KT_gu][kSF8] x's scales
+    uint8_t* dA = smem + j.L.dA;              // [cap_dn][kA] down's A terms
+    uint8_t* dSF = smem + j.L.dSF;            // [cap_dn][2][kSF8] their scales
+    float* red_s = reinterpret_cast<float*>(smem + j.L.red);                // [NT][kRows] accumulator rows 0..7
+    uint64_t* fullB = reinterpret_cast<uint64_t*>(smem + j.L.bars);        // [NS] weight stage landed
+    uint64_t* emptyB = fullB + NS;            // [NS] weight stage consumed by the MMAs
+    uint64_t* fullS = emptyB + NS;            // [0] gate/up's small operands
+    uint64_t* accF = fullS + 2;               // accumulator complete (one phase per segment)
+    uint64_t* accE = accF + 1;                // accumulator read out (one phase per segment)
+    uint64_t* fullD = accE + 1;               // [cap] down stage's A terms and scales loaded
     float* hs = reinterpret_cast<float*>(smem + j.L.hs);     // h = RMSNorm(x) [H]
     uint32_t* holder = reinterpret_cast<uint32_t*>(smem + j.L.misc);
-    int* cnts = reinterpret_cast<int*>(holder + 2);          // [2] partials barrier result, [3] grid barrier result
+    int* cnts = reinterpret_cast<int*>(holder + 2);          // [2] partials barrier / last-arrival flag, [3] grid
     double* red = reinterpret_cast<double*>(cnts + 6);       // [6][32] router sums
     int* ids_s = reinterpret_cast<int*>(red + 7 * 32);       // [8]
     float* w_s = reinterpret_cast<float*>(ids_s + kMaxK);    // [8]
-    float* aval = w_s + kMaxK;                               // [64]
-    Stage* stages = reinterpret_cast<Stage*>(aval + 64);     // [cap]
+    float* aval = w_s + kMaxK;                               // [kRows / 2] activations of one tile
+    Stage* stages = reinterpret_cast<Stage*>(aval + kRows / 2);   // [cap]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, nc = gridDim.x;
@@ -153,24 +191,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     if (j.router_w && lane < j.E && cs0 + warp < cs1)
         w_first = __ldg(reinterpret_cast<const uint4*>(j.router_w) + size_t(lane) * H8 + cs0 + warp);
     const float bias = j.router_w && warp == 0 && lane < j.E ? __ldg(j.router_b + lane) : 0.f;
-    // x and the norm weights, kept in registers: thread t holds float4 chunks t, t + kThreads, ...
+    // the norm weights and x, kept in registers: thread t holds float4 chunks t, t + kThreads, ...
     float4 xv[kMaxX4], gv[kMaxX4];
 #pragma unroll
     for (int r = 0; r < kMaxX4; ++r) {
         const int i = (tid + r * kThreads) * 4;
-        xv[r] = i < j.H ? *reinterpret_cast<const float4*>(j.x + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         gv[r] = i < j.H && j.norm_w ? __ldg(reinterpret_cast<const float4*>(j.norm_w + i))
                                     : make_float4(1.f, 1.f, 1.f, 1.f);
     }
     if (tid == 0) {
-        for (int i = 0; i < NS; ++i) tc::mbar_init(&fullA[i], 1);
-        for (int i = 0; i < NP; ++i) tc::mbar_init(&emptyP[i], 1);
-        tc::mbar_init(&fullS[0], 128);                       // one arrival per epilogue thread after its copies
-        tc::mbar_init(&fullS[1], 128);
-        for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&accF[i], 1);
-            tc::mbar_init(&accE[i], 128);
+        for (int i = 0; i < NS; ++i) {
+            tc::mbar_init(&fullB[i], 1);
+            tc::mbar_init(&emptyB[i], 1);
         }
+        tc::mbar_init(&fullS[0], 128);                       // one arrival per epilogue thread after its copies
+        tc::mbar_init(accF, 1);
+        tc::mbar_init(accE, 1);
+        for (int i = 0; i < cap; ++i) tc::mbar_init(&fullD[i], 1);
         tc::fence_barrier_init();
     }
     const int s_first = __ldg(j.shdr + 4 * c), s_n = __ldg(j.shdr + 4 * c + 1), s_ngu = __ldg(j.shdr + 4 * c + 2);
@@ -181,13 +218,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         const int nw = nst * int(sizeof(Stage) / 4);
         for (int i = tid; i < nw; i += kThreads) dst[i] = __ldg(src + i);
     }
-    if (tid == 0 && s_n > cap) atomicCAS(j.err, 0, 100);    // host sized the stage list too small
-    if (tid == 0) stamp(j, 123);
     if (warp == 1) {
         tc::tmem_alloc(holder, kTmemCols);
         tc::tmem_relinquish();
     }
-
+    // Everything above reads only what no earlier kernel writes (stage table, weights, biases). With programmatic
+    // dependent launch the next layer's kernel is released now and this one waits here for the previous layer's
+    // kernel to finish (x, the residual stream, and the shared workspace are written there).
+    pdl_launch_dependents();
+    pdl_wait();
+    if (tid == 0 && s_n > cap) atomicCAS(j.err, 0, 100);    // host sized the stage list too small
+    if (tid == 0) stamp(j, 123);
+#pragma unroll
+    for (int r = 0; r < kMaxX4; ++r) {
+        const int i = (tid + r * kThreads) * 4;
+        xv[r] = i < j.H ? *reinterpret_cast<const float4*>(j.x + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     // ---------------------------------------------------------------- phase 0: RMSNorm, router, expert ids
     {
         const int H = j.H;
@@ -219,8 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         }
         __syncthreads();
         if (tid == 0) stamp(j, 84);
+        double acc = 0.0;
         if (j.router_w) {
-            double acc = 0.0;
             for (int cc = cs0 + warp; cc < cs1; cc += kThreads / 32) {
                 if (lane < j.E) {
                     const uint4 u = cc == cs0 + warp
@@ -234,44 +280,61 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                     acc = fma(bf16lo(u.w), double(h1.z), acc); acc = fma(bf16hi(u.w), double(h1.w), acc);
                 }
             }
-            red[warp * 32 + lane] = acc;
-            __syncthreads();
-            if (warp == 0) {
+        }
+        red[warp * 32 + lane] = acc;
+        {
+            // this CTA's share of x's 32-blocks -> A terms in global memory, published with the partial sums
+            // (warps 5, 4, 3: the router slice of a CTA rarely has more than 3 chunks, so these warps are free)
+            const int nb = H / 32, b0 = int((long long)c * nb / nc), b1 = int((long long)(c + 1) * nb / nc);
+            bool wrote = false;
+            if (warp >= 3)
+                for (int g = b0 + (kThreads / 32 - 1 - warp); g < b1; g += 3) {
+                    quantize_block_terms_warp32<NT>(hs[g * 32 + lane], j.xq_img + (g / 8) * kA, g % 8,
+                                                    j.xq_sf + (g / 4) * kSF8, g % 4, true);
+                    wrote = true;
+                }
+            if (wrote) __threadfence();
+        }
+        __syncthreads();
+        if (warp == 0) {
+            if (j.router_w) {
                 double t = 0.0;
                 for (int w = 0; w < kThreads / 32; ++w) t += red[w * 32 + lane];
                 j.partials[size_t(c) * 32 + lane] = t;
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) {
-                    atomicAdd(&j.gbar[2], 1u);
-                    stamp(j, 85);
-                }
-                // every CTA's partial sums published (bounded wait; the launch is cooperative)
-                bool done = false;
-                for (uint32_t i = 0; i < tc::kSpinLimit && !done; ++i) {
-                    done = __shfl_sync(kFull, lane == 0 ? ld_acquire(&j.gbar[2]) >= unsigned(nc) : false, 0);
-                    if (!done) __nanosleep(20);
-                }
-                if (lane == 0) {
-                    if (!done) atomicCAS(j.err, 0, 10);
-                    cnts[2] = done;
-                    stamp(j, 86);
-                }
             }
-            __syncthreads();
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+                atomicAdd(&j.gbar[2], 1u);
+                stamp(j, 85);
+            }
+            // every CTA's partial sums and x blocks published (bounded wait; the launch is cooperative)
+            bool done = false;
+            for (uint32_t i = 0; i < tc::kSpinLimit && !done; ++i) {
+                done = __shfl_sync(kFull, lane == 0 ? ld_acquire(&j.gbar[2]) >= unsigned(nc) : false, 0);
+                if (!done) __nanosleep(20);
+            }
+            if (lane == 0) {
+                if (!done) atomicCAS(j.err, 0, 10);
+                cnts[2] = done;
+                stamp(j, 86);
+            }
+        }
+        __syncthreads();
+        if (j.router_w) {
             // every CTA adds all partial sums in the same order: thread (w, e) takes CTAs w, w + 6, ... (loads
-            // issued eight at a time), then warp 0 adds the six sums
+            // issued thirteen at a time), then warp 0 adds the six sums
             double t = 0.0;
             if (cnts[2]) {
-                for (int c0 = warp; c0 < nc; c0 += 8 * (kThreads / 32)) {
-                    double v[8];
+                for (int c0 = warp; c0 < nc; c0 += 13 * (kThreads / 32)) {
+                    double v[13];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
+                    for (int u = 0; u < 13; ++u) {
                         const int cc = c0 + u * (kThreads / 32);
                         v[u] = cc < nc ? __ldcg(&j.partials[size_t(cc) * 32 + lane]) : 0.0;
                     }
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) t += v[u];
+                    for (int u = 0; u < 13; ++u) t += v[u];
                 }
             }
             red[warp * 32 + lane] = t;
@@ -319,16 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         }
         if (tid == 0) stamp(j, 88);
     }
+    tc::fence_proxy_async_smem();             // h's shared memory becomes the TMA ring from here on
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     if (tid == 0) stamp(j, 1);
     const uint32_t tmem = *holder;
-    const bool upfront = j.sf_upfront != 0;
-    // TMEM columns of the scale factors. Up front: stage i's weight scales at kColSF + 8i, x's scale chunk kt at
-    // sfb_gu0 + 4kt, down stage i's B scales at sfb_dn0 + 8(i - ngu). Otherwise copied per stage to kColSF (A) and
-    // kColSF + 8 (B).
-    const uint32_t sfb_gu0 = kColSF + 8u * uint32_t(nst), sfb_dn0 = sfb_gu0 + 4u * uint32_t(j.gu.KT);
 
     auto part_of = [&](const Stage& st) -> const Part& { return st.mode == sk::kGateUp ? j.gu : j.dn; };
 
@@ -340,291 +399,304 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             tc::prefetch_tmap(&tm_dn);
         }
         __syncwarp();
-        // Stages 2p and 2p+1 share slot pair p % NP; the MMA warp releases a pair with one commit.
-        auto wait_pair = [&](int it) -> bool {
-            const int p = (it - NS) >> 1;
-            return __all_sync(kFull, tc::mbar_wait(&emptyP[p % NP], uint32_t(p / NP) & 1u, j.err, 1));
+        auto wait_slot = [&](int it) -> bool {                // stage it - NS released its slot
+            const int p = it - NS;
+            return __all_sync(kFull, tc::mbar_wait(&emptyB[p % NS], uint32_t(p / NS) & 1u, j.err, 1));
         };
         // The tensor map is a compile-time operand of each loop: selecting it at run time made every TMA issue wait
         // for a descriptor fetch.
         bool ok = true;
+        // Each stage: the weight box (TMA) and its scale chunks (one bulk copy of nkt KB, contiguous in the repacked
+        // layout) complete on the slot's barrier.
+        auto scales_of = [&](const Stage& st, const Part& p, const uint8_t* base, int rt) {
+            const int mat = j.sf_by_slot ? int(st.s) : ids_s[st.s];
+            return base + ((size_t(mat) * p.RT + rt) * p.KT + st.ku0 / 2) * 1024;
+        };
         for (int it = 0; it < ngu && ok; ++it) {
-            if (it >= NS && (it & 1) == 0) ok = wait_pair(it);
+            if (it >= NS) ok = wait_slot(it);
             if (ok && tc::elect_one()) {
                 if (it < 32) stamp(j, 2 + it);
                 const Stage& st = stages[it];
-                tc::mbar_arrive_expect_tx(&fullA[it % NS], kA);
-                tc::tma_load_3d(ringA + (it % NS) * kA, &tm_gu, (st.ku0 / 4) * 128, (st.tile % j.gu.RT) * 128,
-                                ids_s[st.s], &fullA[it % NS]);
+                const int rt = st.tile % j.gu.RT;
+                const uint32_t sb = uint32_t(sk::nkt_of(st)) * 1024u;
+                uint8_t* dst = ring + (it % NS) * kSlot;
+                tc::mbar_arrive_expect_tx(&fullB[it % NS], kB + sb);
+                tc::tma_load_3d(dst, &tm_gu, (st.ku0 / 4) * 128, rt * kRows, ids_s[st.s], &fullB[it % NS]);
+                tc::bulk_g2s(dst + kB, scales_of(st, j.gu, j.sf_gu, rt), sb, &fullB[it % NS]);
             }
             __syncwarp();
         }
         for (int it = ngu; it < nst && ok; ++it) {
-            if (it >= NS && (it & 1) == 0) ok = wait_pair(it);
+            if (it >= NS) ok = wait_slot(it);
             if (ok && tc::elect_one()) {
                 if (it < 32) stamp(j, 2 + it);
                 const Stage& st = stages[it];
-                tc::mbar_arrive_expect_tx(&fullA[it % NS], kA);
-                tc::tma_load_3d(ringA + (it % NS) * kA, &tm_dn, (st.ku0 / 4) * 128, st.tile * 128, ids_s[st.s],
-                                &fullA[it % NS]);
+                const uint32_t sb = uint32_t(sk::nkt_of(st)) * 1024u;
+                uint8_t* dst = ring + (it % NS) * kSlot;
+                tc::mbar_arrive_expect_tx(&fullB[it % NS], kB + sb);
+                tc::tma_load_3d(dst, &tm_dn, (st.ku0 / 4) * 128, st.tile * kRows, ids_s[st.s], &fullB[it % NS]);
+                tc::bulk_g2s(dst + kB, scales_of(st, j.dn, j.sf_dn, st.tile), sb, &fullB[it % NS]);
             }
             __syncwarp();
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------------- MMA issuer (converged warp, one lane)
-        // One fixed lane issues every tcgen05 operation, so scale copies and MMAs are ordered. With the scales up
-        // front, each stage's scale chunks are copied into their own TMEM columns before the stage's data is waited
-        // for (the copies overlap that wait); x's scale chunks are copied the first time a stage needs them.
-        const bool leader = tc::elect_one();
-        bool ok = nst == 0 || tc::mbar_wait(&fullS[0], 0, j.err, 6);
-        ok = __all_sync(kFull, ok);
-        unsigned long long x_sf_done = 0;                    // x's scale chunks in TMEM (leader's copy)
-        for (int it = 0; it < nst && ok; ++it) {
-            const Stage& st = stages[it];
-            const int slot = it % NS, ph = (it / NS) & 1;
-            const int buf = st.seg & 1;
-            const int kt0 = st.ku0 / 2, nkt = sk::nkt_of(st);
-            const bool gu = st.mode == sk::kGateUp;
-            if (it == ngu) ok = __all_sync(kFull, tc::mbar_wait(&fullS[1], 0, j.err, 9));   // down's B terms
-            if (ok && upfront) {
+        // ---------------------------------------------------------------- MMA issuer (one lane of warp 1)
+        // One fixed lane issues every tcgen05 operation, so scale copies and MMAs execute in issue order. Per stage:
+        // the activation scales (x's chunk the first time a stage needs it, or down's chunks into the A-scale ring
+        // slot it % NSF) before the stage's data is waited for, then the weight scales (4 chunks from the ring slot:
+        // 2 K chunks x 2 row halves, 8 TMEM columns per K chunk) into weight-scale slot it % NSF, up to 4 MMAs and
+        // one commit.
+        if (tc::elect_one()) {
+            bool ok = nst == 0 || tc::mbar_wait(&fullS[0], 0, j.err, 6);
+            unsigned long long x_sf_done = 0;                // x's scale chunks in TMEM
+            for (int it = 0; it < nst && ok; ++it) {
+                const Stage& st = stages[it];
+                const int slot = it % NS, ph = (it / NS) & 1, f = it % NSF;
+                const int kt0 = st.ku0 / 2, nkt = sk::nkt_of(st);
+                const bool gu = st.mode == sk::kGateUp;
+                if (it >= ngu) ok = tc::mbar_wait(&fullD[it - ngu], 0, j.err, 9);   // this stage's A terms
+                if (!ok) break;
                 tc::tc_fence_after();
-                if (leader) {
-                    for (int q = 0; q < nkt; ++q)
-                        tc::tmem_cp_sf(tmem + kColSF + 8 * it + 4 * q,
-                                       tc::desc_sf_chunk(tc::smem_u32(regSFA + it * 1024 + q * 512)));
-                    if (gu) {
-                        for (int q = 0; q < nkt; ++q) {
-                            const int kt = kt0 + q;
-                            if (!((x_sf_done >> kt) & 1ull)) {
-                                tc::tmem_cp_sf(tmem + sfb_gu0 + 4 * kt,
-                                               tc::desc_sf_chunk(tc::smem_u32(regSFBgu + kt * 512)));
-                                x_sf_done |= 1ull << kt;
-                            }
-                        }
-                    } else {
-                        for (int q = 0; q < nkt; ++q)
-                            tc::tmem_cp_sf(tmem + sfb_dn0 + 8 * (it - ngu) + 4 * q,
-                                           tc::desc_sf_chunk(tc::smem_u32(regSFBdn + (it - ngu) * 1024 + q * 512)));
-                    }
-                }
-                __syncwarp();
-            }
-            if (st.first && st.seg >= 2) ok = ok && tc::mbar_wait(&accE[buf], ((st.seg >> 1) - 1) & 1, j.err, 2);
-            ok = ok && tc::mbar_wait(&fullA[slot], ph, j.err, 3);
-            ok = __all_sync(kFull, ok);
-            if (!ok) break;
-            tc::tc_fence_after();
-            if (leader) {
-                if (it < 32) stamp(j, 34 + it);
-                const uint8_t* bst = gu ? regBgu + (st.ku0 / 4) * kB : regBdn + (it - ngu) * kB;
-                uint32_t sfa_c, sfb_c;
-                if (upfront) {
-                    sfa_c = kColSF + 8u * uint32_t(it);
-                    sfb_c = gu ? sfb_gu0 + 4u * uint32_t(kt0) : sfb_dn0 + 8u * uint32_t(it - ngu);
-                } else {
-                    sfa_c = kColSF;
-                    sfb_c = kColSF + 8;
-                    const uint8_t* sfb = gu ? regSFBgu + kt0 * 512 : regSFBdn + (it - ngu) * 1024;
+                if (gu) {
                     for (int q = 0; q < nkt; ++q) {
-                        tc::tmem_cp_sf(tmem + sfa_c + 4 * q, tc::desc_sf_chunk(tc::smem_u32(regSFA + it * 1024 + q * 512)));
-                        tc::tmem_cp_sf(tmem + sfb_c + 4 * q, tc::desc_sf_chunk(tc::smem_u32(sfb + q * 512)));
+                        const int kt = kt0 + q;
+                        if (!((x_sf_done >> kt) & 1ull)) {
+                            tc::tmem_cp_sf(tmem + kColX + 4 * kt, tc::desc_sf_chunk8(tc::smem_u32(xSF + kt * kSF8)));
+                            x_sf_done |= 1ull << kt;
+                        }
                     }
+                } else {
+                    for (int q = 0; q < nkt; ++q)
+                        tc::tmem_cp_sf(tmem + j.L.colDSF + 8 * f + 4 * q,
+                                       tc::desc_sf_chunk8(tc::smem_u32(dSF + (it - ngu) * 2 * kSF8 + q * kSF8)));
                 }
+                // one accumulator: a segment's first MMA waits until the previous segment has been read out
+                if (st.first && st.seg >= 1) ok = tc::mbar_wait(accE, uint32_t(st.seg - 1) & 1u, j.err, 2);
+                ok = ok && tc::mbar_wait(&fullB[slot], ph, j.err, 3);
+                if (!ok) break;
+                tc::tc_fence_after();
+                if (it < 32) stamp(j, 34 + it);
+                const uint8_t* wslot = ring + slot * kSlot;
+                for (int q = 0; q < nkt; ++q)
+                    for (int h = 0; h < 2; ++h)
+                        tc::tmem_cp_sf(tmem + j.L.colSFB + 16 * f + 8 * q + 4 * h,
+                                       tc::desc_sf_chunk(tc::smem_u32(wslot + kB + (2 * q + h) * 512)));
+                const uint8_t* ast = gu ? xA + (st.ku0 / 4) * kA : dA + (it - ngu) * kA;
                 for (int u = 0; u < st.nu; ++u) {
                     const int ku = st.ku0 + u;
                     const uint32_t sf_id = 2u * (ku & 1);
-                    const uint32_t q = uint32_t(ku / 2 - kt0);
-                    const uint64_t ad = tc::desc_sw128(tc::smem_u32(ringA + slot * kA + u * 32));
-                    const uint64_t bd = tc::desc_sw128(tc::smem_u32(bst + u * 32));
-                    tc::mma_mxf4(tmem + buf * R, ad, bd, tc::idesc_mxf4(128, R, sf_id, sf_id),
-                                 (tmem + sfa_c + 4 * q) | (sf_id << 30), (tmem + sfb_c + 4 * q) | (sf_id << 30),
-                                 !(st.first && u == 0));
+                    const int q = ku / 2 - kt0;
+                    const uint64_t ad = tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32));
+                    const uint64_t bd = tc::desc_sw128(tc::smem_u32(wslot + u * 32));
+                    const uint32_t sfa = gu ? tmem + kColX + 4 * (ku / 2) : tmem + j.L.colDSF + 8 * f + 4 * q;
+                    const uint32_t sfbc = tmem + j.L.colSFB + 16 * f + 8 * q;
+                    tc::mma_mxf4(tmem, ad, bd, tc::idesc_mxf4(128, kRows, sf_id, sf_id), sfa | (sf_id << 30),
+                                 sfbc | (sf_id << 30), !(st.first && u == 0));
                 }
-                if ((it & 1) || it == nst - 1) tc::mma_commit(&emptyP[(it >> 1) % NP]);
-                if (st.last) tc::mma_commit(&accF[buf]);
+                tc::mma_commit(&emptyB[slot]);
+                if (st.last) tc::mma_commit(accF);
                 if (it < 32) stamp(j, 96 + it);
             }
-            __syncwarp();
         }
+        __syncwarp();
     } else {
         // ---------------------------------------------------------------- epilogue warps 2..5
-        const int quad = warp & 3;                  // TMEM lane quadrant this warp may read
-        const int row = quad * 32 + lane;           // row within the 128-row tile
         const int et = tid - 64;                    // 0..127
+        const bool reader = warp == kEpiWarpLane0;  // reads the accumulator (TMEM lanes 0-31)
 
-        // Small operands of gate/up: the weight scale chunks of every stage (asynchronous 16-byte copies, in flight
-        // while x is quantized) and x's B terms and scales, split from h straight into shared memory (warp w - 2
-        // takes 8 blocks per pass, 4 lanes per block).
+        // x's terms and scales (written by all CTAs in phase 0), with asynchronous 16-byte copies.
         {
-            const int n3 = nst * 64;
-            for (int x = et; x < n3; x += 128) {
-                const int i = x >> 6, q16 = x & 63;
-                const Stage& st = stages[i];
-                if (q16 < sk::nkt_of(st) * 32) {
-                    const Part& p = part_of(st);
-                    const bool gu = st.mode == sk::kGateUp;
-                    const int mat = j.sfa_by_slot ? int(st.s) : ids_s[st.s];
-                    const int rt = gu ? st.tile % p.RT : st.tile;
-                    const uint8_t* base = gu ? j.sfa_gu : j.sfa_dn;
-                    tc::cp_async16(regSFA + i * 1024 + 16 * q16,
-                                   base + ((size_t(mat) * p.RT + rt) * p.KT + st.ku0 / 2) * 512 + 16 * q16);
-                }
+            const int n1 = j.gu.SPS * (kA / 16), n2 = j.gu.KT * (kSF8 / 16);
+            for (int x = et; x < n1 + n2; x += 128) {
+                if (x < n1) tc::cp_async16(xA + 16 * x, j.xq_img + 16 * x);
+                else tc::cp_async16(xSF + 16 * (x - n1), j.xq_sf + 16 * (x - n1));
             }
             if (et == 0) stamp(j, 126);
-            const int nb = j.H / 32, sub = lane & 3;
-            for (int g0 = (warp - 2) * 8; g0 < nb; g0 += 32) {
-                const int g = g0 + (lane >> 2);
-                const bool active = g < nb;
-                const int gg = active ? g : 0;
-                const float4 h0 = *reinterpret_cast<const float4*>(hs + gg * 32 + sub * 8);
-                const float4 h1 = *reinterpret_cast<const float4*>(hs + gg * 32 + sub * 8 + 4);
-                float v8[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-                if (!active)
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) v8[i] = 0.f;
-                quantize_block_terms_fixed(v8, regBgu + (gg / 8) * kB, gg % 8, regSFBgu + (gg / 4) * 512, gg % 4,
-                                           sub, active);
-                if (et == 0 && g0 < 96) stamp(j, 127 + g0 / 32);
-            }
-            if (et == 0) stamp(j, 130);
             tc::cp_async_wait_all();
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&fullS[0]);
             if (et == 0) stamp(j, 80);
         }
-        // After the CTA's last gate/up epilogue: count it on the grid barrier, wait for all CTAs, then load down's B
-        // terms and scales for the down stages.
-        auto gate_up_done_then_load_down_b = [&]() {
-            __threadfence();                        // this thread's down-B terms and partial sums are published
-            epi_sync();
-            if (et == 0) {
-                __threadfence();
-                atomicAdd(&j.gbar[0], 1u);
+        // After the CTA's last gate/up epilogue: count it on the grid barrier; once every CTA has finished gate/up
+        // (bounded wait), one thread loads each down stage's A terms and scales with two bulk copies completing on
+        // the stage's barrier.
+        auto load_down_stages = [&]() {
+            epi_sync();                             // every thread's down-A terms and partial sums are written
+            if (et != 0) return;
+            red_add_release(&j.gbar[0], 1u);        // ... and released to the CTAs that acquire the count
+            stamp(j, 131);
+            if (ngu == nst) return;
+            bool done = false;
+            for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
+                done = ld_acquire(&j.gbar[0]) >= unsigned(nc);
+                if (!done) __nanosleep(32);
             }
-            if (ngu == nst) return;                 // no down stages here
-            if (et == 0) {
-                bool done = false;
-                for (uint32_t i = 0; i < tc::kSpinLimit && !done; ++i) {
-                    done = ld_acquire(&j.gbar[0]) >= unsigned(nc);
-                    if (!done) __nanosleep(32);
+            stamp(j, 81);
+            if (done) asm volatile("fence.proxy.async.global;" ::: "memory");   // generic writes -> bulk reads
+            else atomicCAS(j.err, 0, 8);
+            for (int i = ngu; i < nst; ++i) {
+                const Stage& st = stages[i];
+                if (!done) {                          // gave up: release the MMA warp's wait
+                    tc::mbar_arrive(&fullD[i - ngu]);
+                    continue;
                 }
-                if (!done) atomicCAS(j.err, 0, 8);
-                cnts[3] = done;
-                stamp(j, 81);
+                const uint32_t sfb8 = uint32_t(sk::nkt_of(st) * kSF8);
+                tc::mbar_arrive_expect_tx(&fullD[i - ngu], uint32_t(kA) + sfb8);
+                tc::bulk_g2s(dA + (i - ngu) * kA, j.aq_img + (size_t(st.s) * j.dn.SPS + st.ku0 / 4) * kA, kA,
+                             &fullD[i - ngu]);
+                tc::bulk_g2s(dSF + (i - ngu) * 2 * kSF8, j.aq_sf + (size_t(st.s) * j.dn.KT + st.ku0 / 2) * kSF8, sfb8,
+                             &fullD[i - ngu]);
             }
-            epi_sync();
-            if (cnts[3]) {
-                const int nd = (nst - ngu) * 192;
-                for (int x = et; x < nd; x += 128) {
-                    const int i = ngu + x / 192, q = x % 192;
-                    const Stage& st = stages[i];
-                    if (q < 128) {
-                        tc::cp_async16(regBdn + (i - ngu) * kB + 16 * q,
-                                       j.aq_img + (size_t(st.s) * j.dn.SPS + st.ku0 / 4) * kB + 16 * q);
-                    } else if (q - 128 < sk::nkt_of(st) * 32) {
-                        tc::cp_async16(regSFBdn + (i - ngu) * 1024 + 16 * (q - 128),
-                                       j.aq_sf + (size_t(st.s) * j.dn.KT + st.ku0 / 2) * 512 + 16 * (q - 128));
-                    }
-                }
-                tc::cp_async_wait_all();
-                tc::fence_proxy_async_smem();
-            }
-            tc::mbar_arrive(&fullS[1]);
-            if (et == 0) stamp(j, 83);
+            stamp(j, 83);
         };
-        if (ngu == 0) gate_up_done_then_load_down_b();
+        if (ngu == 0) load_down_stages();
         bool ok = true;
         for (int it = 0; it < nst; ++it) {
             const Stage& st = stages[it];
             if (!st.last) continue;
-            const int buf = st.seg & 1;
-            ok = ok && tc::mbar_wait_sleepy(&accF[buf], (st.seg >> 1) & 1, j.err, 5, 64);
-            ok = epi_all(ok);                        // uniform over the 4 epilogue warps before any named barrier
-            float v = 0.f;
-            if (ok) {
-                tc::tc_fence_after();
-                float t0[8], t1[8];
-                tc::tmem_ld_32x32b_x8(tmem + buf * R + (uint32_t(quad * 32) << 16), t0);
-                tc::tmem_ld_32x32b_x8(tmem + buf * R + 8 + (uint32_t(quad * 32) << 16), t1);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v += t0[i];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v += t1[i];
+            // the biases of this thread's two rows, loaded before the accumulator is waited for
+            float b0 = 0.f, b1 = 0.f;
+            if (st.mode == sk::kGateUp) {
+                const int rt = st.tile % j.gu.RT;
+                const float* bb = j.gu_bias + size_t(ids_s[st.tile / j.gu.RT]) * 2 * j.I + rt * kRows;
+                if (rt * kRows + et < 2 * j.I) b0 = __ldg(bb + et);
+                if (rt * kRows + et + 128 < 2 * j.I) b1 = __ldg(bb + et + 128);
+            } else {
+                const int r0 = st.tile * kRows + et;
+                for (int s2 = 0; s2 < j.k; ++s2) {
+                    const float* bb = j.dn_bias + size_t(ids_s[s2]) * j.H;
+                    if (r0 < j.H) b0 = fmaf(w_s[s2], __ldg(bb + r0), b0);
+                    if (r0 + 128 < j.H) b1 = fmaf(w_s[s2], __ldg(bb + r0 + 128), b1);
+                }
             }
-            tc::tc_fence_before();
-            tc::mbar_arrive(&accE[buf]);
+            // the reader warp moves accumulator rows 0..7 (the 8 terms) into shared memory and releases TMEM
+            if (reader) {
+                ok = ok && tc::mbar_wait(accF, uint32_t(st.seg) & 1u, j.err, 5);
+                ok = __all_sync(kFull, ok);
+                if (ok) {
+                    tc::tc_fence_after();
+#pragma unroll 1
+                    for (int r = 0; r < kRows / 32; r += 2) {
+                        uint32_t v[32], w[32];
+                        tmem_ld_32x32b_x32(tmem + 32 * r, v);
+                        tmem_ld_32x32b_x32(tmem + 32 * (r + 1), w);
+                        tc::tmem_ld_wait();
+                        if (lane < NT) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                *reinterpret_cast<float4*>(red_s + lane * kRows + 32 * r + i) =
+                                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
+                                                __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+                                *reinterpret_cast<float4*>(red_s + lane * kRows + 32 * (r + 1) + i) =
+                                    make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]),
+                                                __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
+                            }
+                        }
+                    }
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(accE);
+            }
+            ok = epi_all(ok);                        // uniform over the 4 epilogue warps; red_s written
             if (et == 0 && st.seg < 14) stamp(j, 66 + st.seg);
+            float v0 = 0.f, v1 = 0.f;                // rows et and et + 128 of the tile
+            if (ok) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    v0 += red_s[t * kRows + et];
+                    v1 += red_s[t * kRows + et + 128];
+                }
+            }
+            epi_sync();                              // red_s may be overwritten from here on
             if (ok) {
                 const Part& p = part_of(st);
                 const int t = st.tile;
-                float total = v;
                 bool mine = true;                    // this CTA applies the tile's epilogue
                 if (st.whole < 0) {                  // more CTAs share the tile than there are partial slots
                     if (et == 0) atomicCAS(j.err, 0, 101);
                     mine = false;
                 } else if (!st.whole) {
-                    p.partial[(size_t(t) * sk::kMaxContrib + (c - st.cf)) * 128 + row] = v;
-                    __threadfence();
-                    epi_sync();
-                    if (et == 0) {
-                        __threadfence();
-                        const unsigned old = atomicAdd(&p.cnt[t], unsigned(st.units));
-                        const bool last = old + unsigned(st.units) == unsigned(p.UT);
-                        if (last) p.cnt[t] = 0;      // every contributor has arrived: reset for the next launch
-                        __threadfence();
-                        cnts[2] = last;
+                    // Split tile. Its first contributor (the CTA whose range ends inside it: the tile is that CTA's
+                    // last segment of the part) finalizes it; the others (for whom it is a first or only segment)
+                    // publish their partial sums and count themselves, and the finalizer waits for that count
+                    // (bounded; usually already complete).
+                    mine = c == st.cf;
+                    if (!mine) {
+                        float* pp = p.partial + (size_t(t) * sk::kMaxContrib + (c - st.cf)) * kRows;
+                        __stcg(pp + et, v0);
+                        __stcg(pp + et + 128, v1);
+                        epi_sync();
+                        if (et == 0) red_add_release(&p.cnt[t], 1u);
+                    } else {
+                        if (et == 0) {
+                            const unsigned others = unsigned(__popc(unsigned(st.mask))) - 1u;
+                            bool done = false;
+                            for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
+                                done = ld_acquire(&p.cnt[t]) >= others;
+                                if (!done) __nanosleep(32);
+                            }
+                            if (!done) atomicCAS(j.err, 0, 12);
+                            p.cnt[t] = 0;             // reset for the next launch
+                            cnts[2] = done;
+                        }
+                        epi_sync();
+                        mine = cnts[2] != 0;
                     }
-                    epi_sync();
-                    mine = cnts[2] != 0;
+                    if (et == 0 && st.seg < 8) stamp(j, 132 + st.seg);
                     if (mine) {
-                        // contributors in CTA order; the loads are independent and issue together
-                        total = 0.f;
-                        const float* pp = p.partial + size_t(t) * sk::kMaxContrib * 128 + row;
+                        // own sums first, then the other contributors in CTA order; the loads issue together
+                        const float* pb = p.partial + size_t(t) * sk::kMaxContrib * kRows;
                         const unsigned m = st.mask;
-                        float pv[sk::kMaxContrib];
+                        float a0[sk::kMaxContrib], a1[sk::kMaxContrib];
 #pragma unroll
-                        for (int b = 0; b < sk::kMaxContrib; ++b) pv[b] = (m >> b) & 1u ? __ldcg(pp + b * 128) : 0.f;
+                        for (int b = 1; b < sk::kMaxContrib; ++b) {
+                            const bool on = (m >> b) & 1u;
+                            a0[b] = on ? __ldcg(pb + b * kRows + et) : 0.f;
+                            a1[b] = on ? __ldcg(pb + b * kRows + et + 128) : 0.f;
+                        }
 #pragma unroll
-                        for (int b = 0; b < sk::kMaxContrib; ++b)
-                            if ((m >> b) & 1u) total += pv[b];
+                        for (int b = 1; b < sk::kMaxContrib; ++b)
+                            if ((m >> b) & 1u) {
+                                v0 += a0[b];
+                                v1 += a1[b];
+                            }
                     }
                 }
                 if (mine && st.mode == sk::kGateUp) {
                     const int s = t / p.RT, rt = t % p.RT;
-                    const int e = ids_s[s];
-                    const int grow = rt * 128 + row;
-                    const float y = grow < 2 * j.I ? total + j.gu_bias[size_t(e) * 2 * j.I + grow] : 0.f;
-                    const float lin = __shfl_down_sync(kFull, y, 1);
-                    if ((lane & 1) == 0) {
-                        const float gv = fminf(y, j.limit);
-                        const float lv = fminf(fmaxf(lin, -j.limit), j.limit);
-                        aval[row >> 1] = gv / (1.f + expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
-                    }
-                    epi_sync();
-                    if (quad == 0) {                 // one warp: the tile's two 32-element blocks, 4 lanes each
-                        const int grp = lane >> 2, sub = lane & 3;
-                        const int gb = rt * 2 + (grp & 1);
-                        const bool active = grp < 2 && gb * 32 < j.I;
-                        float v8[8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) v8[i] = aval[(grp & 1) * 32 + sub * 8 + i];
-                        uint8_t* img = j.aq_img + (size_t(s) * j.dn.SPS + gb / 8) * kB;
-                        uint8_t* sf = j.aq_sf + (size_t(s) * j.dn.KT + gb / 4) * 512;
-                        quantize_block_terms_fixed(v8, img, gb % 8, sf, gb % 4, sub, active);
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int col = et + 128 * hh;
+                        const int grow = rt * kRows + col;
+                        const float y = grow < 2 * j.I ? (hh ? v1 + b1 : v0 + b0) : 0.f;
+                        const float lin = __shfl_down_sync(kFull, y, 1);
+                        if ((lane & 1) == 0) {
+                            const float gv = fminf(y, j.limit);
+                            const float lv = fminf(fmaxf(lin, -j.limit), j.limit);
+                            aval[col >> 1] = gv / (1.f + expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
+                        }
                     }
                     epi_sync();
+                    {                                // the tile's four 32-element blocks, one per epilogue warp
+                        const int gb = rt * (kRows / 64) + (warp - 2);
+                        quantize_block_terms_warp32<NT>(aval[(warp - 2) * 32 + lane],
+                                                        j.aq_img + (size_t(s) * j.dn.SPS + gb / 8) * kA, gb % 8,
+                                                        j.aq_sf + (size_t(s) * j.dn.KT + gb / 4) * kSF8, gb % 4,
+                                                        gb * 32 < j.I);
+                    }
+
+                    if (et == 0 && st.seg < 8) stamp(j, 140 + st.seg);
                 } else if (mine) {
-                    const int grow = t * 128 + row;
-                    if (grow < j.H) {
-                        float add = total;
-                        for (int s = 0; s < j.k; ++s) add += w_s[s] * j.dn_bias[size_t(ids_s[s]) * j.H + grow];
-                        j.x_resid[grow] += add;
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int grow = t * kRows + et + 128 * hh;
+                        if (grow < j.H) j.x_resid[grow] += hh ? v1 + b1 : v0 + b0;
                     }
                 }
             }
             // after the last gate/up segment (also when a wait gave up, so other CTAs are not held up)
-            if (st.mode == sk::kGateUp && it == ngu - 1) gate_up_done_then_load_down_b();
+            if (st.mode == sk::kGateUp && it == ngu - 1) load_down_stages();
         }
     }
     tc::tc_fence_before();
@@ -632,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     if (tid == 0) {
         stamp(j, 82);
         __threadfence();
-        if (atomicAdd(&j.gbar[1], 1u) == unsigned(nc - 1)) {   // last CTA out resets the grid barriers
+        if (atomicAdd(&j.gbar[1], 1u) == unsigned(nc - 1)) {   // last CTA out resets the counters and flags
             j.gbar[0] = 0;
             j.gbar[2] = 0;
             j.gbar[1] = 0;
@@ -641,29 +713,33 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
-// Shared-memory plan: NS weight stages, the x image and its scales, per-entry weight-scale chunks (1 KB each),
-// per-down-entry B stages and scale chunks, h (fp32; in the down-B region when it fits there: h is consumed before
-// down's B terms arrive), barriers, and the small per-CTA state.
+// Shared-memory plan: NS ring slots (a 32 KB weight box and its 2 KB of scales each), x's terms and scales, down's A
+// terms and scales per down stage, h (fp32; inside the ring, which phase 0 does not use yet), the accumulator's 8
+// term rows, barriers, and the small per-CTA state. TMEM: the accumulator in columns [0, 256), x's scale chunks, then
+// a ring of NSF weight-scale slots (16 columns each) and of down's A-scale slots (8 columns each).
 Layout make_layout(int NS, int cap, int cap_dn, const Part& gu, int H) {
     Layout L{};
     L.NS = NS;
     L.cap = cap;
+    const int free_cols = int(kTmemCols) - int(kColX) - 4 * gu.KT;
+    L.NSF = std::min(6, free_cols / 24);
+    L.colSFB = kColX + 4u * uint32_t(gu.KT);
+    L.colDSF = L.colSFB + 16u * uint32_t(L.NSF);
     int o = 0;
-    L.ringA = o; o += NS * kA;
-    L.regBgu = o; o += gu.SPS * kB;
-    L.regSFBgu = o; o += (gu.KT * 512 + 1023) & ~1023;
-    L.regSFA = o; o += cap * 1024;
-    L.regBdn = o; o += cap_dn * kB;
-    L.regSFBdn = o; o += cap_dn * 1024;
-    if (H * 4 <= o - L.regBdn) {
-        L.hs = L.regBdn;
-    } else {
+    L.ring = o; o += NS * kSlot;
+    L.xA = o; o += gu.SPS * kA;
+    L.xSF = o; o += (gu.KT * kSF8 + 1023) & ~1023;
+    L.dA = o; o += cap_dn * kA;
+    L.dSF = o; o += cap_dn * 2 * kSF8;
+    L.hs = H * 4 <= NS * kSlot ? L.ring : -1;   // h is read only in phase 0, before the ring's first stage
+    if (L.hs < 0) {
         L.hs = o;
         o += (H * 4 + 15) & ~15;
     }
-    L.bars = o; o += (NS + NS / 2 + 6) * 8;
+    L.red = o; o += NT * kRows * 4;
+    L.bars = o; o += (2 * NS + 4 + cap) * 8;
     o = (o + 15) & ~15;
-    L.misc = o; o += 8 + 24 + 7 * 32 * 8 + 2 * kMaxK * 4 + 64 * 4 + cap * int(sizeof(Stage));
+    L.misc = o; o += 8 + 24 + 7 * 32 * 8 + 2 * kMaxK * 4 + (kRows / 2) * 4 + cap * int(sizeof(Stage));
     L.bytes = 1024 + o;
     return L;
 }
@@ -674,7 +750,7 @@ struct StageTable {
     Stage* st = nullptr;
     int* hdr = nullptr;
     int cap = 1, cap_dn = 1;
-    int cols = 0;                             // TMEM columns needed to hold every scale chunk of the busiest CTA
+    bool crowded = false;                     // some tile is shared by more CTAs than there are partial slots
 };
 
 const StageTable& stage_table(const Part& g, const Part& d, int nc, int k, int H, int I) {
@@ -706,7 +782,7 @@ const StageTable& stage_table(const Part& g, const Part& d, int nc, int k, int H
         hdr[size_t(c) * 4 + 2] = ngu;
         T.cap = std::max(T.cap, n);
         T.cap_dn = std::max(T.cap_dn, n - ngu);
-        T.cols = std::max(T.cols, int(kColSF) + 8 * n + 4 * g.KT + 8 * (n - ngu));
+        for (int i = 0; i < n; ++i) T.crowded = T.crowded || (o[i].last && o[i].whole < 0);
     }
     if (all.empty()) all.resize(1);
     GPT_CHECK(cudaMalloc(&T.st, all.size() * sizeof(Stage)));
@@ -721,26 +797,28 @@ const StageTable& stage_table(const Part& g, const Part& d, int nc, int k, int H
 // ---------------------------------------------------------------------------------------------------- host API
 DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     DecodeTcLayout L{};
-    const int R = kDecodeTerms;
+    const int NT = fz::NT, TR = kDecodeTileRows;
     auto al = [](size_t b) { return (b + 1023) & ~size_t(1023); };
     const int UKd = (I + 63) / 64;
     L.SPS_dn = (UKd + 3) / 4;
     L.KT_dn = (I + 127) / 128;
     L.SPS_gu = ((H + 63) / 64 + 3) / 4;
     L.KT_gu = (H + 127) / 128;
-    L.RT_gu = (2 * I + 127) / 128;
-    L.RT_dn = (H + 127) / 128;
+    L.RT_gu = (2 * I + TR - 1) / TR;
+    L.RT_dn = (H + TR - 1) / TR;
     size_t o = 0;
     L.off_partials = o; o += al(size_t(256) * 32 * 8);
-    L.off_aq_img = o; o += al(size_t(k) * L.SPS_dn * R * 128);
-    L.off_aq_sf = o; o += al(size_t(k) * L.KT_dn * 512);
-    L.off_part_gu = o; o += al(size_t(k) * L.RT_gu * sk::kMaxContrib * 128 * 4);
-    L.off_part_dn = o; o += al(size_t(L.RT_dn) * sk::kMaxContrib * 128 * 4);
+    L.off_xq_img = o; o += al(size_t(L.SPS_gu) * NT * 128);
+    L.off_xq_sf = o; o += al(size_t(L.KT_gu) * fz::kSF8);
+    L.off_aq_img = o; o += al(size_t(k) * L.SPS_dn * NT * 128);
+    L.off_aq_sf = o; o += al(size_t(k) * L.KT_dn * fz::kSF8);
+    L.off_part_gu = o; o += al(size_t(k) * L.RT_gu * sk::kMaxContrib * TR * 4);
+    L.off_part_dn = o; o += al(size_t(L.RT_dn) * sk::kMaxContrib * TR * 4);
     L.off_cnt_gu = o; o += al(size_t(k) * L.RT_gu * 4);
     L.off_cnt_dn = o; o += al(size_t(L.RT_dn) * 4);
     L.off_err = o; o += 1024;                                // error word, then the grid barrier at +256
-    L.off_sfa_gu = o; o += al(sf_repacked_bytes(k, 2 * I, H / 32));
-    L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32));
+    L.off_sfa_gu = o; o += al(sf_repacked_bytes(k, 2 * I, H / 32, TR));
+    L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32, TR));
     L.off_misc = o; o += al(size_t(H) * 4 + 256);
     L.bytes = o;
     L.zero_bytes_from = L.off_cnt_gu;                        // counters, error word and grid barrier start at zero
@@ -786,9 +864,9 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     j.w_in = a.weights;
     j.ids_out = a.ids_out;
     j.w_out = a.w_out;
-    j.sfa_gu = a.sfa_gu;
-    j.sfa_dn = a.sfa_dn;
-    j.sfa_by_slot = a.sfa_by_slot;
+    j.sf_gu = a.sfa_gu;
+    j.sf_dn = a.sfa_dn;
+    j.sf_by_slot = a.sfa_by_slot;
     j.gu_bias = a.gu_bias;
     j.dn_bias = a.dn_bias;
     j.alpha = a.alpha;
@@ -815,6 +893,8 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     d.total = (long long)d.n_tiles * d.UT;
     d.partial = reinterpret_cast<float*>(ws + W.off_part_dn);
     d.cnt = reinterpret_cast<unsigned*>(ws + W.off_cnt_dn);
+    j.xq_img = ws + W.off_xq_img;
+    j.xq_sf = ws + W.off_xq_sf;
     j.aq_img = ws + W.off_aq_img;
     j.aq_sf = ws + W.off_aq_sf;
     j.x_resid = a.x_resid;
@@ -826,13 +906,14 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     // One CTA per SM, all resident (cooperative launch); the stage lists come from the per-shape table.
     const int nc = num_sms();
     const StageTable& T = stage_table(g, d, nc, a.k, a.H, a.I);
+    require(!T.crowded, "moe (tc): a tile would be shared by more CTAs than there are partial-sum slots");
     j.stab = T.st;
     j.shdr = T.hdr;
-    j.sf_upfront = T.cols <= int(kTmemCols);
-    int NS = 8;
+    int NS = 6;
     Layout L = make_layout(NS, T.cap, T.cap_dn, g, a.H);
-    while (L.bytes > 227 * 1024 && NS > 2) L = make_layout(NS -= 2, T.cap, T.cap_dn, g, a.H);
+    while (L.bytes > 227 * 1024 && NS > 2) L = make_layout(--NS, T.cap, T.cap_dn, g, a.H);
     require(L.bytes <= 227 * 1024, "moe (tc): shapes too large for one CTA's shared memory");
+    require(L.NSF >= 2, "moe (tc): H too large for the TMEM scale-factor plan");
     j.L = L;
     set_fused_smem(L.bytes);
 
@@ -841,12 +922,29 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = size_t(L.bytes);
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    GPT_CHECK(cudaLaunchKernelEx(&cfg, moe_fused_kernel, *a.tmap_gu, *a.tmap_dn, j));
+    // Programmatic dependent launch lets the next kernel on the stream start as this one's CTAs exit. If this
+    // runtime refuses it together with a cooperative launch, the first launch on this device finds out and every
+    // later one goes without it.
+    static int pdl_ok[64] = {};                              // 0 unknown, 1 accepted, -1 refused
+    int dev = 0;
+    GPT_CHECK(cudaGetDevice(&dev));
+    cfg.numAttrs = dev < 64 && pdl_ok[dev] >= 0 ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_fused_kernel, *a.tmap_gu, *a.tmap_dn, j);
+    if (e != cudaSuccess && cfg.numAttrs == 2 && dev < 64 && pdl_ok[dev] == 0) {
+        (void)cudaGetLastError();
+        pdl_ok[dev] = -1;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, moe_fused_kernel, *a.tmap_gu, *a.tmap_dn, j);
+    } else if (e == cudaSuccess && cfg.numAttrs == 2 && dev < 64) {
+        pdl_ok[dev] = 1;
+    }
+    GPT_CHECK(e);
     check_launch("moe (tensor cores, fused)");
 }
 

@@ -41,19 +41,24 @@ void launch_moe_decode_simt(const uint8_t* gu_blocks, const uint8_t* gu_scales, 
                             int H, int I, float alpha, float limit, void* scratch, cudaStream_t s,
                             void* mid_event = nullptr);
 
-// Scale-factor repack: raw E8M0 bytes [mats][rows][G] -> tcgen05 chunks [mats][ceil(rows/128)][ceil(G/4)][512],
-// chunk byte (r % 32) * 16 + (r / 32) * 4 + kb for row r and k-block kb of the chunk; zero padded.
-size_t sf_repacked_bytes(long long mats, int rows, int G);
+// Scale-factor repack: raw E8M0 bytes [mats][rows][G] -> tcgen05 chunks of 512 bytes, chunk byte
+// (r % 32) * 16 + (r / 32) * 4 + kb for row r (within its 128 rows) and k-block kb; zero padded. tile_rows = 128:
+// [mats][ceil(rows/128)][ceil(G/4)][512]; tile_rows = 256: [mats][ceil(rows/256)][ceil(G/4)][2][512] (the two
+// 128-row halves of a 256-row tile side by side for each K chunk of 128).
+size_t sf_repacked_bytes(long long mats, int rows, int G, int tile_rows = 128);
 // With ids != nullptr, output matrix m is gathered from raw matrix ids[m] (m < mats).
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
-                      const int* ids = nullptr);
+                      const int* ids = nullptr, int tile_rows = 128);
 
+// Tensor-core decode MoE (decode_tc.cu): one persistent cooperative kernel per MoE layer. Weights are read in tiles
+// of kDecodeTileRows rows (TMA boxes of kDecodeTileRows rows x 128 bytes; scales repacked with that tile size).
+constexpr int kDecodeTileRows = 256;
 // Tensor-core decode MoE (decode_tc.cu): one persistent cooperative kernel per MoE layer. The workspace layout
 // depends only on (k, H, I); the byte range [zero_bytes_from, zero_bytes_to) must be zero before the first launch
 // (tile counters and the grid barrier reset themselves afterwards).
 struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
-    size_t off_partials, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu,
+    size_t off_partials, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu,
         off_cnt_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
 };
@@ -92,7 +97,7 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
                         cudaStream_t s);
 
 // Quantizes x [n] into kDecodeTerms e2m1 residual terms (which = 0: comparison quantizer, 1: converter quantizer,
-// 2: fixed scale schedule with fp32 rounding)
+// 2: fixed scale schedule with fp32 rounding, 3: the same with one warp per block)
 // and decodes them back into out [n]; per_term (optional, [2][n]) receives the first two terms. Synchronizes.
 void selftest_terms(const float* x, int n, float* out, float* per_term, int which, void* scratch, size_t bytes,
                     cudaStream_t s);

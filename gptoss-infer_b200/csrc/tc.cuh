@@ -161,9 +161,17 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 // K-major operand in the 128-byte swizzled layout: 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) { return smem_desc(saddr, 16, 1024, 2); }
 
+// The same layout with all 8-row groups at one address (stride 0): an 8-row operand (1 KB per 128 bytes of K) read as
+// M = 128 rows, rows r and r + 8 identical; the accumulator rows repeat with period 8.
+__device__ __forceinline__ uint64_t desc_sw128_rows8(uint32_t saddr) { return smem_desc(saddr, 16, 0, 2); }
+
 // Scale-factor chunk source for tcgen05.cp 32x128b: 32 rows of 16 bytes, contiguous (core matrices of 8 rows x 16
 // bytes, 128 bytes apart), no swizzle.
 __device__ __forceinline__ uint64_t desc_sf_chunk(uint32_t saddr) { return smem_desc(saddr, 0, 128, 0); }
+
+// The same copy from an 8-row chunk (128 bytes, rows 0-7): all four 8-row groups read the same 128 bytes, so TMEM lanes
+// l and l + 8 receive the same scales (the scales of an 8-row operand read as 128 rows).
+__device__ __forceinline__ uint64_t desc_sf_chunk8(uint32_t saddr) { return smem_desc(saddr, 0, 0, 0); }
 
 // Instruction descriptor of tcgen05.mma kind::mxf4 (block 32, E8M0 scales, K = 64, both operands K-major e2m1):
 // b_sf_id bits 4-5, a/b format (E2M1 = 1) bits 7-9 / 10-12, N >> 3 bits 17-22, scale format E8M0 bit 23,

@@ -75,20 +75,22 @@ CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t
 
 // ---------------------------------------------------------------------------------------------------- SF repack
 namespace {
-// raw [mats][rows][G] E8M0 bytes -> [mats][RT][KT][512] tcgen05 chunks (RT = ceil(rows/128), KT = ceil(G/4)), zero
-// padded. One thread per output word of 4 bytes (one row's 4 k-blocks).
+// raw [mats][rows][G] E8M0 bytes -> [mats][RT][KT][halves][512] tcgen05 chunks (tiles of 128 * halves rows,
+// RT = ceil(rows / tile), KT = ceil(G/4)), zero padded. One thread per output word of 4 bytes (one row's 4 k-blocks).
 __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, long long mats, int rows,
-                                 int G, int RT, int KT, const int* __restrict__ ids) {
-    const long long words = mats * RT * KT * 128;
+                                 int G, int RT, int KT, int halves, const int* __restrict__ ids) {
+    const long long words = mats * RT * KT * halves * 128;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
          i += (long long)gridDim.x * blockDim.x) {
         const int w = int(i % 128);                  // word within the chunk: (row % 32) * 4 + row / 32
         long long c = i / 128;
+        const int h = int(c % halves);               // 128-row half of a 256-row tile
+        c /= halves;
         const int kt = int(c % KT);
         c /= KT;
         const int rt = int(c % RT);
         const long long mat = ids ? (long long)ids[c / RT] : c / RT;
-        const int row = rt * 128 + (w & 3) * 32 + (w >> 2);
+        const int row = (rt * halves + h) * 128 + (w & 3) * 32 + (w >> 2);
         uint32_t v = 0;
         if (row < rows) {
             const uint8_t* src = raw + (mat * rows + row) * G;
@@ -103,16 +105,18 @@ __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __res
 }
 }  // namespace
 
-size_t sf_repacked_bytes(long long mats, int rows, int G) {
-    return size_t(mats) * size_t((rows + 127) / 128) * size_t((G + 3) / 4) * 512;
+size_t sf_repacked_bytes(long long mats, int rows, int G, int tile_rows) {
+    return size_t(mats) * size_t((rows + tile_rows - 1) / tile_rows) * size_t((G + 3) / 4) * size_t(tile_rows / 128) *
+           512;
 }
 
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
-                      const int* ids) {
-    const int RT = (rows + 127) / 128, KT = (G + 3) / 4;
-    const long long words = mats * RT * KT * 128;
+                      const int* ids, int tile_rows) {
+    require(tile_rows == 128 || tile_rows == 256, "repack_sf: tiles of 128 or 256 rows");
+    const int halves = tile_rows / 128, RT = (rows + tile_rows - 1) / tile_rows, KT = (G + 3) / 4;
+    const long long words = mats * RT * KT * halves * 128;
     const int grid = int(std::min<long long>((words + 255) / 256, num_sms() * 8LL));
-    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, ids);
+    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, halves, ids);
     check_launch("repack_sf");
 }
 
@@ -249,9 +253,16 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
 
 namespace {
 // One warp per 8 blocks: quantize x into residual terms with the chosen quantizer (0 = comparisons, 1 = converters,
-// 2 = fixed scale schedule with fp32 rounding, the decode kernel's quantizer).
+// 2 = fixed scale schedule with fp32 rounding, 3 = the same computed by a whole warp per block).
 __global__ void terms_quantize_kernel(const float* x, int n, uint8_t* img, uint8_t* sf, int which) {
     const int lane = threadIdx.x & 31, sub = lane & 3;
+    if (which == 3) {                                        // one block per warp, one element per lane
+        const int warps = gridDim.x * (blockDim.x / 32), w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+        for (int g = w; g < n / 32; g += warps)
+            quantize_block_terms_warp32<kDecodeTerms>(x[g * 32 + lane], img + (g / 8) * (kDecodeTerms * 128), g % 8,
+                                                      sf + (g / 4) * 512, g % 4, true);
+        return;
+    }
     const int g = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 8 + (lane >> 2);
     const bool active = g < n / 32;
     const int gg = active ? g : 0;

@@ -141,12 +141,14 @@ constexpr int kActiveTerms = 10;              // terms quantize_block_terms_fixe
 // taken from each residual's maximum: term 0 keeps the block's maximum within 6 * 2^k0, so its rounding error is at
 // most 2^k0 (the e2m1 grid step is 2 between 4 and 6); term 1 uses k0 - 2 (|y| <= 4), and from then on every
 // rounding error is at most half a grid step of 1, i.e. 2^(k-1), so k drops by 3 per term and |y| stays <= 4.
-// After kActiveTerms = 10 terms the remainder is below 2^-27 of the block's maximum scale (the subtractions are
-// exact); the remaining terms are written as zeros. There is no per-term maximum (no lane shuffles), and the rounding
-// is round_e2m1: each term is a short chain of full-rate fp32 operations per element. Scales below 2^-127 are clamped
-// there (the terms of such tiny remainders are then merely close, never NaN).
-__device__ __forceinline__ void quantize_block_terms_fixed(float (&v)[8], uint8_t* img_stage, int q, uint8_t* sf_chunk,
-                                                           int kb, int sub, bool active) {
+// After n terms the remainder is at most 2^(k0 - 3n + 3) (the subtractions are exact): below 2^-24 of the block's
+// maximum after 8 terms and 2^-27 after 10. NT term rows are written (image row stride 128 bytes, NT rows per stage),
+// the first min(NT, kActiveTerms) computed and the rest zero. There is no per-term maximum (no lane shuffles), and
+// the rounding is round_e2m1: each term is a short chain of full-rate fp32 operations per element. Scales below
+// 2^-127 are clamped there (the terms of such tiny remainders are then merely close, never NaN).
+template <int NT>
+__device__ __forceinline__ void quantize_block_terms_fixed_n(float (&v)[8], uint8_t* img_stage, int q,
+                                                             uint8_t* sf_chunk, int kb, int sub, bool active) {
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -163,7 +165,7 @@ __device__ __forceinline__ void quantize_block_terms_fixed(float (&v)[8], uint8_
         }
     }
 #pragma unroll
-    for (int t = 0; t < kDecodeTerms; ++t) {
+    for (int t = 0; t < NT; ++t) {
         uint32_t word = 0, scale = 0;
         if (t < kActiveTerms) {
             const int kc = max(-127, k);
@@ -181,6 +183,51 @@ __device__ __forceinline__ void quantize_block_terms_fixed(float (&v)[8], uint8_
             *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | (sub * 4))) = word;
             if (sub == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(scale);
         }
+    }
+}
+
+__device__ __forceinline__ void quantize_block_terms_fixed(float (&v)[8], uint8_t* img_stage, int q, uint8_t* sf_chunk,
+                                                           int kb, int sub, bool active) {
+    quantize_block_terms_fixed_n<kDecodeTerms>(v, img_stage, q, sf_chunk, kb, sub, active);
+}
+
+// One 32-element block quantized by a whole warp, one element per lane (lane l holds element l), for latency: the
+// same terms, scales and image format as quantize_block_terms_fixed_n<NT>. The block maximum is one warp reduction;
+// each term's 4-bit codes are gathered into 32-bit words (8 lanes per word) by three shuffles and stored by lanes
+// 0, 8, 16 and 24. `active` must be the same in all lanes (it only suppresses the stores).
+template <int NT>
+__device__ __forceinline__ void quantize_block_terms_warp32(float v, uint8_t* img_stage, int q, uint8_t* sf_chunk,
+                                                            int kb, bool active) {
+    const int lane = threadIdx.x & 31;
+    const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(v))));
+    int k = -127;
+    {
+        const uint32_t bits = __float_as_uint(amax);
+        const int e = int((bits >> 23) & 0xFF);
+        if (e != 0) {
+            const int k0 = e - 127;
+            k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
+            k = max(-127, min(127, k));
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        uint32_t nib = 0, scale = 0;
+        if (t < kActiveTerms) {
+            const int kc = max(-127, k);
+            const float qv = round_e2m1(v * exp2i_exact(-kc));
+            v = fmaf(-qv, exp2i_exact(kc), v);
+            nib = e2m1_code(qv);
+            scale = uint32_t(kc + 127);
+            k -= t == 0 ? 2 : 3;
+        }
+        uint32_t word = nib << (4 * (lane & 7));
+        word |= __shfl_xor_sync(kFull, word, 1);
+        word |= __shfl_xor_sync(kFull, word, 2);
+        word |= __shfl_xor_sync(kFull, word, 4);
+        if (active && (lane & 7) == 0)
+            *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | ((lane >> 3) * 4))) = word;
+        if (active && lane == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(scale);
     }
 }
 

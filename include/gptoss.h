@@ -132,7 +132,8 @@ int gptoss_trace_enable(void* device_buffer, long long bytes);
 
 /* [extension] Self-test of the activation quantizer of the tensor-core path: splits x[n] (n % 256 == 0) into e2m1
  * residual terms with per-32 E8M0 scales (which = 0: comparison rounding, 1: the hardware converters, 2: the
- * fixed scale schedule with fp32 rounding that the decode kernel uses), decodes the terms back into out[n], and, if
+ * fixed scale schedule with fp32 rounding that the decode kernel uses, 3: the same computed by a whole warp per
+ * block), decodes the terms back into out[n], and, if
  * per_term is not NULL, stores the first two terms into per_term[2][n]. Device
  * pointers; synchronizes. */
 int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, int which);

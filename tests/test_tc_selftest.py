@@ -39,7 +39,7 @@ def test_mxf4_gemm_selftest(N, K):
     assert np.linalg.norm(got - want) <= 1e-6 * np.linalg.norm(want)
 
 
-@pytest.mark.parametrize("which", [0, 1, 2])
+@pytest.mark.parametrize("which", [0, 1, 2, 3])
 def test_activation_terms_roundtrip(which):
     """x -> 16 e2m1 residual terms -> decoded sum: within 2^-22 of each 32-block's maximum (fp32 rounding of the sum
     included), and the first term equals the reference quantizer's rounding of x (oracle/mxfp4.quantize: the same

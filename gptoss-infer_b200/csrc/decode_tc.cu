@@ -60,6 +60,7 @@ constexpr int kTraceSlots = 160;
 constexpr int kMaxK = 8;
 constexpr int kMaxX4 = 8;                     // x is held as kMaxX4 float4 per thread: H <= 4 * kThreads * kMaxX4
 constexpr int kEpiWarpLane0 = 4;              // the epilogue warp that may read TMEM lanes 0-31 (warp % 4 == 0)
+constexpr int kMaxGrid = 160;                 // CTAs (SMs) the router reduction is unrolled for
 
 struct Layout {
     int NS, NSF, cap;                         // weight ring depth, TMEM scale ring depth, stage-list capacity
@@ -92,7 +93,7 @@ struct Job {
     uint8_t* aq_img;                          // down's A terms [k][SPS_dn][NT*128]
     uint8_t* aq_sf;                           // down's A scales [k][KT_dn][128]
     float* x_resid;
-    unsigned* gbar;                           // [3]: gate/up done, exits, router partials and x blocks published
+    unsigned* gbar;                           // [4]: gate/up done, exits, router partials published, x blocks written
     double* partials;                         // [grid][32] router partial sums
     int* err;
     long long* trace;                         // optional [grid][kTraceSlots] clock64 stamps
@@ -282,20 +283,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             }
         }
         red[warp * 32 + lane] = acc;
-        {
-            // this CTA's share of x's 32-blocks -> A terms in global memory, published with the partial sums
-            // (warps 5, 4, 3: the router slice of a CTA rarely has more than 3 chunks, so these warps are free)
-            const int nb = H / 32, b0 = int((long long)c * nb / nc), b1 = int((long long)(c + 1) * nb / nc);
-            bool wrote = false;
-            if (warp >= 3)
-                for (int g = b0 + (kThreads / 32 - 1 - warp); g < b1; g += 3) {
-                    quantize_block_terms_warp32<NT>(hs[g * 32 + lane], j.xq_img + (g / 8) * kA, g % 8,
-                                                    j.xq_sf + (g / 4) * kSF8, g % 4, true);
-                    wrote = true;
-                }
-            if (wrote) __threadfence();
-        }
         __syncthreads();
+        if (warp >= 3) {
+            // this CTA's share of x's 32-blocks -> A terms in global memory (warps 5, 4, 3, while warp 0 publishes
+            // the router sums), published on their own counter, which the epilogue checks before reading x's terms
+            const int nb = H / 32, b0 = int((long long)c * nb / nc), b1 = int((long long)(c + 1) * nb / nc);
+            for (int g = b0 + (kThreads / 32 - 1 - warp); g < b1; g += 3)
+                quantize_block_terms_warp32<NT>(hs[g * 32 + lane], j.xq_img + (g / 8) * kA, g % 8,
+                                                j.xq_sf + (g / 4) * kSF8, g % 4, true);
+            asm volatile("bar.sync 2, 96;" ::: "memory");
+            if (warp == 3 && lane == 0) red_add_release(&j.gbar[3], 1u);
+        }
         if (warp == 0) {
             if (j.router_w) {
                 double t = 0.0;
@@ -322,20 +320,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         }
         __syncthreads();
         if (j.router_w) {
-            // every CTA adds all partial sums in the same order: thread (w, e) takes CTAs w, w + 6, ... (loads
-            // issued thirteen at a time), then warp 0 adds the six sums
+            // every CTA adds all partial sums in the same order: thread (w, e) takes CTAs w, w + 6, ... (all its
+            // loads issued together), then warp 0 adds the six sums
             double t = 0.0;
             if (cnts[2]) {
-                for (int c0 = warp; c0 < nc; c0 += 13 * (kThreads / 32)) {
-                    double v[13];
+                constexpr int kPer = (kMaxGrid + kThreads / 32 - 1) / (kThreads / 32);
+                double v[kPer];
 #pragma unroll
-                    for (int u = 0; u < 13; ++u) {
-                        const int cc = c0 + u * (kThreads / 32);
-                        v[u] = cc < nc ? __ldcg(&j.partials[size_t(cc) * 32 + lane]) : 0.0;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 13; ++u) t += v[u];
+                for (int u = 0; u < kPer; ++u) {
+                    const int cc = warp + u * (kThreads / 32);
+                    v[u] = cc < nc ? __ldcg(&j.partials[size_t(cc) * 32 + lane]) : 0.0;
                 }
+#pragma unroll
+                for (int u = 0; u < kPer; ++u) t += v[u];
             }
             red[warp * 32 + lane] = t;
             __syncthreads();
@@ -504,8 +501,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         const int et = tid - 64;                    // 0..127
         const bool reader = warp == kEpiWarpLane0;  // reads the accumulator (TMEM lanes 0-31)
 
-        // x's terms and scales (written by all CTAs in phase 0), with asynchronous 16-byte copies.
+        // x's terms and scales (written by all CTAs in phase 0, counted on gbar[3]), with asynchronous 16-byte copies.
         {
+            if (et == 0) {
+                bool done = false;
+                for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) done = ld_acquire(&j.gbar[3]) >= unsigned(nc);
+                if (!done) atomicCAS(j.err, 0, 13);
+            }
+            epi_sync();
             const int n1 = j.gu.SPS * (kA / 16), n2 = j.gu.KT * (kSF8 / 16);
             for (int x = et; x < n1 + n2; x += 128) {
                 if (x < n1) tc::cp_async16(xA + 16 * x, j.xq_img + 16 * x);
@@ -527,10 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             stamp(j, 131);
             if (ngu == nst) return;
             bool done = false;
-            for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
-                done = ld_acquire(&j.gbar[0]) >= unsigned(nc);
-                if (!done) __nanosleep(32);
-            }
+            for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) done = ld_acquire(&j.gbar[0]) >= unsigned(nc);
             stamp(j, 81);
             if (done) asm volatile("fence.proxy.async.global;" ::: "memory");   // generic writes -> bulk reads
             else atomicCAS(j.err, 0, 8);
@@ -707,6 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         if (atomicAdd(&j.gbar[1], 1u) == unsigned(nc - 1)) {   // last CTA out resets the counters and flags
             j.gbar[0] = 0;
             j.gbar[2] = 0;
+            j.gbar[3] = 0;
             j.gbar[1] = 0;
         }
     }
@@ -847,7 +848,7 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     require(a.H % 64 == 0 && a.I % 64 == 0, "moe (tc): H and I must be multiples of 64");
     require(a.H <= 4 * kThreads * kMaxX4, "moe (tc): H too large for the register-held x");
     require(!a.router_w || (a.E >= a.k && a.E <= 32), "moe (tc): router needs k <= E <= 32");
-    require(num_sms() <= 256, "moe (tc): more than 256 SMs");            // router partial-sum buffer
+    require(num_sms() <= kMaxGrid, "moe (tc): more SMs than the router reduction is written for");
     const DecodeTcLayout W = decode_tc_layout(a.k, a.H, a.I);
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
     Job j{};

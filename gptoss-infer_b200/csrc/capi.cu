@@ -6,6 +6,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "gptoss.h"
@@ -155,12 +156,26 @@ struct gptoss_moe_layer {
     float alpha, limit;
     uint8_t* sfa_gu = nullptr;
     uint8_t* sfa_dn = nullptr;
+    double* w64 = nullptr;                     // router weights as fp64 [H][32] for the batched router
     CUtensorMap tg, td;
     ~gptoss_moe_layer() {
         if (sfa_gu) cudaFree(sfa_gu);
         if (sfa_dn) cudaFree(sfa_dn);
+        if (w64) cudaFree(w64);
     }
 };
+
+namespace {
+// Workspace of the batched path, owned by the calling thread, one per device (grow-only).
+thread_local Scratch g_pws;
+thread_local Scratch g_pws_sf;
+
+void check_prefill_error(char* ws, const gpt::PrefillLayout& L) {
+    int h = 0;
+    GPT_CHECK(cudaMemcpy(&h, ws + L.off_misc + 256, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) throw std::runtime_error("moe_batched: device-side check failed (code " + std::to_string(h) + ")");
+}
+}  // namespace
 
 extern "C" {
 
@@ -365,6 +380,8 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
             gpt::launch_repack_sf(dn_scales, l->sfa_dn, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows);
             l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
             l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
+            GPT_CHECK(cudaMalloc(&l->w64, size_t(H) * 32 * sizeof(double)));
+            gpt::launch_router_w64(router_w, E, H, l->w64, nullptr);
             sync_check("moe_layer_create");
         } catch (...) {
             delete l;
@@ -373,6 +390,102 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
         L = l;
     });
     return L;
+}
+
+int gptoss_kernel_router_batched(const void* W, const float* b, const float* x, int E, int H, int k, int T,
+                                 int32_t* ids, float* weights) {
+    return guard([&] {
+        double* w64 = static_cast<double*>(g_scratch.get(size_t(H) * 32 * sizeof(double)));
+        gpt::launch_router_w64(W, E, H, w64, nullptr);
+        gpt::launch_router_batched(w64, b, x, nullptr, 0.f, T, E, H, k, nullptr, ids, weights, nullptr);
+        sync_check("router_batched");
+    });
+}
+
+int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                              const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                              const float* x_norm, const int32_t* ids, const float* weights, float* x_resid, int T,
+                              int k, int H, int I, float alpha, float limit) {
+    return guard([&] {
+        if (T < 1 || k < 1 || k > 8) throw std::runtime_error("moe_batched: need T >= 1 and 1 <= k <= 8");
+        if (!tc_shape_ok(k, H, I)) throw std::runtime_error("moe_batched: H and I must be multiples of 64");
+        // The expert count is not part of this ABI: the largest id in use bounds the experts read.
+        std::vector<int32_t> hid(size_t(T) * k);
+        GPT_CHECK(cudaMemcpy(hid.data(), ids, hid.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+        int E = 0;
+        for (int32_t v : hid) {
+            if (v < 0 || v >= 32) throw std::runtime_error("moe_batched: expert ids must be in 0..31");
+            E = std::max(E, int(v) + 1);
+        }
+        E = std::max(E, k);
+        const size_t sgu = gpt::sf_repacked_bytes(E, 2 * I, H / 32, gpt::kDecodeTileRows);
+        const size_t sdn = gpt::sf_repacked_bytes(E, H, I / 32, gpt::kDecodeTileRows);
+        uint8_t* sf = static_cast<uint8_t*>(g_pws_sf.get(sgu + sdn));
+        gpt::launch_repack_sf(gu_scales, sf, E, 2 * I, H / 32, nullptr, nullptr, gpt::kDecodeTileRows);
+        gpt::launch_repack_sf(dn_scales, sf + sgu, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows);
+        const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
+        const CUtensorMap td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
+        const gpt::PrefillLayout L = gpt::prefill_layout(T, k, E, H, I);
+        char* ws = static_cast<char*>(g_pws.get(L.bytes));
+        GPT_CHECK(cudaMemset(ws + L.off_misc, 0, 1024));
+        gpt::PrefillArgs a{};
+        a.tmap_gu = &tg;
+        a.tmap_dn = &td;
+        a.sf_gu = sf;
+        a.sf_dn = sf + sgu;
+        a.gu_bias = gu_bias;
+        a.dn_bias = dn_bias;
+        a.h = x_norm;
+        a.ids = ids;
+        a.weights = weights;
+        a.x_resid = x_resid;
+        a.T = T;
+        a.k = k;
+        a.E = E;
+        a.H = H;
+        a.I = I;
+        a.alpha = alpha;
+        a.limit = limit;
+        a.workspace = ws;
+        gpt::launch_moe_batched(a, nullptr);
+        sync_check("moe_batched");
+        check_prefill_error(ws, L);
+    });
+}
+
+int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float* x_resid, int T, void* stream) {
+    return guard([&] {
+        if (!l) throw std::runtime_error("moe_layer_forward_batched: null layer");
+        if (T < 1) throw std::runtime_error("moe_layer_forward_batched: T must be positive");
+        const gpt::PrefillLayout L = gpt::prefill_layout(T, l->k, l->E, l->H, l->I);
+        char* ws = static_cast<char*>(g_pws.get(L.bytes));
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        GPT_CHECK(cudaMemsetAsync(ws + L.off_misc, 0, 1024, s));
+        float* h = reinterpret_cast<float*>(ws + L.off_h);
+        int* ids = reinterpret_cast<int*>(ws + L.off_ids);
+        float* wts = reinterpret_cast<float*>(ws + L.off_w);
+        gpt::launch_router_batched(l->w64, l->router_b, x, l->norm_w, l->eps, T, l->E, l->H, l->k, h, ids, wts, s);
+        gpt::PrefillArgs a{};
+        a.tmap_gu = &l->tg;
+        a.tmap_dn = &l->td;
+        a.sf_gu = l->sfa_gu;
+        a.sf_dn = l->sfa_dn;
+        a.gu_bias = l->gu_bias;
+        a.dn_bias = l->dn_bias;
+        a.h = h;
+        a.ids = ids;
+        a.weights = wts;
+        a.x_resid = x_resid;
+        a.T = T;
+        a.k = l->k;
+        a.E = l->E;
+        a.H = l->H;
+        a.I = l->I;
+        a.alpha = l->alpha;
+        a.limit = l->limit;
+        a.workspace = ws;
+        gpt::launch_moe_batched(a, s);
+    });
 }
 
 void gptoss_moe_layer_destroy(gptoss_moe_layer* layer) { delete layer; }

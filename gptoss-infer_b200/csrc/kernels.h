@@ -90,6 +90,37 @@ struct DecodeTcArgs {
 };
 void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
 
+// Batched (prefill) MoE on tensor cores (prefill_tc.cu). Workspace layout for T tokens.
+struct PrefillLayout {
+    int max_tiles, SPS_gu, KT_gu, SPS_dn, KT_dn;
+    size_t off_h, off_ids, off_w, off_row_of, off_tok_of, off_slot_of, off_tiles, off_misc, off_img, off_sf, off_act,
+        off_w64, bytes;
+};
+PrefillLayout prefill_layout(int T, int k, int E, int H, int I);
+
+// Router weights bf16 [E][H] -> fp64 [H][32] (zero columns for experts >= E).
+void launch_router_w64(const void* W, int E, int H, double* W64, cudaStream_t s);
+// RMSNorm (norm_w != null) and router for T tokens: h_out (optional) = normalized x, ids / wts [T][k].
+void launch_router_batched(const double* W64, const float* b, const float* x, const float* norm_w, float eps, int T,
+                           int E, int H, int k, float* h_out, int* ids, float* wts, cudaStream_t s);
+
+struct PrefillArgs {
+    const CUtensorMap* tmap_gu;   // gate/up blocks [E][2I][H/2] bytes, boxes of kDecodeTileRows rows x 128 bytes
+    const CUtensorMap* tmap_dn;
+    const uint8_t* sf_gu;         // scales repacked with kDecodeTileRows-row tiles for all E experts
+    const uint8_t* sf_dn;
+    const float* gu_bias;         // [E][2I]
+    const float* dn_bias;         // [E][H]
+    const float* h;               // normalized tokens [T][H]
+    const int* ids;               // [T][k]
+    const float* weights;         // [T][k]
+    float* x_resid;               // [T][H], += the MoE output
+    int T, k, E, H, I;
+    float alpha, limit;
+    void* workspace;              // prefill_layout(T, k, E, H, I).bytes
+};
+void launch_moe_batched(const PrefillArgs& a, cudaStream_t s);
+
 // Single-CTA tcgen05 kind::mxf4 GEMM, D[128][N] = dequant(A)[128][K] . dequant(B)[N][K]^T, from raw MXFP4 arrays
 // (checkpoint layout). Pins the layout conventions of the tensor-core kernels. Synchronizes.
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,

@@ -117,6 +117,27 @@ void gptoss_moe_layer_destroy(gptoss_moe_layer* layer);
 int gptoss_moe_layer_forward(gptoss_moe_layer* layer, const float* x, float* x_resid, void* stream,
                              void* const* events);
 
+/* [extension] Router for T tokens: ids[T][k] and weights[T][k] as gptoss_kernel_router computes them for each row
+ * of x [T][H] (already normalized). fp64 logits from exact products; ties to the lower expert id. Device pointers;
+ * synchronizes. */
+int gptoss_kernel_router_batched(const void* W, const float* b, const float* x, int E, int H, int k, int T,
+                                 int32_t* ids, float* weights);
+
+/* [extension] Batched (prefill) MoE on tensor cores: x_resid[t] += sum_s w[t][s] (W2[e] swiglu(W1[e] x_norm[t] + b1)
+ * + b2) with e = ids[t][s], for T tokens (grouped GEMM over the experts: permute, tcgen05 block-scaled FP4 MMAs with
+ * the activations split into 8 e2m1 residual terms, unpermute, slot-ordered combine). Layouts as gptoss_kernel_moe
+ * with x_norm, ids, weights, x_resid of T rows; expert ids in 0..31; H and I multiples of 64; T <= 32768. Device
+ * pointers; synchronizes. */
+int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
+                              const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
+                              const float* x_norm, const int32_t* ids, const float* weights, float* x_resid, int T,
+                              int k, int H, int I, float alpha, float limit);
+
+/* [extension] x_resid[t] += MoE(RMSNorm(x[t])) for T tokens with a prepared layer (batched router, then the batched
+ * MoE above), asynchronous on `stream`. x_resid may alias x. Uses the calling thread's batched-path workspace: calls
+ * from one thread must not overlap on the GPU. */
+int gptoss_moe_layer_forward_batched(gptoss_moe_layer* layer, const float* x, float* x_resid, int T, void* stream);
+
 /* [extension] Self-test of the tensor-core block-scaled MMA path: D[128, N] (fp32, row-major) =
  * dequant(a_blocks [128, K/32, 16], a_scales [128, K/32]) . dequant(b_blocks [N, K/32, 16], b_scales [N, K/32])^T
  * computed by one CTA with TMA, tcgen05.cp scale factors and tcgen05.mma kind::mxf4. N % 8 == 0, 8 <= N <= 256,

@@ -1,0 +1,150 @@
+"""Batched (prefill) MoE path on tensor cores against the CPU oracle.
+
+The batched form of the reference's MoE (gptoss_ref/model.py:100-104): every expert applied to the rows that
+selected it, results weighted and added in slot order. Tolerances as the decode tests (the reference's own
+test_kernels.py:148-174 bound): allclose rtol 1e-4 / atol 1e-3 against float64, plus max-abs <= 2e-5 * max|ref|.
+Router ids must equal the float64 ranking on every token without a near-tie (rel 1e-5).
+"""
+import numpy as np
+import pytest
+import torch
+
+from gptoss_b200 import capi, synth
+from oracle import moe as omoe
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+P = capi.ptr
+PX = "model.layers.0."
+EX = PX + "mlp.experts."
+
+
+def _experts(t):
+    return [t[EX + "gate_up_proj_blocks"], t[EX + "gate_up_proj_scales"], t[EX + "gate_up_proj_bias"].float(),
+            t[EX + "down_proj_blocks"], t[EX + "down_proj_scales"], t[EX + "down_proj_bias"].float()]
+
+
+def _ok(lib, rc):
+    assert rc == 0, lib.gptoss_last_error().decode()
+
+
+def _check(got, want):
+    got = np.asarray(got, np.float64)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
+    assert np.abs(got - want).max() <= 2e-5 * np.abs(want).max()
+
+
+def _run_batched(lib, ex_cpu, x, ids, w, resid):
+    ex = [e.to(DEV) for e in ex_cpu]
+    dx, did, dw, dr = (torch.as_tensor(a).to(DEV).contiguous() for a in (x, ids, w, resid))
+    T, k = ids.shape
+    _ok(lib, lib.gptoss_kernel_moe_batched(*(P(e) for e in ex), P(dx), P(did), P(dw), P(dr), T, k, 2880, 2880,
+                                           1.702, 7.0))
+    return dr.cpu().numpy()
+
+
+def _oracle(ex_cpu, x, ids, w, resid):
+    n = [e.numpy() for e in ex_cpu]
+    return omoe.moe_batched_f64(*n, x, ids, w, resid)
+
+
+def _random_routing(T, E, k, seed):
+    g = np.random.default_rng(seed)
+    ids = np.stack([g.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    w = torch.softmax(torch.from_numpy(g.standard_normal((T, k)).astype(np.float32)), -1).numpy()
+    return ids, w
+
+
+def test_router_batched_exact_ids():
+    lib = capi.load()
+    t = synth.moe_layer(seed=0)
+    W = t[PX + "mlp.router.weight"]
+    b = t[PX + "mlp.router.bias"].float()
+    x = synth.tokens(512, seed=5).numpy()
+    h = omoe.rms_norm(x, t[PX + "post_attention_layernorm.weight"].float().numpy())
+    ids = torch.empty(512, 4, dtype=torch.int32, device=DEV)
+    w = torch.empty(512, 4, device=DEV)
+    dW, db, dh = W.to(DEV), b.to(DEV), torch.from_numpy(h).to(DEV)      # kept alive across the call
+    _ok(lib, lib.gptoss_kernel_router_batched(P(dW), P(db), P(dh), 32, 2880, 4, 512, P(ids), P(w)))
+    logits = h.astype(np.float64) @ W.float().numpy().astype(np.float64).T + b.numpy().astype(np.float64)
+    want = omoe.topk_ids(logits, 4)
+    ties = omoe.near_tie_rows(logits, 4)
+    got = ids.cpu().numpy()
+    assert np.array_equal(got[~ties], want[~ties])
+    sel = np.take_along_axis(logits, want, 1)
+    ww = np.exp(sel - sel[:, :1])
+    ww /= ww.sum(1, keepdims=True)
+    np.testing.assert_allclose(w.cpu().numpy()[~ties], ww[~ties], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("T", [1, 37])
+def test_moe_batched_random_routing(T):
+    lib = capi.load()
+    t = synth.moe_layer(seed=3, E=8)
+    ex = _experts(t)
+    g = np.random.default_rng(T)
+    x = g.standard_normal((T, 2880)).astype(np.float32)
+    resid = g.standard_normal((T, 2880)).astype(np.float32)
+    ids, w = _random_routing(T, 8, 4, T + 1)
+    _check(_run_batched(lib, ex, x, ids, w, resid), _oracle(ex, x, ids, w, resid))
+
+
+def test_moe_batched_skewed():
+    """Every token picks experts 0..3 (in varying order): 50 rows per expert, several M tiles, a partial last tile."""
+    lib = capi.load()
+    t = synth.moe_layer(seed=4, E=4)
+    ex = _experts(t)
+    g = np.random.default_rng(2)
+    T = 50
+    x = g.standard_normal((T, 2880)).astype(np.float32)
+    resid = np.zeros((T, 2880), np.float32)
+    ids = np.stack([g.permutation(4) for _ in range(T)]).astype(np.int32)
+    w = np.full((T, 4), 0.25, np.float32)
+    _check(_run_batched(lib, ex, x, ids, w, resid), _oracle(ex, x, ids, w, resid))
+
+
+def test_layer_forward_batched_matches_decode_and_oracle():
+    """Prepared layer, 20 tokens: the batched forward (RMSNorm + router + MoE) agrees with the float64 oracle on the
+    oracle's routing, with the per-token decode kernel, and is deterministic."""
+    lib = capi.load()
+    t = synth.moe_layer(seed=0)
+    d = {k_: v.to(DEV) for k_, v in t.items()}
+    ln = d[PX + "post_attention_layernorm.weight"].float()
+    W, b = d[PX + "mlp.router.weight"], d[PX + "mlp.router.bias"].float()
+    ex = [e.to(DEV) for e in _experts(t)]
+    L = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), 32, 4, 2880, 2880, 1.702, 7.0)
+    assert L, lib.gptoss_last_error().decode()
+    try:
+        T = 20
+        x = synth.tokens(T, seed=8)
+        xb = x.to(DEV).contiguous()
+        outs = []
+        for _ in range(2):
+            y = xb.clone()
+            _ok(lib, lib.gptoss_moe_layer_forward_batched(L, P(xb), P(y), T, None))
+            torch.cuda.synchronize()
+            outs.append(y.cpu().numpy())
+        assert np.array_equal(outs[0], outs[1])
+        dec = []
+        for i in range(T):
+            y = xb[i].clone()
+            _ok(lib, lib.gptoss_moe_layer_forward(L, P(xb[i]), P(y), None, None))
+            dec.append(y)
+        torch.cuda.synchronize()
+        dec = torch.stack(dec).cpu().numpy()
+        # oracle on its own float64 routing
+        xn = x.numpy()
+        h = omoe.rms_norm(xn, t[PX + "post_attention_layernorm.weight"].float().numpy())
+        logits = h.astype(np.float64) @ t[PX + "mlp.router.weight"].float().numpy().astype(np.float64).T + \
+            t[PX + "mlp.router.bias"].float().numpy().astype(np.float64)
+        ids = omoe.topk_ids(logits, 4)
+        assert not omoe.near_tie_rows(logits, 4).any()
+        sel = np.take_along_axis(logits, ids, 1)
+        w = np.exp(sel - sel[:, :1])
+        w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+        want = _oracle(_experts(t), h, ids.astype(np.int32), w, xn)
+        _check(outs[0], want)
+        _check(dec, want)
+    finally:
+        lib.gptoss_moe_layer_destroy(L)

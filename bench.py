@@ -40,7 +40,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode"])
+    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode", "prefill"])
+    ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 2: 2048)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--moe-impl", type=int, default=None, help="0 = SIMT, 1 = tensor cores (default: library's)")
     ap.add_argument("--layers", type=int, default=LAYERS)
@@ -226,8 +227,198 @@ def run_reference(args):
     print(json.dumps(line))
 
 
+PREFILL_METRIC = "prefill tok/s (2048 tokens x 1 MoE layer, Zipf s=1.1 routing)"
+
+
+def prefill_flops(T):
+    """Algorithmic FLOPs of one batched MoE layer: 2 * (T * k) * (2I * H + H * I)."""
+    return 2.0 * T * K_TOP * (2 * I * H + H * I)
+
+
+def prefill_inputs(T):
+    """Config 2: layer 0 (synth seed 0) with the router bias skewed towards Zipf s=1.1 over a seeded expert order,
+    tokens bf16 N(0,1) [T, H] (passed as fp32; the conversion is exact)."""
+    import torch
+    from gptoss_b200 import synth
+    t = synth.moe_layer(seed=0)
+    perm = synth.zipf_router_bias(t, s=1.1, beta=1.0, seed=7)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).float()
+    return t, perm, x
+
+
+def run_prefill_reference(args):
+    """Reference arm for the prefill workload: Reference.moe (numpy fp32 restatement, per-call dequant) on a bounded
+    sample of the same tokens per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from gptoss_b200 import synth
+    from oracle import moe as omoe
+    t, _, x = prefill_inputs(args.tokens)
+    tn = synth.to_numpy(t)
+    p = "model.layers.0."
+    h = omoe.rms_norm(x.numpy(), tn[p + "post_attention_layernorm.weight"])
+    n_s = 64                                                   # tokens per step (a bounded sample)
+    omoe.moe(tn, p, h[:n_s])
+    el, done = 0.0, 0
+    for i in range(args.warmup):
+        omoe.moe(tn, p, h[:n_s])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        omoe.moe(tn, p, h[(i * n_s) % args.tokens:(i * n_s) % args.tokens + n_s])
+        done += n_s
+    el = time.perf_counter() - t0
+    value = done / el
+    line = {"impl": "reference", "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "prefill (configs[2])", "tokens": args.tokens},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{n_s} tokens per step through Reference.moe (numpy fp32, per-call MXFP4 "
+                                       f"dequant of every selected expert)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_prefill(args):
+    """Config 2 on one GPU (replicas with N > 1): per step x_resid = x + MoE(RMSNorm(x)) for T tokens through the
+    prepared layer's batched forward (batched router, permute, grouped tcgen05 GEMMs, combine), one CUDA graph."""
+    import torch
+    from gptoss_b200 import capi, synth
+    ws, rank, local = dist_init()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = capi.load()
+    P = capi.ptr
+    T = args.tokens
+    t, perm, x_cpu = prefill_inputs(T)
+    p = "model.layers.0."
+    d = {k[len(p):]: v.to(dev) for k, v in t.items()}
+    ln = d["post_attention_layernorm.weight"].float()
+    W, b = d["mlp.router.weight"].contiguous(), d["mlp.router.bias"].float()
+    ex = [d["mlp.experts.gate_up_proj_blocks"], d["mlp.experts.gate_up_proj_scales"],
+          d["mlp.experts.gate_up_proj_bias"].float(), d["mlp.experts.down_proj_blocks"],
+          d["mlp.experts.down_proj_scales"], d["mlp.experts.down_proj_bias"].float()]
+    L = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), E, K_TOP, H, I, 1.702, 7.0)
+    if not L:
+        raise RuntimeError(lib.gptoss_last_error().decode())
+    x = x_cpu.to(dev)
+    y = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # realised routing (per-expert token counts), from the library's own batched router
+    ids = torch.empty(T, K_TOP, dtype=torch.int32, device=dev)
+    wts = torch.empty(T, K_TOP, device=dev)
+    h = torch.nn.functional.rms_norm(x, (H,), ln, 1e-5)
+    if lib.gptoss_kernel_router_batched(P(W), P(b), P(h), E, H, K_TOP, T, P(ids), P(wts)) != 0:
+        raise RuntimeError(lib.gptoss_last_error().decode())
+    counts = torch.bincount(ids.flatten().long(), minlength=E).tolist()
+
+    def step(sp):
+        y.copy_(x)
+        if lib.gptoss_moe_layer_forward_batched(L, P(x), P(y), T, sp) != 0:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+
+    for _ in range(max(args.warmup, 1)):                 # eager warm-up also sizes the workspace
+        step(stream.cuda_stream)
+    barrier()
+    cap = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        step(cap.cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    barrier()
+    with ClockSampler(local) as clocks:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        tt = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+    step_s = ms / args.steps / 1e3
+    value = ws * T / step_s
+    # end to end: host x in (pinned), host result out, every step
+    xh = x_cpu.pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        x.copy_(xh, non_blocking=True)
+        graph.replay()
+        yh.copy_(y, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    if ws > 1:
+        tt = torch.tensor([ms_e2e], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(tt.item())
+    e2e = ws * T / (ms_e2e / args.steps / 1e3)
+    del graph
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        from oracle import moe as omoe
+        tn = synth.to_numpy(t)
+        hn = omoe.rms_norm(x_cpu.numpy(), tn[p + "post_attention_layernorm.weight"])
+        n_s = 64
+        omoe.moe(tn, p, hn[:n_s])                             # cold run
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 15.0 and reps < 4:
+            omoe.moe(tn, p, hn[reps * n_s:(reps + 1) * n_s])
+            reps += 1
+        el = time.perf_counter() - t0
+        cpu = {"value": reps * n_s / el, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{reps} x {n_s} tokens through Reference.moe (numpy fp32, per-call dequant of every "
+                         f"selected expert)"}
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = peaks.get("bf16_tflops_sustained")
+    peak_fp4 = 4.0 * bf16 if bf16 else 4.0 * 1400.0
+    achieved = prefill_flops(T) / step_s / 1e12
+    lib.gptoss_moe_layer_destroy(L)
+    if rank == 0:
+        line = {
+            "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e2m1 x e2m1 (fp32 accumulate; activations as 8 residual terms)",
+            "data": "synthetic (seeded random-init 20b-shaped MoE layer, bf16 N(0,1) tokens)",
+            "config": {"workload": "prefill (configs[2])", "tokens": T, "experts": E, "top_k": K_TOP, "hidden": H,
+                       "intermediate": I, "zipf_s": 1.1, "expert_token_counts": counts,
+                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                       "l2": "423 MB of experts per layer, larger than L2"},
+            "roofline": {"bound": "tensor", "kernel": "whole batched MoE step (grouped tcgen05 GEMMs dominate)",
+                         "achieved": achieved, "unit": "TFLOP/s", "peak": peak_fp4,
+                         "peak_source": "4 x measured sustained bf16 (dense FP4 is 4x the bf16 rate)",
+                         "frac": achieved / peak_fp4, "frac_of_9PF_nominal": achieved / 9000.0,
+                         "algorithmic_flops_per_step": prefill_flops(T), "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                    "api": "gptoss_moe_layer_forward_batched in a CUDA graph; host tokens copied in and out"},
+            "gpu_launches": args.steps * 7,   # router, permute, 2 x (quantize, grouped GEMM), combine
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.workload == "prefill":
+        return run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
     if args.impl == "reference":
         return run_reference(args)
     import torch

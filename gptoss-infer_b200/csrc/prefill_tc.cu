@@ -55,16 +55,18 @@ __global__ void router_w64_kernel(const __nv_bfloat16* __restrict__ W, int E, in
     }
 }
 
-// 8 tokens per CTA, 256 threads: RMSNorm (warp w on token w), h in shared memory as fp64, then thread (e = tid % 32,
-// kp = tid / 32) accumulates expert e over k = kp, kp + 8, ... for the 8 tokens; the 8 partial sums are added in
-// order and warp w picks token w's top k on order-preserving integer keys of the fp64 logits.
-__global__ void __launch_bounds__(256) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
+// 8 tokens per CTA, 512 threads: RMSNorm (warp w < 8 on token w), h in shared memory as fp64, then thread
+// (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp, kp + 16, ... for the 8 tokens (the weight loads of
+// four k issued ahead of their FMAs); the 16 partial sums are added in order and warp w picks token w's top k on
+// order-preserving integer keys of the fp64 logits.
+constexpr int kRtParts = 16;
+__global__ void __launch_bounds__(512) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
                                                              const float* __restrict__ x, const float* __restrict__ g,
                                                              float eps, int T, int E, int H, int k,
                                                              float* __restrict__ h_out, int* __restrict__ ids,
                                                              float* __restrict__ wts) {
     extern __shared__ double h64[];                          // [kRtTok][H]
-    __shared__ double red[8][kRtTok][32];
+    __shared__ double red[kRtParts][kRtTok][32];
     __shared__ float rn_s[kRtTok];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.x * kRtTok, nt = min(kRtTok, T - t0);
@@ -79,7 +81,7 @@ __global__ void __launch_bounds__(256) router_batched_kernel(const double* __res
         if (lane == 0) rn_s[warp] = g ? 1.0f / sqrtf(ss / float(H) + eps) : 1.f;
     }
     __syncthreads();
-    for (int i = tid * 4; i < nt * H; i += 256 * 4) {
+    for (int i = tid * 4; i < nt * H; i += 512 * 4) {
         const int tb = i / H, kk = i - tb * H;
         float4 v = *reinterpret_cast<const float4*>(x + size_t(t0) * H + i);
         if (g) {
@@ -90,16 +92,27 @@ __global__ void __launch_bounds__(256) router_batched_kernel(const double* __res
         if (h_out) *reinterpret_cast<float4*>(h_out + size_t(t0) * H + i) = v;
         h64[i] = v.x; h64[i + 1] = v.y; h64[i + 2] = v.z; h64[i + 3] = v.w;
     }
-    for (int i = nt * H + tid; i < kRtTok * H; i += 256) h64[i] = 0.0;
+    for (int i = nt * H + tid; i < kRtTok * H; i += 512) h64[i] = 0.0;
     __syncthreads();
     const int e = lane, kp = warp;
     double acc[kRtTok];
 #pragma unroll
     for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = 0.0;
-    for (int kk = kp; kk < H; kk += 8) {
-        const double wk = W64[size_t(kk) * 32 + e];
+    for (int kk0 = kp; kk0 < H; kk0 += 4 * kRtParts) {
+        double wk[4];
 #pragma unroll
-        for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk, h64[tb * H + kk], acc[tb]);
+        for (int u = 0; u < 4; ++u) {
+            const int kk = kk0 + u * kRtParts;
+            wk[u] = kk < H ? W64[size_t(kk) * 32 + e] : 0.0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int kk = kk0 + u * kRtParts;
+            if (kk < H) {
+#pragma unroll
+                for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk[u], h64[tb * H + kk], acc[tb]);
+            }
+        }
     }
 #pragma unroll
     for (int tb = 0; tb < kRtTok; ++tb) red[kp][tb][e] = acc[tb];
@@ -108,7 +121,7 @@ __global__ void __launch_bounds__(256) router_batched_kernel(const double* __res
         const int t = t0 + warp;
         double v = 0.0;
         if (lane < E) {
-            for (int p = 0; p < 8; ++p) v += red[p][warp][lane];
+            for (int p = 0; p < kRtParts; ++p) v += red[p][warp][lane];
             v += double(b[lane]);
         }
         const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(v));
@@ -503,7 +516,7 @@ void launch_router_batched(const double* W64, const float* b, const float* x, co
             done[dev] = smem;
         }
     }
-    pf::router_batched_kernel<<<(T + pf::kRtTok - 1) / pf::kRtTok, 256, smem, s>>>(W64, b, x, norm_w, eps, T, E, H, k,
+    pf::router_batched_kernel<<<(T + pf::kRtTok - 1) / pf::kRtTok, 512, smem, s>>>(W64, b, x, norm_w, eps, T, E, H, k,
                                                                                    h_out, ids, wts);
     check_launch("router_batched");
 }

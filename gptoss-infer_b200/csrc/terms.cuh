@@ -126,6 +126,19 @@ __device__ __forceinline__ float round_e2m1(float y) {
     return __fsub_rn(__fadd_rn(y, c), c);
 }
 
+// round_e2m1 that also returns the e2m1 code (sign in bit 3): after the magic add the integer difference of the float
+// bits is the rounded multiple of the grid step (0.5, 1 or 2), and the code is that multiple's magnitude plus 0, 2 or
+// 4 for the three step ranges (2.0 = code 4, 4.0 = code 6, 6.0 = code 7).
+__device__ __forceinline__ float round_e2m1_code(float y, uint32_t& code) {
+    const float a = fabsf(y);
+    const bool lo = a < 2.f, mid = a < 4.f;
+    const float c = lo ? 0x1.8p22f : (mid ? 0x1.8p23f : 0x1.8p24f);
+    const float sm = __fadd_rn(y, c);
+    const int m = __float_as_int(sm) - __float_as_int(c);
+    code = (uint32_t(abs(m) + (lo ? 0 : (mid ? 2 : 4))) & 7u) | ((__float_as_uint(y) >> 28) & 8u);
+    return __fsub_rn(sm, c);
+}
+
 // e2m1 code (sign in bit 3) of a value q that is exactly an e2m1 value (other inputs give some code, never more
 // than 4 bits).
 __device__ __forceinline__ uint32_t e2m1_code(float q) {
@@ -172,9 +185,10 @@ __device__ __forceinline__ void quantize_block_terms_fixed_n(float (&v)[8], uint
             const float inv = exp2i_exact(-kc), sc = exp2i_exact(kc);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float qv = round_e2m1(v[i] * inv);
+                uint32_t code;
+                const float qv = round_e2m1_code(v[i] * inv, code);
                 v[i] = fmaf(-qv, sc, v[i]);
-                word |= e2m1_code(qv) << (4 * i);
+                word |= code << (4 * i);
             }
             scale = uint32_t(kc + 127);
             k -= t == 0 ? 2 : 3;
@@ -215,9 +229,8 @@ __device__ __forceinline__ void quantize_block_terms_warp32(float v, uint8_t* im
         uint32_t nib = 0, scale = 0;
         if (t < kActiveTerms) {
             const int kc = max(-127, k);
-            const float qv = round_e2m1(v * exp2i_exact(-kc));
+            const float qv = round_e2m1_code(v * exp2i_exact(-kc), nib);
             v = fmaf(-qv, exp2i_exact(kc), v);
-            nib = e2m1_code(qv);
             scale = uint32_t(kc + 127);
             k -= t == 0 ? 2 : 3;
         }

@@ -402,6 +402,16 @@ int gptoss_kernel_router_batched(const void* W, const float* b, const float* x, 
     });
 }
 
+int gptoss_moe_route_batched(const void* W, const float* b, const float* x, const float* norm_w, float eps, int E,
+                             int H, int k, int T, float* h_out, int32_t* ids, float* weights, void* stream) {
+    return guard([&] {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        double* w64 = static_cast<double*>(g_scratch.get(size_t(H) * 32 * sizeof(double)));
+        gpt::launch_router_w64(W, E, H, w64, s);
+        gpt::launch_router_batched(w64, b, x, norm_w, eps, T, E, H, k, h_out, ids, weights, s);
+    });
+}
+
 int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
                               const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
                               const float* x_norm, const int32_t* ids, const float* weights, float* x_resid, int T,
@@ -478,6 +488,39 @@ int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float*
         a.x_resid = x_resid;
         a.T = T;
         a.k = l->k;
+        a.E = l->E;
+        a.H = l->H;
+        a.I = l->I;
+        a.alpha = l->alpha;
+        a.limit = l->limit;
+        a.workspace = ws;
+        gpt::launch_moe_batched(a, s);
+    });
+}
+
+int gptoss_moe_layer_experts_batched(gptoss_moe_layer* l, const float* h, const int32_t* ids, const float* weights,
+                                     float* x_resid, int T, int k, void* stream) {
+    return guard([&] {
+        if (!l) throw std::runtime_error("moe_layer_experts_batched: null layer");
+        if (T < 1 || k < 1 || k > 8 || k > l->E)
+            throw std::runtime_error("moe_layer_experts_batched: need T >= 1 and 1 <= k <= min(8, E)");
+        const gpt::PrefillLayout L = gpt::prefill_layout(T, k, l->E, l->H, l->I);
+        char* ws = static_cast<char*>(g_pws.get(L.bytes));
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        GPT_CHECK(cudaMemsetAsync(ws + L.off_misc, 0, 1024, s));
+        gpt::PrefillArgs a{};
+        a.tmap_gu = &l->tg;
+        a.tmap_dn = &l->td;
+        a.sf_gu = l->sfa_gu;
+        a.sf_dn = l->sfa_dn;
+        a.gu_bias = l->gu_bias;
+        a.dn_bias = l->dn_bias;
+        a.h = h;
+        a.ids = ids;
+        a.weights = weights;
+        a.x_resid = x_resid;
+        a.T = T;
+        a.k = k;
         a.E = l->E;
         a.H = l->H;
         a.I = l->I;

@@ -1,0 +1,107 @@
+"""Expert parallelism for the batched MoE path: experts sharded contiguously over the G ranks of a process group
+(E / G per rank), tokens data-parallel (each rank routes its own shard).
+
+One layer call on every rank (all ranks take the same collective steps in the same order):
+  1. route the rank's tokens (RMSNorm, router, top k, softmax) with the library's batched router;
+  2. dispatch: each (token, slot) pair goes to the rank owning its expert. The per-destination counts are exchanged
+     with one all-to-all, then the normalized token rows (fp32) and their (local expert id, gate weight) with one
+     all-to-all each, packed in destination order (token, then slot, ascending within a destination);
+  3. the received rows run through the rank's local experts (the library's batched tensor-core MoE with k = 1, so
+     each row comes back as w * (W2 swiglu(W1 h + b1) + b2));
+  4. combine: the results return with the reverse all-to-all and are added to the residual stream in slot order.
+
+Because every row's expert computation and the slot-ordered combine are the same operations as in the single-GPU
+batched path, the result is bit-identical to it for any G. Collectives are torch.distributed all_to_all_single (NCCL
+over NVLink between GPUs, gloo for the CPU tests). The routing and local expert steps are injectable so the
+dispatch/combine logic runs on CPU with a reference compute.
+"""
+import torch
+import torch.distributed as dist
+
+from . import capi
+
+
+def _a2a(out, inp, out_splits, in_splits, group):
+    dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+
+
+class ExpertParallelMoE:
+    """x <- x + MoE(RMSNorm(x)) for a rank's token shard, experts [rank * El, (rank + 1) * El) held locally.
+
+    route(x) -> (h [T, H] fp32, ids [T, k] int32 (global expert ids), w [T, k] fp32)
+    compute(h_rows [n, H], local_ids [n] int32, w [n] fp32) -> y [n, H] fp32 (w already applied)
+    """
+
+    def __init__(self, route, compute, rank, world, E, k, H, group=None):
+        if E % world:
+            raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+        self.route, self.compute = route, compute
+        self.rank, self.world, self.E, self.k, self.H = rank, world, E, k, H
+        self.El = E // world
+        self.group = group
+
+    def forward(self, x):
+        T, H = x.shape
+        k, G = self.k, self.world
+        h, ids, w = self.route(x)
+        dest = ids.long() // self.El                                   # [T, k]
+        flat = dest.reshape(-1)
+        order = torch.argsort(flat, stable=True)                       # (token, slot) grouped by destination
+        send = torch.bincount(flat, minlength=G)
+        recv = torch.empty_like(send)
+        _a2a(recv, send, None, None, self.group)
+        sc, rc = send.tolist(), recv.tolist()
+        n_send, n_recv = sum(sc), sum(rc)
+        h_send = h[order // k].contiguous()
+        meta_send = torch.stack([(ids.reshape(-1)[order].long() - flat[order] * self.El).to(w.dtype),
+                                 w.reshape(-1)[order]], 1).contiguous()   # local ids are exact in w's type
+        h_recv = torch.empty(n_recv, H, dtype=h.dtype, device=h.device)
+        meta_recv = torch.empty(n_recv, 2, dtype=w.dtype, device=h.device)
+        _a2a(h_recv, h_send, rc, sc, self.group)
+        _a2a(meta_recv, meta_send, rc, sc, self.group)
+        if n_recv:
+            y_recv = self.compute(h_recv, meta_recv[:, 0].to(torch.int32).contiguous(), meta_recv[:, 1].contiguous())
+        else:
+            y_recv = torch.empty(0, H, dtype=h.dtype, device=h.device)
+        y_back = torch.empty(n_send, H, dtype=h.dtype, device=h.device)
+        _a2a(y_back, y_recv.contiguous(), sc, rc, self.group)
+        y_ts = torch.empty(T * k, H, dtype=h.dtype, device=h.device)
+        y_ts[order] = y_back
+        y_ts = y_ts.view(T, k, H)
+        for s in range(k):                                             # slot order, as the single-GPU combine
+            x += y_ts[:, s]
+        return x
+
+
+def gpu_route(lib, norm_w, router_w, router_b, E, k, eps=1e-5):
+    """The library's batched router (RMSNorm, fp64 logits, top k, softmax) on the current stream."""
+    P = capi.ptr
+
+    def route(x):
+        T, H = x.shape
+        h = torch.empty_like(x)
+        ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=x.device)
+        rc = lib.gptoss_moe_route_batched(P(router_w), P(router_b), P(x), P(norm_w), eps, E, H, k, T, P(h), P(ids),
+                                          P(w), torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+        return h, ids, w
+
+    return route
+
+
+def gpu_compute(lib, layer):
+    """The local experts of a prepared layer (gptoss_moe_layer_create with this rank's experts) on given rows."""
+    P = capi.ptr
+
+    def compute(h_rows, lids, w):
+        n, H = h_rows.shape
+        y = torch.zeros_like(h_rows)
+        rc = lib.gptoss_moe_layer_experts_batched(layer, P(h_rows), P(lids), P(w), P(y), n, 1,
+                                                  torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+        return y
+
+    return compute

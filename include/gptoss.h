@@ -123,6 +123,12 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* layer, const float* x, float* x_r
 int gptoss_kernel_router_batched(const void* W, const float* b, const float* x, int E, int H, int k, int T,
                                  int32_t* ids, float* weights);
 
+/* [extension] Routing for T tokens, asynchronous on `stream`: h_out[T][H] = RMSNorm(x; norm_w, eps) (norm_w NULL:
+ * h_out = x), ids[T][k] and weights[T][k] as gptoss_kernel_router_batched. Uses the calling thread's scratch for the
+ * router weights in fp64: calls from one thread must not overlap on the GPU. */
+int gptoss_moe_route_batched(const void* W, const float* b, const float* x, const float* norm_w, float eps, int E,
+                             int H, int k, int T, float* h_out, int32_t* ids, float* weights, void* stream);
+
 /* [extension] Batched (prefill) MoE on tensor cores: x_resid[t] += sum_s w[t][s] (W2[e] swiglu(W1[e] x_norm[t] + b1)
  * + b2) with e = ids[t][s], for T tokens (grouped GEMM over the experts: permute, tcgen05 block-scaled FP4 MMAs with
  * the activations split into 8 e2m1 residual terms, unpermute, slot-ordered combine). Layouts as gptoss_kernel_moe
@@ -137,6 +143,13 @@ int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales
  * MoE above), asynchronous on `stream`. x_resid may alias x. Uses the calling thread's batched-path workspace: calls
  * from one thread must not overlap on the GPU. */
 int gptoss_moe_layer_forward_batched(gptoss_moe_layer* layer, const float* x, float* x_resid, int T, void* stream);
+
+/* [extension] The experts of a prepared layer applied to T given rows, asynchronous on `stream`: x_resid[t] +=
+ * sum_s w[t][s] (W2[e] swiglu(W1[e] h[t] + b1) + b2) with e = ids[t][s] < the layer's E (the router is not used).
+ * The building block of expert parallelism: a rank's layer holds only its own experts and gets the rows routed to
+ * them. Same workspace rule as gptoss_moe_layer_forward_batched. */
+int gptoss_moe_layer_experts_batched(gptoss_moe_layer* layer, const float* h, const int32_t* ids, const float* weights,
+                                     float* x_resid, int T, int k, void* stream);
 
 /* [extension] Self-test of the tensor-core block-scaled MMA path: D[128, N] (fp32, row-major) =
  * dequant(a_blocks [128, K/32, 16], a_scales [128, K/32]) . dequant(b_blocks [N, K/32, 16], b_scales [N, K/32])^T

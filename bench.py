@@ -11,6 +11,13 @@ Timed region: W untimed steps, then exactly K steps between a barrier + synchron
 the launching stream, max over ranks. With N > 1 every rank runs an independent replica (bs=1 decode does not
 shard): value = N * K * bytes / max time ("replicas only", scaling "weak").
 
+Workload "prefill": 2048 tokens x 1 MoE layer per step on one GPU through the batched forward (batched
+router, permute, grouped tcgen05 block-scaled FP4 GEMMs, combine) in a CUDA graph; replicas with N > 1.
+
+Workload "ep": 8192 tokens (over all ranks) x 24 MoE layers per step, the 32 experts of every layer
+sharded contiguously over the N ranks and the tokens split evenly; per layer, all-to-all dispatch and combine around
+each rank's local experts (gptoss_b200/ep.py). Strong scaling: value = 8192 / max-over-ranks step time.
+
 --impl reference times the reference's own CPU algorithm for this path (the fp32 Reference.moe of
 openvang/gptoss-infer, restated in oracle/moe.py, dequantizing each selected expert per call as the reference does)
 on the host cores, on a bounded sample per step, and prints the same metric.
@@ -32,6 +39,7 @@ EXPERT_BYTES = 8_294_400 + 518_400 + 4_147_200 + 259_200            # blocks + s
 LAYER_BYTES = K_TOP * EXPERT_BYTES + 184_320 + K_TOP * (5760 + 2880) * 2   # + router + bf16 biases = 53,130,240
 GATEUP_BYTES = K_TOP * (8_294_400 + 518_400 + 5760 * 4) + H * 4 + K_TOP * I * 4   # per launch, fp32 bias/in/out
 METRIC = "bs=1 decode MoE-layer HBM GB/s (20b-shaped, 24 layers)"
+REF_BUDGET_S = 90.0                  # timed seconds at most for the prefill / expert-parallel reference arms
 UNIT = "GB/s"
 
 
@@ -40,8 +48,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode", "prefill"])
-    ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 2: 2048)")
+    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode", "prefill", "ep"])
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="prefill: tokens per step (config 2: 2048); ep: tokens per step over all ranks (config 3: 8192)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--moe-impl", type=int, default=None, help="0 = SIMT, 1 = tensor cores (default: library's)")
     ap.add_argument("--layers", type=int, default=LAYERS)
@@ -263,16 +272,21 @@ def run_prefill_reference(args):
     n_s = 64                                                   # tokens per step (a bounded sample)
     omoe.moe(tn, p, h[:n_s])
     el, done = 0.0, 0
-    for i in range(args.warmup):
+    for i in range(min(args.warmup, 1)):
         omoe.moe(tn, p, h[:n_s])
     t0 = time.perf_counter()
+    timed = 0
     for i in range(args.steps):
         omoe.moe(tn, p, h[(i * n_s) % args.tokens:(i * n_s) % args.tokens + n_s])
         done += n_s
+        timed += 1
+        if time.perf_counter() - t0 > REF_BUDGET_S:               # bounded: the run ends within a few minutes
+            break
     el = time.perf_counter() - t0
     value = done / el
     line = {"impl": "reference", "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "steps": args.steps, "steps_timed": timed, "warmup": args.warmup, "ms_per_step": el / timed * 1e3,
+            "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "prefill (configs[2])", "tokens": args.tokens},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
@@ -415,8 +429,208 @@ def run_prefill(args):
         torch.distributed.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------------ expert parallel
+EP_METRIC = "expert-parallel prefill tok/s (8192 tokens x 24 MoE layers, Zipf s=1.2 routing)"
+
+
+def run_ep_reference(args):
+    """Reference arm for the expert-parallel workload: Reference.moe (numpy fp32 restatement, per-call dequant of
+    every selected expert) on the host cores, a bounded sample of tokens through one layer per step, reported as
+    tokens through all 24 layers per second."""
+    rank = int(os.environ.get("RANK", "0"))
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import torch
+    from gptoss_b200 import synth
+    from oracle import moe as omoe
+    T = args.tokens
+    n_s = 32                                                    # tokens per step (a bounded sample)
+    t = {}
+    p = "model.layers.0."
+    ln, W, b = synth.ep_router(0)
+    t[p + "post_attention_layernorm.weight"], t[p + "mlp.router.weight"], t[p + "mlp.router.bias"] = ln, W.float(), b
+    ex = synth.ep_experts(0, 0, E, "cpu")
+    for n, v in zip(["gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+                     "down_proj_scales", "down_proj_bias"], ex):
+        t[p + "mlp.experts." + n] = v
+    tn = synth.to_numpy(t)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16).float().numpy()
+    h = omoe.rms_norm(x[:min(T, 8 * n_s)], ln.numpy())
+    for i in range(min(args.warmup, 1)):
+        omoe.moe(tn, p, h[:n_s])
+    done = 0
+    t0 = time.perf_counter()
+    timed = 0
+    for i in range(args.steps):
+        j = (i * n_s) % (len(h) - n_s + 1)
+        omoe.moe(tn, p, h[j:j + n_s])
+        done += n_s
+        timed += 1
+        if time.perf_counter() - t0 > REF_BUDGET_S:               # bounded: the run ends within a few minutes
+            break
+    el = time.perf_counter() - t0
+    value = done / el / LAYERS
+    line = {"impl": "reference", "metric": EP_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "steps_timed": timed, "warmup": args.warmup, "ms_per_step": el / timed * 1e3 * LAYERS,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "expert-parallel prefill (configs[3])", "tokens": T, "layers": LAYERS},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{n_s} tokens per step through one layer of Reference.moe (numpy fp32, "
+                                       f"per-call MXFP4 dequant), scaled by 1/{LAYERS} layers"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ep(args):
+    """Config 3: T tokens (over all ranks, T / N per rank) through 24 MoE layers per step, experts sharded
+    contiguously over the N ranks (32 / N each), tokens data-parallel. Per layer and rank: the library's batched
+    router on the rank's tokens, all-to-all dispatch of the (token, slot) rows to the experts' owners (NCCL over
+    NVLink), the local experts on tensor cores (gptoss_moe_layer_experts_batched, k = 1), reverse all-to-all and
+    slot-ordered combine (gptoss_b200/ep.py). Strong scaling: the total token count is fixed."""
+    import torch
+    from gptoss_b200 import capi, ep, synth
+    ws, rank, local = dist_init()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = capi.load()
+    P = capi.ptr
+    T = args.tokens
+    if T % ws or E % ws:
+        raise SystemExit(f"ep: {T} tokens and {E} experts must split evenly over {ws} ranks")
+    Tl, El = T // ws, E // ws
+    group = None
+    layers, handles = [], []
+    for li in range(args.layers):
+        ln, W, b = (v.to(dev) for v in synth.ep_router(li))
+        ex = synth.ep_experts(li, rank * El, (rank + 1) * El, dev)
+        hdl = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), El, min(K_TOP, El), H, I,
+                                          1.702, 7.0)
+        if not hdl:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+        handles.append(hdl)
+        layers.append((ex, ln, W, b, ep.ExpertParallelMoE(ep.gpu_route(lib, ln, W, b, E, K_TOP),
+                                                          ep.gpu_compute(lib, hdl), rank, ws, E, K_TOP, H, group)))
+    g = torch.Generator().manual_seed(0)
+    x_all = torch.randn(T, H, generator=g).to(torch.bfloat16).float()
+    x_cpu = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
+    x0 = x_cpu.to(dev)
+    x = torch.empty_like(x0)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def step():
+        x.copy_(x0)
+        for L in layers:
+            L[4].forward(x)
+
+    # realised routing of layer 0 over this rank's tokens (rows sent to each rank)
+    h0, ids0, _ = layers[0][4].route(x0)
+    rows_to = torch.bincount(ids0.flatten().long() // El, minlength=ws)
+    if ws > 1:
+        torch.distributed.all_reduce(rows_to)
+    rows_to = rows_to.tolist()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    with ClockSampler(local) as clocks:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        tt = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+    step_s = ms / args.steps / 1e3
+    value = T / step_s
+    # end to end: this rank's host tokens in (pinned), host result out, every step
+    xh = x_cpu.pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        x0.copy_(xh, non_blocking=True)
+        step()
+        yh.copy_(x, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    if ws > 1:
+        tt = torch.tensor([ms_e2e], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(tt.item())
+    e2e = T / (ms_e2e / args.steps / 1e3)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        from oracle import moe as omoe
+        p = "model.layers.0."
+        ex, ln, W, b, _ = layers[0]
+        t = {p + "post_attention_layernorm.weight": ln.cpu(), p + "mlp.router.weight": W.float().cpu(),
+             p + "mlp.router.bias": b.cpu()}
+        for n, v in zip(["gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+                         "down_proj_scales", "down_proj_bias"], ex):
+            t[p + "mlp.experts." + n] = v.cpu()
+        tn = synth.to_numpy(t)
+        hn = omoe.rms_norm(x_cpu.numpy(), tn[p + "post_attention_layernorm.weight"])
+        n_s = 32
+        omoe.moe(tn, p, hn[:n_s])                             # cold run
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 15.0 and reps < 4:
+            omoe.moe(tn, p, hn[reps * n_s:(reps + 1) * n_s])
+            reps += 1
+        el = time.perf_counter() - t0
+        cpu = {"value": reps * n_s / el / args.layers, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{reps} x {n_s} tokens through layer 0 of Reference.moe (numpy fp32, per-call dequant), "
+                         f"scaled by 1/{args.layers} layers"}
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = peaks.get("bf16_tflops_sustained")
+    peak_fp4 = 4.0 * bf16 if bf16 else 4.0 * 1400.0
+    flops = prefill_flops(T) * args.layers
+    achieved = flops / ws / step_s / 1e12
+    for hdl in handles:
+        lib.gptoss_moe_layer_destroy(hdl)
+    if rank == 0:
+        line = {
+            "metric": EP_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e2m1 x e2m1 (fp32 accumulate; activations as 8 residual terms)",
+            "data": "synthetic (seeded random-init 20b-shaped MoE layers, bf16 N(0,1) tokens)",
+            "config": {"workload": "expert-parallel prefill (configs[3])", "tokens": T, "tokens_per_rank": Tl,
+                       "layers": args.layers, "experts": E, "experts_per_rank": El, "top_k": K_TOP, "zipf_s": 1.2,
+                       "layer0_rows_per_rank": rows_to, "parallelism": f"ep{ws} (experts) x dp{ws} (tokens)",
+                       "dispatch": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (one rank)",
+                       "l2": "423 MB of experts per layer, larger than L2"},
+            "roofline": {"bound": "tensor", "kernel": "whole expert-parallel step per GPU (grouped tcgen05 GEMMs, "
+                                                      "router, all-to-all)",
+                         "achieved": achieved, "unit": "TFLOP/s", "peak": peak_fp4,
+                         "peak_source": "4 x measured sustained bf16 (dense FP4 is 4x the bf16 rate)",
+                         "frac": achieved / peak_fp4, "algorithmic_flops_per_step": flops, "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                    "api": "ExpertParallelMoE.forward per layer; host tokens copied in and out every step"},
+            "gpu_launches": args.steps * args.layers * 8,  # w64, router, permute, 2 x (quantize, GEMM), combine
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.tokens is None:
+        args.tokens = 8192 if args.workload == "ep" else 2048
+    if args.workload == "ep":
+        return run_ep_reference(args) if args.impl == "reference" else run_ep(args)
     if args.workload == "prefill":
         return run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
     if args.impl == "reference":

@@ -21,8 +21,11 @@ import torch.distributed as dist
 from . import capi
 
 
-def _a2a(out, inp, out_splits, in_splits, group):
-    dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+def _a2a(out, inp, out_splits, in_splits, group, world):
+    if world == 1:
+        out.copy_(inp)
+    else:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
 
 
 class ExpertParallelMoE:
@@ -49,7 +52,7 @@ class ExpertParallelMoE:
         order = torch.argsort(flat, stable=True)                       # (token, slot) grouped by destination
         send = torch.bincount(flat, minlength=G)
         recv = torch.empty_like(send)
-        _a2a(recv, send, None, None, self.group)
+        _a2a(recv, send, None, None, self.group, G)
         sc, rc = send.tolist(), recv.tolist()
         n_send, n_recv = sum(sc), sum(rc)
         h_send = h[order // k].contiguous()
@@ -57,14 +60,14 @@ class ExpertParallelMoE:
                                  w.reshape(-1)[order]], 1).contiguous()   # local ids are exact in w's type
         h_recv = torch.empty(n_recv, H, dtype=h.dtype, device=h.device)
         meta_recv = torch.empty(n_recv, 2, dtype=w.dtype, device=h.device)
-        _a2a(h_recv, h_send, rc, sc, self.group)
-        _a2a(meta_recv, meta_send, rc, sc, self.group)
+        _a2a(h_recv, h_send, rc, sc, self.group, G)
+        _a2a(meta_recv, meta_send, rc, sc, self.group, G)
         if n_recv:
             y_recv = self.compute(h_recv, meta_recv[:, 0].to(torch.int32).contiguous(), meta_recv[:, 1].contiguous())
         else:
             y_recv = torch.empty(0, H, dtype=h.dtype, device=h.device)
         y_back = torch.empty(n_send, H, dtype=h.dtype, device=h.device)
-        _a2a(y_back, y_recv.contiguous(), sc, rc, self.group)
+        _a2a(y_back, y_recv.contiguous(), sc, rc, self.group, G)
         y_ts = torch.empty(T * k, H, dtype=h.dtype, device=h.device)
         y_ts[order] = y_back
         y_ts = y_ts.view(T, k, H)

@@ -83,3 +83,32 @@ def digest(t):
         raw = v.view(torch.uint8) if v.dtype != torch.uint8 else v
         h.update(np.ascontiguousarray(raw.numpy()).tobytes())
     return h.hexdigest()
+
+
+def ep_router(layer, H=H, E=E, zipf_s=1.2, beta=1.0):
+    """The RMSNorm weight and router of layer `layer` of the expert-parallel benchmark model (CPU generator, seed
+    10_000 + layer, the moe_layer distributions), with the router bias skewed towards Zipf `zipf_s` over a seeded
+    expert order (seed 20_000 + layer). Identical on every rank. Returns (ln fp32, W bf16, b fp32)."""
+    g = torch.Generator().manual_seed(10_000 + layer)
+    ln = (1 + torch.randn(H, generator=g) * 0.02).to(torch.bfloat16).float()
+    W = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(E, generator=g) * 0.01).to(torch.bfloat16)
+    t = {"r.mlp.router.bias": b}
+    zipf_router_bias(t, prefix="r.", s=zipf_s, beta=beta, seed=20_000 + layer)
+    return ln, W, t["r.mlp.router.bias"].float()
+
+
+def ep_experts(layer, e0, e1, device, H=H, I=I, scale_lo=120, scale_hi=126):
+    """Experts e0..e1-1 of layer `layer` of the expert-parallel benchmark model, drawn on `device` expert by expert
+    from a generator seeded by (layer, expert), so every split of the experts over ranks holds the same weights.
+    Returns [gu_blocks, gu_scales, gu_bias fp32, dn_blocks, dn_scales, dn_bias fp32], experts stacked on dim 0."""
+    parts = [[] for _ in range(6)]
+    for e in range(e0, e1):
+        g = torch.Generator(device=device).manual_seed(1_000_003 * (layer + 1) + 7_919 * e)
+        for j, (rows, k) in enumerate(((2 * I, H), (H, I))):
+            parts[3 * j].append(torch.randint(0, 256, (rows, k // 32, 16), generator=g, device=device,
+                                              dtype=torch.uint8))
+            parts[3 * j + 1].append(torch.randint(scale_lo, scale_hi + 1, (rows, k // 32), generator=g,
+                                                  device=device, dtype=torch.uint8))
+            parts[3 * j + 2].append((torch.randn(rows, generator=g, device=device) * 0.01).to(torch.bfloat16).float())
+    return [torch.stack(p).contiguous() for p in parts]

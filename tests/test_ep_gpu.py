@@ -1,0 +1,141 @@
+"""Expert-parallel batched MoE (gptoss_b200/ep.py) on the GPU: routing by the library's batched router, dispatch and
+combine by all-to-all, the local experts by the batched tensor-core path with k = 1.
+
+Every row's expert computation and the slot-ordered combine are the operations of the single-GPU batched forward
+(gptoss_moe_layer_forward_batched, the batched form of gptoss_ref/model.py:100-104), so the expert-parallel result
+must be bit-identical to it: on one GPU (no collective), and over two GPUs with NCCL (skipped with fewer GPUs),
+including a step where one rank receives no rows.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from gptoss_b200 import capi, ep, synth
+
+pytestmark = pytest.mark.gpu
+PX = "model.layers.0."
+EX = PX + "mlp.experts."
+E8 = 8
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _model(skew_to_first_half):
+    t = synth.moe_layer(seed=3, E=E8)
+    if skew_to_first_half:                    # every token picks experts 0..3 only
+        b = t[PX + "mlp.router.bias"].float()
+        b[E8 // 2:] -= 100.0
+        t[PX + "mlp.router.bias"] = b.to(torch.bfloat16)
+    return t
+
+
+def _router(t, dev):
+    return (t[PX + "post_attention_layernorm.weight"].float().to(dev), t[PX + "mlp.router.weight"].to(dev),
+            t[PX + "mlp.router.bias"].float().to(dev))
+
+
+def _experts(t, dev, e0, e1):
+    names = ["gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+             "down_proj_scales", "down_proj_bias"]
+    out = []
+    for n in names:
+        v = t[EX + n][e0:e1]
+        out.append((v.float() if v.dtype == torch.bfloat16 else v).contiguous().to(dev))
+    return out
+
+
+def _layer(lib, ln, W, b, ex, E, k):
+    P = capi.ptr
+    L = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), E, k, 2880, 2880, 1.702, 7.0)
+    assert L, lib.gptoss_last_error().decode()
+    return L
+
+
+def _single_gpu_reference(t, x, dev):
+    """The single-GPU batched forward over all tokens (all experts on one device)."""
+    lib = capi.load()
+    ln, W, b = _router(t, dev)
+    ex = _experts(t, dev, 0, E8)
+    L = _layer(lib, ln, W, b, ex, E8, 4)
+    try:
+        xd = x.to(dev).contiguous()
+        y = xd.clone()
+        assert lib.gptoss_moe_layer_forward_batched(L, capi.ptr(xd), capi.ptr(y), x.shape[0], None) == 0, \
+            lib.gptoss_last_error().decode()
+        torch.cuda.synchronize()
+        return y.cpu()
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+
+
+def _ep_forward(lib, t, x_shard, rank, world, dev, group=None):
+    El = E8 // world
+    ln, W, b = _router(t, dev)
+    ex = _experts(t, dev, rank * El, (rank + 1) * El)
+    L = _layer(lib, ln, W, b, ex, El, min(4, El))
+    try:
+        m = ep.ExpertParallelMoE(ep.gpu_route(lib, ln, W, b, E8, 4), ep.gpu_compute(lib, L), rank, world, E8, 4,
+                                 2880, group)
+        y = m.forward(x_shard.to(dev).contiguous())
+        torch.cuda.synchronize()
+        return y.cpu()
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+
+
+@pytest.mark.parametrize("skew", [False, True])
+def test_ep_one_gpu_bit_identical_to_batched_forward(skew):
+    lib = capi.load()
+    t = _model(skew)
+    x = synth.tokens(40, seed=11)
+    want = _single_gpu_reference(t, x, "cuda")
+    got = _ep_forward(lib, t, x, 0, 1, "cuda")
+    assert torch.equal(got, want)
+
+
+def _worker(rank, world, port, skew, x, q):
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        lib = capi.load()
+        t = _model(skew)
+        y = _ep_forward(lib, t, x[rank::world], rank, world, dev)
+        q.put((rank, y.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("skew", [False, True])
+def test_ep_two_gpus_bit_identical_to_batched_forward(skew):
+    import torch.multiprocessing as mp
+    world = 2
+    x = synth.tokens(40, seed=12)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    os.environ.update(env)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, skew, x, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    out = torch.empty(40, 2880)
+    for r in range(world):
+        out[r::world] = torch.from_numpy(got[r])
+    want = _single_gpu_reference(_model(skew), x, "cuda:0")
+    assert torch.equal(out, want)

@@ -457,6 +457,7 @@ int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales
         a.alpha = alpha;
         a.limit = limit;
         a.workspace = ws;
+        a.trace = g_trace;
         gpt::launch_moe_batched(a, nullptr);
         sync_check("moe_batched");
         check_prefill_error(ws, L);
@@ -494,6 +495,7 @@ int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float*
         a.alpha = l->alpha;
         a.limit = l->limit;
         a.workspace = ws;
+        a.trace = g_trace;
         gpt::launch_moe_batched(a, s);
     });
 }
@@ -527,6 +529,7 @@ int gptoss_moe_layer_experts_batched(gptoss_moe_layer* l, const float* h, const 
         a.alpha = l->alpha;
         a.limit = l->limit;
         a.workspace = ws;
+        a.trace = g_trace;
         gpt::launch_moe_batched(a, s);
     });
 }

@@ -92,9 +92,9 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
 
 // Batched (prefill) MoE on tensor cores (prefill_tc.cu). Workspace layout for T tokens.
 struct PrefillLayout {
-    int max_tiles, SPS_gu, KT_gu, SPS_dn, KT_dn;
-    size_t off_h, off_ids, off_w, off_row_of, off_tok_of, off_slot_of, off_tiles, off_misc, off_img, off_sf, off_act,
-        off_w64, bytes;
+    int max_tiles, KB_gu, KB_dn;
+    size_t off_h, off_ids, off_w, off_pos_of, off_tok_of, off_slot_of, off_tiles, off_misc, off_img_gu, off_img_dn,
+        off_out, off_w64, bytes;
 };
 PrefillLayout prefill_layout(int T, int k, int E, int H, int I);
 
@@ -118,6 +118,7 @@ struct PrefillArgs {
     int T, k, E, H, I;
     float alpha, limit;
     void* workspace;              // prefill_layout(T, k, E, H, I).bytes
+    long long* trace = nullptr;   // optional: grouped GEMM wait totals per CTA, [160][160], slots 64 * mode + i
 };
 void launch_moe_batched(const PrefillArgs& a, cudaStream_t s);
 

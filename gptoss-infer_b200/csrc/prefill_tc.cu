@@ -6,16 +6,17 @@
 //   1. router_batched_kernel: RMSNorm (optional) and the router for 8 tokens per CTA; logits accumulated in fp64
 //      from exact products in a fixed order, top k with ties to the lower id, softmax over the k. Writes h (fp32).
 //   2. permute_kernel (one CTA): the (token, slot) pairs sorted by expert, then token, into "rows"; the rows of each
-//      expert cut into M tiles of 16 tokens.
-//   3. quantize_tiles_kernel: every token of an M tile split into NT = 8 e2m1 residual terms with E8M0 scales per 32
-//      values (exact to 2^-24 of each block's maximum) - A operand images laid out exactly as shared memory wants them
-//      (128 rows = 16 tokens x 8 terms, 128-byte swizzle) and scale chunks.
-//   4. grouped_gemm_kernel (persistent, one CTA per SM): tiles of (M tile, 256 weight rows); the weights are the MMA's B
-//      operand straight from the checkpoint layout (TMA boxes of 256 rows x 128 bytes), tcgen05.mma kind::mxf4 with
-//      M = 128, N = 256, K = 64, the accumulator in TMEM. Gate/up epilogue: the 8 term rows of each token added
-//      (fixed butterfly), bias, clamped SwiGLU -> activations (fp32). Down epilogue: bias, times the gate weight ->
-//      the (token, slot) result row.
-//   5. quantize_tiles_kernel again on the activations, then the down GEMM.
+//      expert cut into M tiles of 128; pos_of[(token, slot)] = 128 * tile + row in the tile.
+//   3. quantize_h_kernel: every token's h split once into NT = 8 e2m1 residual terms with E8M0 scales per 32 values
+//      (exact to 2^-24 of each block's maximum) and written into the A images of the k tiles that hold it. An A
+//      "piece" is one term of one 256-wide K block of one M tile: 128 rows x 128 bytes in the 128-byte-swizzled
+//      layout shared memory wants, followed by its two scale chunks - one bulk copy.
+//   4. grouped_gemm_kernel (persistent, one CTA per SM), gate/up: tiles of (M tile, 256 weight rows); the weights
+//      are the MMA's B operand straight from the checkpoint layout (TMA boxes of 256 rows x 128 bytes). Per K block
+//      the 8 terms are 8 MMAs of M = 128 tokens, N = 256, K = 64 x 4 (tcgen05.mma kind::mxf4) into the SAME TMEM
+//      accumulator, so the tensor core adds the terms and one B tile serves 8 x 128 token-terms. Epilogue: bias,
+//      clamped SwiGLU, and the activations quantized into the down projection's A pieces (terms, scales) in place.
+//   5. grouped_gemm_kernel, down: the same mainloop; epilogue w * (y + b2) -> the (token, slot) result row.
 //   6. combine_kernel: x_resid[t] += sum over slots in slot order (deterministic).
 #include <algorithm>
 #include <map>
@@ -33,17 +34,24 @@ namespace gpt {
 namespace pf {
 
 constexpr int NT = 8;                          // terms per token
-constexpr int kTok = 16;                       // tokens per M tile (16 x 8 = 128 A rows)
+constexpr int kTileM = 128;                    // tokens (rows of one expert) per M tile = the MMA's M
 constexpr int kRows = kDecodeTileRows;         // weight rows per N tile (the MMA's N)
-constexpr int kThreads = 192;                  // warp 0 producer, warp 1 MMA issuer, warps 2-5 epilogue
-constexpr int kAst = 128 * 128;                // A stage: 128 rows x 128 bytes of K (16 KB)
-constexpr int kBst = kRows * 128;              // B stage: 256 rows x 128 bytes (32 KB)
-constexpr int kSFAst = 2 * 512;                // A scales of a stage: 2 K chunks
-constexpr int kSFBst = 2 * 1024;               // B scales of a stage: 2 K chunks x 2 row halves
-constexpr int kSlot = kAst + kBst + kSFAst + kSFBst;
+constexpr int kEpiWarps = 8;                   // two per TMEM lane quadrant, 128 columns each
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 producer, warp 1 MMA issuer, warps 2.. epilogue
+constexpr int kImg = kTileM * 128;             // one term's A image for a 256-wide K block (16 KB)
+constexpr int kSFA = 4096;                     // its scales, replicated per lane quadrant (tcgen05.cp 128x256b source)
+constexpr int kTermA = kImg + kSFA;            // 20 KB
+constexpr int kPT = 2;                         // terms per A piece (one barrier wait per 8 MMAs)
+constexpr int kPieceA = kPT * kTermA;
+constexpr int kBImg = kRows * 128;             // B tile for a 256-wide K block (32 KB)
+constexpr int kPieceB = kBImg + 4 * 512;       // + its scale chunks (2 K chunks x 2 row halves)
+constexpr int kSeg = 2;                        // K blocks per accumulation segment
+constexpr int NSA = 3, NSB = kSeg + 1;         // ring slots: A pieces, B pieces
 constexpr uint32_t kTmemCols = 512;
-constexpr int kNSF = 8;                        // TMEM scale slots (8 A-scale + 16 B-scale columns each)
-constexpr uint32_t kColSFA = kRows, kColSFB = kRows + 8 * kNSF;
+constexpr uint32_t kColSFA = kRows;            // 8 columns per term, 16 per A slot
+constexpr uint32_t kColSFB = kRows + 16 * NSA; // 16 columns per B slot
+static_assert(kColSFB + 16 * NSB <= kTmemCols, "TMEM budget");
+static_assert(NT % kPT == 0, "terms per piece");
 constexpr int kRtTok = 8;                      // tokens per router CTA
 
 // ------------------------------------------------------------------------------------------------ router (batched)
@@ -152,14 +160,15 @@ __global__ void __launch_bounds__(512) router_batched_kernel(const double* __res
 // ------------------------------------------------------------------------------------------------ permute
 // One CTA of 1024 threads. Thread i owns tokens [i * per, (i + 1) * per); its per-expert counts are scanned over the
 // threads (expert e by warp e), giving every (token, slot) its row: experts in id order, tokens ascending within an
-// expert. Rows of expert e are cut into M tiles of kTok rows: tiles[m] = (expert, first row, rows).
+// expert. Rows of expert e are cut into M tiles of kTileM rows: tiles[m] = (expert, first row, rows), and
+// pos_of[t * k + s] = kTileM * (tile) + (row within the tile), or -1 for an invalid id.
 __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ ids, int T, int k, int E,
-                                                       int* __restrict__ row_of, int* __restrict__ tok_of,
+                                                       int* __restrict__ pos_of, int* __restrict__ tok_of,
                                                        int* __restrict__ slot_of, int4* __restrict__ tiles,
                                                        int* __restrict__ n_tiles, int* __restrict__ err) {
     extern __shared__ unsigned short cnt_raw[];
     unsigned short (*cnt)[1024] = reinterpret_cast<unsigned short (*)[1024]>(cnt_raw);   // [32][1024]
-    __shared__ int total[32], base[33];
+    __shared__ int total[32], base[33], tile0[32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int per = (T + 1023) / 1024, tb = min(T, tid * per), te = min(T, tb + per);
     for (int e = 0; e < 32; ++e) cnt[e][tid] = 0;
@@ -196,7 +205,8 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ i
         int acc = 0, m = 0;
         for (int e = 0; e < 32; ++e) {
             base[e] = acc;
-            for (int r = 0; r < total[e]; r += kTok) tiles[m++] = make_int4(e, acc + r, min(kTok, total[e] - r), 0);
+            tile0[e] = m;
+            for (int r = 0; r < total[e]; r += kTileM) tiles[m++] = make_int4(e, acc + r, min(kTileM, total[e] - r), 0);
             acc += total[e];
         }
         base[32] = acc;
@@ -206,71 +216,145 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ i
     for (int t = tb; t < te; ++t)
         for (int s = 0; s < k; ++s) {
             const int e = ids[size_t(t) * k + s];
-            if (e < 0 || e >= E) continue;
-            const int row = base[e] + cnt[e][tid];
-            cnt[e][tid] = (unsigned short)(cnt[e][tid] + 1);
-            row_of[size_t(t) * k + s] = row;
+            if (e < 0 || e >= E) {
+                pos_of[size_t(t) * k + s] = -1;
+                continue;
+            }
+            const int r = cnt[e][tid];
+            const int row = base[e] + r;
+            cnt[e][tid] = (unsigned short)(r + 1);
+            pos_of[size_t(t) * k + s] = (tile0[e] + r / kTileM) * kTileM + r % kTileM;
             tok_of[row] = t;
             slot_of[row] = s;
         }
 }
 
 // ------------------------------------------------------------------------------------------------ A images
-// Work item (M tile m, stage st, token slot j): one warp quantizes the token's 8 blocks of the stage (4 lanes per
-// block) into rows 8j .. 8j + 7 of the stage image and its scale bytes; slots past the tile's rows get zero terms.
-// src row of slot j: tok_of[first row + j] (by_token) or first row + j.
-__global__ void __launch_bounds__(256) quantize_tiles_kernel(const float* __restrict__ src, int by_token,
-                                                             const int* __restrict__ tok_of,
-                                                             const int4* __restrict__ tiles,
-                                                             const int* __restrict__ n_tiles, int K, int SPS, int KT,
-                                                             uint8_t* __restrict__ img, uint8_t* __restrict__ sf) {
+// A images: per (M tile, K block) the NT terms in DESCENDING order (term NT - 1 first), each kTermA bytes: the
+// 128 x 128-byte image in the 128-byte swizzle, then its scales. Pieces of kPT consecutive terms are one bulk copy.
+__device__ __forceinline__ uint8_t* a_term(uint8_t* img, int m, int KB, int kb, int t) {
+    return img + ((size_t(m) * KB + kb) * NT + (NT - 1 - t)) * kTermA;
+}
+
+// Term t's 16-byte unit of block g (0..7 within the K block) in row r (128-byte swizzle).
+__device__ __forceinline__ int a_unit_off(int r, int g) { return r * 128 + ((g ^ (r & 7)) << 4); }
+
+// The scales of a term as the source of one tcgen05.cp 128x256b (128 rows x 32 bytes in 8-row x 16-byte core
+// matrices: row L byte b at (L / 8) 256 + (b / 16) 128 + (L % 8) 16 + b % 16): row L holds what the 32x128b.warpx4
+// copy of the term's two 512-byte chunks would put in TMEM lane L, i.e. chunk c's 16-byte row L % 32 at bytes
+// 16 c .. 16 c + 15, where byte 4 j + kk of chunk row i is the scale of token row i + 32 j, block 4 c + kk. Each
+// scale therefore appears in the 4 rows L = r % 32 + 32 q. Offset of the copy for quadrant q of row r, block g:
+__device__ __forceinline__ int a_sf_off(int r, int g, int q) {
+    const int L = (r & 31) + 32 * q, b = (g >> 2) * 16 + (r >> 5) * 4 + (g & 3);
+    return kImg + (L >> 3) * 256 + (b >> 4) * 128 + (L & 7) * 16 + (b & 15);
+}
+
+__device__ __forceinline__ uint64_t desc_sfa_128x256b(uint32_t saddr) { return tc::smem_desc(saddr, 128, 256, 0); }
+
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t tmem_col, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(tmem_col), "l"(sdesc) : "memory");
+}
+
+// One warp quantizes 8 blocks (K block kb, 4 lanes per 32-value block) of the source row `src` once and writes the
+// terms into the A terms of `nd` destination rows (pos = 128 * tile + row in the tile; negative = none).
+__device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ src, int K, int kb, const int (&pos)[8],
+                                                    int nd, int KB, uint8_t* __restrict__ img) {
     const int lane = threadIdx.x & 31, sub = lane & 3, gl = lane >> 2;
-    const long long items = (long long)(*n_tiles) * SPS * kTok;
+    const int g = kb * 8 + gl;
+    const bool valid = g * 32 < K;
+    float v8[8];
+    if (valid) {
+        const float* sr = src + g * 32 + sub * 8;
+        const float4 a = *reinterpret_cast<const float4*>(sr);
+        const float4 c = *reinterpret_cast<const float4*>(sr + 4);
+        v8[0] = a.x; v8[1] = a.y; v8[2] = a.z; v8[3] = a.w; v8[4] = c.x; v8[5] = c.y; v8[6] = c.z; v8[7] = c.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v8[i] = 0.f;
+    }
+    quantize_block_terms_lanes4<NT>(v8, [&](int term, uint32_t word, uint32_t scale) {
+        if (!valid) return;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            if (s >= nd || pos[s] < 0) continue;
+            const int m = pos[s] / kTileM, r = pos[s] % kTileM;
+            uint8_t* pc = a_term(img, m, KB, kb, term);
+            *reinterpret_cast<uint32_t*>(pc + a_unit_off(r, gl) + sub * 4) = word;
+            pc[a_sf_off(r, gl, sub)] = uint8_t(scale);          // lane sub writes quadrant sub's copy
+        }
+    });
+}
+
+// Gate/up A terms from h: work item (token t, K block kb) per warp; the token's terms are computed once and written
+// to the k tiles that hold it (pos_of).
+__global__ void __launch_bounds__(256) quantize_h_kernel(const float* __restrict__ h, int T, int H, int k,
+                                                         const int* __restrict__ pos_of, int KB,
+                                                         uint8_t* __restrict__ img) {
+    const long long items = (long long)T * KB;
     const long long warps = (long long)gridDim.x * (blockDim.x / 32);
     for (long long w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < items; w += warps) {
-        const int j = int(w % kTok);
-        const long long ms = w / kTok;
-        const int st = int(ms % SPS), m = int(ms / SPS);
-        const int4 tl = tiles[m];
-        const int g = st * 8 + gl;                       // block (32 values) along K
-        float v8[8];
-        if (j < tl.z && g * 32 < K) {
-            const int row = tl.y + j;
-            const float* sr = src + size_t(by_token ? tok_of[row] : row) * K + g * 32 + sub * 8;
-            const float4 a = *reinterpret_cast<const float4*>(sr);
-            const float4 c = *reinterpret_cast<const float4*>(sr + 4);
-            v8[0] = a.x; v8[1] = a.y; v8[2] = a.z; v8[3] = a.w; v8[4] = c.x; v8[5] = c.y; v8[6] = c.z; v8[7] = c.w;
-        } else {
+        const int t = int(w / KB), kb = int(w % KB);
+        int pos[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v8[i] = 0.f;
-        }
-        uint8_t* stage_img = img + (size_t(m) * SPS + st) * kAst + j * (NT * 128);
-        const int kt = st * 2 + (gl >> 2);
-        uint8_t* chunk = sf + (size_t(m) * KT + min(kt, KT - 1)) * 512 + 128 * (j & 3) + 4 * (j >> 2);
-        quantize_block_terms_fixed_n<NT>(v8, stage_img, gl, chunk, gl & 3, sub, kt < KT);
+        for (int s = 0; s < 8; ++s) pos[s] = s < k ? pos_of[size_t(t) * k + s] : -1;
+        quantize_row_kblock(h + size_t(t) * H, H, kb, pos, k, KB, img);
+    }
+}
+
+// Down A terms from the activations act [rows][I] (rows in tile order): work item (tile m, row j, K block kb).
+__global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ act, int I,
+                                                           const int4* __restrict__ tiles,
+                                                           const int* __restrict__ n_tiles, int KB,
+                                                           uint8_t* __restrict__ img) {
+    const long long items = (long long)(*n_tiles) * kTileM * KB;
+    const long long warps = (long long)gridDim.x * (blockDim.x / 32);
+    for (long long w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < items; w += warps) {
+        const int kb = int(w % KB);
+        const int jm = int(w / KB), j = jm % kTileM, m = jm / kTileM;
+        const int4 tl = tiles[m];
+        if (j >= tl.z) continue;
+        int pos[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) pos[s] = s == 0 ? m * kTileM + j : -1;
+        quantize_row_kblock(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, img);
     }
 }
 
 // ------------------------------------------------------------------------------------------------ grouped GEMM
 struct GemmJob {
-    int mode;                                  // 0: gate/up (SwiGLU -> act), 1: down (gate weight -> out_ts)
+    int mode;                                  // 0: gate/up (SwiGLU -> down A pieces), 1: down (w (y + b) -> out_ts)
     int K, N;                                  // reduction length, weight rows of one expert
-    int UK, SPS, KT, RT;                       // K / 64, stages of 256, chunks of 128, 256-row tiles of N
-    const uint8_t* a_img;                      // [tiles][SPS][kAst]
-    const uint8_t* a_sf;                       // [tiles][KT][512]
+    int UK, KB, KT, RT;                        // K / 64, 256-wide K blocks, 128-wide K chunks, 256-row N tiles
+    const uint8_t* a_img;                      // [tiles][KB][NT] terms, descending
     const uint8_t* b_sf;                       // [E][RT][KT][2][512]
     const int4* tiles;
     const int* n_tiles;
     const float* bias;                         // [E][N]
     float alpha, limit;
-    float* act;                                // gate/up: [rows][N / 2]
+    float* act;                                // gate/up: activations [rows][I]
+    int I;
     const int* tok_of;                         // down
     const int* slot_of;
     const float* wts;                          // [T][k]
     int k;
     float* out_ts;                             // down: [T][k][N]
     int* err;
+    long long* trace;                          // optional: per CTA (< 160) 160 stamps, slots 64 mode + i
 };
+
+// Named barrier 1 over the epilogue warps (warps 2 ..), so that only one of their threads polls an mbarrier.
+__device__ __forceinline__ void epi_bar_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+}
+
+// Timed wait: adds the cycles spent in the wait to *acc when tracing.
+__device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity, int* err, int where, long long* acc) {
+    if (!acc) return tc::mbar_wait(bar, parity, err, where);
+    const long long t0 = clock64();
+    const bool ok = tc::mbar_wait(bar, parity, err, where);
+    *acc += clock64() - t0;
+    return ok;
+}
 
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -284,25 +368,42 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 
 // Persistent: CTA c takes output tiles c, c + grid, ... of (M tile m, N tile nt) = (tau / RT, tau % RT), so the CTAs
-// working at one time share an expert's weights (and each M tile's A image) through L2. Per stage one 51 KB ring slot:
-// A (bulk copy), B (TMA box), A and B scales (bulk copies), all completing on the slot's barrier.
+// working at one time share an expert's weights (and each M tile's A pieces) through L2. Two rings: B pieces (TMA box +
+// scale chunks, one per K block) and A pieces (one bulk copy per (K block, term)); the producer and the MMA issuer are
+// single threads.
+//
+// Accumulation order. The tensor core adds each MMA's result into D with an error that scales with |D| (about one
+// unit in the last place of fp32 per MMA), so the number of MMAs added into a large accumulator decides the
+// precision. The K blocks of a tile are processed in segments of kSeg: within a segment the terms go from the
+// smallest (NT - 1) to the largest (0), each over the segment's K blocks (whose B pieces stay resident), so the small
+// terms are added while D is still small; after each segment the epilogue warps add D into fp32 registers and D
+// restarts from zero. Term 0, the only term of full magnitude, then meets at most 4 kSeg MMAs per accumulator.
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_b,
-                                                                   const __grid_constant__ GemmJob j, int NS) {
+                                                                   const __grid_constant__ GemmJob j) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * kSlot);
-    uint64_t* empty = full + NS;
-    uint64_t* accF = empty + NS;
+    uint8_t* ringA = smem;
+    uint8_t* ringB = smem + NSA * kPieceA;
+    uint64_t* fullA = reinterpret_cast<uint64_t*>(ringB + NSB * kPieceB);
+    uint64_t* emptyA = fullA + NSA;
+    uint64_t* fullB = emptyA + NSA;
+    uint64_t* emptyB = fullB + NSB;
+    uint64_t* accF = emptyB + NSB;
     uint64_t* accE = accF + 1;
     uint32_t* holder = reinterpret_cast<uint32_t*>(accE + 1);
+    int* epi_flag = reinterpret_cast<int*>(holder + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < NS; ++i) {
-            tc::mbar_init(&full[i], 1);
-            tc::mbar_init(&empty[i], 1);
+        for (int i = 0; i < NSA; ++i) {
+            tc::mbar_init(&fullA[i], 1);
+            tc::mbar_init(&emptyA[i], 1);
+        }
+        for (int i = 0; i < NSB; ++i) {
+            tc::mbar_init(&fullB[i], 1);
+            tc::mbar_init(&emptyB[i], 1);
         }
         tc::mbar_init(accF, 1);
-        tc::mbar_init(accE, 128);
+        tc::mbar_init(accE, kEpiWarps);
         tc::fence_barrier_init();
     }
     if (warp == 1) {
@@ -317,131 +418,207 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     const int c = blockIdx.x, nc = gridDim.x;
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- producer
-        if (tc::elect_one()) {
+        // ---------------------------------------------------------------- producer (one thread)
+        if (lane == 0) {
             tc::prefetch_tmap(&tm_b);
             bool ok = true;
-            int it = 0;
+            int ia = 0, ib = 0;
+            long long wA = 0, wB = 0;
+            long long* twA = j.trace && c < 160 ? &wA : nullptr;
+            long long* twB = j.trace && c < 160 ? &wB : nullptr;
             for (int tau = c; tau < n_tiles && ok; tau += nc) {
                 const int m = tau / j.RT, nt = tau % j.RT;
                 const int e = j.tiles[m].x;
-                for (int st = 0; st < j.SPS && ok; ++st, ++it) {
-                    const int slot = it % NS;
-                    if (it >= NS) ok = tc::mbar_wait(&empty[slot], uint32_t((it - NS) / NS) & 1u, j.err, 31);
-                    if (!ok) break;
-                    const int ku0 = 4 * st, nu = min(4, j.UK - ku0);
-                    const int nkt = (ku0 + nu - 1) / 2 - ku0 / 2 + 1;
-                    uint8_t* d = smem + slot * kSlot;
-                    tc::mbar_arrive_expect_tx(&full[slot], uint32_t(kAst + kBst + nkt * 512 + nkt * 1024));
-                    tc::bulk_g2s(d, j.a_img + (size_t(m) * j.SPS + st) * kAst, kAst, &full[slot]);
-                    tc::tma_load_3d(d + kAst, &tm_b, st * 128, nt * kRows, e, &full[slot]);
-                    tc::bulk_g2s(d + kAst + kBst, j.a_sf + (size_t(m) * j.KT + 2 * st) * 512, nkt * 512, &full[slot]);
-                    tc::bulk_g2s(d + kAst + kBst + kSFAst, j.b_sf + ((size_t(e) * j.RT + nt) * j.KT + 2 * st) * 1024,
-                                 nkt * 1024, &full[slot]);
+                for (int s0 = 0; s0 < j.KB && ok; s0 += kSeg) {
+                    const int s1 = min(j.KB, s0 + kSeg);
+                    for (int pc = 0; pc < NT / kPT && ok; ++pc)
+                        for (int kb = s0; kb < s1; ++kb) {
+                            if (pc == 0) {
+                                const int nkq = min(2, j.KT - 2 * kb);
+                                const int sb = ib % NSB;
+                                if (ib >= NSB) ok = twait(&emptyB[sb], uint32_t(ib / NSB - 1) & 1u, j.err, 31, twB);
+                                if (!ok) break;
+                                uint8_t* pb = ringB + sb * kPieceB;
+                                tc::mbar_arrive_expect_tx(&fullB[sb], uint32_t(kBImg + nkq * 1024));
+                                tc::tma_load_3d(pb, &tm_b, kb * 128, nt * kRows, e, &fullB[sb]);
+                                tc::bulk_g2s(pb + kBImg, j.b_sf + ((size_t(e) * j.RT + nt) * j.KT + 2 * kb) * 1024,
+                                             nkq * 1024, &fullB[sb]);
+                                ++ib;
+                            }
+                            const int sa = ia % NSA;
+                            if (ia >= NSA) ok = twait(&emptyA[sa], uint32_t(ia / NSA - 1) & 1u, j.err, 32, twA);
+                            if (!ok) break;
+                            tc::mbar_arrive_expect_tx(&fullA[sa], uint32_t(kPieceA));
+                            tc::bulk_g2s(ringA + sa * kPieceA,
+                                         a_term(const_cast<uint8_t*>(j.a_img), m, j.KB, kb, NT - 1 - kPT * pc),
+                                         kPieceA, &fullA[sa]);
+                            ++ia;
+                        }
                 }
+            }
+            if (twA) {
+                long long* tr = j.trace + c * 160 + 64 * j.mode;
+                tr[6] = wA;
+                tr[7] = wB;
             }
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------------------------------------------------------- MMA issuer (one lane)
-        if (tc::elect_one()) {
+        // ---------------------------------------------------------------- MMA issuer (one thread)
+        if (lane == 0) {
             bool ok = true;
-            int it = 0, nt_done = 0;
-            for (int tau = c; tau < n_tiles && ok; tau += nc, ++nt_done) {
-                for (int st = 0; st < j.SPS && ok; ++st, ++it) {
-                    const int slot = it % NS, f = it % kNSF;
-                    const int ku0 = 4 * st, nu = min(4, j.UK - ku0);
-                    const int nkt = (ku0 + nu - 1) / 2 - ku0 / 2 + 1;
-                    if (st == 0 && nt_done > 0) ok = tc::mbar_wait(accE, uint32_t(nt_done - 1) & 1u, j.err, 32);
-                    ok = ok && tc::mbar_wait(&full[slot], uint32_t(it / NS) & 1u, j.err, 33);
-                    if (!ok) break;
-                    tc::tc_fence_after();
-                    const uint8_t* d = smem + slot * kSlot;
-                    for (int q = 0; q < nkt; ++q) {
-                        tc::tmem_cp_sf(tmem + kColSFA + 8 * f + 4 * q,
-                                       tc::desc_sf_chunk(tc::smem_u32(d + kAst + kBst + q * 512)));
-                        for (int h = 0; h < 2; ++h)
-                            tc::tmem_cp_sf(tmem + kColSFB + 16 * f + 8 * q + 4 * h,
-                                           tc::desc_sf_chunk(tc::smem_u32(d + kAst + kBst + kSFAst + (2 * q + h) * 512)));
-                    }
-                    for (int u = 0; u < nu; ++u) {
-                        const int ku = ku0 + u, q = ku / 2 - ku0 / 2;
-                        const uint32_t sf_id = 2u * (ku & 1);
-                        tc::mma_mxf4(tmem, tc::desc_sw128(tc::smem_u32(d + u * 32)),
-                                     tc::desc_sw128(tc::smem_u32(d + kAst + u * 32)),
-                                     tc::idesc_mxf4(128, kRows, sf_id, sf_id),
-                                     (tmem + kColSFA + 8 * f + 4 * q) | (sf_id << 30),
-                                     (tmem + kColSFB + 16 * f + 8 * q) | (sf_id << 30), !(st == 0 && u == 0));
-                    }
-                    tc::mma_commit(&empty[slot]);
-                    if (st == j.SPS - 1) tc::mma_commit(accF);
+            int ia = 0, ib = 0, seg = 0;
+            long long wA = 0, wB = 0, wE = 0, t_start = clock64();
+            const bool trc = j.trace && c < 160;
+            const uint32_t idesc0 = tc::idesc_mxf4(128, kRows, 0, 0), idesc2 = tc::idesc_mxf4(128, kRows, 2, 2);
+            for (int tau = c; tau < n_tiles && ok; tau += nc) {
+                for (int s0 = 0; s0 < j.KB && ok; s0 += kSeg, ++seg) {
+                    const int s1 = min(j.KB, s0 + kSeg);
+                    if (seg > 0) ok = twait(accE, uint32_t(seg - 1) & 1u, j.err, 33, trc ? &wE : nullptr);
+                    for (int pc = 0; pc < NT / kPT && ok; ++pc)
+                        for (int kb = s0; kb < s1; ++kb) {
+                            const int nu = min(4, j.UK - 4 * kb), nkq = (nu + 1) / 2;
+                            const int sb = (ib + kb - s0) % NSB;
+                            const uint8_t* pb = ringB + sb * kPieceB;
+                            const uint32_t csfb = tmem + kColSFB + 16 * sb;
+                            if (pc == 0) {
+                                ok = twait(&fullB[sb], uint32_t((ib + kb - s0) / NSB) & 1u, j.err, 34, trc ? &wB : nullptr);
+                                if (!ok) break;
+                                tc::tc_fence_after();
+                                for (int q = 0; q < nkq; ++q)
+                                    for (int hh = 0; hh < 2; ++hh)
+                                        tc::tmem_cp_sf(csfb + 8 * q + 4 * hh,
+                                                       tc::desc_sf_chunk(tc::smem_u32(pb + kBImg + (2 * q + hh) * 512)));
+                            }
+                            const int sa = ia % NSA;
+                            ok = twait(&fullA[sa], uint32_t(ia / NSA) & 1u, j.err, 35, trc ? &wA : nullptr);
+                            if (!ok) break;
+                            tc::tc_fence_after();
+#pragma unroll
+                            for (int w = 0; w < kPT; ++w) {
+                                const uint8_t* pa = ringA + sa * kPieceA + w * kTermA;
+                                const uint32_t csfa = tmem + kColSFA + 16 * sa + 8 * w;
+                                tmem_cp_128x256b(csfa, desc_sfa_128x256b(tc::smem_u32(pa + kImg)));
+                                for (int u = 0; u < nu; ++u) {
+                                    const uint32_t sfid = 2u * (u & 1), q = u >> 1;
+                                    tc::mma_mxf4(tmem, tc::desc_sw128(tc::smem_u32(pa + u * 32)),
+                                                 tc::desc_sw128(tc::smem_u32(pb + u * 32)), (u & 1) ? idesc2 : idesc0,
+                                                 (csfa + 4 * q) | (sfid << 30), (csfb + 8 * q) | (sfid << 30),
+                                                 !(pc == 0 && w == 0 && kb == s0 && u == 0));
+                                }
+                            }
+                            tc::mma_commit(&emptyA[sa]);
+                            ++ia;
+                            if (pc == NT / kPT - 1) tc::mma_commit(&emptyB[sb]);
+                        }
+                    ib += s1 - s0;
+                    if (ok) tc::mma_commit(accF);
                 }
+            }
+            if (trc) {
+                long long* tr = j.trace + c * 160 + 64 * j.mode;
+                tr[0] = t_start;
+                tr[1] = wA;
+                tr[2] = wB;
+                tr[3] = wE;
+                tr[4] = seg;
+                tr[5] = clock64();
             }
         }
         __syncwarp();
     } else {
-        // ---------------------------------------------------------------- epilogue warps 2..5
-        // Warp w reads TMEM lanes 32 (w % 4) .. + 31 = token slots 4 (w % 4) .. + 3, 8 term rows each. Per 32
-        // columns: the 8 terms of each token added by a fixed butterfly over lanes, lane i of a token group keeping
-        // columns 4i .. 4i + 3.
-        const int quad = warp & 3, jslot = quad * 4 + (lane >> 3), i8 = lane & 7;
-        int nt_done = 0;
-        for (int tau = c; tau < n_tiles; tau += nc, ++nt_done) {
+        // ---------------------------------------------------------------- epilogue warps
+        // Thread = one token row of the tile and 128 of the 256 columns: warp w reads TMEM lanes 32 (w % 4) .. + 31,
+        // columns 128 hc .. + 127 (hc = 0 for warps 2..5, 1 for warps 6..9). Per segment: D added into sums.
+        const int quad = warp & 3, hc = (warp - 2) >> 2, row_t = quad * 32 + lane;
+        const uint32_t tl_base = tmem + (uint32_t(quad * 32) << 16) + 128 * hc;
+        int seg = 0;
+        const bool trc = j.trace && c < 160 && warp == 2 && lane == 0;
+        long long wF = 0, tEpi = 0;
+        for (int tau = c; tau < n_tiles; tau += nc) {
             const int m = tau / j.RT, nt = tau % j.RT;
             const int4 tl = j.tiles[m];
-            bool ok = tc::mbar_wait(accF, uint32_t(nt_done) & 1u, j.err, 34);
-            ok = __all_sync(kFull, ok);
-            float vals[8][4];
-            if (ok) {
-                tc::tc_fence_after();
+            float sums[128];
 #pragma unroll
-                for (int r = 0; r < kRows / 32; ++r) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem + (uint32_t(quad * 32) << 16) + 32 * r, v);
-                    tc::tmem_ld_wait();
+            for (int i = 0; i < 128; ++i) sums[i] = 0.f;
+            bool ok = true;
+            for (int s0 = 0; s0 < j.KB; s0 += kSeg, ++seg) {
+                // One thread polls the accumulator barrier; the other epilogue warps sleep in a named barrier.
+                if (warp == 2 && lane == 0)
+                    epi_flag[seg & 1] = (ok && twait(accF, uint32_t(seg) & 1u, j.err, 36, trc ? &wF : nullptr)) ? 1 : 0;
+                epi_bar_sync();
+                const bool got = reinterpret_cast<volatile int*>(epi_flag)[seg & 1] != 0;   // two flags: no reuse race
+                if (got) {
+                    tc::tc_fence_after();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        float s = __uint_as_float(v[i]);
-                        s += __shfl_xor_sync(kFull, s, 1);
-                        s += __shfl_xor_sync(kFull, s, 2);
-                        s += __shfl_xor_sync(kFull, s, 4);
-                        if ((i >> 2) == i8) vals[r][i & 3] = s;
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t v[32];
+                        tmem_ld_32x32b_x32(tl_base + 32 * cc, v);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) sums[32 * cc + i] += __uint_as_float(v[i]);
                     }
                 }
+                ok = got;
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(accE);
             }
-            tc::tc_fence_before();
-            tc::mbar_arrive(accE);
-            if (!ok || jslot >= tl.z) continue;
-            const int row = tl.y + jslot, e = tl.x;
-            if (j.mode == 0) {
-                const float* bb = j.bias + size_t(e) * j.N;
-                float* ar = j.act + size_t(row) * (j.N / 2);
+            if (!ok) continue;
+            const long long te0 = clock64();
+            const int e = tl.x;
+            const float* bb = j.bias + size_t(e) * j.N;
+            const bool live = row_t < tl.z;
+            const int n0 = nt * kRows + 128 * hc;
+            if (j.mode == 0 && live) {
+                // columns n0 .. n0 + 127 = 64 (gate, up) pairs = activations 64 (2 nt + hc) .. + 63
+                const int a0 = nt * (kRows / 2) + 64 * hc;
+                float* arow = j.act + size_t(tl.y + row_t) * j.I + a0;
+                if (a0 < j.I) {
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const int n0 = nt * kRows + 32 * r + 4 * i8;
+                    for (int i = 0; i < 64; i += 4) {
+                        float o[4];
 #pragma unroll
-                    for (int pr = 0; pr < 2; ++pr) {
-                        const int n = n0 + 2 * pr;
-                        if (n + 1 < j.N) {
-                            const float gv = fminf(vals[r][2 * pr] + bb[n], j.limit);
-                            const float lv = fminf(fmaxf(vals[r][2 * pr + 1] + bb[n + 1], -j.limit), j.limit);
-                            ar[n / 2] = gv / (1.f + expf(-j.alpha * gv)) * (lv + 1.f);
+                        for (int d = 0; d < 4; ++d) {
+                            const int n = min(n0 + 2 * (i + d), j.N - 2);     // I % 64 == 0: never clamped
+                            const float gv = fminf(sums[2 * (i + d)] + __ldg(bb + (n)), j.limit);
+                            const float lv = fminf(fmaxf(sums[2 * (i + d) + 1] + __ldg(bb + (n + 1)), -j.limit), j.limit);
+                            o[d] = __fdividef(gv, 1.f + __expf(-j.alpha * gv)) * (lv + 1.f);
                         }
+                        if (a0 + i + 3 < j.I) *reinterpret_cast<float4*>(arow + i) = make_float4(o[0], o[1], o[2], o[3]);
+                        else
+                            for (int d = 0; d < 4; ++d)
+                                if (a0 + i + d < j.I) arow[i + d] = o[d];
                     }
                 }
-            } else {
+            } else if (j.mode == 1 && live && n0 < j.N) {
+                const int row = tl.y + row_t;
                 const int t = j.tok_of[row], s = j.slot_of[row];
                 const float w = j.wts[size_t(t) * j.k + s];
-                const float* bb = j.bias + size_t(e) * j.N;
                 float* orow = j.out_ts + (size_t(t) * j.k + s) * j.N;
+                if (n0 + 128 <= j.N) {
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const int n0 = nt * kRows + 32 * r + 4 * i8;
+                    for (int i = 0; i < 128; i += 4) {
+                        float4 o;
+                        o.x = w * (sums[i] + __ldg(bb + (n0 + i)));
+                        o.y = w * (sums[i + 1] + __ldg(bb + (n0 + i + 1)));
+                        o.z = w * (sums[i + 2] + __ldg(bb + (n0 + i + 2)));
+                        o.w = w * (sums[i + 3] + __ldg(bb + (n0 + i + 3)));
+                        *reinterpret_cast<float4*>(orow + n0 + i) = o;
+                    }
+                } else {
 #pragma unroll
-                    for (int d = 0; d < 4; ++d)
-                        if (n0 + d < j.N) orow[n0 + d] = w * (vals[r][d] + bb[n0 + d]);
+                    for (int i = 0; i < 128; ++i)
+                        if (n0 + i < j.N) orow[n0 + i] = w * (sums[i] + __ldg(bb + (n0 + i)));
                 }
             }
+            if (trc) tEpi += clock64() - te0;
+        }
+        if (trc) {
+            long long* tr = j.trace + c * 160 + 64 * j.mode;
+            tr[8] = wF;
+            tr[9] = tEpi;
+            tr[10] = clock64();
         }
     }
     tc::tc_fence_before();
@@ -460,7 +637,8 @@ __global__ void combine_kernel(const float* __restrict__ out_ts, int T, int k, i
     }
 }
 
-int gemm_smem_bytes(int NS) { return 1024 + NS * kSlot + (2 * NS + 2) * 8 + 16; }
+constexpr int kGemmSmem = 1024 + NSA * kPieceA + NSB * kPieceB + (2 * NSA + 2 * NSB + 2) * 8 + 32;
+static_assert(kGemmSmem <= 227 * 1024, "shared memory budget");
 
 }  // namespace pf
 
@@ -469,24 +647,21 @@ PrefillLayout prefill_layout(int T, int k, int E, int H, int I) {
     PrefillLayout L{};
     auto al = [](size_t b) { return (b + 1023) & ~size_t(1023); };
     const long long rows = (long long)T * k;
-    L.max_tiles = int((rows + pf::kTok - 1) / pf::kTok) + E;
-    L.SPS_gu = ((H + 63) / 64 + 3) / 4;
-    L.KT_gu = (H + 127) / 128;
-    L.SPS_dn = ((I + 63) / 64 + 3) / 4;
-    L.KT_dn = (I + 127) / 128;
+    L.max_tiles = int((rows + pf::kTileM - 1) / pf::kTileM) + E;
+    L.KB_gu = (H + 255) / 256;
+    L.KB_dn = (I + 255) / 256;
     size_t o = 0;
     L.off_h = o; o += al(size_t(T) * H * 4);
     L.off_ids = o; o += al(size_t(rows) * 4);
     L.off_w = o; o += al(size_t(rows) * 4);
-    L.off_row_of = o; o += al(size_t(rows) * 4);
+    L.off_pos_of = o; o += al(size_t(rows) * 4);
     L.off_tok_of = o; o += al(size_t(rows) * 4);
     L.off_slot_of = o; o += al(size_t(rows) * 4);
     L.off_tiles = o; o += al(size_t(L.max_tiles) * 16);
     L.off_misc = o; o += 1024;                              // [0] tile count, [64] error word
-    const size_t img = size_t(L.max_tiles) * std::max(L.SPS_gu, L.SPS_dn) * pf::kAst;
-    L.off_img = o; o += al(img);
-    L.off_sf = o; o += al(size_t(L.max_tiles) * std::max(L.KT_gu, L.KT_dn) * 512);
-    L.off_act = o; o += al(size_t(rows) * std::max(H, I) * 4);   // activations, then the (token, slot) results
+    L.off_img_gu = o; o += al(size_t(L.max_tiles) * L.KB_gu * pf::NT * pf::kTermA);
+    L.off_img_dn = o; o += al(size_t(L.max_tiles) * L.KB_dn * pf::NT * pf::kTermA);
+    L.off_out = o; o += al(size_t(rows) * std::max(H, I) * 4);   // activations, then the (token, slot) results
     L.off_w64 = o; o += al(size_t(H) * 32 * 8);
     L.bytes = o;
     return L;
@@ -526,82 +701,71 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
     require(a.T >= 1, "moe_batched: T must be positive");
     require(a.k >= 1 && a.k <= 8 && a.k <= a.E && a.E <= 32, "moe_batched: needs 1 <= k <= 8 and k <= E <= 32");
     require(a.H % 64 == 0 && a.I % 64 == 0, "moe_batched: H and I must be multiples of 64");
+    require(a.T <= 32768, "moe_batched: at most 32768 tokens per call");
     const PrefillLayout L = prefill_layout(a.T, a.k, a.E, a.H, a.I);
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+    int* pos_of = reinterpret_cast<int*>(ws + L.off_pos_of);
     int* tok_of = reinterpret_cast<int*>(ws + L.off_tok_of);
     int* slot_of = reinterpret_cast<int*>(ws + L.off_slot_of);
     int4* tiles = reinterpret_cast<int4*>(ws + L.off_tiles);
     int* n_tiles = reinterpret_cast<int*>(ws + L.off_misc);
     int* err = reinterpret_cast<int*>(ws + L.off_misc + 64 * 4);
-    uint8_t* img = ws + L.off_img;
-    uint8_t* sf = ws + L.off_sf;
-    float* act = reinterpret_cast<float*>(ws + L.off_act);
+    uint8_t* img_gu = ws + L.off_img_gu;
+    uint8_t* img_dn = ws + L.off_img_dn;
+    float* out = reinterpret_cast<float*>(ws + L.off_out);
     const int sms = num_sms();
 
-    require(a.T <= 32768, "moe_batched: at most 32768 tokens per call");
-    static std::mutex pmu;
-    static std::map<int, bool> pdone;
-    {
-        int dev = 0;
-        GPT_CHECK(cudaGetDevice(&dev));
-        std::lock_guard<std::mutex> lock(pmu);
-        if (!pdone[dev]) {
-            GPT_CHECK(cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * 1024 * 2));
-            pdone[dev] = true;
-        }
-    }
-    permute_kernel<<<1, 1024, 32 * 1024 * 2, s>>>(a.ids, a.T, a.k, a.E, reinterpret_cast<int*>(ws + L.off_row_of),
-                                                   tok_of, slot_of, tiles, n_tiles, err);
-    check_launch("moe_batched permute");
-
-    int NS = 4;
-    while (gemm_smem_bytes(NS) > 227 * 1024 && NS > 2) --NS;
-    const int smem = gemm_smem_bytes(NS);
     static std::mutex mu;
-    static std::map<int, int> done;
+    static std::map<int, bool> done;
     {
         int dev = 0;
         GPT_CHECK(cudaGetDevice(&dev));
         std::lock_guard<std::mutex> lock(mu);
-        if (done[dev] < smem) {
-            GPT_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            done[dev] = smem;
+        if (!done[dev]) {
+            GPT_CHECK(cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * 1024 * 2));
+            GPT_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+            done[dev] = true;
         }
     }
+    permute_kernel<<<1, 1024, 32 * 1024 * 2, s>>>(a.ids, a.T, a.k, a.E, pos_of, tok_of, slot_of, tiles, n_tiles, err);
+    check_launch("moe_batched permute");
+    quantize_h_kernel<<<sms * 8, 256, 0, s>>>(a.h, a.T, a.H, a.k, pos_of, L.KB_gu, img_gu);
+    check_launch("moe_batched quantize");
     for (int pass = 0; pass < 2; ++pass) {
         const bool gu = pass == 0;
         const int K = gu ? a.H : a.I, N = gu ? 2 * a.I : a.H;
-        const int SPS = gu ? L.SPS_gu : L.SPS_dn, KT = gu ? L.KT_gu : L.KT_dn;
-        quantize_tiles_kernel<<<sms * 8, 256, 0, s>>>(gu ? a.h : act, gu ? 1 : 0, tok_of, tiles, n_tiles, K, SPS, KT,
-                                                      img, sf);
-        check_launch("moe_batched quantize");
         GemmJob g{};
         g.mode = gu ? 0 : 1;
         g.K = K;
         g.N = N;
         g.UK = K / 64;
-        g.SPS = SPS;
-        g.KT = KT;
+        g.KB = gu ? L.KB_gu : L.KB_dn;
+        g.KT = (K + 127) / 128;
         g.RT = (N + kRows - 1) / kRows;
-        g.a_img = img;
-        g.a_sf = sf;
+        g.a_img = gu ? img_gu : img_dn;
         g.b_sf = gu ? a.sf_gu : a.sf_dn;
         g.tiles = tiles;
         g.n_tiles = n_tiles;
         g.bias = gu ? a.gu_bias : a.dn_bias;
         g.alpha = a.alpha;
         g.limit = a.limit;
-        g.act = act;
+        g.act = out;                                       // consumed by quantize_act before the down GEMM
+        g.I = a.I;
         g.tok_of = tok_of;
         g.slot_of = slot_of;
         g.wts = a.weights;
         g.k = a.k;
-        g.out_ts = act;                                    // the activations are consumed by then
+        g.out_ts = out;
         g.err = err;
-        grouped_gemm_kernel<<<sms, kThreads, smem, s>>>(gu ? *a.tmap_gu : *a.tmap_dn, g, NS);
+        g.trace = a.trace;
+        grouped_gemm_kernel<<<sms, kThreads, kGemmSmem, s>>>(gu ? *a.tmap_gu : *a.tmap_dn, g);
         check_launch("moe_batched grouped gemm");
+        if (gu) {
+            quantize_act_kernel<<<sms * 8, 256, 0, s>>>(out, a.I, tiles, n_tiles, L.KB_dn, img_dn);
+            check_launch("moe_batched quantize act");
+        }
     }
-    combine_kernel<<<sms * 8, 256, 0, s>>>(act, a.T, a.k, a.H, a.x_resid);
+    combine_kernel<<<sms * 8, 256, 0, s>>>(out, a.T, a.k, a.H, a.x_resid);
     check_launch("moe_batched combine");
 }
 

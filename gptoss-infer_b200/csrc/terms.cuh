@@ -159,6 +159,80 @@ constexpr int kActiveTerms = 10;              // terms quantize_block_terms_fixe
 // the first min(NT, kActiveTerms) computed and the rest zero. There is no per-term maximum (no lane shuffles), and
 // the rounding is round_e2m1: each term is a short chain of full-rate fp32 operations per element. Scales below
 // 2^-127 are clamped there (the terms of such tiny remainders are then merely close, never NaN).
+// First scale exponent of the fixed schedule for a block whose largest magnitude is amax: the block maximum fits
+// within 6 * 2^k (k = floor(log2 amax) - 2, or - 1 when the mantissa is above 1.5), clamped to E8M0's range.
+__device__ __forceinline__ int fixed_schedule_k0(float amax) {
+    int k = -127;
+    const uint32_t bits = __float_as_uint(amax);
+    const int e = int((bits >> 23) & 0xFF);
+    if (e != 0) {
+        const int k0 = e - 127;
+        k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
+        k = max(-127, min(127, k));
+    }
+    return k;
+}
+
+// One 32-element block held by ONE thread (v[32]) into NT terms with the fixed schedule of
+// quantize_block_terms_fixed_n: the same codes and scales bit for bit. emit(t, codes, scale) receives term t's 32
+// codes as 16 bytes (element 2i in the low nibble of byte i) and its E8M0 scale byte. v is consumed.
+template <int NT, class Emit>
+__device__ __forceinline__ void quantize_block32_terms_thread(float (&v)[32], Emit&& emit) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    int k = fixed_schedule_k0(amax);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u}, scale = 0;
+        if (t < kActiveTerms) {
+            const int kc = max(-127, k);
+            const float inv = exp2i_exact(-kc), sc = exp2i_exact(kc);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                uint32_t code;
+                const float qv = round_e2m1_code(v[i] * inv, code);
+                v[i] = fmaf(-qv, sc, v[i]);
+                w[i >> 3] |= code << (4 * (i & 7));
+            }
+            scale = uint32_t(kc + 127);
+            k -= t == 0 ? 2 : 3;
+        }
+        emit(t, make_uint4(w[0], w[1], w[2], w[3]), scale);
+    }
+}
+
+// The four-lanes-per-block form (lane `sub` of the block's 4 holds elements 8 sub .. 8 sub + 7) with the fixed
+// schedule: emit(t, word, scale) receives term t's 8 codes of this lane as one 32-bit word (element 8 sub + i in
+// bits 4i .. 4i + 3) and the block's E8M0 scale byte. v is consumed.
+template <int NT, class Emit>
+__device__ __forceinline__ void quantize_block_terms_lanes4(float (&v)[8], Emit&& emit) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+    int k = fixed_schedule_k0(amax);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        uint32_t word = 0, scale = 0;
+        if (t < kActiveTerms) {
+            const int kc = max(-127, k);
+            const float inv = exp2i_exact(-kc), sc = exp2i_exact(kc);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                uint32_t code;
+                const float qv = round_e2m1_code(v[i] * inv, code);
+                v[i] = fmaf(-qv, sc, v[i]);
+                word |= code << (4 * i);
+            }
+            scale = uint32_t(kc + 127);
+            k -= t == 0 ? 2 : 3;
+        }
+        emit(t, word, scale);
+    }
+}
+
 template <int NT>
 __device__ __forceinline__ void quantize_block_terms_fixed_n(float (&v)[8], uint8_t* img_stage, int q,
                                                              uint8_t* sf_chunk, int kb, int sub, bool active) {
@@ -167,16 +241,7 @@ __device__ __forceinline__ void quantize_block_terms_fixed_n(float (&v)[8], uint
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
     amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
-    int k = -127;
-    {
-        const uint32_t bits = __float_as_uint(amax);
-        const int e = int((bits >> 23) & 0xFF);
-        if (e != 0) {
-            const int k0 = e - 127;
-            k = ((bits & 0x7FFFFFu) <= 0x400000u) ? k0 - 2 : k0 - 1;
-            k = max(-127, min(127, k));
-        }
-    }
+    int k = fixed_schedule_k0(amax);
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
         uint32_t word = 0, scale = 0;

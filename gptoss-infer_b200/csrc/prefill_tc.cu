@@ -272,15 +272,20 @@ __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ sr
 #pragma unroll
         for (int i = 0; i < 8; ++i) v8[i] = 0.f;
     }
-    quantize_block_terms_lanes4<NT>(v8, [&](int term, uint32_t word, uint32_t scale) {
-        if (!valid) return;
+    // The scale bytes of the 8 blocks as two words per (row, quadrant copy): lane l < 8 stores word (l >> 2) of
+    // quadrant copy l & 3, gathered from the lanes holding blocks 4 (l >> 2) .. + 3.
+    const int wsel = (lane >> 2) & 1, qsel = lane & 3;
+    quantize_block_digits_lanes4(v8, [&](int term, uint32_t word, uint32_t scale) {
+        uint32_t sw = 0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) sw |= __shfl_sync(kFull, scale, 4 * (4 * wsel + kk)) << (8 * kk);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             if (s >= nd || pos[s] < 0) continue;
             const int m = pos[s] / kTileM, r = pos[s] % kTileM;
             uint8_t* pc = a_term(img, m, KB, kb, term);
-            *reinterpret_cast<uint32_t*>(pc + a_unit_off(r, gl) + sub * 4) = word;
-            pc[a_sf_off(r, gl, sub)] = uint8_t(scale);          // lane sub writes quadrant sub's copy
+            if (valid) *reinterpret_cast<uint32_t*>(pc + a_unit_off(r, gl) + sub * 4) = word;
+            if (lane < 8) *reinterpret_cast<uint32_t*>(pc + a_sf_off(r, 4 * wsel, qsel)) = sw;
         }
     });
 }

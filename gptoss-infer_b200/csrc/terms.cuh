@@ -173,35 +173,6 @@ __device__ __forceinline__ int fixed_schedule_k0(float amax) {
     return k;
 }
 
-// One 32-element block held by ONE thread (v[32]) into NT terms with the fixed schedule of
-// quantize_block_terms_fixed_n: the same codes and scales bit for bit. emit(t, codes, scale) receives term t's 32
-// codes as 16 bytes (element 2i in the low nibble of byte i) and its E8M0 scale byte. v is consumed.
-template <int NT, class Emit>
-__device__ __forceinline__ void quantize_block32_terms_thread(float (&v)[32], Emit&& emit) {
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    int k = fixed_schedule_k0(amax);
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        uint32_t w[4] = {0u, 0u, 0u, 0u}, scale = 0;
-        if (t < kActiveTerms) {
-            const int kc = max(-127, k);
-            const float inv = exp2i_exact(-kc), sc = exp2i_exact(kc);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                uint32_t code;
-                const float qv = round_e2m1_code(v[i] * inv, code);
-                v[i] = fmaf(-qv, sc, v[i]);
-                w[i >> 3] |= code << (4 * (i & 7));
-            }
-            scale = uint32_t(kc + 127);
-            k -= t == 0 ? 2 : 3;
-        }
-        emit(t, make_uint4(w[0], w[1], w[2], w[3]), scale);
-    }
-}
-
 // The four-lanes-per-block form (lane `sub` of the block's 4 holds elements 8 sub .. 8 sub + 7) with the fixed
 // schedule: emit(t, word, scale) receives term t's 8 codes of this lane as one 32-bit word (element 8 sub + i in
 // bits 4i .. 4i + 3) and the block's E8M0 scale byte. v is consumed.
@@ -230,6 +201,53 @@ __device__ __forceinline__ void quantize_block_terms_lanes4(float (&v)[8], Emit&
             k -= t == 0 ? 2 : 3;
         }
         emit(t, word, scale);
+    }
+}
+
+// Eight terms per 32-value block from one round and an integer split (the prefill path's A operand), four lanes per
+// block (lane `sub` holds elements 8 sub .. 8 sub + 7): term 0 is the RNE e2m1 value of v / 2^k (k from the block
+// maximum as in fixed_schedule_k0, so |v / 2^k| <= 6 and the remainder r satisfies |r| <= 2^k); then
+// R = rint(r 2^(20 - k)) (|R| <= 2^20, the only rounding after term 0) is written in balanced base 8, digits in
+// [-4, 3] for 8^0 .. 8^5 and the top one in [-4, 4]: adding 4 (8^7 - 1) / 7 makes every digit the plain octal digit
+// plus 4, so each is a 3-bit field. A digit d in units of 2^(k_t - 1) is the e2m1 value d / 2 (0, 0.5, 1, 1.5, 2)
+// with scale 2^k_t: term 1 (top digit) has k_1 = k - 1 and term t = 2..7 has k_t = k + 2 - 3t (digit 7 - t). The
+// represented value is exact up to the rint: |error| <= 2^(k - 21). Terms whose scale would fall below 2^-127 (blocks
+// under about 2^-105) are left zero. emit(t, word, scale) as quantize_block_terms_lanes4.
+__device__ __forceinline__ uint32_t balanced_digit_code(uint32_t u) {     // u = digit + 4 in 0..7 -> e2m1 code
+    return (0x32109ABCu >> (4 * u)) & 0xFu;
+}
+
+template <class Emit>
+__device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8], Emit&& emit) {
+    constexpr int kOff = 4 * 299593;                            // 4 (8^7 - 1) / 7
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+    const int k = fixed_schedule_k0(amax);
+    const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+    uint32_t w0 = 0, w1 = 0;
+    int Rp[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t code;
+        const float q0 = round_e2m1_code(v[i] * inv, code);
+        w0 |= code << (4 * i);
+        const float r = fmaf(-q0, sc, v[i]);                    // exact
+        Rp[i] = __float2int_rn((r * inv) * 1048576.f) + kOff;    // in 0 .. 2^20 + kOff
+        const uint32_t u1 = uint32_t(Rp[i]) >> 18;               // top digit + 4, 0..8
+        w1 |= (u1 < 4 ? 12u - u1 : u1 - 4u) << (4 * i);
+    }
+    emit(0, w0, uint32_t(k + 127));
+    emit(1, (k - 1 >= -127) ? w1 : 0u, uint32_t(max(k - 1 + 127, 0)));
+#pragma unroll
+    for (int t = 2; t < 8; ++t) {
+        const int kt = k + 2 - 3 * t, j = 7 - t;
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w |= balanced_digit_code((uint32_t(Rp[i]) >> (3 * j)) & 7u) << (4 * i);
+        emit(t, kt >= -127 ? w : 0u, uint32_t(max(kt + 127, 0)));
     }
 }
 

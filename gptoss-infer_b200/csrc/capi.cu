@@ -464,7 +464,8 @@ int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales
     });
 }
 
-int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float* x_resid, int T, void* stream) {
+int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float* x_resid, int T, void* stream,
+                                     void* const* events) {
     return guard([&] {
         if (!l) throw std::runtime_error("moe_layer_forward_batched: null layer");
         if (T < 1) throw std::runtime_error("moe_layer_forward_batched: T must be positive");
@@ -496,6 +497,7 @@ int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float*
         a.limit = l->limit;
         a.workspace = ws;
         a.trace = g_trace;
+        a.events = events;
         gpt::launch_moe_batched(a, s);
     });
 }

@@ -119,6 +119,7 @@ struct PrefillArgs {
     float alpha, limit;
     void* workspace;              // prefill_layout(T, k, E, H, I).bytes
     long long* trace = nullptr;   // optional: grouped GEMM wait totals per CTA, [160][160], slots 64 * mode + i
+    void* const* events = nullptr;   // optional: 4 cudaEvent_t around the gate/up and the down grouped GEMM
 };
 void launch_moe_batched(const PrefillArgs& a, cudaStream_t s);
 

@@ -763,8 +763,14 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
         g.out_ts = out;
         g.err = err;
         g.trace = a.trace;
+        auto rec = [&](int i) {
+            if (a.events)
+                GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a.events[i]), s, cudaEventRecordExternal));
+        };
+        rec(2 * pass);
         grouped_gemm_kernel<<<sms, kThreads, kGemmSmem, s>>>(gu ? *a.tmap_gu : *a.tmap_dn, g);
         check_launch("moe_batched grouped gemm");
+        rec(2 * pass + 1);
         if (gu) {
             quantize_act_kernel<<<sms * 8, 256, 0, s>>>(out, a.I, tiles, n_tiles, L.KB_dn, img_dn);
             check_launch("moe_batched quantize act");

@@ -29,7 +29,7 @@ SIGNATURES = {
     "gptoss_kernel_router_batched": ([P, P, P, I32, I32, I32, I32, P, P], I32),
     "gptoss_moe_route_batched": ([P, P, P, P, F32, I32, I32, I32, I32, P, P, P, P], I32),
     "gptoss_kernel_moe_batched": ([P, P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32], I32),
-    "gptoss_moe_layer_forward_batched": ([P, P, P, I32, P], I32),
+    "gptoss_moe_layer_forward_batched": ([P, P, P, I32, P, P], I32),
     "gptoss_moe_layer_experts_batched": ([P, P, P, P, P, I32, I32, P], I32),
     "gptoss_set_moe_impl": ([I32], I32),
     "gptoss_trace_enable": ([P, I64], I32),

@@ -141,8 +141,10 @@ int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales
 
 /* [extension] x_resid[t] += MoE(RMSNorm(x[t])) for T tokens with a prepared layer (batched router, then the batched
  * MoE above), asynchronous on `stream`. x_resid may alias x. Uses the calling thread's batched-path workspace: calls
- * from one thread must not overlap on the GPU. */
-int gptoss_moe_layer_forward_batched(gptoss_moe_layer* layer, const float* x, float* x_resid, int T, void* stream);
+ * from one thread must not overlap on the GPU. events: NULL, or 4 cudaEvent_t recorded (external, so capturable)
+ * before and after the gate/up grouped GEMM and before and after the down grouped GEMM. */
+int gptoss_moe_layer_forward_batched(gptoss_moe_layer* layer, const float* x, float* x_resid, int T, void* stream,
+                                     void* const* events);
 
 /* [extension] The experts of a prepared layer applied to T given rows, asynchronous on `stream`: x_resid[t] +=
  * sum_s w[t][s] (W2[e] swiglu(W1[e] h[t] + b1) + b2) with e = ids[t][s] < the layer's E (the router is not used).

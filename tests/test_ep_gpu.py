@@ -68,7 +68,7 @@ def _single_gpu_reference(t, x, dev):
     try:
         xd = x.to(dev).contiguous()
         y = xd.clone()
-        assert lib.gptoss_moe_layer_forward_batched(L, capi.ptr(xd), capi.ptr(y), x.shape[0], None) == 0, \
+        assert lib.gptoss_moe_layer_forward_batched(L, capi.ptr(xd), capi.ptr(y), x.shape[0], None, None) == 0, \
             lib.gptoss_last_error().decode()
         torch.cuda.synchronize()
         return y.cpu()

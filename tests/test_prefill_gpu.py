@@ -122,7 +122,7 @@ def test_layer_forward_batched_matches_decode_and_oracle():
         outs = []
         for _ in range(2):
             y = xb.clone()
-            _ok(lib, lib.gptoss_moe_layer_forward_batched(L, P(xb), P(y), T, None))
+            _ok(lib, lib.gptoss_moe_layer_forward_batched(L, P(xb), P(y), T, None, None))
             torch.cuda.synchronize()
             outs.append(y.cpu().numpy())
         assert np.array_equal(outs[0], outs[1])

@@ -674,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                         if ((lane & 1) == 0) {
                             const float gv = fminf(y, j.limit);
                             const float lv = fminf(fmaxf(lin, -j.limit), j.limit);
-                            aval[col >> 1] = gv / (1.f + expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
+                            aval[col >> 1] = __fdividef(gv, 1.f + __expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
                         }
                     }
                     epi_sync();

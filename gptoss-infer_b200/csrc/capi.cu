@@ -3,6 +3,7 @@
 // returning (runtime/src/capi.cpp:34-37).
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -169,6 +170,9 @@ namespace {
 // Workspace of the batched path, owned by the calling thread, one per device (grow-only).
 thread_local Scratch g_pws;
 thread_local Scratch g_pws_sf;
+
+// Private workspace of the expert-parallel path (per calling thread and device, grow-only).
+thread_local Scratch g_ews;
 
 void check_prefill_error(char* ws, const gpt::PrefillLayout& L) {
     int h = 0;
@@ -593,6 +597,105 @@ int gptoss_trace_enable(void* device_buffer, long long bytes) {
         if (device_buffer && bytes < 160LL * 160 * 8)
             throw std::runtime_error("trace buffer too small: need 160 * 160 * 8 bytes");
         g_trace = static_cast<long long*>(device_buffer);
+    });
+}
+
+int gptoss_router_w64(const void* W, int E, int H, double* w64, void* stream) {
+    return guard([&] {
+        if (E < 1 || E > 32 || H < 1) throw std::runtime_error("router_w64: need 1 <= E <= 32, H >= 1");
+        gpt::launch_router_w64(W, E, H, w64, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int gptoss_ep_region_bytes(int E, int k, int H, int I, int world, int T_max, long long* bytes) {
+    return guard([&] {
+        if (!bytes) throw std::runtime_error("ep_region_bytes: null output");
+        *bytes = (long long)gpt::ep_layout(T_max, k, E, world, H, I).region_bytes;
+    });
+}
+
+int gptoss_ep_region_alloc(long long bytes, void** region) {
+    return guard([&] {
+        if (!region || bytes <= 0) throw std::runtime_error("ep_region_alloc: bad arguments");
+        *region = nullptr;
+        GPT_CHECK(cudaMalloc(region, size_t(bytes)));
+        GPT_CHECK(cudaMemset(*region, 0, size_t(bytes)));
+    });
+}
+
+int gptoss_ep_region_free(void* region) {
+    return guard([&] { GPT_CHECK(cudaFree(region)); });
+}
+
+int gptoss_ipc_handle(void* device_ptr, void* handle_out) {
+    return guard([&] {
+        static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+        cudaIpcMemHandle_t hd;
+        GPT_CHECK(cudaIpcGetMemHandle(&hd, device_ptr));
+        std::memcpy(handle_out, &hd, sizeof(hd));
+    });
+}
+
+int gptoss_ipc_open(const void* handle, void** device_ptr) {
+    return guard([&] {
+        cudaIpcMemHandle_t hd;
+        std::memcpy(&hd, handle, sizeof(hd));
+        GPT_CHECK(cudaIpcOpenMemHandle(device_ptr, hd, cudaIpcMemLazyEnablePeerAccess));
+    });
+}
+
+int gptoss_ipc_close(void* device_ptr) {
+    return guard([&] { GPT_CHECK(cudaIpcCloseMemHandle(device_ptr)); });
+}
+
+int gptoss_ep_layer_forward(gptoss_moe_layer* l, const double* router_w64, const float* router_b, const float* norm_w,
+                            float eps, int E, int rank, int world, const float* x, float* x_resid, int T, int T_max,
+                            void* const* peers, unsigned epoch, void* stream) {
+    return guard([&] {
+        if (!l || !peers) throw std::runtime_error("ep_layer_forward: null layer or peer table");
+        if (world < 1 || world > 8 || E % world || l->E != E / world)
+            throw std::runtime_error("ep_layer_forward: the layer must hold E / world experts, 1 <= world <= 8");
+        if (epoch == 0) throw std::runtime_error("ep_layer_forward: epochs start at 1");
+        const gpt::EpLayout L = gpt::ep_layout(T_max, l->k, E, world, l->H, l->I);
+        gpt::EpArgs a{};
+        a.tmap_gu = &l->tg;
+        a.tmap_dn = &l->td;
+        a.sf_gu = l->sfa_gu;
+        a.sf_dn = l->sfa_dn;
+        a.gu_bias = l->gu_bias;
+        a.dn_bias = l->dn_bias;
+        a.w64 = router_w64;
+        a.router_b = router_b;
+        a.norm_w = norm_w;
+        a.eps = eps;
+        a.x = x;
+        a.x_resid = x_resid;
+        a.T = T;
+        a.T_max = T_max;
+        a.k = l->k;
+        a.E = E;
+        a.H = l->H;
+        a.I = l->I;
+        a.rank = rank;
+        a.world = world;
+        a.alpha = l->alpha;
+        a.limit = l->limit;
+        a.peers = peers;
+        a.epoch = epoch;
+        a.local_ws = g_ews.get(L.local_bytes);
+        a.trace = g_trace;
+        gpt::launch_ep_layer(a, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int gptoss_ep_status(int E, int k, int H, int I, int world, int T_max, int* code) {
+    return guard([&] {
+        const gpt::EpLayout L = gpt::ep_layout(T_max, k, E, world, H, I);
+        char* ws = static_cast<char*>(g_ews.get(L.local_bytes));
+        GPT_CHECK(cudaDeviceSynchronize());
+        int h = 0;
+        GPT_CHECK(cudaMemcpy(&h, ws + L.off_misc + 256, sizeof(int), cudaMemcpyDeviceToHost));
+        *code = h;
     });
 }
 

@@ -123,6 +123,38 @@ struct PrefillArgs {
 };
 void launch_moe_batched(const PrefillArgs& a, cudaStream_t s);
 
+// Expert parallelism over `world` ranks (one GPU each): the shared region (allocated zeroed, mapped on every rank) and
+// this rank's private workspace, for at most T_max tokens per rank.
+struct EpLayout {
+    long long max_rows;
+    int max_tiles, KB_gu, KB_dn;
+    size_t off_flags, off_counts, off_meta, off_img, off_out, region_bytes;
+    size_t off_h, off_ids, off_w, off_pos, off_dest, off_tiles, off_misc, off_img_dn, off_act, local_bytes;
+};
+EpLayout ep_layout(int T_max, int k, int E, int world, int H, int I);
+
+struct EpArgs {
+    const CUtensorMap* tmap_gu;   // this rank's experts (E / world of them), as PrefillArgs
+    const CUtensorMap* tmap_dn;
+    const uint8_t* sf_gu;
+    const uint8_t* sf_dn;
+    const float* gu_bias;
+    const float* dn_bias;
+    const double* w64;            // the full router (E experts) as fp64 [H][32]
+    const float* router_b;        // [E]
+    const float* norm_w;          // [H]
+    float eps;
+    const float* x;               // this rank's tokens [T][H]
+    float* x_resid;               // [T][H], += the MoE output
+    int T, T_max, k, E, H, I, rank, world;
+    float alpha, limit;
+    void* const* peers;           // host array [world]: every rank's region as mapped here (peers[rank] = own)
+    unsigned epoch;               // the same on every rank for one layer call; increases from 1
+    void* local_ws;               // ep_layout(...).local_bytes
+    long long* trace = nullptr;
+};
+void launch_ep_layer(const EpArgs& a, cudaStream_t s);
+
 // Single-CTA tcgen05 kind::mxf4 GEMM, D[128][N] = dequant(A)[128][K] . dequant(B)[N][K]^T, from raw MXFP4 arrays
 // (checkpoint layout). Pins the layout conventions of the tensor-core kernels. Synchronizes.
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,

@@ -258,7 +258,7 @@ __device__ __forceinline__ void tmem_cp_128x256b(uint32_t tmem_col, uint64_t sde
 // One warp quantizes 8 blocks (K block kb, 4 lanes per 32-value block) of the source row `src` once and writes the
 // terms into the A terms of `nd` destination rows (pos = 128 * tile + row in the tile; negative = none).
 __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ src, int K, int kb, const int (&pos)[8],
-                                                    int nd, int KB, uint8_t* __restrict__ img) {
+                                                    int nd, int KB, uint8_t* const (&img)[8]) {
     const int lane = threadIdx.x & 31, sub = lane & 3, gl = lane >> 2;
     const int g = kb * 8 + gl;
     const bool valid = g * 32 < K;
@@ -283,27 +283,38 @@ __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ sr
         for (int s = 0; s < 8; ++s) {
             if (s >= nd || pos[s] < 0) continue;
             const int m = pos[s] / kTileM, r = pos[s] % kTileM;
-            uint8_t* pc = a_term(img, m, KB, kb, term);
+            uint8_t* pc = a_term(img[s], m, KB, kb, term);
             if (valid) *reinterpret_cast<uint32_t*>(pc + a_unit_off(r, gl) + sub * 4) = word;
             if (lane < 8) *reinterpret_cast<uint32_t*>(pc + a_sf_off(r, 4 * wsel, qsel)) = sw;
         }
     });
 }
 
+// Image bases by rank (expert parallelism: index = the rank that owns the row's expert, the peer's mapping of its
+// region); one rank: all equal.
+struct ImgBases {
+    uint8_t* p[8];
+};
+
 // Gate/up A terms from h: work item (token t, K block kb) per warp; the token's terms are computed once and written
-// to the k tiles that hold it (pos_of).
+// to the k tiles that hold it (pos_of; dest_of = the owning rank, or null for one rank).
 __global__ void __launch_bounds__(256) quantize_h_kernel(const float* __restrict__ h, int T, int H, int k,
-                                                         const int* __restrict__ pos_of, int KB,
-                                                         uint8_t* __restrict__ img) {
+                                                         const int* __restrict__ pos_of, const int* __restrict__ dest_of,
+                                                         int KB, const __grid_constant__ ImgBases imgs) {
     const long long items = (long long)T * KB;
     const long long warps = (long long)gridDim.x * (blockDim.x / 32);
     for (long long w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < items; w += warps) {
         const int t = int(w / KB), kb = int(w % KB);
         int pos[8];
+        uint8_t* img[8];
 #pragma unroll
-        for (int s = 0; s < 8; ++s) pos[s] = s < k ? pos_of[size_t(t) * k + s] : -1;
+        for (int s = 0; s < 8; ++s) {
+            pos[s] = s < k ? pos_of[size_t(t) * k + s] : -1;
+            img[s] = imgs.p[(s < k && dest_of) ? (dest_of[size_t(t) * k + s] & 7) : 0];
+        }
         quantize_row_kblock(h + size_t(t) * H, H, kb, pos, k, KB, img);
     }
+    if (dest_of) __threadfence_system();                    // expert parallel: stores into peers' regions
 }
 
 // Down A terms from the activations act [rows][I] (rows in tile order): work item (tile m, row j, K block kb).
@@ -319,9 +330,13 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
         const int4 tl = tiles[m];
         if (j >= tl.z) continue;
         int pos[8];
+        uint8_t* im[8];
 #pragma unroll
-        for (int s = 0; s < 8; ++s) pos[s] = s == 0 ? m * kTileM + j : -1;
-        quantize_row_kblock(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, img);
+        for (int s = 0; s < 8; ++s) {
+            pos[s] = s == 0 ? m * kTileM + j : -1;
+            im[s] = img;
+        }
+        quantize_row_kblock(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, im);
     }
 }
 
@@ -343,6 +358,8 @@ struct GemmJob {
     const float* wts;                          // [T][k]
     int k;
     float* out_ts;                             // down: [T][k][N]
+    const int4* meta;                          // expert parallel: per row (pos) source rank, token, slot, weight bits
+    float* out_rank[8];                        // expert parallel: each source rank's result rows as mapped here
     int* err;
     long long* trace;                          // optional: per CTA (< 160) 160 stamps, slots 64 mode + i
 };
@@ -598,9 +615,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 }
             } else if (j.mode == 1 && live && n0 < j.N) {
                 const int row = tl.y + row_t;
-                const int t = j.tok_of[row], s = j.slot_of[row];
-                const float w = j.wts[size_t(t) * j.k + s];
-                float* orow = j.out_ts + (size_t(t) * j.k + s) * j.N;
+                float w;
+                float* orow;
+                if (j.meta) {                        // the row came from rank src: its result goes back there
+                    const int4 mt = j.meta[row];
+                    w = __int_as_float(mt.w);
+                    orow = j.out_rank[mt.x & 7] + (size_t(mt.y) * j.k + mt.z) * j.N;
+                } else {
+                    const int t = j.tok_of[row], s = j.slot_of[row];
+                    w = j.wts[size_t(t) * j.k + s];
+                    orow = j.out_ts + (size_t(t) * j.k + s) * j.N;
+                }
                 if (n0 + 128 <= j.N) {
 #pragma unroll
                     for (int i = 0; i < 128; i += 4) {
@@ -619,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             }
             if (trc) tEpi += clock64() - te0;
         }
+        if (j.meta) __threadfence_system();                  // expert parallel: result rows went to peers
         if (trc) {
             long long* tr = j.trace + c * 160 + 64 * j.mode;
             tr[8] = wF;
@@ -640,6 +666,174 @@ __global__ void combine_kernel(const float* __restrict__ out_ts, int T, int k, i
         for (int s = 0; s < k; ++s) acc += out_ts[(t * k + s) * H + h];
         x_resid[i] = acc;
     }
+}
+
+// ------------------------------------------------------------------------------------------------ expert parallel
+// The batched MoE with the experts spread over G ranks (one GPU each), tokens split over the ranks. Every rank
+// allocates one zero-initialised "region" (cudaMalloc, shared with the others through CUDA IPC) and gets every
+// peer's region mapped into its address space (NVLink peer memory). Per layer call:
+//   counts:   each rank counts its (token, slot) pairs per expert and writes its row of the count matrix into every
+//             region; barrier 0;
+//   permute:  from the full count matrix every rank knows where each of its pairs goes: rows of an expert on its
+//             owner are ordered by source rank, then by the source's token order, cut into 128-row tiles; the pair's
+//             (source rank, token, slot, gate weight) is written to the owner's row metadata;
+//   dispatch: the h quantizer writes each token's A terms straight into the owners' A images (the data crosses
+//             NVLink once, as e2m1 terms); barrier 1;
+//   compute:  each rank runs the grouped GEMMs over the rows it received; the down epilogue writes every row's
+//             w (y + b2) straight into its source rank's result rows; barrier 2;
+//   combine:  each rank adds its result rows into its residual stream in slot order.
+// Every row's computation and the combine order are those of the single-GPU batched forward, so the result is
+// bit-identical to it. Barriers are epoch flags (release / acquire at system scope) with bounded waits.
+constexpr int kMaxRanks = 8;
+
+struct EpDev {
+    uint8_t* base[kMaxRanks];                  // every rank's region as mapped on this device (base[rank] = own)
+    int rank, G, E, El;
+    size_t off_flags, off_counts, off_meta;
+    unsigned epoch;
+    int* err;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread: tells every rank (flag `which` of its region, slot = this rank) that this rank reached the barrier in
+// layer call `epoch`, after a system-scope fence that orders everything this rank's earlier kernels wrote; then waits
+// (bounded: about a second) until every rank did the same. Epochs only grow, so a flag at or past `epoch` counts.
+__device__ void ep_barrier(const EpDev& d, int which) {
+    __threadfence_system();
+    for (int r = 0; r < d.G; ++r)
+        st_release_sys(reinterpret_cast<unsigned*>(d.base[r] + d.off_flags) + which * kMaxRanks + d.rank, d.epoch);
+    const unsigned* own = reinterpret_cast<const unsigned*>(d.base[d.rank] + d.off_flags) + which * kMaxRanks;
+    for (int r = 0; r < d.G; ++r) {
+        bool ok = false;
+        for (uint32_t i = 0; i < (1u << 24) && !ok; ++i) {
+            ok = ld_acquire_sys(own + r) >= d.epoch;
+            if (!ok) __nanosleep(64);
+        }
+        if (!ok) {
+            atomicCAS(d.err, 0, 60 + which);
+            return;
+        }
+    }
+}
+
+__global__ void ep_barrier_kernel(const __grid_constant__ EpDev d, int which) {
+    if (threadIdx.x == 0) ep_barrier(d, which);
+}
+
+// Counts of this rank's (token, slot) pairs per expert -> row `rank` of every region's count matrix; barrier 0.
+__global__ void __launch_bounds__(256) ep_counts_kernel(const int* __restrict__ ids, int T, int k,
+                                                        const __grid_constant__ EpDev d) {
+    __shared__ int cnt[32];
+    const int tid = threadIdx.x;
+    if (tid < 32) cnt[tid] = 0;
+    __syncthreads();
+    bool bad = false;
+    for (int i = tid; i < T * k; i += blockDim.x) {
+        const int e = ids[i];
+        if (e < 0 || e >= d.E) bad = true;
+        else atomicAdd(&cnt[e], 1);
+    }
+    if (bad) atomicCAS(d.err, 0, 20);
+    __syncthreads();
+    if (tid < 32) {
+        for (int r = 0; r < d.G; ++r)
+            reinterpret_cast<int*>(d.base[r] + d.off_counts)[d.rank * 32 + tid] = tid < d.E ? cnt[tid] : 0;
+        __threadfence_system();                              // peer stores ordered before the barrier's flags
+    }
+    __syncthreads();
+    if (tid == 0) ep_barrier(d, 0);
+}
+
+// One CTA of 1024 threads. Local tiles: this rank's experts' received rows in 128-row tiles, tiles[m] = (local
+// expert, 128 m, rows). Own pairs: pos_of / dest_of (tile row on the owner, owner rank), and the owner's metadata
+// row = (this rank, token, slot, gate weight). Thread i owns tokens [i * per, (i + 1) * per); per-expert counts are
+// scanned over the threads (expert e by warp e), as in permute_kernel.
+__global__ void __launch_bounds__(1024) ep_permute_kernel(const int* __restrict__ ids, const float* __restrict__ wts,
+                                                          int T, int k, const __grid_constant__ EpDev d,
+                                                          int* __restrict__ pos_of, int* __restrict__ dest_of,
+                                                          int4* __restrict__ tiles, int* __restrict__ n_tiles) {
+    extern __shared__ unsigned short cnt_raw[];
+    unsigned short (*cnt)[1024] = reinterpret_cast<unsigned short (*)[1024]>(cnt_raw);   // [32][1024]
+    __shared__ int before[32], tile0[32], total[32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int* C = reinterpret_cast<const int*>(d.base[d.rank] + d.off_counts);          // [G][32]
+    if (tid < 32) {
+        int tot = 0, bef = 0;
+        for (int r = 0; r < d.G; ++r) {
+            const int c = tid < d.E ? C[r * 32 + tid] : 0;
+            tot += c;
+            if (r < d.rank) bef += c;
+        }
+        total[tid] = tot;
+        before[tid] = bef;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int m = 0;
+        for (int e = 0; e < d.E; ++e) {
+            if (e % d.El == 0) m = 0;                       // tile numbers restart on every owner
+            tile0[e] = m;
+            const bool mine = e / d.El == d.rank;
+            for (int r = 0; r < total[e]; r += kTileM) {
+                if (mine) tiles[m] = make_int4(e - d.rank * d.El, m * kTileM, min(kTileM, total[e] - r), 0);
+                ++m;
+            }
+            if (mine && (e + 1) % d.El == 0) *n_tiles = m;
+        }
+    }
+    const int per = (T + 1023) / 1024, tb = min(T, tid * per), te = min(T, tb + per);
+    for (int e = 0; e < 32; ++e) cnt[e][tid] = 0;
+    for (int t = tb; t < te; ++t)
+        for (int s = 0; s < k; ++s) {
+            const int e = ids[size_t(t) * k + s];
+            if (e >= 0 && e < d.E) ++cnt[e][tid];
+        }
+    __syncthreads();
+    {
+        const int e = warp;
+        int local = 0;
+        for (int i = 0; i < 32; ++i) local += cnt[e][lane * 32 + i];
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < 32; ++i) {
+            const int c = cnt[e][lane * 32 + i];
+            cnt[e][lane * 32 + i] = (unsigned short)run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    for (int t = tb; t < te; ++t)
+        for (int s = 0; s < k; ++s) {
+            const size_t i = size_t(t) * k + s;
+            const int e = ids[i];
+            if (e < 0 || e >= d.E) {
+                pos_of[i] = -1;
+                dest_of[i] = 0;
+                continue;
+            }
+            const int r = before[e] + cnt[e][tid];
+            cnt[e][tid] = (unsigned short)(cnt[e][tid] + 1);
+            const int owner = e / d.El;
+            const int pos = (tile0[e] + r / kTileM) * kTileM + r % kTileM;
+            pos_of[i] = pos;
+            dest_of[i] = owner;
+            reinterpret_cast<int4*>(d.base[owner] + d.off_meta)[pos] = make_int4(d.rank, t, s, __float_as_int(wts[i]));
+        }
+    __threadfence_system();
 }
 
 constexpr int kGemmSmem = 1024 + NSA * kPieceA + NSB * kPieceB + (2 * NSA + 2 * NSB + 2) * 8 + 32;
@@ -734,7 +928,9 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
     }
     permute_kernel<<<1, 1024, 32 * 1024 * 2, s>>>(a.ids, a.T, a.k, a.E, pos_of, tok_of, slot_of, tiles, n_tiles, err);
     check_launch("moe_batched permute");
-    quantize_h_kernel<<<sms * 8, 256, 0, s>>>(a.h, a.T, a.H, a.k, pos_of, L.KB_gu, img_gu);
+    ImgBases ib{};
+    for (int r = 0; r < 8; ++r) ib.p[r] = img_gu;
+    quantize_h_kernel<<<sms * 8, 256, 0, s>>>(a.h, a.T, a.H, a.k, pos_of, nullptr, L.KB_gu, ib);
     check_launch("moe_batched quantize");
     for (int pass = 0; pass < 2; ++pass) {
         const bool gu = pass == 0;
@@ -778,6 +974,137 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
     }
     combine_kernel<<<sms * 8, 256, 0, s>>>(out, a.T, a.k, a.H, a.x_resid);
     check_launch("moe_batched combine");
+}
+
+
+EpLayout ep_layout(int T_max, int k, int E, int world, int H, int I) {
+    EpLayout L{};
+    auto al = [](size_t b) { return (b + 1023) & ~size_t(1023); };
+    require(world >= 1 && world <= pf::kMaxRanks && E % world == 0, "ep: 1 <= world <= 8 and E % world == 0");
+    const int El = E / world;
+    L.max_rows = (long long)world * T_max * k;
+    L.max_tiles = int((L.max_rows + pf::kTileM - 1) / pf::kTileM) + El;
+    L.KB_gu = (H + 255) / 256;
+    L.KB_dn = (I + 255) / 256;
+    size_t o = 0;                                            // the shared region
+    L.off_flags = o; o += 1024;                              // [3][8] epoch flags
+    L.off_counts = o; o += al(size_t(pf::kMaxRanks) * 32 * 4);
+    L.off_meta = o; o += al(size_t(L.max_tiles) * pf::kTileM * 16);
+    L.off_img = o; o += al(size_t(L.max_tiles) * L.KB_gu * pf::NT * pf::kTermA);
+    L.off_out = o; o += al(size_t(T_max) * k * H * 4);
+    L.region_bytes = o;
+    o = 0;                                                   // this rank's private workspace
+    L.off_h = o; o += al(size_t(T_max) * H * 4);
+    L.off_ids = o; o += al(size_t(T_max) * k * 4);
+    L.off_w = o; o += al(size_t(T_max) * k * 4);
+    L.off_pos = o; o += al(size_t(T_max) * k * 4);
+    L.off_dest = o; o += al(size_t(T_max) * k * 4);
+    L.off_tiles = o; o += al(size_t(L.max_tiles) * 16);
+    L.off_misc = o; o += 1024;                               // [0] tile count, [64] error word
+    L.off_img_dn = o; o += al(size_t(L.max_tiles) * L.KB_dn * pf::NT * pf::kTermA);
+    L.off_act = o; o += al(size_t(L.max_tiles) * pf::kTileM * I * 4);
+    L.local_bytes = o;
+    return L;
+}
+
+void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
+    using namespace pf;
+    require(a.T >= 0 && a.T <= a.T_max && a.T_max <= 32768, "ep: 0 <= T <= T_max <= 32768");
+    require(a.k >= 1 && a.k <= 8 && a.E <= 32 && a.rank >= 0 && a.rank < a.world, "ep: bad k, E or rank");
+    require(a.H % 64 == 0 && a.I % 64 == 0, "ep: H and I must be multiples of 64");
+    const EpLayout L = ep_layout(a.T_max, a.k, a.E, a.world, a.H, a.I);
+    uint8_t* ws = static_cast<uint8_t*>(a.local_ws);
+    float* h = reinterpret_cast<float*>(ws + L.off_h);
+    int* ids = reinterpret_cast<int*>(ws + L.off_ids);
+    float* wts = reinterpret_cast<float*>(ws + L.off_w);
+    int* pos_of = reinterpret_cast<int*>(ws + L.off_pos);
+    int* dest_of = reinterpret_cast<int*>(ws + L.off_dest);
+    int4* tiles = reinterpret_cast<int4*>(ws + L.off_tiles);
+    int* n_tiles = reinterpret_cast<int*>(ws + L.off_misc);
+    int* err = reinterpret_cast<int*>(ws + L.off_misc + 64 * 4);
+    uint8_t* img_dn = ws + L.off_img_dn;
+    float* act = reinterpret_cast<float*>(ws + L.off_act);
+    uint8_t* own = static_cast<uint8_t*>(a.peers[a.rank]);
+    const int sms = num_sms();
+
+    EpDev d{};
+    for (int r = 0; r < a.world; ++r) d.base[r] = static_cast<uint8_t*>(a.peers[r]);
+    d.rank = a.rank;
+    d.G = a.world;
+    d.E = a.E;
+    d.El = a.E / a.world;
+    d.off_flags = L.off_flags;
+    d.off_counts = L.off_counts;
+    d.off_meta = L.off_meta;
+    d.epoch = a.epoch;
+    d.err = err;
+
+    static std::mutex mu;
+    static std::map<int, bool> done;
+    {
+        int dev = 0;
+        GPT_CHECK(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lock(mu);
+        if (!done[dev]) {
+            GPT_CHECK(cudaFuncSetAttribute(ep_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * 1024 * 2));
+            GPT_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+            done[dev] = true;
+        }
+    }
+    GPT_CHECK(cudaMemsetAsync(ws + L.off_misc, 0, 1024, s));
+    if (a.T > 0)
+        launch_router_batched(a.w64, a.router_b, a.x, a.norm_w, a.eps, a.T, a.E, a.H, a.k, h, ids, wts, s);
+    ep_counts_kernel<<<1, 256, 0, s>>>(ids, a.T, a.k, d);
+    check_launch("ep counts");
+    ep_permute_kernel<<<1, 1024, 32 * 1024 * 2, s>>>(ids, wts, a.T, a.k, d, pos_of, dest_of, tiles, n_tiles);
+    check_launch("ep permute");
+    if (a.T > 0) {
+        ImgBases ib{};
+        for (int r = 0; r < kMaxRanks; ++r) ib.p[r] = r < a.world ? d.base[r] + L.off_img : nullptr;
+        quantize_h_kernel<<<sms * 8, 256, 0, s>>>(h, a.T, a.H, a.k, pos_of, dest_of, L.KB_gu, ib);
+        check_launch("ep dispatch");
+    }
+    ep_barrier_kernel<<<1, 32, 0, s>>>(d, 1);
+    check_launch("ep barrier 1");
+    for (int pass = 0; pass < 2; ++pass) {
+        const bool gu = pass == 0;
+        const int K = gu ? a.H : a.I, N = gu ? 2 * a.I : a.H;
+        GemmJob g{};
+        g.mode = gu ? 0 : 1;
+        g.K = K;
+        g.N = N;
+        g.UK = K / 64;
+        g.KB = gu ? L.KB_gu : L.KB_dn;
+        g.KT = (K + 127) / 128;
+        g.RT = (N + kRows - 1) / kRows;
+        g.a_img = gu ? own + L.off_img : img_dn;
+        g.b_sf = gu ? a.sf_gu : a.sf_dn;
+        g.tiles = tiles;
+        g.n_tiles = n_tiles;
+        g.bias = gu ? a.gu_bias : a.dn_bias;
+        g.alpha = a.alpha;
+        g.limit = a.limit;
+        g.act = act;
+        g.I = a.I;
+        g.k = a.k;
+        g.meta = reinterpret_cast<const int4*>(own + L.off_meta);
+        for (int r = 0; r < a.world; ++r) g.out_rank[r] = reinterpret_cast<float*>(d.base[r] + L.off_out);
+        g.err = err;
+        g.trace = a.trace;
+        grouped_gemm_kernel<<<sms, kThreads, kGemmSmem, s>>>(gu ? *a.tmap_gu : *a.tmap_dn, g);
+        check_launch("ep grouped gemm");
+        if (gu) {
+            quantize_act_kernel<<<sms * 8, 256, 0, s>>>(act, a.I, tiles, n_tiles, L.KB_dn, img_dn);
+            check_launch("ep quantize act");
+        }
+    }
+    ep_barrier_kernel<<<1, 32, 0, s>>>(d, 2);
+    check_launch("ep barrier 2");
+    if (a.T > 0) {
+        combine_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float*>(own + L.off_out), a.T, a.k, a.H,
+                                                 a.x_resid);
+        check_launch("ep combine");
+    }
 }
 
 }  // namespace gpt

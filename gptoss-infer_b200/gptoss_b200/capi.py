@@ -31,6 +31,15 @@ SIGNATURES = {
     "gptoss_kernel_moe_batched": ([P, P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32], I32),
     "gptoss_moe_layer_forward_batched": ([P, P, P, I32, P, P], I32),
     "gptoss_moe_layer_experts_batched": ([P, P, P, P, P, I32, I32, P], I32),
+    "gptoss_router_w64": ([P, I32, I32, P, P], I32),
+    "gptoss_ep_region_bytes": ([I32, I32, I32, I32, I32, I32, P], I32),
+    "gptoss_ep_region_alloc": ([ctypes.c_longlong, P], I32),
+    "gptoss_ep_region_free": ([P], I32),
+    "gptoss_ipc_handle": ([P, P], I32),
+    "gptoss_ipc_open": ([P, P], I32),
+    "gptoss_ipc_close": ([P], I32),
+    "gptoss_ep_layer_forward": ([P, P, P, P, F32, I32, I32, I32, P, P, I32, I32, P, ctypes.c_uint, P], I32),
+    "gptoss_ep_status": ([I32, I32, I32, I32, I32, I32, P], I32),
     "gptoss_set_moe_impl": ([I32], I32),
     "gptoss_trace_enable": ([P, I64], I32),
     "gptoss_selftest_terms": ([P, I32, P, P, I32], I32),

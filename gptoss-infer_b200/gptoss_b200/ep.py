@@ -108,3 +108,92 @@ def gpu_compute(lib, layer):
         return y
 
     return compute
+
+
+class EpGroup:
+    """The shared state of the library's peer-memory expert parallelism for one process group: every rank's region
+    (allocated zeroed here, exported with a CUDA IPC handle, the handles exchanged with all_gather_object and the
+    peers' regions mapped into this process) and the layer-call epoch, which all ranks advance together. One group
+    serves every layer of a model; its calls must be issued in the same order on every rank."""
+
+    def __init__(self, lib, E, k, H, I, rank, world, T_max, group=None):
+        import ctypes
+        self.lib, self.E, self.k, self.H, self.I = lib, E, k, H, I
+        self.rank, self.world, self.T_max = rank, world, T_max
+        nbytes = ctypes.c_longlong()
+        _ok(lib, lib.gptoss_ep_region_bytes(E, k, H, I, world, T_max, ctypes.byref(nbytes)))
+        region = ctypes.c_void_p()
+        _ok(lib, lib.gptoss_ep_region_alloc(nbytes, ctypes.byref(region)))
+        self.region = region.value
+        handle = ctypes.create_string_buffer(64)
+        _ok(lib, lib.gptoss_ipc_handle(self.region, handle))
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, handle.raw, group=group)
+        else:
+            handles = [handle.raw]
+        self._opened = []
+        peers = []
+        for r, hb in enumerate(handles):
+            if r == rank:
+                peers.append(self.region)
+                continue
+            p = ctypes.c_void_p()
+            buf = ctypes.create_string_buffer(hb, 64)
+            _ok(lib, lib.gptoss_ipc_open(buf, ctypes.byref(p)))
+            peers.append(p.value)
+            self._opened.append(p.value)
+        self.peers = (ctypes.c_void_p * world)(*peers)
+        self.epoch = 0
+        self.group = group
+
+    def status(self):
+        import ctypes
+        code = ctypes.c_int()
+        _ok(self.lib, self.lib.gptoss_ep_status(self.E, self.k, self.H, self.I, self.world, self.T_max,
+                                                ctypes.byref(code)))
+        return code.value
+
+    def close(self):
+        """Every rank calls this after its last layer call; the barrier keeps a region alive until no peer can
+        still write into it."""
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._opened:
+            self.lib.gptoss_ipc_close(p)
+        self._opened = []
+        if self.region:
+            self.lib.gptoss_ep_region_free(self.region)
+            self.region = None
+
+
+class PeerExpertParallelMoE:
+    """x <- x + MoE(RMSNorm(x)) for this rank's token shard, experts [rank E/world, (rank + 1) E/world) in `layer`
+    (gptoss_moe_layer_create with those experts and the full k), dispatch and combine inside the library's kernels
+    over NVLink peer memory (gptoss_ep_layer_forward); bit-identical to the single-GPU batched forward."""
+
+    def __init__(self, ep_group, layer, router_w, router_b, norm_w, eps=1e-5):
+        g = ep_group
+        self.g, self.layer, self.eps = g, layer, eps
+        self.router_b, self.norm_w = router_b, norm_w
+        self.w64 = torch.empty(g.H * 32, dtype=torch.float64, device=router_w.device)
+        _ok(g.lib, g.lib.gptoss_router_w64(capi.ptr(router_w), g.E, g.H, capi.ptr(self.w64),
+                                           torch.cuda.current_stream().cuda_stream))
+
+    def forward(self, x):
+        g = self.g
+        T = x.shape[0]
+        if T > g.T_max:
+            raise ValueError(f"{T} tokens > T_max {g.T_max}")
+        g.epoch += 1
+        P = capi.ptr
+        _ok(g.lib, g.lib.gptoss_ep_layer_forward(self.layer, P(self.w64), P(self.router_b), P(self.norm_w), self.eps,
+                                                 g.E, g.rank, g.world, P(x), P(x), T, g.T_max, g.peers, g.epoch,
+                                                 torch.cuda.current_stream().cuda_stream))
+        return x
+
+
+def _ok(lib, rc):
+    if rc != 0:
+        raise RuntimeError(lib.gptoss_last_error().decode())

@@ -153,6 +153,34 @@ int gptoss_moe_layer_forward_batched(gptoss_moe_layer* layer, const float* x, fl
 int gptoss_moe_layer_experts_batched(gptoss_moe_layer* layer, const float* h, const int32_t* ids, const float* weights,
                                      float* x_resid, int T, int k, void* stream);
 
+/* [extension] Expert parallelism with dispatch and combine in the kernels over NVLink peer memory (no counterpart in
+ * the reference; SURVEY's "EP layer call taking per-rank token shards").
+ *
+ * Every rank (one GPU each) allocates one zeroed region of gptoss_ep_region_bytes() with gptoss_ep_region_alloc(),
+ * exports it with gptoss_ipc_handle() (64 bytes), receives every other rank's handle (any host channel) and maps
+ * them with gptoss_ipc_open(). gptoss_ep_layer_forward() then runs one MoE layer for this rank's T <= T_max tokens:
+ * routing over all E experts, each (token, slot) row's activation terms written straight into the owning rank's
+ * region, the grouped GEMMs over the rows this rank received (its `layer` holds experts [rank E/world, (rank + 1)
+ * E/world) and the full k), each result row written straight back into its source rank's region, and the combine
+ * into x_resid in slot order: bit-identical to gptoss_moe_layer_forward_batched over all tokens on one GPU.
+ * peers: host array of `world` device addresses (every rank's region as mapped on this device; peers[rank] is the
+ * own region). epoch: the same value on every rank for one layer call, increasing from 1. All ranks must make the
+ * same sequence of calls; a rank that stops makes the others' bounded waits (about a second) fail, reported by
+ * gptoss_ep_status(). router_w64: the router as fp64 [H][32] (gptoss_router_w64). Asynchronous on `stream`. */
+int gptoss_router_w64(const void* W /* bf16 [E,H] */, int E, int H, double* w64, void* stream);
+int gptoss_ep_region_bytes(int E, int k, int H, int I, int world, int T_max, long long* bytes);
+int gptoss_ep_region_alloc(long long bytes, void** region);
+int gptoss_ep_region_free(void* region);
+int gptoss_ipc_handle(void* device_ptr, void* handle_out /* 64 bytes */);
+int gptoss_ipc_open(const void* handle /* 64 bytes */, void** device_ptr);
+int gptoss_ipc_close(void* device_ptr);
+int gptoss_ep_layer_forward(gptoss_moe_layer* layer, const double* router_w64, const float* router_b,
+                            const float* norm_w, float eps, int E, int rank, int world, const float* x,
+                            float* x_resid, int T, int T_max, void* const* peers, unsigned epoch, void* stream);
+/* Synchronizes the device and returns in *code the calling thread's expert-parallel error word (0: none; 20 bad id,
+ * 60-62 a cross-rank wait gave up, 31-36 a pipeline wait gave up). */
+int gptoss_ep_status(int E, int k, int H, int I, int world, int T_max, int* code);
+
 /* [extension] Self-test of the tensor-core block-scaled MMA path: D[128, N] (fp32, row-major) =
  * dequant(a_blocks [128, K/32, 16], a_scales [128, K/32]) . dequant(b_blocks [N, K/32, 16], b_scales [N, K/32])^T
  * computed by one CTA with TMA, tcgen05.cp scale factors and tcgen05.mma kind::mxf4. N % 8 == 0, 8 <= N <= 256,

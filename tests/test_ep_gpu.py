@@ -139,3 +139,75 @@ def test_ep_two_gpus_bit_identical_to_batched_forward(skew):
         out[r::world] = torch.from_numpy(got[r])
     want = _single_gpu_reference(_model(skew), x, "cuda:0")
     assert torch.equal(out, want)
+
+
+# ---------------------------------------------------------------- dispatch and combine over peer memory (one kernel
+# sequence per layer, gptoss_ep_layer_forward)
+def _peer_forward(lib, t, x_shard, rank, world, dev, T_max, calls=2):
+    El = E8 // world
+    ln, W, b = _router(t, dev)
+    ex = _experts(t, dev, rank * El, (rank + 1) * El)
+    L = _layer(lib, ln, W, b, ex, El, 4)
+    g = ep.EpGroup(lib, E8, 4, 2880, 2880, rank, world, T_max)
+    try:
+        m = ep.PeerExpertParallelMoE(g, L, W, b, ln)
+        outs = []
+        for _ in range(calls):                       # several layer calls: epochs advance, regions are reused
+            y = m.forward(x_shard.to(dev).contiguous().clone())
+            torch.cuda.synchronize()
+            outs.append(y.cpu())
+        assert g.status() == 0
+        return outs
+    finally:
+        g.close()
+        lib.gptoss_moe_layer_destroy(L)
+
+
+@pytest.mark.parametrize("skew", [False, True])
+def test_peer_ep_one_gpu_bit_identical_to_batched_forward(skew):
+    lib = capi.load()
+    t = _model(skew)
+    x = synth.tokens(40, seed=13)
+    want = _single_gpu_reference(t, x, "cuda")
+    for got in _peer_forward(lib, t, x, 0, 1, "cuda", T_max=64):
+        assert torch.equal(got, want)
+
+
+def _peer_worker(rank, world, port, skew, x, split, q):
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        lib = capi.load()
+        t = _model(skew)
+        lo, hi = split[rank], split[rank + 1]
+        outs = _peer_forward(lib, t, x[lo:hi], rank, world, dev, T_max=40)
+        q.put((rank, [o.numpy() for o in outs]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("skew,split", [(False, (0, 20, 40)), (True, (0, 13, 40)), (False, (0, 40, 40))])
+def test_peer_ep_two_gpus_bit_identical_to_batched_forward(skew, split):
+    """Two GPUs; uneven token splits, one rank with no tokens, and (skew) one rank that receives no rows."""
+    import torch.multiprocessing as mp
+    world = 2
+    x = synth.tokens(40, seed=14)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, skew, x, split, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    want = _single_gpu_reference(_model(skew), x, "cuda:0")
+    for c in range(2):
+        out = torch.cat([torch.from_numpy(got[r][c]) for r in range(world)])
+        assert torch.equal(out, want)

@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=None,
                     help="prefill: tokens per step (config 2: 2048); ep: tokens per step over all ranks (config 3: 8192)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
+                    help="ep: dispatch/combine inside the kernels over peer memory, or NCCL all-to-all around them")
     ap.add_argument("--moe-impl", type=int, default=None, help="0 = SIMT, 1 = tensor cores (default: library's)")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -533,17 +535,21 @@ def run_ep(args):
         raise SystemExit(f"ep: {T} tokens and {E} experts must split evenly over {ws} ranks")
     Tl, El = T // ws, E // ws
     group = None
+    peer = args.ep_impl == "peer"
+    epg = ep.EpGroup(lib, E, K_TOP, H, I, rank, ws, Tl) if peer else None
     layers, handles = [], []
     for li in range(args.layers):
         ln, W, b = (v.to(dev) for v in synth.ep_router(li))
         ex = synth.ep_experts(li, rank * El, (rank + 1) * El, dev)
-        hdl = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), El, min(K_TOP, El), H, I,
-                                          1.702, 7.0)
+        hdl = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), El,
+                                          K_TOP if peer else min(K_TOP, El), H, I, 1.702, 7.0)
         if not hdl:
             raise RuntimeError(lib.gptoss_last_error().decode())
         handles.append(hdl)
-        layers.append((ex, ln, W, b, ep.ExpertParallelMoE(ep.gpu_route(lib, ln, W, b, E, K_TOP),
-                                                          ep.gpu_compute(lib, hdl), rank, ws, E, K_TOP, H, group)))
+        moe = (ep.PeerExpertParallelMoE(epg, hdl, W, b, ln) if peer else
+               ep.ExpertParallelMoE(ep.gpu_route(lib, ln, W, b, E, K_TOP), ep.gpu_compute(lib, hdl), rank, ws, E,
+                                    K_TOP, H, group))
+        layers.append((ex, ln, W, b, moe))
     g = torch.Generator().manual_seed(0)
     x_all = torch.randn(T, H, generator=g).to(torch.bfloat16).float()
     x_cpu = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
@@ -562,7 +568,13 @@ def run_ep(args):
             L[4].forward(x)
 
     # realised routing of layer 0 over this rank's tokens (rows sent to each rank)
-    h0, ids0, _ = layers[0][4].route(x0)
+    ids0 = torch.empty(Tl, K_TOP, dtype=torch.int32, device=dev)
+    w0 = torch.empty(Tl, K_TOP, device=dev)
+    h0 = torch.empty_like(x0)
+    _, ln0, W0, b0, _ = layers[0]
+    if lib.gptoss_moe_route_batched(P(W0), P(b0), P(x0), P(ln0), 1e-5, E, H, K_TOP, Tl, P(h0), P(ids0), P(w0),
+                                    stream.cuda_stream) != 0:
+        raise RuntimeError(lib.gptoss_last_error().decode())
     rows_to = torch.bincount(ids0.flatten().long() // El, minlength=ws)
     if ws > 1:
         torch.distributed.all_reduce(rows_to)
@@ -630,8 +642,13 @@ def run_ep(args):
     peak_fp4 = 4.0 * bf16 if bf16 else 4.0 * 1400.0
     flops = prefill_flops(T) * args.layers
     achieved = flops / ws / step_s / 1e12
+    ep_status = epg.status() if peer else 0
+    if peer:
+        epg.close()
     for hdl in handles:
         lib.gptoss_moe_layer_destroy(hdl)
+    if ep_status:
+        raise RuntimeError(f"expert-parallel device check failed (code {ep_status})")
     if rank == 0:
         line = {
             "metric": EP_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
@@ -641,7 +658,9 @@ def run_ep(args):
             "config": {"workload": "expert-parallel prefill (configs[3])", "tokens": T, "tokens_per_rank": Tl,
                        "layers": args.layers, "experts": E, "experts_per_rank": El, "top_k": K_TOP, "zipf_s": 1.2,
                        "layer0_rows_per_rank": rows_to, "parallelism": f"ep{ws} (experts) x dp{ws} (tokens)",
-                       "dispatch": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (one rank)",
+                       "dispatch": ("inside the kernels: A terms and result rows stored into peer memory over "
+                                    "NVLink (gptoss_ep_layer_forward)" if peer else
+                                    "torch.distributed all_to_all_single (NCCL)") if ws > 1 else "none (one rank)",
                        "l2": "423 MB of experts per layer, larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "whole expert-parallel step per GPU (grouped tcgen05 GEMMs, "
                                                       "router, all-to-all)",
@@ -650,8 +669,11 @@ def run_ep(args):
                          "frac": achieved / peak_fp4, "algorithmic_flops_per_step": flops, "traffic": None},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
-                    "api": "ExpertParallelMoE.forward per layer; host tokens copied in and out every step"},
-            "gpu_launches": args.steps * args.layers * 8,  # w64, router, permute, 2 x (quantize, GEMM), combine
+                    "api": ("PeerExpertParallelMoE" if peer else "ExpertParallelMoE") +
+                           ".forward per layer; host tokens copied in and out every step"},
+            # peer: router, counts, permute, quantize, barrier, GEMM, quantize, GEMM, barrier, combine;
+            # nccl: w64, router, permute, 2 x (quantize, GEMM), combine
+            "gpu_launches": args.steps * args.layers * (10 if peer else 8),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line))

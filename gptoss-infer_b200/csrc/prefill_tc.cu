@@ -65,7 +65,7 @@ __global__ void router_w64_kernel(const __nv_bfloat16* __restrict__ W, int E, in
 
 // 8 tokens per CTA, 512 threads: RMSNorm (warp w < 8 on token w), h in shared memory as fp64, then thread
 // (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp, kp + 16, ... for the 8 tokens (the weight loads of
-// four k issued ahead of their FMAs); the 16 partial sums are added in order and warp w picks token w's top k on
+// twelve k issued ahead of their FMAs); the 16 partial sums are added in order and warp w picks token w's top k on
 // order-preserving integer keys of the fp64 logits.
 constexpr int kRtParts = 16;
 __global__ void __launch_bounds__(512) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
@@ -106,15 +106,16 @@ __global__ void __launch_bounds__(512) router_batched_kernel(const double* __res
     double acc[kRtTok];
 #pragma unroll
     for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = 0.0;
-    for (int kk0 = kp; kk0 < H; kk0 += 4 * kRtParts) {
-        double wk[4];
+    constexpr int kAhead = 12;                               // weight loads in flight per thread
+    for (int kk0 = kp; kk0 < H; kk0 += kAhead * kRtParts) {
+        double wk[kAhead];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kAhead; ++u) {
             const int kk = kk0 + u * kRtParts;
             wk[u] = kk < H ? W64[size_t(kk) * 32 + e] : 0.0;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kAhead; ++u) {
             const int kk = kk0 + u * kRtParts;
             if (kk < H) {
 #pragma unroll

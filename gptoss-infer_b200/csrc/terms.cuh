@@ -150,15 +150,6 @@ __device__ __forceinline__ uint32_t e2m1_code(float q) {
 
 constexpr int kActiveTerms = 10;              // terms quantize_block_terms_fixed computes; the rest are zero
 
-// Same image format and first term as quantize_block_terms_cvt, with the later terms' scales fixed instead of
-// taken from each residual's maximum: term 0 keeps the block's maximum within 6 * 2^k0, so its rounding error is at
-// most 2^k0 (the e2m1 grid step is 2 between 4 and 6); term 1 uses k0 - 2 (|y| <= 4), and from then on every
-// rounding error is at most half a grid step of 1, i.e. 2^(k-1), so k drops by 3 per term and |y| stays <= 4.
-// After n terms the remainder is at most 2^(k0 - 3n + 3) (the subtractions are exact): below 2^-24 of the block's
-// maximum after 8 terms and 2^-27 after 10. NT term rows are written (image row stride 128 bytes, NT rows per stage),
-// the first min(NT, kActiveTerms) computed and the rest zero. There is no per-term maximum (no lane shuffles), and
-// the rounding is round_e2m1: each term is a short chain of full-rate fp32 operations per element. Scales below
-// 2^-127 are clamped there (the terms of such tiny remainders are then merely close, never NaN).
 // First scale exponent of the fixed schedule for a block whose largest magnitude is amax: the block maximum fits
 // within 6 * 2^k (k = floor(log2 amax) - 2, or - 1 when the mantissa is above 1.5), clamped to E8M0's range.
 __device__ __forceinline__ int fixed_schedule_k0(float amax) {
@@ -171,37 +162,6 @@ __device__ __forceinline__ int fixed_schedule_k0(float amax) {
         k = max(-127, min(127, k));
     }
     return k;
-}
-
-// The four-lanes-per-block form (lane `sub` of the block's 4 holds elements 8 sub .. 8 sub + 7) with the fixed
-// schedule: emit(t, word, scale) receives term t's 8 codes of this lane as one 32-bit word (element 8 sub + i in
-// bits 4i .. 4i + 3) and the block's E8M0 scale byte. v is consumed.
-template <int NT, class Emit>
-__device__ __forceinline__ void quantize_block_terms_lanes4(float (&v)[8], Emit&& emit) {
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
-    int k = fixed_schedule_k0(amax);
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        uint32_t word = 0, scale = 0;
-        if (t < kActiveTerms) {
-            const int kc = max(-127, k);
-            const float inv = exp2i_exact(-kc), sc = exp2i_exact(kc);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t code;
-                const float qv = round_e2m1_code(v[i] * inv, code);
-                v[i] = fmaf(-qv, sc, v[i]);
-                word |= code << (4 * i);
-            }
-            scale = uint32_t(kc + 127);
-            k -= t == 0 ? 2 : 3;
-        }
-        emit(t, word, scale);
-    }
 }
 
 // Eight terms per 32-value block from one round and an integer split (the prefill path's A operand), four lanes per
@@ -251,6 +211,15 @@ __device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8]
     }
 }
 
+// Same image format and first term as quantize_block_terms_cvt, with the later terms' scales fixed instead of
+// taken from each residual's maximum: term 0 keeps the block's maximum within 6 * 2^k0, so its rounding error is at
+// most 2^k0 (the e2m1 grid step is 2 between 4 and 6); term 1 uses k0 - 2 (|y| <= 4), and from then on every
+// rounding error is at most half a grid step of 1, i.e. 2^(k-1), so k drops by 3 per term and |y| stays <= 4.
+// After n terms the remainder is at most 2^(k0 - 3n + 3) (the subtractions are exact): below 2^-24 of the block's
+// maximum after 8 terms and 2^-27 after 10. NT term rows are written (image row stride 128 bytes, NT rows per stage),
+// the first min(NT, kActiveTerms) computed and the rest zero. There is no per-term maximum (no lane shuffles), and
+// the rounding is round_e2m1: each term is a short chain of full-rate fp32 operations per element. Scales below
+// 2^-127 are clamped there (the terms of such tiny remainders are then merely close, never NaN).
 template <int NT>
 __device__ __forceinline__ void quantize_block_terms_fixed_n(float (&v)[8], uint8_t* img_stage, int q,
                                                              uint8_t* sf_chunk, int kb, int sub, bool active) {

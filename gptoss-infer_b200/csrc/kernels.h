@@ -43,8 +43,8 @@ void launch_moe_decode_simt(const uint8_t* gu_blocks, const uint8_t* gu_scales, 
 
 // Scale-factor repack: raw E8M0 bytes [mats][rows][G] -> tcgen05 chunks of 512 bytes, chunk byte
 // (r % 32) * 16 + (r / 32) * 4 + kb for row r (within its 128 rows) and k-block kb; zero padded. tile_rows = 128:
-// [mats][ceil(rows/128)][ceil(G/4)][512]; tile_rows = 256: [mats][ceil(rows/256)][ceil(G/4)][2][512] (the two
-// 128-row halves of a 256-row tile side by side for each K chunk of 128).
+// [mats][ceil(rows/128)][ceil(G/4)][512]; tile_rows = 192 or 256: [mats][ceil(rows/tile_rows)][ceil(G/4)][2][512]
+// (the tile's two 128-row parts side by side for each K chunk of 128; a 192-row tile's second part holds 64 rows).
 size_t sf_repacked_bytes(long long mats, int rows, int G, int tile_rows = 128);
 // With ids != nullptr, output matrix m is gathered from raw matrix ids[m] (m < mats).
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,

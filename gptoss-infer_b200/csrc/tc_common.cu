@@ -78,21 +78,22 @@ namespace {
 // raw [mats][rows][G] E8M0 bytes -> [mats][RT][KT][halves][512] tcgen05 chunks (tiles of 128 * halves rows,
 // RT = ceil(rows / tile), KT = ceil(G/4)), zero padded. One thread per output word of 4 bytes (one row's 4 k-blocks).
 __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, long long mats, int rows,
-                                 int G, int RT, int KT, int halves, const int* __restrict__ ids) {
+                                 int G, int RT, int KT, int halves, int tile_rows, const int* __restrict__ ids) {
     const long long words = mats * RT * KT * halves * 128;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
          i += (long long)gridDim.x * blockDim.x) {
         const int w = int(i % 128);                  // word within the chunk: (row % 32) * 4 + row / 32
         long long c = i / 128;
-        const int h = int(c % halves);               // 128-row half of a 256-row tile
+        const int h = int(c % halves);               // 128-row part of the tile (the last one may be partial)
         c /= halves;
         const int kt = int(c % KT);
         c /= KT;
         const int rt = int(c % RT);
         const long long mat = ids ? (long long)ids[c / RT] : c / RT;
-        const int row = (rt * halves + h) * 128 + (w & 3) * 32 + (w >> 2);
+        const int in_tile = h * 128 + (w & 3) * 32 + (w >> 2);
+        const int row = rt * tile_rows + in_tile;
         uint32_t v = 0;
-        if (row < rows) {
+        if (in_tile < tile_rows && row < rows) {
             const uint8_t* src = raw + (mat * rows + row) * G;
 #pragma unroll
             for (int kb = 0; kb < 4; ++kb) {
@@ -106,17 +107,17 @@ __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __res
 }  // namespace
 
 size_t sf_repacked_bytes(long long mats, int rows, int G, int tile_rows) {
-    return size_t(mats) * size_t((rows + tile_rows - 1) / tile_rows) * size_t((G + 3) / 4) * size_t(tile_rows / 128) *
-           512;
+    return size_t(mats) * size_t((rows + tile_rows - 1) / tile_rows) * size_t((G + 3) / 4) *
+           size_t((tile_rows + 127) / 128) * 512;
 }
 
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
                       const int* ids, int tile_rows) {
-    require(tile_rows == 128 || tile_rows == 256, "repack_sf: tiles of 128 or 256 rows");
-    const int halves = tile_rows / 128, RT = (rows + tile_rows - 1) / tile_rows, KT = (G + 3) / 4;
+    require(tile_rows == 128 || tile_rows == 192 || tile_rows == 256, "repack_sf: tiles of 128, 192 or 256 rows");
+    const int halves = (tile_rows + 127) / 128, RT = (rows + tile_rows - 1) / tile_rows, KT = (G + 3) / 4;
     const long long words = mats * RT * KT * halves * 128;
     const int grid = int(std::min<long long>((words + 255) / 256, num_sms() * 8LL));
-    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, halves, ids);
+    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, halves, tile_rows, ids);
     check_launch("repack_sf");
 }
 

@@ -17,7 +17,8 @@ DEV = "cuda"
 P = capi.ptr
 
 
-@pytest.mark.parametrize("N,K", [(8, 64), (8, 576), (16, 1024), (64, 512), (128, 256), (256, 256), (24, 320)])
+@pytest.mark.parametrize("N,K", [(8, 64), (8, 576), (16, 1024), (64, 512), (128, 256), (256, 256), (24, 320),
+                                 (192, 512)])
 def test_mxf4_gemm_selftest(N, K):
     lib = capi.load()
     g = torch.Generator().manual_seed(N * 1000 + K)

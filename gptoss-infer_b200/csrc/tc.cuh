@@ -62,13 +62,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-suspending probe of a phase (mbarrier.test_wait): cheaper than try_wait when the phase has already completed.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Every wait is bounded: mbarrier.try_wait suspends the thread in hardware until the phase completes or a short
 // system-defined window passes, so the loop needs no sleep of its own (one would only delay the wake-up); after
 // kSpinLimit unsuccessful tries (well over a second) the wait gives up, records `where` in *err (first error wins)
-// and returns false; callers then skip the dependent work, drain and exit.
+// and returns false; callers then skip the dependent work, drain and exit. A phase that has already completed is
+// caught by one test_wait first.
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int where) {
+    if (mbar_test_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < kSpinLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     if (err) atomicCAS(err, 0, where);

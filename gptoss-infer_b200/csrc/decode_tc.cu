@@ -105,8 +105,11 @@ struct Job {
 // known, 1 phase 0 done, 89 producer start, 2+i producer issues stage i, 126 scale copies issued, 127+p x terms pass
 // p, 80 small operands in shared memory, 34+i MMA warp sees stage i landed, 96+i its MMAs issued, 66+g epilogue
 // finished segment g, 81 grid barrier passed, 83 down's A terms in shared memory, 82 end.
+// Tracing is a compile-time choice: the untraced kernel carries no stamp code at all (branches over it in the
+// single-thread issue loops measurably slowed them).
+template <bool kTrace>
 __device__ __forceinline__ void stamp(const Job& j, int slot) {
-    if (j.trace) j.trace[size_t(blockIdx.x) * kTraceSlots + slot] = clock64();
+    if constexpr (kTrace) j.trace[size_t(blockIdx.x) * kTraceSlots + slot] = clock64();
 }
 
 __device__ __forceinline__ bool epi_all(bool p) {            // AND over the 128 epilogue threads (barrier 1)
@@ -154,6 +157,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         : "r"(taddr));
 }
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_constant__ CUtensorMap tm_gu,
                                                                 const __grid_constant__ CUtensorMap tm_dn,
                                                                 const __grid_constant__ Job j) {
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, nc = gridDim.x;
-    if (tid == 0) stamp(j, 0);
+    if (tid == 0) stamp<kTrace>(j, 0);
     // this CTA's slice of the router weights: thread (expert = lane, o = warp) takes chunks cs0 + o, cs0 + o + 6, ...
     // of 8 weights; the first is loaded before anything else (it does not depend on x)
     const int H8 = j.H >> 3;
@@ -229,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     pdl_launch_dependents();
     pdl_wait();
     if (tid == 0 && s_n > cap) atomicCAS(j.err, 0, 100);    // host sized the stage list too small
-    if (tid == 0) stamp(j, 123);
+    if (tid == 0) stamp<kTrace>(j, 123);
 #pragma unroll
     for (int r = 0; r < kMaxX4; ++r) {
         const int i = (tid + r * kThreads) * 4;
@@ -244,9 +248,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             ss = fmaf(xv[r].x, xv[r].x, fmaf(xv[r].y, xv[r].y, fmaf(xv[r].z, xv[r].z, fmaf(xv[r].w, xv[r].w, ss))));
         ss = warp_sum(ss);
         if (lane == 0) aval[warp] = ss;
-        if (tid == 0) stamp(j, 124);
+        if (tid == 0) stamp<kTrace>(j, 124);
         __syncthreads();
-        if (tid == 0) stamp(j, 125);
+        if (tid == 0) stamp<kTrace>(j, 125);
         float rn = 1.f;
         if (j.norm_w) {
             float tot = 0.f;
@@ -265,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             }
         }
         __syncthreads();
-        if (tid == 0) stamp(j, 84);
+        if (tid == 0) stamp<kTrace>(j, 84);
         double acc = 0.0;
         if (j.router_w) {
             for (int cc = cs0 + warp; cc < cs1; cc += kThreads / 32) {
@@ -304,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             __syncwarp();
             if (lane == 0) {
                 atomicAdd(&j.gbar[2], 1u);
-                stamp(j, 85);
+                stamp<kTrace>(j, 85);
             }
             // every CTA's partial sums and x blocks published (bounded wait; the launch is cooperative)
             bool done = false;
@@ -315,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             if (lane == 0) {
                 if (!done) atomicCAS(j.err, 0, 10);
                 cnts[2] = done;
-                stamp(j, 86);
+                stamp<kTrace>(j, 86);
             }
         }
         __syncthreads();
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             }
             red[warp * 32 + lane] = t;
             __syncthreads();
-            if (tid == 0) stamp(j, 87);
+            if (tid == 0) stamp<kTrace>(j, 87);
             if (warp == 0) {
                 // top k on order-preserving 64-bit keys of the fp64 logits (integer warp reductions; ties to the
                 // lower id; NaN, picked experts and lanes >= E get key 0 and never win while a real logit is left)
@@ -349,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(v));
                 unsigned long long key = (bits >> 63) ? ~bits : (bits | (1ull << 63));
                 if ((bits & 0x7FFFFFFFFFFFFFFFull) > 0x7FF0000000000000ull || lane >= j.E) key = 0;   // NaN / unused
-                if (lane == 0) stamp(j, 120);
+                if (lane == 0) stamp<kTrace>(j, 120);
                 unsigned id = lane < j.E ? unsigned(lane) : 32u + lane;
                 float sel = -INFINITY;
                 int sel_id = 0;
@@ -362,11 +366,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                     if (lane == q) { sel = float(wv); sel_id = int(win); }
                     if (id == win) { key = 0; id = 32u + lane; }
                 }
-                if (lane == 0) stamp(j, 121);
+                if (lane == 0) stamp<kTrace>(j, 121);
                 const float top = __shfl_sync(kFull, sel, 0);
                 const float pz = lane < j.k ? expf(sel - top) : 0.f;
                 const float sum = warp_sum(pz);
-                if (lane == 0) stamp(j, 122);
+                if (lane == 0) stamp<kTrace>(j, 122);
                 if (lane < j.k) {
                     ids_s[lane] = sel_id;
                     w_s[lane] = pz / sum;
@@ -377,13 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             ids_s[tid] = j.ids_in[tid];
             w_s[tid] = j.w_in[tid];
         }
-        if (tid == 0) stamp(j, 88);
+        if (tid == 0) stamp<kTrace>(j, 88);
     }
     tc::fence_proxy_async_smem();             // h's shared memory becomes the TMA ring from here on
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
-    if (tid == 0) stamp(j, 1);
+    if (tid == 0) stamp<kTrace>(j, 1);
     const uint32_t tmem = *holder;
 
     auto part_of = [&](const Stage& st) -> const Part& { return st.mode == sk::kGateUp ? j.gu : j.dn; };
@@ -391,14 +395,24 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     if (warp == 0) {
         // ---------------------------------------------------------------- producer (converged warp, elected lane)
         if (tc::elect_one()) {
-            stamp(j, 89);
+            stamp<kTrace>(j, 89);
             tc::prefetch_tmap(&tm_gu);
             tc::prefetch_tmap(&tm_dn);
         }
         __syncwarp();
-        auto wait_slot = [&](int it) -> bool {                // stage it - NS released its slot
-            const int p = it - NS;
-            return __all_sync(kFull, tc::mbar_wait(&emptyB[p % NS], uint32_t(p / NS) & 1u, j.err, 1));
+        // Ring position of stage it: slot = it % NS, phase = (it / NS) & 1, kept as counters (a division by the
+        // run-time ring depth per stage is measurable on a single issuing thread). Stage it - NS, which used the slot
+        // in the previous phase, must have released it.
+        int slot = 0;
+        uint32_t ph = 0;
+        auto next_slot = [&]() {
+            if (++slot == NS) {
+                slot = 0;
+                ph ^= 1u;
+            }
+        };
+        auto wait_slot = [&]() -> bool {
+            return __all_sync(kFull, tc::mbar_wait(&emptyB[slot], ph ^ 1u, j.err, 1));
         };
         // The tensor map is a compile-time operand of each loop: selecting it at run time made every TMA issue wait
         // for a descriptor fetch.
@@ -409,30 +423,30 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             const int mat = j.sf_by_slot ? int(st.s) : ids_s[st.s];
             return base + ((size_t(mat) * p.RT + rt) * p.KT + st.ku0 / 2) * 1024;
         };
-        for (int it = 0; it < ngu && ok; ++it) {
-            if (it >= NS) ok = wait_slot(it);
+        for (int it = 0; it < ngu && ok; ++it, next_slot()) {
+            if (it >= NS) ok = wait_slot();
             if (ok && tc::elect_one()) {
-                if (it < 32) stamp(j, 2 + it);
+                if (it < 32) stamp<kTrace>(j, 2 + it);
                 const Stage& st = stages[it];
-                const int rt = st.tile % j.gu.RT;
+                const int rt = st.tile - st.s * j.gu.RT;     // gate/up tiles are numbered slot * RT + row tile
                 const uint32_t sb = uint32_t(sk::nkt_of(st)) * 1024u;
-                uint8_t* dst = ring + (it % NS) * kSlot;
-                tc::mbar_arrive_expect_tx(&fullB[it % NS], kB + sb);
-                tc::tma_load_3d(dst, &tm_gu, (st.ku0 / 4) * 128, rt * kRows, ids_s[st.s], &fullB[it % NS]);
-                tc::bulk_g2s(dst + kB, scales_of(st, j.gu, j.sf_gu, rt), sb, &fullB[it % NS]);
+                uint8_t* dst = ring + slot * kSlot;
+                tc::mbar_arrive_expect_tx(&fullB[slot], kB + sb);
+                tc::tma_load_3d(dst, &tm_gu, (st.ku0 / 4) * 128, rt * kRows, ids_s[st.s], &fullB[slot]);
+                tc::bulk_g2s(dst + kB, scales_of(st, j.gu, j.sf_gu, rt), sb, &fullB[slot]);
             }
             __syncwarp();
         }
-        for (int it = ngu; it < nst && ok; ++it) {
-            if (it >= NS) ok = wait_slot(it);
+        for (int it = ngu; it < nst && ok; ++it, next_slot()) {
+            if (it >= NS) ok = wait_slot();
             if (ok && tc::elect_one()) {
-                if (it < 32) stamp(j, 2 + it);
+                if (it < 32) stamp<kTrace>(j, 2 + it);
                 const Stage& st = stages[it];
                 const uint32_t sb = uint32_t(sk::nkt_of(st)) * 1024u;
-                uint8_t* dst = ring + (it % NS) * kSlot;
-                tc::mbar_arrive_expect_tx(&fullB[it % NS], kB + sb);
-                tc::tma_load_3d(dst, &tm_dn, (st.ku0 / 4) * 128, st.tile * kRows, ids_s[st.s], &fullB[it % NS]);
-                tc::bulk_g2s(dst + kB, scales_of(st, j.dn, j.sf_dn, st.tile), sb, &fullB[it % NS]);
+                uint8_t* dst = ring + slot * kSlot;
+                tc::mbar_arrive_expect_tx(&fullB[slot], kB + sb);
+                tc::tma_load_3d(dst, &tm_dn, (st.ku0 / 4) * 128, st.tile * kRows, ids_s[st.s], &fullB[slot]);
+                tc::bulk_g2s(dst + kB, scales_of(st, j.dn, j.sf_dn, st.tile), sb, &fullB[slot]);
             }
             __syncwarp();
         }
@@ -445,54 +459,88 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         // one commit.
         if (tc::elect_one()) {
             bool ok = nst == 0 || tc::mbar_wait(&fullS[0], 0, j.err, 6);
+            // Gate/up stages: x's scale chunks (first use of each K chunk), the weight scales, 4 MMAs, commits.
             unsigned long long x_sf_done = 0;                // x's scale chunks in TMEM
-            for (int it = 0; it < nst && ok; ++it) {
+            // ring slot, its phase and the TMEM scale slot of stage it (it % NS, (it / NS) & 1, it % NSF) as counters
+            int slot = 0, f = 0;
+            uint32_t ph = 0;
+            auto advance = [&]() {
+                if (++slot == NS) {
+                    slot = 0;
+                    ph ^= 1u;
+                }
+                if (++f == NSF) f = 0;
+            };
+            for (int it = 0; it < ngu && ok; ++it, advance()) {
                 const Stage& st = stages[it];
-                const int slot = it % NS, ph = (it / NS) & 1, f = it % NSF;
                 const int kt0 = st.ku0 / 2, nkt = sk::nkt_of(st);
-                const bool gu = st.mode == sk::kGateUp;
-                if (it >= ngu) ok = tc::mbar_wait(&fullD[it - ngu], 0, j.err, 9);   // this stage's A terms
-                if (!ok) break;
                 tc::tc_fence_after();
-                if (gu) {
-                    for (int q = 0; q < nkt; ++q) {
-                        const int kt = kt0 + q;
-                        if (!((x_sf_done >> kt) & 1ull)) {
-                            tc::tmem_cp_sf(tmem + kColX + 4 * kt, tc::desc_sf_chunk8(tc::smem_u32(xSF + kt * kSF8)));
-                            x_sf_done |= 1ull << kt;
-                        }
+                for (int q = 0; q < nkt; ++q) {
+                    const int kt = kt0 + q;
+                    if (!((x_sf_done >> kt) & 1ull)) {
+                        tc::tmem_cp_sf(tmem + kColX + 4 * kt, tc::desc_sf_chunk8(tc::smem_u32(xSF + kt * kSF8)));
+                        x_sf_done |= 1ull << kt;
                     }
-                } else {
-                    for (int q = 0; q < nkt; ++q)
-                        tc::tmem_cp_sf(tmem + j.L.colDSF + 8 * f + 4 * q,
-                                       tc::desc_sf_chunk8(tc::smem_u32(dSF + (it - ngu) * 2 * kSF8 + q * kSF8)));
                 }
                 // one accumulator: a segment's first MMA waits until the previous segment has been read out
                 if (st.first && st.seg >= 1) ok = tc::mbar_wait(accE, uint32_t(st.seg - 1) & 1u, j.err, 2);
                 ok = ok && tc::mbar_wait(&fullB[slot], ph, j.err, 3);
                 if (!ok) break;
                 tc::tc_fence_after();
-                if (it < 32) stamp(j, 34 + it);
+                if (it < 32) stamp<kTrace>(j, 34 + it);
                 const uint8_t* wslot = ring + slot * kSlot;
                 for (int q = 0; q < nkt; ++q)
                     for (int h = 0; h < 2; ++h)
                         tc::tmem_cp_sf(tmem + j.L.colSFB + 16 * f + 8 * q + 4 * h,
                                        tc::desc_sf_chunk(tc::smem_u32(wslot + kB + (2 * q + h) * 512)));
-                const uint8_t* ast = gu ? xA + (st.ku0 / 4) * kA : dA + (it - ngu) * kA;
+                const uint8_t* ast = xA + (st.ku0 / 4) * kA;
+                for (int u = 0; u < st.nu; ++u) {
+                    const int ku = st.ku0 + u;
+                    const uint32_t sf_id = 2u * (ku & 1);
+                    tc::mma_mxf4(tmem, tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32)),
+                                 tc::desc_sw128(tc::smem_u32(wslot + u * 32)), tc::idesc_mxf4(128, kRows, sf_id, sf_id),
+                                 (tmem + kColX + 4 * (ku / 2)) | (sf_id << 30),
+                                 (tmem + j.L.colSFB + 16 * f + 8 * (ku / 2 - kt0)) | (sf_id << 30),
+                                 !(st.first && u == 0));
+                }
+                tc::mma_commit(&emptyB[slot]);
+                if (st.last) tc::mma_commit(accF);
+                if (it < 32) stamp<kTrace>(j, 96 + it);
+            }
+            // Down stages: wait for the stage's A terms, their scales and the weight scales, 4 MMAs, commits.
+            for (int it = ngu; it < nst && ok; ++it, advance()) {
+                const Stage& st = stages[it];
+                const int d = it - ngu;
+                const int kt0 = st.ku0 / 2, nkt = sk::nkt_of(st);
+                ok = tc::mbar_wait(&fullD[d], 0, j.err, 9);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int q = 0; q < nkt; ++q)
+                    tc::tmem_cp_sf(tmem + j.L.colDSF + 8 * f + 4 * q,
+                                   tc::desc_sf_chunk8(tc::smem_u32(dSF + d * 2 * kSF8 + q * kSF8)));
+                if (st.first && st.seg >= 1) ok = tc::mbar_wait(accE, uint32_t(st.seg - 1) & 1u, j.err, 2);
+                ok = ok && tc::mbar_wait(&fullB[slot], ph, j.err, 3);
+                if (!ok) break;
+                tc::tc_fence_after();
+                if (it < 32) stamp<kTrace>(j, 34 + it);
+                const uint8_t* wslot = ring + slot * kSlot;
+                for (int q = 0; q < nkt; ++q)
+                    for (int h = 0; h < 2; ++h)
+                        tc::tmem_cp_sf(tmem + j.L.colSFB + 16 * f + 8 * q + 4 * h,
+                                       tc::desc_sf_chunk(tc::smem_u32(wslot + kB + (2 * q + h) * 512)));
+                const uint8_t* ast = dA + d * kA;
                 for (int u = 0; u < st.nu; ++u) {
                     const int ku = st.ku0 + u;
                     const uint32_t sf_id = 2u * (ku & 1);
                     const int q = ku / 2 - kt0;
-                    const uint64_t ad = tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32));
-                    const uint64_t bd = tc::desc_sw128(tc::smem_u32(wslot + u * 32));
-                    const uint32_t sfa = gu ? tmem + kColX + 4 * (ku / 2) : tmem + j.L.colDSF + 8 * f + 4 * q;
-                    const uint32_t sfbc = tmem + j.L.colSFB + 16 * f + 8 * q;
-                    tc::mma_mxf4(tmem, ad, bd, tc::idesc_mxf4(128, kRows, sf_id, sf_id), sfa | (sf_id << 30),
-                                 sfbc | (sf_id << 30), !(st.first && u == 0));
+                    tc::mma_mxf4(tmem, tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32)),
+                                 tc::desc_sw128(tc::smem_u32(wslot + u * 32)), tc::idesc_mxf4(128, kRows, sf_id, sf_id),
+                                 (tmem + j.L.colDSF + 8 * f + 4 * q) | (sf_id << 30),
+                                 (tmem + j.L.colSFB + 16 * f + 8 * q) | (sf_id << 30), !(st.first && u == 0));
                 }
                 tc::mma_commit(&emptyB[slot]);
                 if (st.last) tc::mma_commit(accF);
-                if (it < 32) stamp(j, 96 + it);
+                if (it < 32) stamp<kTrace>(j, 96 + it);
             }
         }
         __syncwarp();
@@ -514,11 +562,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 if (x < n1) tc::cp_async16(xA + 16 * x, j.xq_img + 16 * x);
                 else tc::cp_async16(xSF + 16 * (x - n1), j.xq_sf + 16 * (x - n1));
             }
-            if (et == 0) stamp(j, 126);
+            if (et == 0) stamp<kTrace>(j, 126);
             tc::cp_async_wait_all();
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&fullS[0]);
-            if (et == 0) stamp(j, 80);
+            if (et == 0) stamp<kTrace>(j, 80);
         }
         // After the CTA's last gate/up epilogue: count it on the grid barrier; once every CTA has finished gate/up
         // (bounded wait), one thread loads each down stage's A terms and scales with two bulk copies completing on
@@ -527,11 +575,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             epi_sync();                             // every thread's down-A terms and partial sums are written
             if (et != 0) return;
             red_add_release(&j.gbar[0], 1u);        // ... and released to the CTAs that acquire the count
-            stamp(j, 131);
+            stamp<kTrace>(j, 131);
             if (ngu == nst) return;
             bool done = false;
             for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) done = ld_acquire(&j.gbar[0]) >= unsigned(nc);
-            stamp(j, 81);
+            stamp<kTrace>(j, 81);
             if (done) asm volatile("fence.proxy.async.global;" ::: "memory");   // generic writes -> bulk reads
             else atomicCAS(j.err, 0, 8);
             for (int i = ngu; i < nst; ++i) {
@@ -547,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 tc::bulk_g2s(dSF + (i - ngu) * 2 * kSF8, j.aq_sf + (size_t(st.s) * j.dn.KT + st.ku0 / 2) * kSF8, sfb8,
                              &fullD[i - ngu]);
             }
-            stamp(j, 83);
+            stamp<kTrace>(j, 83);
         };
         if (ngu == 0) load_down_stages();
         bool ok = true;
@@ -557,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             // the biases of this thread's two rows, loaded before the accumulator is waited for
             float b0 = 0.f, b1 = 0.f;
             if (st.mode == sk::kGateUp) {
-                const int rt = st.tile % j.gu.RT;
+                const int rt = st.tile - st.s * j.gu.RT;
                 const float* bb = j.gu_bias + size_t(ids_s[st.tile / j.gu.RT]) * 2 * j.I + rt * kRows;
                 if (rt * kRows + et < 2 * j.I) b0 = __ldg(bb + et);
                 if (rt * kRows + et + 128 < 2 * j.I) b1 = __ldg(bb + et + 128);
@@ -599,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 if (lane == 0) tc::mbar_arrive(accE);
             }
             ok = epi_all(ok);                        // uniform over the 4 epilogue warps; red_s written
-            if (et == 0 && st.seg < 14) stamp(j, 66 + st.seg);
+            if (et == 0 && st.seg < 14) stamp<kTrace>(j, 66 + st.seg);
             float v0 = 0.f, v1 = 0.f;                // rows et and et + 128 of the tile
             if (ok) {
 #pragma unroll
@@ -643,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                         epi_sync();
                         mine = cnts[2] != 0;
                     }
-                    if (et == 0 && st.seg < 8) stamp(j, 132 + st.seg);
+                    if (et == 0 && st.seg < 8) stamp<kTrace>(j, 132 + st.seg);
                     if (mine) {
                         // own sums first, then the other contributors in CTA order; the loads issue together
                         const float* pb = p.partial + size_t(t) * sk::kMaxContrib * kRows;
@@ -686,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                                                         gb * 32 < j.I);
                     }
 
-                    if (et == 0 && st.seg < 8) stamp(j, 140 + st.seg);
+                    if (et == 0 && st.seg < 8) stamp<kTrace>(j, 140 + st.seg);
                 } else if (mine) {
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
@@ -702,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     tc::tc_fence_before();
     __syncthreads();
     if (tid == 0) {
-        stamp(j, 82);
+        stamp<kTrace>(j, 82);
         __threadfence();
         if (atomicAdd(&j.gbar[1], 1u) == unsigned(nc - 1)) {   // last CTA out resets the counters and flags
             j.gbar[0] = 0;
@@ -836,7 +884,8 @@ void set_fused_smem(int bytes) {
     std::lock_guard<std::mutex> lock(mu);
     if (bytes > current[dev]) {
         require(bytes <= 227 * 1024, "moe (tc): shared-memory plan exceeds 227 KB");
-        GPT_CHECK(cudaFuncSetAttribute(fz::moe_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        GPT_CHECK(cudaFuncSetAttribute(fz::moe_fused_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        GPT_CHECK(cudaFuncSetAttribute(fz::moe_fused_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
         current[dev] = bytes;
     }
 }
@@ -936,12 +985,13 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     int dev = 0;
     GPT_CHECK(cudaGetDevice(&dev));
     cfg.numAttrs = dev < 64 && pdl_ok[dev] >= 0 ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_fused_kernel, *a.tmap_gu, *a.tmap_dn, j);
+    auto kernel = a.trace ? moe_fused_kernel<true> : moe_fused_kernel<false>;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, *a.tmap_gu, *a.tmap_dn, j);
     if (e != cudaSuccess && cfg.numAttrs == 2 && dev < 64 && pdl_ok[dev] == 0) {
         (void)cudaGetLastError();
         pdl_ok[dev] = -1;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, moe_fused_kernel, *a.tmap_gu, *a.tmap_dn, j);
+        e = cudaLaunchKernelEx(&cfg, kernel, *a.tmap_gu, *a.tmap_dn, j);
     } else if (e == cudaSuccess && cfg.numAttrs == 2 && dev < 64) {
         pdl_ok[dev] = 1;
     }

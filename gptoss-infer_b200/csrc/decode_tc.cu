@@ -18,13 +18,13 @@
 //   2. Down stream-K GEMV over K' = k * I: the k experts' rows form one long GEMV because A carries the gate
 //      weights; the CTA finishing a tile adds sum_slot w b2 and the residual.
 // Roles: warp 0 streams the weights (TMA, gate/up and down through one ring, so down's weights arrive while the grid
-// finishes gate/up); warp 1 issues the tcgen05 operations (per stage: the weight scales into a ring of TMEM columns,
-// x's scales the first time they are needed, 4 MMAs, one commit); warps 2-5 split h into x's terms in shared memory
-// and load the weight scale chunks with asynchronous 16-byte copies, run the tile epilogues (the accumulator is read
-// out by the warp that owns TMEM lanes 0-31), and after the grid barrier (all gate/up epilogues done) load down's A
-// terms. Every wait is bounded: the launch is cooperative, so all CTAs are resident and every barrier completes; a
-// timeout records an error instead of hanging. Split tiles are reduced by their last contributor (deterministic
-// order), never by spinning. The per-CTA stage lists are computed on the host once per shape (stream-K partition,
+// finishes gate/up); warp 1 issues the tcgen05 operations (per stage: the activation scales, the weight scales into
+// a ring of TMEM columns, 4 MMAs, commits); warps 2-5 copy x's terms (written to global memory by all CTAs in phase 0)
+// into shared memory, run the tile epilogues (each reads a quarter of the accumulator's columns from its own TMEM lane
+// quadrant) and, after the grid barrier (all gate/up epilogues done), load down's A terms. A tile split between CTAs
+// is finished by one designated contributor, which adds the others' published partial sums in a fixed order. Every
+// wait is bounded: the launch is cooperative, so all CTAs are resident and every barrier completes; a timeout records
+// an error instead of hanging. The per-CTA stage lists are computed on the host once per shape (stream-K partition,
 // segment boundaries and which CTAs share each tile) and read by each CTA at start.
 #include <algorithm>
 #include <map>
@@ -59,7 +59,6 @@ constexpr uint32_t kColX = kRows;             // accumulator in columns [0, 256)
 constexpr int kTraceSlots = 160;
 constexpr int kMaxK = 8;
 constexpr int kMaxX4 = 8;                     // x is held as kMaxX4 float4 per thread: H <= 4 * kThreads * kMaxX4
-constexpr int kEpiWarpLane0 = 4;              // the epilogue warp that may read TMEM lanes 0-31 (warp % 4 == 0)
 constexpr int kMaxGrid = 160;                 // CTAs (SMs) the router reduction is unrolled for
 
 struct Layout {
@@ -211,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         }
         tc::mbar_init(&fullS[0], 128);                       // one arrival per epilogue thread after its copies
         tc::mbar_init(accF, 1);
-        tc::mbar_init(accE, 1);
+        tc::mbar_init(accE, 4);                              // one arrival per epilogue warp after its TMEM reads
         for (int i = 0; i < cap; ++i) tc::mbar_init(&fullD[i], 1);
         tc::fence_barrier_init();
     }
@@ -547,7 +546,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     } else {
         // ---------------------------------------------------------------- epilogue warps 2..5
         const int et = tid - 64;                    // 0..127
-        const bool reader = warp == kEpiWarpLane0;  // reads the accumulator (TMEM lanes 0-31)
 
         // x's terms and scales (written by all CTAs in phase 0, counted on gbar[3]), with asynchronous 16-byte copies.
         {
@@ -617,28 +615,35 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                     if (r0 + 128 < j.H) b1 = fmaf(w_s[s2], __ldg(bb + r0 + 128), b1);
                 }
             }
-            // the reader warp moves accumulator rows 0..7 (the 8 terms) into shared memory and releases TMEM
-            if (reader) {
-                ok = ok && tc::mbar_wait(accF, uint32_t(st.seg) & 1u, j.err, 5);
-                ok = __all_sync(kFull, ok);
+            // Each epilogue warp moves a quarter of the columns of accumulator rows 0..7 (the 8 terms) into shared
+            // memory and releases its part of TMEM. A's 8-row groups all alias the same 8 rows, so accumulator row
+            // 8g + r equals row r and every TMEM lane quadrant holds the 8 terms in its first 8 lanes: warp w reads
+            // columns 64 (w - 2) .. + 63 of lanes 32 (w % 4) .. + 31, which it may access.
+            // Warp 4 alone polls the accumulator barrier (warp 5 shares a scheduler with the MMA warp, whose issue
+            // rate it would take); the others sleep in the named barrier until it reports.
+            {
+                if (warp == 4) {
+                    ok = ok && tc::mbar_wait(accF, uint32_t(st.seg) & 1u, j.err, 5);
+                    ok = __all_sync(kFull, ok);
+                }
+                ok = epi_all(ok);
                 if (ok) {
                     tc::tc_fence_after();
-#pragma unroll 1
-                    for (int r = 0; r < kRows / 32; r += 2) {
-                        uint32_t v[32], w[32];
-                        tmem_ld_32x32b_x32(tmem + 32 * r, v);
-                        tmem_ld_32x32b_x32(tmem + 32 * (r + 1), w);
-                        tc::tmem_ld_wait();
-                        if (lane < NT) {
+                    const int c0 = 64 * (warp - 2);
+                    const uint32_t ta = tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(c0);
+                    uint32_t v[32], w[32];
+                    tmem_ld_32x32b_x32(ta, v);
+                    tmem_ld_32x32b_x32(ta + 32, w);
+                    tc::tmem_ld_wait();
+                    if (lane < NT) {
 #pragma unroll
-                            for (int i = 0; i < 32; i += 4) {
-                                *reinterpret_cast<float4*>(red_s + lane * kRows + 32 * r + i) =
-                                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
-                                                __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-                                *reinterpret_cast<float4*>(red_s + lane * kRows + 32 * (r + 1) + i) =
-                                    make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]),
-                                                __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
-                            }
+                        for (int i = 0; i < 32; i += 4) {
+                            *reinterpret_cast<float4*>(red_s + lane * kRows + c0 + i) =
+                                make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
+                                            __uint_as_float(v[i + 3]));
+                            *reinterpret_cast<float4*>(red_s + lane * kRows + c0 + 32 + i) =
+                                make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]), __uint_as_float(w[i + 2]),
+                                            __uint_as_float(w[i + 3]));
                         }
                     }
                 }

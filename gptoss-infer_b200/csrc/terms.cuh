@@ -264,6 +264,7 @@ __device__ __forceinline__ void quantize_block_terms_fixed(float (&v)[8], uint8_
 template <int NT>
 __device__ __forceinline__ void quantize_block_terms_warp32(float v, uint8_t* img_stage, int q, uint8_t* sf_chunk,
                                                             int kb, bool active) {
+    static_assert(NT <= 32, "one 16-byte scale row per term in a 512-byte chunk");
     const int lane = threadIdx.x & 31;
     const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(v))));
     int k = -127;
@@ -292,7 +293,10 @@ __device__ __forceinline__ void quantize_block_terms_warp32(float v, uint8_t* im
         word |= __shfl_xor_sync(kFull, word, 4);
         if (active && (lane & 7) == 0)
             *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ (t & 7)) << 4) | ((lane >> 3) * 4))) = word;
-        if (active && lane == 0) sf_chunk[(t & 31) * 16 + (t >> 5) * 4 + kb] = uint8_t(scale);
+        // The scale byte goes to all four 4-byte groups of the term's 16-byte row (lanes 0-3 one each): an M = 128
+        // operand whose 8-row groups alias these rows then finds term t's scale in every TMEM lane quadrant (row r
+        // reads byte (r / 32) * 4 + kb of row r % 8), so every quadrant's first 8 accumulator lanes hold the terms.
+        if (active && lane < 4) sf_chunk[t * 16 + lane * 4 + kb] = uint8_t(scale);
     }
 }
 

@@ -470,6 +470,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 }
                 if (++f == NSF) f = 0;
             };
+            // A stage's MMAs. Stages start on 4-unit boundaries, so unit u uses scale id 2 (u & 1) of K chunk u / 2;
+            // sfa / sfb are the TMEM columns of the stage's first activation / weight scale chunk. A full stage (the
+            // common case) is issued fully unrolled.
+            auto issue_mmas = [&](const uint8_t* ast, const uint8_t* wslot, uint32_t sfa, uint32_t sfb, int nu,
+                                  bool first) {
+                auto one = [&](int u) {
+                    const uint32_t sf_id = 2u * uint32_t(u & 1), q = uint32_t(u >> 1);
+                    tc::mma_mxf4(tmem, tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32)),
+                                 tc::desc_sw128(tc::smem_u32(wslot + u * 32)), tc::idesc_mxf4(128, kRows, sf_id, sf_id),
+                                 (sfa + 4 * q) | (sf_id << 30), (sfb + 8 * q) | (sf_id << 30), !(first && u == 0));
+                };
+                if (nu == 4) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) one(u);
+                } else {
+                    for (int u = 0; u < nu; ++u) one(u);
+                }
+            };
+            // the weight scales of a stage (2 chunks of a full stage unrolled)
+            auto copy_wsf = [&](const uint8_t* wslot, int nkt) {
+                const uint32_t col = tmem + j.L.colSFB + 16 * f;
+                if (nkt == 2) {
+#pragma unroll
+                    for (int x = 0; x < 4; ++x)
+                        tc::tmem_cp_sf(col + 4 * x, tc::desc_sf_chunk(tc::smem_u32(wslot + kB + x * 512)));
+                } else {
+                    for (int x = 0; x < 2 * nkt; ++x)
+                        tc::tmem_cp_sf(col + 4 * x, tc::desc_sf_chunk(tc::smem_u32(wslot + kB + x * 512)));
+                }
+            };
             for (int it = 0; it < ngu && ok; ++it, advance()) {
                 const Stage& st = stages[it];
                 const int kt0 = st.ku0 / 2, nkt = sk::nkt_of(st);
@@ -488,20 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 tc::tc_fence_after();
                 if (it < 32) stamp<kTrace>(j, 34 + it);
                 const uint8_t* wslot = ring + slot * kSlot;
-                for (int q = 0; q < nkt; ++q)
-                    for (int h = 0; h < 2; ++h)
-                        tc::tmem_cp_sf(tmem + j.L.colSFB + 16 * f + 8 * q + 4 * h,
-                                       tc::desc_sf_chunk(tc::smem_u32(wslot + kB + (2 * q + h) * 512)));
-                const uint8_t* ast = xA + (st.ku0 / 4) * kA;
-                for (int u = 0; u < st.nu; ++u) {
-                    const int ku = st.ku0 + u;
-                    const uint32_t sf_id = 2u * (ku & 1);
-                    tc::mma_mxf4(tmem, tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32)),
-                                 tc::desc_sw128(tc::smem_u32(wslot + u * 32)), tc::idesc_mxf4(128, kRows, sf_id, sf_id),
-                                 (tmem + kColX + 4 * (ku / 2)) | (sf_id << 30),
-                                 (tmem + j.L.colSFB + 16 * f + 8 * (ku / 2 - kt0)) | (sf_id << 30),
-                                 !(st.first && u == 0));
-                }
+                copy_wsf(wslot, nkt);
+                issue_mmas(xA + (st.ku0 / 4) * kA, wslot, tmem + kColX + 4 * kt0, tmem + j.L.colSFB + 16 * f, st.nu,
+                           st.first);
                 tc::mma_commit(&emptyB[slot]);
                 if (st.last) tc::mma_commit(accF);
                 if (it < 32) stamp<kTrace>(j, 96 + it);
@@ -523,20 +542,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 tc::tc_fence_after();
                 if (it < 32) stamp<kTrace>(j, 34 + it);
                 const uint8_t* wslot = ring + slot * kSlot;
-                for (int q = 0; q < nkt; ++q)
-                    for (int h = 0; h < 2; ++h)
-                        tc::tmem_cp_sf(tmem + j.L.colSFB + 16 * f + 8 * q + 4 * h,
-                                       tc::desc_sf_chunk(tc::smem_u32(wslot + kB + (2 * q + h) * 512)));
-                const uint8_t* ast = dA + d * kA;
-                for (int u = 0; u < st.nu; ++u) {
-                    const int ku = st.ku0 + u;
-                    const uint32_t sf_id = 2u * (ku & 1);
-                    const int q = ku / 2 - kt0;
-                    tc::mma_mxf4(tmem, tc::desc_sw128_rows8(tc::smem_u32(ast + u * 32)),
-                                 tc::desc_sw128(tc::smem_u32(wslot + u * 32)), tc::idesc_mxf4(128, kRows, sf_id, sf_id),
-                                 (tmem + j.L.colDSF + 8 * f + 4 * q) | (sf_id << 30),
-                                 (tmem + j.L.colSFB + 16 * f + 8 * q) | (sf_id << 30), !(st.first && u == 0));
-                }
+                copy_wsf(wslot, nkt);
+                issue_mmas(dA + d * kA, wslot, tmem + j.L.colDSF + 8 * f, tmem + j.L.colSFB + 16 * f, st.nu, st.first);
                 tc::mma_commit(&emptyB[slot]);
                 if (st.last) tc::mma_commit(accF);
                 if (it < 32) stamp<kTrace>(j, 96 + it);

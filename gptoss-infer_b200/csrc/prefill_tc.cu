@@ -274,19 +274,40 @@ __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ sr
         for (int i = 0; i < 8; ++i) v8[i] = 0.f;
     }
     // The scale bytes of the 8 blocks as two words per (row, quadrant copy): lane l < 8 stores word (l >> 2) of
-    // quadrant copy l & 3, gathered from the lanes holding blocks 4 (l >> 2) .. + 3.
+    // quadrant copy l & 3, covering blocks 4 (l >> 2) .. + 3. A term's scale follows from its block's k (term 0
+    // carries k + 127; term 1 k - 1; term t >= 2 k + 2 - 3t; clamped at 0), so the four blocks' k are gathered once,
+    // at term 0, and every term's scale word is computed locally.
     const int wsel = (lane >> 2) & 1, qsel = lane & 3;
+    // Per destination, once: where this lane's code word and scale word of term NT - 1 go (the terms follow in
+    // descending order, kTermA apart).
+    uint8_t* pw[8];
+    uint8_t* ps[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const bool on = s < nd && pos[s] >= 0;
+        const int ps_ = on ? pos[s] : 0, m = ps_ / kTileM, r = ps_ % kTileM;
+        uint8_t* piece = a_term(img[s], m, KB, kb, NT - 1);
+        pw[s] = on ? piece + a_unit_off(r, gl) + sub * 4 : nullptr;
+        ps[s] = on ? piece + a_sf_off(r, 4 * wsel, qsel) : nullptr;
+    }
+    int kq[4] = {0, 0, 0, 0};
     quantize_block_digits_lanes4(v8, [&](int term, uint32_t word, uint32_t scale) {
+        if (term == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) kq[kk] = int(__shfl_sync(kFull, scale, 4 * (4 * wsel + kk))) - 127;
+        }
         uint32_t sw = 0;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) sw |= __shfl_sync(kFull, scale, 4 * (4 * wsel + kk)) << (8 * kk);
+        for (int kk = 0; kk < 4; ++kk) {
+            const int kt = term == 0 ? kq[kk] : (term == 1 ? kq[kk] - 1 : kq[kk] + 2 - 3 * term);
+            sw |= uint32_t(max(kt + 127, 0)) << (8 * kk);
+        }
+        const size_t toff = size_t(NT - 1 - term) * kTermA;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-            if (s >= nd || pos[s] < 0) continue;
-            const int m = pos[s] / kTileM, r = pos[s] % kTileM;
-            uint8_t* pc = a_term(img[s], m, KB, kb, term);
-            if (valid) *reinterpret_cast<uint32_t*>(pc + a_unit_off(r, gl) + sub * 4) = word;
-            if (lane < 8) *reinterpret_cast<uint32_t*>(pc + a_sf_off(r, 4 * wsel, qsel)) = sw;
+            if (!pw[s]) continue;
+            if (valid) *reinterpret_cast<uint32_t*>(pw[s] + toff) = word;
+            if (lane < 8) *reinterpret_cast<uint32_t*>(ps[s] + toff) = sw;
         }
     });
 }

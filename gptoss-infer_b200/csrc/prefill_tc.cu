@@ -52,7 +52,7 @@ constexpr uint32_t kColSFA = kRows;            // 8 columns per term, 16 per A s
 constexpr uint32_t kColSFB = kRows + 16 * NSA; // 16 columns per B slot
 static_assert(kColSFB + 16 * NSB <= kTmemCols, "TMEM budget");
 static_assert(NT % kPT == 0, "terms per piece");
-constexpr int kRtTok = 8;                      // tokens per router CTA
+constexpr int kRtTok = 14;                     // tokens per router CTA (2048 tokens: 147 CTAs, one wave)
 
 // ------------------------------------------------------------------------------------------------ router (batched)
 // W bf16 [E][H] -> W64 [H][32] fp64 (experts >= E zero): the router's weights once per layer (or call).
@@ -63,18 +63,24 @@ __global__ void router_w64_kernel(const __nv_bfloat16* __restrict__ W, int E, in
     }
 }
 
-// 8 tokens per CTA, 512 threads: RMSNorm (warp w < 8 on token w), h in shared memory as fp64, then thread
-// (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp, kp + 16, ... for the 8 tokens (the weight loads of
-// twelve k issued ahead of their FMAs); the 16 partial sums are added in order and warp w picks token w's top k on
-// order-preserving integer keys of the fp64 logits.
+// kRtTok tokens per CTA, 512 threads: RMSNorm (warp w < kRtTok on token w), h in shared memory (fp32; each value is
+// widened exactly to fp64 at its FMA), then thread (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp,
+// kp + 16, ... for the CTA's tokens (the weight loads of twelve k issued ahead of their FMAs, each load serving all
+// the tokens); the 16 partial sums (stored over h, which is dead by then) are added in order and warp w picks token
+// w's top k on order-preserving integer keys of the fp64 logits.
 constexpr int kRtParts = 16;
-__global__ void __launch_bounds__(512) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
+static_assert(kRtTok <= 16, "one top-k warp per token");
+__host__ __device__ constexpr int router_smem_bytes(int H) {
+    return kRtTok * H * 4 > kRtParts * kRtTok * 32 * 8 ? kRtTok * H * 4 : kRtParts * kRtTok * 32 * 8;
+}
+__global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
                                                              const float* __restrict__ x, const float* __restrict__ g,
                                                              float eps, int T, int E, int H, int k,
                                                              float* __restrict__ h_out, int* __restrict__ ids,
                                                              float* __restrict__ wts) {
-    extern __shared__ double h64[];                          // [kRtTok][H]
-    __shared__ double red[kRtParts][kRtTok][32];
+    extern __shared__ __align__(16) uint8_t rt_smem[];
+    float* hs = reinterpret_cast<float*>(rt_smem);           // [kRtTok][H]
+    double (*red)[kRtTok][32] = reinterpret_cast<double (*)[kRtTok][32]>(rt_smem);   // [kRtParts]: after the FMAs
     __shared__ float rn_s[kRtTok];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.x * kRtTok, nt = min(kRtTok, T - t0);
@@ -98,9 +104,9 @@ __global__ void __launch_bounds__(512) router_batched_kernel(const double* __res
             v.x = v.x * r * gg.x; v.y = v.y * r * gg.y; v.z = v.z * r * gg.z; v.w = v.w * r * gg.w;
         }
         if (h_out) *reinterpret_cast<float4*>(h_out + size_t(t0) * H + i) = v;
-        h64[i] = v.x; h64[i + 1] = v.y; h64[i + 2] = v.z; h64[i + 3] = v.w;
+        *reinterpret_cast<float4*>(hs + i) = v;
     }
-    for (int i = nt * H + tid; i < kRtTok * H; i += 512) h64[i] = 0.0;
+    for (int i = nt * H + tid; i < kRtTok * H; i += 512) hs[i] = 0.f;
     __syncthreads();
     const int e = lane, kp = warp;
     double acc[kRtTok];
@@ -119,10 +125,11 @@ __global__ void __launch_bounds__(512) router_batched_kernel(const double* __res
             const int kk = kk0 + u * kRtParts;
             if (kk < H) {
 #pragma unroll
-                for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk[u], h64[tb * H + kk], acc[tb]);
+                for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk[u], double(hs[tb * H + kk]), acc[tb]);
             }
         }
     }
+    __syncthreads();                                         // h is dead: the partial sums go over it
 #pragma unroll
     for (int tb = 0; tb < kRtTok; ++tb) red[kp][tb][e] = acc[tb];
     __syncthreads();
@@ -899,7 +906,7 @@ void launch_router_batched(const double* W64, const float* b, const float* x, co
     require(T >= 1, "router_batched: T must be positive");
     require(H % 8 == 0 && H >= 8, "router_batched: H must be a positive multiple of 8");
     require(k >= 1 && k <= 8 && k <= E && E <= 32, "router_batched: needs 1 <= k <= 8 and k <= E <= 32");
-    const int smem = pf::kRtTok * H * 8;
+    const int smem = pf::router_smem_bytes(H);
     require(smem <= 200 * 1024, "router_batched: H too large");
     static std::mutex mu;
     static std::map<int, int> done;

@@ -92,7 +92,8 @@ struct Job {
     uint8_t* aq_img;                          // down's A terms [k][SPS_dn][NT*128]
     uint8_t* aq_sf;                           // down's A scales [k][KT_dn][128]
     float* x_resid;
-    unsigned* gbar;                           // [4]: gate/up done, exits, router partials published, x blocks written
+    unsigned* gbar;                           // [5]: gate/up done, exits, router partials published, x blocks written,
+                                              // the last launch's epoch
     double* partials;                         // [grid][32] router partial sums
     int* err;
     long long* trace;                         // optional [grid][kTraceSlots] clock64 stamps
@@ -136,6 +137,20 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
 }
 __device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Split-tile partial sums travel as one 64-bit word each, (launch epoch << 32) | fp32 bits: a single-copy-atomic
+// relaxed store and load, so a word read with the current epoch carries the current value and no fence or counter is
+// needed between the contributor's store and the finalizer's read.
+__device__ __forceinline__ void st_relaxed64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long tag_sum(float v, unsigned ep) {
+    return (static_cast<unsigned long long>(ep) << 32) | __float_as_uint(v);
 }
 __device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -231,6 +246,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     // kernel to finish (x, the residual stream, and the shared workspace are written there).
     pdl_launch_dependents();
     pdl_wait();
+    // This launch's epoch (tags its split-tile partial sums): one more than the previous launch's, which that
+    // launch's last CTA out stored; never 0, the value of a zeroed word.
+    const unsigned ep = __ldcg(&j.gbar[4]) + 1u;
     if (tid == 0 && s_n > cap) atomicCAS(j.err, 0, 100);    // host sized the stage list too small
     if (tid == 0) stamp<kTrace>(j, 123);
 #pragma unroll
@@ -679,49 +697,50 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 } else if (!st.whole) {
                     // Split tile. Its first contributor (the CTA whose range ends inside it: the tile is that CTA's
                     // last segment of the part) finalizes it; the others (for whom it is a first or only segment)
-                    // publish their partial sums and count themselves, and the finalizer waits for that count
-                    // (bounded; usually already complete).
+                    // store their partial sums, tagged with the launch's epoch, and the finalizer polls the words
+                    // themselves until each carries this epoch (bounded; usually already the case).
                     mine = c == st.cf;
+                    unsigned long long* pb = p.partial + size_t(t) * sk::kMaxContrib * kRows;
                     if (!mine) {
-                        float* pp = p.partial + (size_t(t) * sk::kMaxContrib + (c - st.cf)) * kRows;
-                        __stcg(pp + et, v0);
-                        __stcg(pp + et + 128, v1);
-                        epi_sync();
-                        if (et == 0) red_add_release(&p.cnt[t], 1u);
+                        unsigned long long* pp = pb + size_t(c - st.cf) * kRows;
+                        st_relaxed64(pp + et, tag_sum(v0, ep));
+                        st_relaxed64(pp + et + 128, tag_sum(v1, ep));
                     } else {
-                        if (et == 0) {
-                            const unsigned others = unsigned(__popc(unsigned(st.mask))) - 1u;
-                            bool done = false;
-                            for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
-                                done = ld_acquire(&p.cnt[t]) >= others;
-                                if (!done) __nanosleep(32);
-                            }
-                            if (!done) atomicCAS(j.err, 0, 12);
-                            p.cnt[t] = 0;             // reset for the next launch
-                            cnts[2] = done;
+                        const unsigned m = st.mask;
+                        const unsigned long long none = static_cast<unsigned long long>(ep) << 32;
+                        unsigned long long w0[sk::kMaxContrib], w1[sk::kMaxContrib];
+#pragma unroll
+                        for (int b = 1; b < sk::kMaxContrib; ++b) {   // all loads issued together
+                            const bool on = (m >> b) & 1u;
+                            w0[b] = on ? ld_relaxed64(pb + b * kRows + et) : none;
+                            w1[b] = on ? ld_relaxed64(pb + b * kRows + et + 128) : none;
                         }
-                        epi_sync();
-                        mine = cnts[2] != 0;
+                        bool done = false;
+                        for (uint32_t w = 0; w < tc::kSpinLimit; ++w) {
+                            done = true;
+#pragma unroll
+                            for (int b = 1; b < sk::kMaxContrib; ++b)
+                                done = done && unsigned(w0[b] >> 32) == ep && unsigned(w1[b] >> 32) == ep;
+                            if (done) break;
+                            __nanosleep(32);
+#pragma unroll
+                            for (int b = 1; b < sk::kMaxContrib; ++b) {
+                                if (unsigned(w0[b] >> 32) != ep) w0[b] = ld_relaxed64(pb + b * kRows + et);
+                                if (unsigned(w1[b] >> 32) != ep) w1[b] = ld_relaxed64(pb + b * kRows + et + 128);
+                            }
+                        }
+                        mine = epi_all(done);
+                        if (!mine && et == 0) atomicCAS(j.err, 0, 12);
+                        if (mine) {                  // own sums first, then the other contributors in CTA order
+#pragma unroll
+                            for (int b = 1; b < sk::kMaxContrib; ++b)
+                                if ((m >> b) & 1u) {
+                                    v0 += __uint_as_float(unsigned(w0[b]));
+                                    v1 += __uint_as_float(unsigned(w1[b]));
+                                }
+                        }
                     }
                     if (et == 0 && st.seg < 8) stamp<kTrace>(j, 132 + st.seg);
-                    if (mine) {
-                        // own sums first, then the other contributors in CTA order; the loads issue together
-                        const float* pb = p.partial + size_t(t) * sk::kMaxContrib * kRows;
-                        const unsigned m = st.mask;
-                        float a0[sk::kMaxContrib], a1[sk::kMaxContrib];
-#pragma unroll
-                        for (int b = 1; b < sk::kMaxContrib; ++b) {
-                            const bool on = (m >> b) & 1u;
-                            a0[b] = on ? __ldcg(pb + b * kRows + et) : 0.f;
-                            a1[b] = on ? __ldcg(pb + b * kRows + et + 128) : 0.f;
-                        }
-#pragma unroll
-                        for (int b = 1; b < sk::kMaxContrib; ++b)
-                            if ((m >> b) & 1u) {
-                                v0 += a0[b];
-                                v1 += a1[b];
-                            }
-                    }
                 }
                 if (mine && st.mode == sk::kGateUp) {
                     const int s = t / p.RT, rt = t % p.RT;
@@ -768,6 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             j.gbar[0] = 0;
             j.gbar[2] = 0;
             j.gbar[3] = 0;
+            j.gbar[4] = ep;                                  // the next launch's epoch is this + 1
             j.gbar[1] = 0;
         }
     }
@@ -873,8 +893,8 @@ DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     L.off_xq_sf = o; o += al(size_t(L.KT_gu) * fz::kSF8);
     L.off_aq_img = o; o += al(size_t(k) * L.SPS_dn * NT * 128);
     L.off_aq_sf = o; o += al(size_t(k) * L.KT_dn * fz::kSF8);
-    L.off_part_gu = o; o += al(size_t(k) * L.RT_gu * sk::kMaxContrib * TR * 4);
-    L.off_part_dn = o; o += al(size_t(L.RT_dn) * sk::kMaxContrib * TR * 4);
+    L.off_part_gu = o; o += al(size_t(k) * L.RT_gu * sk::kMaxContrib * TR * 8);
+    L.off_part_dn = o; o += al(size_t(L.RT_dn) * sk::kMaxContrib * TR * 8);
     L.off_cnt_gu = o; o += al(size_t(k) * L.RT_gu * 4);
     L.off_cnt_dn = o; o += al(size_t(L.RT_dn) * 4);
     L.off_err = o; o += 1024;                                // error word, then the grid barrier at +256
@@ -882,7 +902,7 @@ DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32, TR));
     L.off_misc = o; o += al(size_t(H) * 4 + 256);
     L.bytes = o;
-    L.zero_bytes_from = L.off_cnt_gu;                        // counters, error word and grid barrier start at zero
+    L.zero_bytes_from = L.off_part_gu;                        // partial sums (epoch 0), counters, error word, barrier
     L.zero_bytes_to = L.off_err + 1024;
     return L;
 }
@@ -942,8 +962,7 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     g.SPS = W.SPS_gu;
     g.UT = g.UK;
     g.total = (long long)g.n_tiles * g.UT;
-    g.partial = reinterpret_cast<float*>(ws + W.off_part_gu);
-    g.cnt = reinterpret_cast<unsigned*>(ws + W.off_cnt_gu);
+    g.partial = reinterpret_cast<unsigned long long*>(ws + W.off_part_gu);
     Part& d = j.dn;
     d.mode = sk::kDown;
     d.RT = W.RT_dn;
@@ -953,8 +972,7 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     d.SPS = W.SPS_dn;
     d.UT = a.k * d.UK;
     d.total = (long long)d.n_tiles * d.UT;
-    d.partial = reinterpret_cast<float*>(ws + W.off_part_dn);
-    d.cnt = reinterpret_cast<unsigned*>(ws + W.off_cnt_dn);
+    d.partial = reinterpret_cast<unsigned long long*>(ws + W.off_part_dn);
     j.xq_img = ws + W.off_xq_img;
     j.xq_sf = ws + W.off_xq_sf;
     j.aq_img = ws + W.off_aq_img;

@@ -1,10 +1,11 @@
 // Stream-K work partition of the tensor-core MoE GEMVs, shared by host (shared-memory sizing) and device.
 //
-// The MMA unit is K = 64 of one 128-row tile. A GEMV "part" is n_tiles tiles of UT units each (gate/up: a tile is
-// 128 rows of one selected expert and UT = UK units of K; down: a tile is 128 output rows and UT = k * UK units,
-// the k experts' rows laid end to end). CTA c of nc takes units [begin(c), begin(c+1)), begin rounded up to a
-// 4-unit stage (one 128-byte-wide TMA box of K) within its slot, so every CTA streams about the same bytes. A tile
-// split between CTAs is reduced by whichever contributor finishes it last.
+// The MMA unit is K = 64 of one tile of weight rows (256 in the decode kernel). A GEMV "part" is n_tiles tiles of UT
+// units each (gate/up: a tile is rows of one selected expert and UT = UK units of K; down: a tile is output rows and
+// UT = k * UK units, the k experts' rows laid end to end). CTA c of nc takes units [begin(c), begin(c+1)), begin
+// rounded up to a 4-unit stage (one 128-byte-wide TMA box of K) within its slot, so every CTA streams about the same
+// bytes. A tile split between CTAs is finished by its first contributor (for which the tile is its last segment),
+// which adds the others' partial sums in CTA order.
 #pragma once
 #include <cstdint>
 
@@ -24,8 +25,7 @@ struct Part {
     int SPS;            // stages (K = 256) per slot
     int UT;             // units per tile
     long long total;    // n_tiles * UT
-    float* partial;     // [n_tiles][kMaxContrib][128]
-    unsigned* cnt;      // [n_tiles], zero between launches
+    unsigned long long* partial;   // [n_tiles][kMaxContrib][rows]: (launch epoch << 32) | fp32 bits of a partial sum
 };
 
 struct Stage {

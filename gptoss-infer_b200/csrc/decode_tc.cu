@@ -846,18 +846,24 @@ const StageTable& stage_table(const Part& g, const Part& d, int nc, int k, int H
     StageTable T;
     std::vector<Stage> all;
     std::vector<int> hdr(size_t(nc) * 4, 0);
+    // Gate/up streams from HBM, a resource all CTAs share, so its ranges hold equal unit counts. Down's weights are
+    // resident by the time its stages run, which are then bound by each CTA's issue rate: its ranges balance a cost
+    // model (cycles, clock64 trace of this kernel on a B200): a stage ≈ 500 + 145 per unit (1.08K for 4 units), a
+    // segment's drain and publication ≈ 1.5K, finalizing a tile (partial sums, residual) ≈ 1.5K.
+    const std::vector<long long> Bg = sk::equal_bounds(g, nc);
+    const std::vector<long long> Bd = sk::balanced_bounds(d, nc, sk::CostModel{500.0, 145.0, 1500.0, 1500.0});
     for (int c = 0; c < nc; ++c) {
         int seg = 0;
-        const int ngu = sk::build_stages(g, c, nc, nullptr, 0, 0, 0, &seg);
-        const int n = sk::build_stages(d, c, nc, nullptr, ngu, 0, seg, nullptr);
+        const int ngu = sk::build_stages(g, Bg.data(), c, nullptr, 0, 0, 0, &seg);
+        const int n = sk::build_stages(d, Bd.data(), c, nullptr, ngu, 0, seg, nullptr);
         const size_t n0 = all.size();
         all.resize(n0 + size_t(n));
         Stage* o = all.data() + n0;
         seg = 0;
-        sk::build_stages(g, c, nc, o, 0, n, 0, &seg);
-        sk::build_stages(d, c, nc, o, ngu, n, seg, nullptr);
-        sk::fill_tile_info(g, c, nc, o, 0, ngu);
-        sk::fill_tile_info(d, c, nc, o, ngu, n);
+        sk::build_stages(g, Bg.data(), c, o, 0, n, 0, &seg);
+        sk::build_stages(d, Bd.data(), c, o, ngu, n, seg, nullptr);
+        sk::fill_tile_info(g, Bg.data(), nc, c, o, 0, ngu);
+        sk::fill_tile_info(d, Bd.data(), nc, c, o, ngu, n);
         hdr[size_t(c) * 4 + 0] = int(n0);
         hdr[size_t(c) * 4 + 1] = n;
         hdr[size_t(c) * 4 + 2] = ngu;

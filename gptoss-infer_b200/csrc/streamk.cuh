@@ -2,12 +2,14 @@
 //
 // The MMA unit is K = 64 of one tile of weight rows (256 in the decode kernel). A GEMV "part" is n_tiles tiles of UT
 // units each (gate/up: a tile is rows of one selected expert and UT = UK units of K; down: a tile is output rows and
-// UT = k * UK units, the k experts' rows laid end to end). CTA c of nc takes units [begin(c), begin(c+1)), begin
-// rounded up to a 4-unit stage (one 128-byte-wide TMA box of K) within its slot, so every CTA streams about the same
-// bytes. A tile split between CTAs is finished by its first contributor (for which the tile is its last segment),
-// which adds the others' partial sums in CTA order.
+// UT = k * UK units, the k experts' rows laid end to end). CTA c of nc takes the contiguous units [B(c), B(c+1)),
+// cut at stage starts (a stage is at most 4 units, one 128-byte-wide TMA box of K, within one slot); the cuts
+// balance a per-CTA cost (stages, segments, tiles finalized) rather than the unit count, because every tile ends in
+// a short stage and finalizing a tile costs about as much as three stages. A tile split between CTAs is finished by
+// its first contributor (for which the tile is its last segment), which adds the others' partial sums in CTA order.
 #pragma once
 #include <cstdint>
+#include <vector>
 
 namespace gpt {
 namespace sk {
@@ -41,23 +43,90 @@ struct Stage {
     unsigned short mask;  // bit i: CTA cf + i computes part of the tile
 };
 
-__host__ __device__ __forceinline__ long long stage_round(const Part& p, long long u) {
+// Units of the stage that starts at unit u (stages are at most 4 units and never cross a slot).
+inline int stage_units_at(const Part& p, long long u) {
     const long long t = u / p.UT;
     const int m = int(u - t * p.UT);
-    const int s = m / p.UK, ku = m - s * p.UK;
-    const int ku2 = (ku + 3) & ~3;
-    return t * p.UT + (long long)s * p.UK + (ku2 < p.UK ? ku2 : p.UK);
+    const int ku = p.mode == kGateUp ? m : m % p.UK;
+    const int left = p.UK - ku;
+    return left < 4 ? left : 4;
 }
 
-__host__ __device__ __forceinline__ long long cta_begin(const Part& p, int c, int nc) {
-    return stage_round(p, (long long)c * p.total / nc);
+// Cost model of a CTA's range (cycles on a B200, from the kernel's clock64 trace): each stage a fixed issue cost plus
+// a cost per unit, each segment (the part of one tile in the range) an accumulator drain and publication, and each
+// tile whose first unit lies in the range its finalization (the range's CTA is the tile's first contributor).
+struct CostModel {
+    double stage, unit, segment, finalize;
+};
+
+// Range boundaries of nc CTAs with equal unit counts: unit c * total / nc rounded up to the next stage start.
+inline std::vector<long long> equal_bounds(const Part& p, int nc) {
+    std::vector<long long> B(size_t(nc) + 1);
+    for (int c = 0; c <= nc; ++c) {
+        const long long u = (long long)c * p.total / nc, t = u / p.UT;
+        const int m = int(u - t * p.UT), s = m / p.UK, ku = m - s * p.UK, ku2 = (ku + 3) & ~3;
+        B[c] = t * p.UT + (long long)s * p.UK + (ku2 < p.UK ? ku2 : p.UK);
+    }
+    return B;
 }
 
-// Appends CTA c's stages of part p to out[n0..] (at most cap entries in total); returns the new count. Segments are
-// numbered from seg0.
-__host__ __device__ inline int build_stages(const Part& p, int c, int nc, Stage* out, int n0, int cap, int seg0,
-                                            int* seg_end) {
-    const long long B0 = cta_begin(p, c, nc), B1 = cta_begin(p, c + 1, nc);
+// Range boundaries [B(0) = 0, ..., B(nc) = total] of the nc CTAs, cut only at stage starts, chosen so that the
+// largest range cost is as small as possible (binary search over the cost bound, greedy filling); trailing CTAs may
+// get empty ranges.
+inline std::vector<long long> balanced_bounds(const Part& p, int nc, const CostModel& cm) {
+    std::vector<long long> start;                  // unit of every stage start, then total
+    std::vector<double> cost;                      // the stage's own cost
+    std::vector<char> tile_first;                  // the stage starts a tile
+    for (long long u = 0; u < p.total;) {
+        const int nu = stage_units_at(p, u);
+        start.push_back(u);
+        cost.push_back(cm.stage + cm.unit * nu);
+        tile_first.push_back(u % p.UT == 0);
+        u += nu;
+    }
+    const size_t ns = start.size();
+    start.push_back(p.total);
+    // greedy: each range takes stages while its cost stays within X; returns the number of ranges
+    auto fill = [&](double X, std::vector<long long>* out) {
+        int n = 0;
+        size_t i = 0;
+        if (out) out->assign(1, 0);
+        while (i < ns) {
+            double c = 0.0;
+            long long tile = -1;
+            size_t j = i;
+            while (j < ns) {
+                const long long t = start[j] / p.UT;
+                double add = cost[j] + (t != tile ? cm.segment : 0.0) + (tile_first[j] ? cm.finalize : 0.0);
+                if (j > i && c + add > X) break;
+                c += add;
+                tile = t;
+                ++j;
+            }
+            ++n;
+            if (out) out->push_back(start[j]);
+            i = j;
+        }
+        return n;
+    };
+    double lo = 0.0, hi = 0.0;
+    for (size_t i = 0; i < ns; ++i) hi += cost[i] + cm.segment + cm.finalize;
+    for (int it = 0; it < 60; ++it) {
+        const double mid = 0.5 * (lo + hi);
+        if (fill(mid, nullptr) <= nc) hi = mid;
+        else lo = mid;
+    }
+    std::vector<long long> B;
+    fill(hi, &B);
+    while (int(B.size()) < nc + 1) B.push_back(p.total);
+    return B;
+}
+
+// Appends CTA c's stages of part p (range [B[c], B[c + 1])) to out[n0..] (at most cap entries in total); returns
+// the new count. Segments are numbered from seg0.
+inline int build_stages(const Part& p, const long long* B, int c, Stage* out, int n0, int cap, int seg0,
+                        int* seg_end) {
+    const long long B0 = B[c], B1 = B[c + 1];
     int n = n0, seg = seg0;
     for (long long u = B0; u < B1;) {
         const int t = int(u / p.UT);
@@ -85,38 +154,39 @@ __host__ __device__ inline int build_stages(const Part& p, int c, int nc, Stage*
     return n;
 }
 
-// CTAs whose ranges intersect tile t: [c_first, c_last].
-__host__ __device__ inline void tile_contributors(const Part& p, int t, int nc, int& c_first, int& c_last) {
+// CTAs whose ranges intersect tile t: [c_first, c_last] (the CTAs holding its first and last unit).
+inline void tile_contributors(const Part& p, const long long* B, int nc, int t, int& c_first, int& c_last) {
     const long long T0 = (long long)t * p.UT, T1 = T0 + p.UT;
-    int c = int(T0 * nc / p.total);
-    c = c < 0 ? 0 : (c > nc - 1 ? nc - 1 : c);
-    while (c > 0 && cta_begin(p, c, nc) > T0) --c;
-    while (c + 1 < nc && cta_begin(p, c + 1, nc) <= T0) ++c;
-    c_first = c;
-    int d = int((T1 - 1) * nc / p.total);
-    d = d < c_first ? c_first : (d > nc - 1 ? nc - 1 : d);
-    while (d > c_first && cta_begin(p, d, nc) > T1 - 1) --d;
-    while (d + 1 < nc && cta_begin(p, d + 1, nc) <= T1 - 1) ++d;
-    c_last = d;
+    auto owner = [&](long long u) {                  // the CTA whose (non-empty) range holds unit u
+        int lo = 0, hi = nc - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) / 2;
+            if (B[mid] <= u) lo = mid;
+            else hi = mid - 1;
+        }
+        return lo;
+    };
+    c_first = owner(T0);
+    c_last = owner(T1 - 1);
 }
 
 // Completes the segment-end entries of a stage list with who shares each tile.
-inline void fill_tile_info(const Part& p, int c, int nc, Stage* st, int n0, int n1) {
+inline void fill_tile_info(const Part& p, const long long* B, int nc, int c, Stage* st, int n0, int n1) {
     for (int i = n0; i < n1; ++i) {
         if (!st[i].last) continue;
         const int t = st[i].tile;
         const long long T0 = (long long)t * p.UT, T1 = T0 + p.UT;
-        long long a = cta_begin(p, c, nc), b = cta_begin(p, c + 1, nc);
+        long long a = B[c], b = B[c + 1];
         a = a > T0 ? a : T0;
         b = b < T1 ? b : T1;
         st[i].units = short(b - a);
         st[i].whole = short(b - a == p.UT);
         int cf, cl;
-        tile_contributors(p, t, nc, cf, cl);
+        tile_contributors(p, B, nc, t, cf, cl);
         st[i].cf = short(cf);
         unsigned m = 0;
         for (int cc = cf; cc <= cl && cc - cf < kMaxContrib; ++cc) {
-            long long x0 = cta_begin(p, cc, nc), x1 = cta_begin(p, cc + 1, nc);
+            long long x0 = B[cc], x1 = B[cc + 1];
             x0 = x0 > T0 ? x0 : T0;
             x1 = x1 < T1 ? x1 : T1;
             if (x0 < x1) m |= 1u << (cc - cf);

@@ -256,6 +256,31 @@ def test_layer_forward_is_deterministic_and_in_place(lib, config0):
         lib.gptoss_moe_layer_destroy(L)
 
 
+def test_traced_kernel_matches_untraced(lib, config0):
+    """gptoss_trace_enable switches to the traced instantiation of the decode kernel (clock64 stamps compiled in):
+    its results are bit-identical to the untraced kernel's, and it writes its stamps (slot 0 = start, slot 82 = end,
+    per CTA)."""
+    d, g = config0
+    L = make_layer(lib, d)
+    tr = torch.zeros(160 * 160, dtype=torch.int64, device=DEV)
+    try:
+        x = dev(g["x"][2])
+        plain, traced = x.clone(), x.clone()
+        ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(plain), None, None))
+        ok(lib, lib.gptoss_trace_enable(P(tr), tr.numel() * 8))
+        try:
+            ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(traced), None, None))
+        finally:
+            ok(lib, lib.gptoss_trace_enable(None, 0))
+        torch.cuda.synchronize()
+        assert torch.equal(plain, traced)
+        t = tr.view(160, 160).cpu()
+        ctas = int((t[:, 0] != 0).sum())
+        assert ctas > 0 and bool(((t[:ctas, 82] - t[:ctas, 0]) > 0).all())
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+
+
 def test_layer_create_rejects_bad_shapes(lib, config0):
     d, _ = config0
     L = lib.gptoss_moe_layer_create(P(d["ln"]), 1e-5, P(d["W"]), P(d["b"]), *(P(e) for e in d["ex"]), 32, 9, 2880,

@@ -204,9 +204,13 @@ __device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8]
 #pragma unroll
     for (int t = 2; t < 8; ++t) {
         const int kt = k + 2 - 3 * t, j = 7 - t;
-        uint32_t w = 0;
+        uint32_t u = 0;                                         // the 8 elements' digit fields, one per nibble
 #pragma unroll
-        for (int i = 0; i < 8; ++i) w |= balanced_digit_code((uint32_t(Rp[i]) >> (3 * j)) & 7u) << (4 * i);
+        for (int i = 0; i < 8; ++i) u |= ((uint32_t(Rp[i]) >> (3 * j)) & 7u) << (4 * i);
+        // balanced_digit_code of all 8 nibbles at once: u >= 4 -> u - 4 = u & 3; u < 4 -> 8 | (4 - u) = 8 | ((~u & 3)
+        // + 1) (no carry leaves a nibble)
+        const uint32_t hi = ((u >> 2) & 0x11111111u) * 0xFu;
+        const uint32_t w = (u & 0x33333333u & hi) | ((0x88888888u | ((~u & 0x33333333u) + 0x11111111u)) & ~hi);
         emit(t, kt >= -127 ? w : 0u, uint32_t(max(kt + 127, 0)));
     }
 }

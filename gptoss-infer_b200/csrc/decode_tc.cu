@@ -901,14 +901,12 @@ DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     L.off_aq_sf = o; o += al(size_t(k) * L.KT_dn * fz::kSF8);
     L.off_part_gu = o; o += al(size_t(k) * L.RT_gu * sk::kMaxContrib * TR * 8);
     L.off_part_dn = o; o += al(size_t(L.RT_dn) * sk::kMaxContrib * TR * 8);
-    L.off_cnt_gu = o; o += al(size_t(k) * L.RT_gu * 4);
-    L.off_cnt_dn = o; o += al(size_t(L.RT_dn) * 4);
     L.off_err = o; o += 1024;                                // error word, then the grid barrier at +256
     L.off_sfa_gu = o; o += al(sf_repacked_bytes(k, 2 * I, H / 32, TR));
     L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32, TR));
     L.off_misc = o; o += al(size_t(H) * 4 + 256);
     L.bytes = o;
-    L.zero_bytes_from = L.off_part_gu;                        // partial sums (epoch 0), counters, error word, barrier
+    L.zero_bytes_from = L.off_part_gu;                        // partial sums (epoch 0), error word, grid barrier
     L.zero_bytes_to = L.off_err + 1024;
     return L;
 }

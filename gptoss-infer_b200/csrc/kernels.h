@@ -55,11 +55,10 @@ void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows
 constexpr int kDecodeTileRows = 256;
 // Tensor-core decode MoE (decode_tc.cu): one persistent cooperative kernel per MoE layer. The workspace layout
 // depends only on (k, H, I); the byte range [zero_bytes_from, zero_bytes_to) must be zero before the first launch
-// (tile counters and the grid barrier reset themselves afterwards).
+// (the partial-sum words carry the launch epoch and the grid barrier resets itself afterwards).
 struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
-    size_t off_partials, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_cnt_gu,
-        off_cnt_dn, off_err;
+    size_t off_partials, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
 };
 DecodeTcLayout decode_tc_layout(int k, int H, int I);

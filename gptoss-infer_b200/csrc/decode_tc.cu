@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     uint64_t* fullD = accE + 1;               // [cap] down stage's A terms and scales loaded
     float* hs = reinterpret_cast<float*>(smem + j.L.hs);     // h = RMSNorm(x) [H]
     uint32_t* holder = reinterpret_cast<uint32_t*>(smem + j.L.misc);
-    int* cnts = reinterpret_cast<int*>(holder + 2);          // [2] partials barrier / last-arrival flag, [3] grid
+    int* cnts = reinterpret_cast<int*>(holder + 2);          // [2] router partials published everywhere
     double* red = reinterpret_cast<double*>(cnts + 6);       // [6][32] router sums
     int* ids_s = reinterpret_cast<int*>(red + 7 * 32);       // [8]
     float* w_s = reinterpret_cast<float*>(ids_s + kMaxK);    // [8]
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             for (int it = ngu; it < nst && ok; ++it, advance()) {
                 const Stage& st = stages[it];
                 const int d = it - ngu;
-                const int kt0 = st.ku0 / 2, nkt = sk::nkt_of(st);
+                const int nkt = sk::nkt_of(st);
                 ok = tc::mbar_wait(&fullD[d], 0, j.err, 9);
                 if (!ok) break;
                 tc::tc_fence_after();

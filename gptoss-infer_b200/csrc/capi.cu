@@ -61,12 +61,15 @@ struct Scratch {
 };
 thread_local Scratch g_scratch;
 
-// Workspace of the tensor-core decode path (B terms, partial sums, tile counters, gathered scales), owned by the
-// calling thread, one per device. Zero-filled whenever it is (re)allocated: the tile counters must start at zero
-// and reset themselves after every launch.
+// Workspace of the tensor-core decode path (activation terms, epoch-tagged partial sums, grid-barrier words, gathered
+// scales), owned by the calling thread, one per device. Zero-filled whenever it is (re)allocated. The words that carry
+// state from one launch to the next (barrier counters that reset themselves, the launch epoch, the tagged partial
+// sums) sit at offsets that depend on the shape (k, H, I), so they are valid only for the layout that last used them:
+// for_layout() zeroes the new layout's range of them, on the call's stream, whenever the shape changes.
 struct DecodeWs {
     void* p[64] = {};
     size_t n[64] = {};
+    unsigned long long shape[64] = {};        // (k, H, I) whose layout the state words follow; 0: none yet
     ~DecodeWs() {
         for (int d = 0; d < 64; ++d)
             if (p[d]) cudaFree(p[d]);
@@ -82,8 +85,22 @@ struct DecodeWs {
             GPT_CHECK(cudaMalloc(&p[dev], bytes));
             GPT_CHECK(cudaMemset(p[dev], 0, bytes));
             n[dev] = bytes;
+            shape[dev] = 0;
         }
         return p[dev];
+    }
+    void* for_layout(const gpt::DecodeTcLayout& L, int k, int H, int I, cudaStream_t s) {
+        void* w = get(L.bytes);
+        int dev = 0;
+        GPT_CHECK(cudaGetDevice(&dev));
+        const unsigned long long key =
+            (static_cast<unsigned long long>(k) << 48) | (static_cast<unsigned long long>(H) << 24) | unsigned(I);
+        if (shape[dev] != key) {
+            GPT_CHECK(cudaMemsetAsync(static_cast<char*>(w) + L.zero_bytes_from, 0, L.zero_bytes_to - L.zero_bytes_from,
+                                      s));
+            shape[dev] = key;
+        }
+        return w;
     }
 };
 thread_local DecodeWs g_dws;
@@ -240,7 +257,7 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
         if (k < 1 || k > 8) throw std::runtime_error("moe: k must be in 1..8");
         if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
-            void* ws = g_dws.get(L.bytes);
+            void* ws = g_dws.for_layout(L, k, H, I, nullptr);
             moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
                        H, I, alpha, limit, ws, L, nullptr);
             sync_check("moe");
@@ -335,7 +352,7 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
         if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
             // raw scales: the router runs first (its ids select which scales to repack), then the fused kernel
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
-            char* tw = static_cast<char*>(g_dws.get(L.bytes));
+            char* tw = static_cast<char*>(g_dws.for_layout(L, k, H, I, s));
             float* th = reinterpret_cast<float*>(tw + L.off_misc);
             int* tids = reinterpret_cast<int*>(tw + L.off_misc + ((size_t(H) * 4 + 127) & ~size_t(127)));
             float* tgw = reinterpret_cast<float*>(tids + 32);
@@ -546,10 +563,10 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
     return guard([&] {
         if (!l) throw std::runtime_error("moe_layer_forward: null layer");
         const gpt::DecodeTcLayout L = gpt::decode_tc_layout(l->k, l->H, l->I);
-        char* w = static_cast<char*>(g_dws.get(L.bytes));
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        char* w = static_cast<char*>(g_dws.for_layout(L, l->k, l->H, l->I, s));
         int* ids = reinterpret_cast<int*>(w + L.off_misc + ((size_t(l->H) * 4 + 127) & ~size_t(127)));
         float* gw = reinterpret_cast<float*>(ids + 32);
-        cudaStream_t s = static_cast<cudaStream_t>(stream);
         auto rec = [&](int i) {
             if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
         };

@@ -59,8 +59,17 @@ struct CostModel {
     double stage, unit, segment, finalize;
 };
 
-// Range boundaries of nc CTAs with equal unit counts: unit c * total / nc rounded up to the next stage start.
+// Range boundaries of nc CTAs with equal unit counts: unit c * total / nc rounded up to the next stage start. A part
+// of at most nc stages gets one stage per CTA for its first CTAs instead, so that no empty range falls between two
+// CTAs sharing a tile (the partial-sum slots of a tile are indexed by CTA distance).
 inline std::vector<long long> equal_bounds(const Part& p, int nc) {
+    std::vector<long long> starts;
+    for (long long u = 0; u < p.total && long(starts.size()) <= nc; u += stage_units_at(p, u)) starts.push_back(u);
+    if (long(starts.size()) <= nc) {
+        std::vector<long long> B(size_t(nc) + 1, p.total);
+        for (size_t i = 0; i < starts.size(); ++i) B[i] = starts[i];
+        return B;
+    }
     std::vector<long long> B(size_t(nc) + 1);
     for (int c = 0; c <= nc; ++c) {
         const long long u = (long long)c * p.total / nc, t = u / p.UT;
@@ -86,10 +95,13 @@ inline std::vector<long long> balanced_bounds(const Part& p, int nc, const CostM
     }
     const size_t ns = start.size();
     start.push_back(p.total);
-    // greedy: each range takes stages while its cost stays within X; returns the number of ranges
+    // greedy: each range takes stages while its cost stays within X; returns the number of ranges, or nc + 1 when a
+    // tile would be shared by more than kMaxContrib ranges (it has that many partial-sum slots)
     auto fill = [&](double X, std::vector<long long>* out) {
         int n = 0;
         size_t i = 0;
+        long long last_tile = -1;
+        int ranges_on_tile = 0;
         if (out) out->assign(1, 0);
         while (i < ns) {
             double c = 0.0;
@@ -105,6 +117,11 @@ inline std::vector<long long> balanced_bounds(const Part& p, int nc, const CostM
             }
             ++n;
             if (out) out->push_back(start[j]);
+            const long long t0 = start[i] / p.UT, t1 = (start[j] - 1) / p.UT;   // tiles the range touches
+            ranges_on_tile = t0 == last_tile ? ranges_on_tile + 1 : 1;
+            if (ranges_on_tile > kMaxContrib) return nc + 1;
+            if (t1 != t0) ranges_on_tile = 1;
+            last_tile = t1;
             i = j;
         }
         return n;

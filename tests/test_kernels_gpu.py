@@ -137,6 +137,50 @@ def real_shape_case(E=6, seed=4):
     return [gu_b, gu_s, gu_bias, dn_b, dn_s, dn_bias, x, ids, weights], resid, H, I, k
 
 
+def small_shape_case(seed=9):
+    """A second tensor-core shape (k = 2, H = 512, I = 256, 4 experts) for the shape-switch test."""
+    g = torch.Generator().manual_seed(seed)
+    E, H, I, k = 4, 512, 256, 2
+    gu_b = torch.randint(0, 256, (E, 2 * I, H // 32, 16), generator=g, dtype=torch.uint8)
+    gu_s = torch.randint(118, 124, (E, 2 * I, H // 32), generator=g, dtype=torch.uint8)
+    dn_b = torch.randint(0, 256, (E, H, I // 32, 16), generator=g, dtype=torch.uint8)
+    dn_s = torch.randint(118, 124, (E, H, I // 32), generator=g, dtype=torch.uint8)
+    gu_bias, dn_bias = torch.randn(E, 2 * I, generator=g) * 0.1, torch.randn(E, H, generator=g) * 0.1
+    x = torch.randn(H, generator=g)
+    resid = torch.randn(H, generator=g)
+    ids = torch.tensor([3, 1], dtype=torch.int32)
+    weights = torch.softmax(torch.randn(k, generator=g), 0)
+    return [gu_b, gu_s, gu_bias, dn_b, dn_s, dn_bias, x, ids, weights], resid, H, I, k
+
+
+def test_moe_tensor_cores_alternating_shapes(lib):
+    """Two shapes alternating on one thread share its decode workspace, whose launch-to-launch state (barrier words,
+    launch epoch, epoch-tagged partial sums) sits at shape-dependent offsets: every call must give the result the
+    shape gives alone (bit-identical), and the small shape must meet the float64 bound."""
+    cases = [real_shape_case(), small_shape_case()]
+    dev_cases = [([t.to(DEV).contiguous() for t in args], resid.to(DEV), H, I, k) for args, resid, H, I, k in cases]
+
+    def run(i):
+        d, resid, H, I, k = dev_cases[i]
+        out = resid.clone()
+        ok(lib, lib.gptoss_kernel_moe(*(P(t) for t in d), P(out), k, H, I, 1.702, 7.0))
+        return out.cpu()
+
+    prev = lib.gptoss_set_moe_impl(1)
+    try:
+        alone = [run(0), run(0), run(1), run(1)]
+        assert torch.equal(alone[0], alone[1]) and torch.equal(alone[2], alone[3])
+        for i in (0, 1, 0, 1, 1, 0):
+            assert torch.equal(run(i), alone[2 * i]), i
+    finally:
+        lib.gptoss_set_moe_impl(prev)
+    args, resid, H, I, k = cases[1]
+    want = omoe.kernel_moe_f64(*[a.numpy() for a in args[:6]], args[6].numpy(), args[7].numpy(), args[8].numpy(),
+                               resid.numpy())
+    got = alone[2].double().numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
+
+
 @pytest.mark.parametrize("impl", [0, 1])
 def test_moe_real_shape(lib, impl):
     args, resid, H, I, k = real_shape_case()

@@ -416,6 +416,9 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
 int gptoss_kernel_router_batched(const void* W, const float* b, const float* x, int E, int H, int k, int T,
                                  int32_t* ids, float* weights) {
     return guard([&] {
+        // shapes are checked before any device work (the batched router repeats the checks)
+        if (T < 1 || E < 1 || E > 32 || k < 1 || k > 8 || k > E || H < 8 || H % 8)
+            throw std::runtime_error("router_batched: need T >= 1, 1 <= k <= 8, k <= E <= 32, H % 8 == 0");
         double* w64 = static_cast<double*>(g_scratch.get(size_t(H) * 32 * sizeof(double)));
         gpt::launch_router_w64(W, E, H, w64, nullptr);
         gpt::launch_router_batched(w64, b, x, nullptr, 0.f, T, E, H, k, nullptr, ids, weights, nullptr);

@@ -34,6 +34,25 @@ def test_library_exports_every_declared_symbol(lib):
     assert set(capi.SIGNATURES) <= set(capi.header_functions())
 
 
+def test_invalid_shapes_are_rejected_before_any_device_work(lib):
+    """Argument checks that run before the first CUDA call, so they hold without a GPU: k > E must fail
+    (runtime/tests/test_kernels.py:145), and so must k outside 1..8, an empty batch and H not a multiple of 8."""
+    cases = [
+        (lambda: lib.gptoss_kernel_router(None, None, None, 4, 64, 5, None, None), b"k <= E"),
+        (lambda: lib.gptoss_kernel_router(None, None, None, 32, 60, 4, None, None), b"H % 8"),
+        (lambda: lib.gptoss_kernel_router_batched(None, None, None, 4, 64, 5, 16, None, None), b"k <= E"),
+        (lambda: lib.gptoss_kernel_router_batched(None, None, None, 32, 64, 4, 0, None, None), b"T >= 1"),
+        (lambda: lib.gptoss_kernel_moe(None, None, None, None, None, None, None, None, None, None, 9, 64, 64,
+                                       1.702, 7.0), b"k must be in 1..8"),
+        (lambda: lib.gptoss_kernel_moe_batched(None, None, None, None, None, None, None, None, None, None, 0, 4,
+                                               64, 64, 1.702, 7.0), b"T >= 1"),
+        (lambda: lib.gptoss_moe_layer_forward_batched(None, None, None, 4, None, None), b"null layer"),
+    ]
+    for call, msg in cases:
+        assert call() == -1
+        assert msg in lib.gptoss_last_error(), (msg, lib.gptoss_last_error())
+
+
 def test_errors_cross_the_abi_as_minus_one(lib):
     assert lib.gptoss_set_moe_impl(7) == -1
     assert b"impl" in lib.gptoss_last_error()

@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     double* red = reinterpret_cast<double*>(cnts + 6);       // [6][32] router sums
     int* ids_s = reinterpret_cast<int*>(red + 7 * 32);       // [8]
     float* w_s = reinterpret_cast<float*>(ids_s + kMaxK);    // [8]
-    float* aval = w_s + kMaxK;                               // [kRows / 2] activations of one tile
+    float* aval = w_s + kMaxK;                               // [kRows / 2] phase 0's per-warp sums of squares
     Stage* stages = reinterpret_cast<Stage*>(aval + kRows / 2);   // [cap]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -625,19 +625,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         for (int it = 0; it < nst; ++it) {
             const Stage& st = stages[it];
             if (!st.last) continue;
-            // the biases of this thread's two rows, loaded before the accumulator is waited for
+            // The thread's two rows of the tile are r0 = 2 et and r0 + 1: for gate/up that is one activation's glu and
+            // linear rows, so thread et computes activation et and epilogue warp w holds the tile's 32-element block w.
+            // Their biases are loaded before the accumulator is waited for.
+            const int r0 = 2 * et;
             float b0 = 0.f, b1 = 0.f;
             if (st.mode == sk::kGateUp) {
                 const int rt = st.tile - st.s * j.gu.RT;
                 const float* bb = j.gu_bias + size_t(ids_s[st.tile / j.gu.RT]) * 2 * j.I + rt * kRows;
-                if (rt * kRows + et < 2 * j.I) b0 = __ldg(bb + et);
-                if (rt * kRows + et + 128 < 2 * j.I) b1 = __ldg(bb + et + 128);
+                if (rt * kRows + r0 < 2 * j.I) b0 = __ldg(bb + r0);
+                if (rt * kRows + r0 + 1 < 2 * j.I) b1 = __ldg(bb + r0 + 1);
             } else {
-                const int r0 = st.tile * kRows + et;
+                const int g0 = st.tile * kRows + r0;
                 for (int s2 = 0; s2 < j.k; ++s2) {
                     const float* bb = j.dn_bias + size_t(ids_s[s2]) * j.H;
-                    if (r0 < j.H) b0 = fmaf(w_s[s2], __ldg(bb + r0), b0);
-                    if (r0 + 128 < j.H) b1 = fmaf(w_s[s2], __ldg(bb + r0 + 128), b1);
+                    if (g0 < j.H) b0 = fmaf(w_s[s2], __ldg(bb + g0), b0);
+                    if (g0 + 1 < j.H) b1 = fmaf(w_s[s2], __ldg(bb + g0 + 1), b1);
                 }
             }
             // Each epilogue warp moves a quarter of the columns of accumulator rows 0..7 (the 8 terms) into shared
@@ -678,12 +681,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             }
             ok = epi_all(ok);                        // uniform over the 4 epilogue warps; red_s written
             if (et == 0 && st.seg < 14) stamp<kTrace>(j, 66 + st.seg);
-            float v0 = 0.f, v1 = 0.f;                // rows et and et + 128 of the tile
+            float v0 = 0.f, v1 = 0.f;                // rows r0 and r0 + 1 of the tile
             if (ok) {
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    v0 += red_s[t * kRows + et];
-                    v1 += red_s[t * kRows + et + 128];
+                    const float2 q = *reinterpret_cast<const float2*>(red_s + t * kRows + r0);
+                    v0 += q.x;
+                    v1 += q.y;
                 }
             }
             epi_sync();                              // red_s may be overwritten from here on
@@ -703,8 +707,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                     unsigned long long* pb = p.partial + size_t(t) * sk::kMaxContrib * kRows;
                     if (!mine) {
                         unsigned long long* pp = pb + size_t(c - st.cf) * kRows;
-                        st_relaxed64(pp + et, tag_sum(v0, ep));
-                        st_relaxed64(pp + et + 128, tag_sum(v1, ep));
+                        st_relaxed64(pp + r0, tag_sum(v0, ep));
+                        st_relaxed64(pp + r0 + 1, tag_sum(v1, ep));
                     } else {
                         const unsigned m = st.mask;
                         const unsigned long long none = static_cast<unsigned long long>(ep) << 32;
@@ -712,8 +716,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
 #pragma unroll
                         for (int b = 1; b < sk::kMaxContrib; ++b) {   // all loads issued together
                             const bool on = (m >> b) & 1u;
-                            w0[b] = on ? ld_relaxed64(pb + b * kRows + et) : none;
-                            w1[b] = on ? ld_relaxed64(pb + b * kRows + et + 128) : none;
+                            w0[b] = on ? ld_relaxed64(pb + b * kRows + r0) : none;
+                            w1[b] = on ? ld_relaxed64(pb + b * kRows + r0 + 1) : none;
                         }
                         bool done = false;
                         for (uint32_t w = 0; w < tc::kSpinLimit; ++w) {
@@ -725,8 +729,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                             __nanosleep(32);
 #pragma unroll
                             for (int b = 1; b < sk::kMaxContrib; ++b) {
-                                if (unsigned(w0[b] >> 32) != ep) w0[b] = ld_relaxed64(pb + b * kRows + et);
-                                if (unsigned(w1[b] >> 32) != ep) w1[b] = ld_relaxed64(pb + b * kRows + et + 128);
+                                if (unsigned(w0[b] >> 32) != ep) w0[b] = ld_relaxed64(pb + b * kRows + r0);
+                                if (unsigned(w1[b] >> 32) != ep) w1[b] = ld_relaxed64(pb + b * kRows + r0 + 1);
                             }
                         }
                         mine = epi_all(done);
@@ -744,22 +748,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 }
                 if (mine && st.mode == sk::kGateUp) {
                     const int s = t / p.RT, rt = t % p.RT;
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const int col = et + 128 * hh;
-                        const int grow = rt * kRows + col;
-                        const float y = grow < 2 * j.I ? (hh ? v1 + b1 : v0 + b0) : 0.f;
-                        const float lin = __shfl_down_sync(kFull, y, 1);
-                        if ((lane & 1) == 0) {
-                            const float gv = fminf(y, j.limit);
-                            const float lv = fminf(fmaxf(lin, -j.limit), j.limit);
-                            aval[col >> 1] = __fdividef(gv, 1.f + __expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
-                        }
-                    }
-                    epi_sync();
+                    const int grow = rt * kRows + r0;
+                    const float y = grow < 2 * j.I ? v0 + b0 : 0.f;          // glu row
+                    const float lin = grow + 1 < 2 * j.I ? v1 + b1 : 0.f;    // linear row
+                    const float gv = fminf(y, j.limit);
+                    const float lv = fminf(fmaxf(lin, -j.limit), j.limit);
+                    const float act = __fdividef(gv, 1.f + __expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
                     {                                // the tile's four 32-element blocks, one per epilogue warp
                         const int gb = rt * (kRows / 64) + (warp - 2);
-                        quantize_block_terms_warp32<NT>(aval[(warp - 2) * 32 + lane],
+                        quantize_block_terms_warp32<NT>(act,
                                                         j.aq_img + (size_t(s) * j.dn.SPS + gb / 8) * kA, gb % 8,
                                                         j.aq_sf + (size_t(s) * j.dn.KT + gb / 4) * kSF8, gb % 4,
                                                         gb * 32 < j.I);
@@ -767,11 +764,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
 
                     if (et == 0 && st.seg < 8) stamp<kTrace>(j, 140 + st.seg);
                 } else if (mine) {
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const int grow = t * kRows + et + 128 * hh;
-                        if (grow < j.H) j.x_resid[grow] += hh ? v1 + b1 : v0 + b0;
-                    }
+                    const int grow = t * kRows + r0;
+                    if (grow < j.H) j.x_resid[grow] += v0 + b0;
+                    if (grow + 1 < j.H) j.x_resid[grow + 1] += v1 + b1;
                 }
             }
             // after the last gate/up segment (also when a wait gave up, so other CTAs are not held up)

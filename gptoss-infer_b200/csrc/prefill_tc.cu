@@ -265,6 +265,7 @@ __device__ __forceinline__ void tmem_cp_128x256b(uint32_t tmem_col, uint64_t sde
 
 // One warp quantizes 8 blocks (K block kb, 4 lanes per 32-value block) of the source row `src` once and writes the
 // terms into the A terms of `nd` destination rows (pos = 128 * tile + row in the tile; negative = none).
+template <int MaxD>                                 // destinations the caller may pass (nd <= MaxD <= 8)
 __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ src, int K, int kb, const int (&pos)[8],
                                                     int nd, int KB, uint8_t* const (&img)[8]) {
     const int lane = threadIdx.x & 31, sub = lane & 3, gl = lane >> 2;
@@ -282,36 +283,38 @@ __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ sr
     }
     // The scale bytes of the 8 blocks as two words per (row, quadrant copy): lane l < 8 stores word (l >> 2) of
     // quadrant copy l & 3, covering blocks 4 (l >> 2) .. + 3. A term's scale follows from its block's k (term 0
-    // carries k + 127; term 1 k - 1; term t >= 2 k + 2 - 3t; clamped at 0), so the four blocks' k are gathered once,
-    // at term 0, and every term's scale word is computed locally.
+    // carries k + 127; term 1 k - 1; term t >= 2 k + 2 - 3t; clamped at 0), so the four blocks' term-0 scales are
+    // gathered once and every later word is a bytewise saturating subtraction (saturating step by step equals
+    // clamping the total, the amounts only grow).
     const int wsel = (lane >> 2) & 1, qsel = lane & 3;
     // Per destination, once: where this lane's code word and scale word of term NT - 1 go (the terms follow in
     // descending order, kTermA apart).
-    uint8_t* pw[8];
-    uint8_t* ps[8];
+    uint8_t* pw[MaxD];
+    uint8_t* ps[MaxD];
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
+    for (int s = 0; s < MaxD; ++s) {
         const bool on = s < nd && pos[s] >= 0;
         const int ps_ = on ? pos[s] : 0, m = ps_ / kTileM, r = ps_ % kTileM;
         uint8_t* piece = a_term(img[s], m, KB, kb, NT - 1);
         pw[s] = on ? piece + a_unit_off(r, gl) + sub * 4 : nullptr;
         ps[s] = on ? piece + a_sf_off(r, 4 * wsel, qsel) : nullptr;
     }
-    int kq[4] = {0, 0, 0, 0};
+    uint32_t sw0 = 0, sw = 0;
     quantize_block_digits_lanes4(v8, [&](int term, uint32_t word, uint32_t scale) {
         if (term == 0) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) kq[kk] = int(__shfl_sync(kFull, scale, 4 * (4 * wsel + kk))) - 127;
-        }
-        uint32_t sw = 0;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            const int kt = term == 0 ? kq[kk] : (term == 1 ? kq[kk] - 1 : kq[kk] + 2 - 3 * term);
-            sw |= uint32_t(max(kt + 127, 0)) << (8 * kk);
+            for (int kk = 0; kk < 4; ++kk) sw0 |= (__shfl_sync(kFull, scale, 4 * (4 * wsel + kk)) & 0xFFu) << (8 * kk);
+            sw = sw0;
+        } else if (term == 1) {
+            sw = __vsubus4(sw0, 0x01010101u);
+        } else if (term == 2) {
+            sw = __vsubus4(sw0, 0x04040404u);
+        } else {
+            sw = __vsubus4(sw, 0x03030303u);
         }
         const size_t toff = size_t(NT - 1 - term) * kTermA;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
+        for (int s = 0; s < MaxD; ++s) {
             if (!pw[s]) continue;
             if (valid) *reinterpret_cast<uint32_t*>(pw[s] + toff) = word;
             if (lane < 8) *reinterpret_cast<uint32_t*>(ps[s] + toff) = sw;
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(256) quantize_h_kernel(const float* __restrict
             pos[s] = s < k ? pos_of[size_t(t) * k + s] : -1;
             img[s] = imgs.p[(s < k && dest_of) ? (dest_of[size_t(t) * k + s] & 7) : 0];
         }
-        quantize_row_kblock(h + size_t(t) * H, H, kb, pos, k, KB, img);
+        quantize_row_kblock<8>(h + size_t(t) * H, H, kb, pos, k, KB, img);
     }
     if (dest_of) __threadfence_system();                    // expert parallel: stores into peers' regions
 }
@@ -365,7 +368,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
             pos[s] = s == 0 ? m * kTileM + j : -1;
             im[s] = img;
         }
-        quantize_row_kblock(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, im);
+        quantize_row_kblock<1>(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, im);
     }
 }
 

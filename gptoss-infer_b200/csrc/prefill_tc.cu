@@ -700,6 +700,32 @@ __global__ void combine_kernel(const float* __restrict__ out_ts, int T, int k, i
     }
 }
 
+// The same four values per thread (H % 4 == 0, both arrays 16-byte aligned); each value's additions in the same order.
+__global__ void combine4_kernel(const float4* __restrict__ out_ts, int T, int k, int H4, float4* __restrict__ x_resid) {
+    const long long n = (long long)T * H4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long t = i / H4, h = i - t * H4;
+        float4 acc = x_resid[i];
+        for (int s = 0; s < k; ++s) {
+            const float4 o = out_ts[(t * k + s) * H4 + h];
+            acc.x += o.x;
+            acc.y += o.y;
+            acc.z += o.z;
+            acc.w += o.w;
+        }
+        x_resid[i] = acc;
+    }
+}
+
+// x_resid[t] += the k result rows of token t, slot by slot.
+void launch_combine(const float* out_ts, int T, int k, int H, float* x_resid, int grid, cudaStream_t s) {
+    if (H % 4 == 0 && ((reinterpret_cast<uintptr_t>(out_ts) | reinterpret_cast<uintptr_t>(x_resid)) & 15) == 0)
+        combine4_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(out_ts), T, k, H / 4,
+                                             reinterpret_cast<float4*>(x_resid));
+    else
+        combine_kernel<<<grid, 256, 0, s>>>(out_ts, T, k, H, x_resid);
+}
+
 // ------------------------------------------------------------------------------------------------ expert parallel
 // The batched MoE with the experts spread over G ranks (one GPU each), tokens split over the ranks. Every rank
 // allocates one zero-initialised "region" (cudaMalloc, shared with the others through CUDA IPC) and gets every
@@ -1004,7 +1030,7 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
             check_launch("moe_batched quantize act");
         }
     }
-    combine_kernel<<<sms * 8, 256, 0, s>>>(out, a.T, a.k, a.H, a.x_resid);
+    launch_combine(out, a.T, a.k, a.H, a.x_resid, sms * 8, s);
     check_launch("moe_batched combine");
 }
 
@@ -1133,8 +1159,7 @@ void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
     ep_barrier_kernel<<<1, 32, 0, s>>>(d, 2);
     check_launch("ep barrier 2");
     if (a.T > 0) {
-        combine_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float*>(own + L.off_out), a.T, a.k, a.H,
-                                                 a.x_resid);
+        launch_combine(reinterpret_cast<const float*>(own + L.off_out), a.T, a.k, a.H, a.x_resid, sms * 8, s);
         check_launch("ep combine");
     }
 }

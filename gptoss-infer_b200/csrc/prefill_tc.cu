@@ -63,16 +63,22 @@ __global__ void router_w64_kernel(const __nv_bfloat16* __restrict__ W, int E, in
     }
 }
 
-// kRtTok tokens per CTA, 512 threads: RMSNorm (warp w < kRtTok on token w), h in shared memory (fp32; each value is
-// widened exactly to fp64 at its FMA), then thread (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp,
-// kp + 16, ... for the CTA's tokens (the weight loads of twelve k issued ahead of their FMAs, each load serving all
-// the tokens); the 16 partial sums (stored over h, which is dead by then) are added in order and warp w picks token
-// w's top k on order-preserving integer keys of the fp64 logits.
+// kRtTok tokens per CTA, 512 threads: RMSNorm (warp w < kRtTok on token w), h in shared memory (fp32), then thread
+// (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp, kp + 16, ... for the CTA's tokens, chunk by chunk of
+// K: the chunk's twelve weight loads per thread are issued first, the CTA widens the chunk's h values to fp64 once
+// (exact; widening at every FMA kept the conversion pipe saturated), then each load serves all the tokens; the 16
+// partial sums (stored over h, which is dead by then) are added in order and warp w picks token w's top k on
+// order-preserving integer keys of the fp64 logits.
 constexpr int kRtParts = 16;
 static_assert(kRtTok <= 16, "one top-k warp per token");
-__host__ __device__ constexpr int router_smem_bytes(int H) {
-    return kRtTok * H * 4 > kRtParts * kRtTok * 32 * 8 ? kRtTok * H * 4 : kRtParts * kRtTok * 32 * 8;
+constexpr int kRtAhead = 12;                   // weight loads in flight per router thread
+constexpr int kRtChunk = kRtAhead * kRtParts;  // K values widened to fp64 at a time (192)
+// Router shared memory: h (fp32, [kRtTok][H]; the partial sums go over it after the FMAs), then one chunk of h
+// widened to fp64 ([kRtTok][kRtChunk]).
+__host__ __device__ constexpr int router_chunk_off(int H) {
+    return ((kRtTok * H * 4 > kRtParts * kRtTok * 32 * 8 ? kRtTok * H * 4 : kRtParts * kRtTok * 32 * 8) + 15) & ~15;
 }
+__host__ __device__ constexpr int router_smem_bytes(int H) { return router_chunk_off(H) + kRtTok * kRtChunk * 8; }
 __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
                                                              const float* __restrict__ x, const float* __restrict__ g,
                                                              float eps, int T, int E, int H, int k,
@@ -112,22 +118,28 @@ __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __
     double acc[kRtTok];
 #pragma unroll
     for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = 0.0;
-    constexpr int kAhead = 12;                               // weight loads in flight per thread
-    for (int kk0 = kp; kk0 < H; kk0 += kAhead * kRtParts) {
-        double wk[kAhead];
+    double* hc = reinterpret_cast<double*>(rt_smem + router_chunk_off(H));   // [kRtTok][kRtChunk]
+    for (int c0 = 0; c0 < H; c0 += kRtChunk) {
+        double wk[kRtAhead];
 #pragma unroll
-        for (int u = 0; u < kAhead; ++u) {
-            const int kk = kk0 + u * kRtParts;
+        for (int u = 0; u < kRtAhead; ++u) {
+            const int kk = c0 + kp + u * kRtParts;
             wk[u] = kk < H ? W64[size_t(kk) * 32 + e] : 0.0;
         }
+        for (int i = tid; i < kRtTok * kRtChunk; i += 512) {
+            const int tb = i / kRtChunk, jj = i - tb * kRtChunk;
+            hc[i] = c0 + jj < H ? double(hs[tb * H + c0 + jj]) : 0.0;
+        }
+        __syncthreads();
 #pragma unroll
-        for (int u = 0; u < kAhead; ++u) {
-            const int kk = kk0 + u * kRtParts;
-            if (kk < H) {
+        for (int u = 0; u < kRtAhead; ++u) {
+            const int jj = kp + u * kRtParts;
+            if (c0 + jj < H) {
 #pragma unroll
-                for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk[u], double(hs[tb * H + kk]), acc[tb]);
+                for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk[u], hc[tb * kRtChunk + jj], acc[tb]);
             }
         }
+        __syncthreads();                                     // the chunk buffer is refilled next
     }
     __syncthreads();                                         // h is dead: the partial sums go over it
 #pragma unroll
@@ -936,7 +948,7 @@ void launch_router_batched(const double* W64, const float* b, const float* x, co
     require(H % 8 == 0 && H >= 8, "router_batched: H must be a positive multiple of 8");
     require(k >= 1 && k <= 8 && k <= E && E <= 32, "router_batched: needs 1 <= k <= 8 and k <= E <= 32");
     const int smem = pf::router_smem_bytes(H);
-    require(smem <= 200 * 1024, "router_batched: H too large");
+    require(smem <= 220 * 1024, "router_batched: H too large");
     static std::mutex mu;
     static std::map<int, int> done;
     {

@@ -842,11 +842,10 @@ const StageTable& stage_table(const Part& g, const Part& d, int nc, int k, int H
     std::vector<Stage> all;
     std::vector<int> hdr(size_t(nc) * 4, 0);
     // Gate/up streams from HBM, a resource all CTAs share, so its ranges hold equal unit counts. Down's weights are
-    // resident by the time its stages run, which are then bound by each CTA's issue rate: its ranges balance a cost
-    // model (cycles, clock64 trace of this kernel on a B200): a stage ≈ 500 + 145 per unit (1.08K for 4 units), a
-    // segment's drain and publication ≈ 1.5K, finalizing a tile (partial sums, residual) ≈ 1.5K.
+    // resident by the time its stages run, which are then bound by each CTA's issue rate: its ranges balance the
+    // per-CTA cost model sk::kDownCost.
     const std::vector<long long> Bg = sk::equal_bounds(g, nc);
-    const std::vector<long long> Bd = sk::balanced_bounds(d, nc, sk::CostModel{500.0, 145.0, 1500.0, 1500.0});
+    const std::vector<long long> Bd = sk::balanced_bounds(d, nc, sk::kDownCost);
     for (int c = 0; c < nc; ++c) {
         int seg = 0;
         const int ngu = sk::build_stages(g, Bg.data(), c, nullptr, 0, 0, 0, &seg);

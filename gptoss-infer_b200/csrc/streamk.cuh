@@ -59,6 +59,11 @@ struct CostModel {
     double stage, unit, segment, finalize;
 };
 
+// The decode kernel's down part, from its clock64 trace on a B200: a stage ≈ 500 + 145 per unit (1.08K for 4 units,
+// the weights already resident), a segment's drain and publication ≈ 1.5K, finalizing a tile (partial sums,
+// residual) ≈ 1.5K.
+constexpr CostModel kDownCost{500.0, 145.0, 1500.0, 1500.0};
+
 // Range boundaries of nc CTAs with equal unit counts: unit c * total / nc rounded up to the next stage start. A part
 // of at most nc stages gets one stage per CTA for its first CTAs instead, so that no empty range falls between two
 // CTAs sharing a tile (the partial-sum slots of a tile are indexed by CTA distance).

@@ -113,7 +113,8 @@ void gptoss_moe_layer_destroy(gptoss_moe_layer* layer);
  * cudaStream_t; NULL = legacy default stream): one persistent cooperative kernel (RMSNorm, router, top-k, softmax,
  * gate/up with SwiGLU, down with the weighted combine, all on tensor cores). x_resid may alias x. `events`, if not
  * NULL, points to 4 cudaEvent_t: [0], [1], [2] are recorded before the kernel and [3] after it. Calls from one
- * thread share its workspace and must not overlap on the GPU. */
+ * thread share its workspace and must not overlap on the GPU; the first call after a change of shape (k, H, I) on
+ * that thread also clears the workspace's state words, on `stream`. */
 int gptoss_moe_layer_forward(gptoss_moe_layer* layer, const float* x, float* x_resid, void* stream,
                              void* const* events);
 

@@ -60,6 +60,24 @@ struct Scratch {
     }
 };
 thread_local Scratch g_scratch;
+thread_local Scratch g_flag;                // one device int for the NaN-scale check
+
+// Error code the scale repack stores when it meets an E8M0 byte 0xFF (NaN): the reference refuses such a scale at
+// load (runtime/src/engine.cu:119-122); here every path that repacks scales refuses it.
+constexpr int kNanScaleCode = 200;
+
+// Runs f(flag) with a zeroed device int and throws if f's kernels stored kNanScaleCode into it (synchronizes).
+template <class F>
+void with_nan_scale_check(const char* what, F&& f) {
+    int* flag = static_cast<int*>(g_flag.get(sizeof(int)));
+    GPT_CHECK(cudaMemset(flag, 0, sizeof(int)));
+    f(flag);
+    sync_check(what);
+    int h = 0;
+    GPT_CHECK(cudaMemcpy(&h, flag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h == kNanScaleCode)
+        throw std::runtime_error(std::string(what) + ": an E8M0 scale byte is 0xFF (NaN); refusing the weights");
+}
 
 // Workspace of the tensor-core decode path (activation terms, epoch-tagged partial sums, grid-barrier words, gathered
 // scales), owned by the calling thread, one per device. Zero-filled whenever it is (re)allocated. The words that carry
@@ -114,6 +132,8 @@ void check_tc_error(void* ws, const gpt::DecodeTcLayout& L) {
     GPT_CHECK(cudaMemcpy(&h, static_cast<char*>(ws) + L.off_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (h) {
         GPT_CHECK(cudaMemset(static_cast<char*>(ws) + L.zero_bytes_from, 0, L.zero_bytes_to - L.zero_bytes_from));
+        if (h == kNanScaleCode)
+            throw std::runtime_error("moe: an E8M0 scale of a selected expert is 0xFF (NaN); refusing to use it");
         throw std::runtime_error("moe (tensor cores): a bounded wait gave up (site " + std::to_string(h) + ")");
     }
 }
@@ -125,10 +145,11 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
                 const float* weights, float* x_resid, int k, int H, int I, float alpha, float limit, void* ws,
                 const gpt::DecodeTcLayout& L, cudaStream_t s) {
     char* w = static_cast<char*>(ws);
+    int* err = reinterpret_cast<int*>(w + L.off_err);      // a NaN scale is reported through the error word
     gpt::launch_repack_sf(gu_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_gu), k, 2 * I, H / 32, s, ids,
-                          gpt::kDecodeTileRows);
+                          gpt::kDecodeTileRows, err, kNanScaleCode);
     gpt::launch_repack_sf(dn_scales, reinterpret_cast<uint8_t*>(w + L.off_sfa_dn), k, H, I / 32, s, ids,
-                          gpt::kDecodeTileRows);
+                          gpt::kDecodeTileRows, err, kNanScaleCode);
     // The expert count is not part of this ABI: the maps span the 32 experts the format allows; only the selected
     // experts' rows are ever read.
     const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, 32, 128, gpt::kDecodeTileRows);
@@ -397,8 +418,13 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
         try {
             GPT_CHECK(cudaMalloc(&l->sfa_gu, gpt::sf_repacked_bytes(E, 2 * I, H / 32, gpt::kDecodeTileRows)));
             GPT_CHECK(cudaMalloc(&l->sfa_dn, gpt::sf_repacked_bytes(E, H, I / 32, gpt::kDecodeTileRows)));
-            gpt::launch_repack_sf(gu_scales, l->sfa_gu, E, 2 * I, H / 32, nullptr, nullptr, gpt::kDecodeTileRows);
-            gpt::launch_repack_sf(dn_scales, l->sfa_dn, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows);
+            // every scale byte of every expert passes through the repack once, which also refuses 0xFF (NaN)
+            with_nan_scale_check("moe_layer_create", [&](int* flag) {
+                gpt::launch_repack_sf(gu_scales, l->sfa_gu, E, 2 * I, H / 32, nullptr, nullptr, gpt::kDecodeTileRows,
+                                      flag, kNanScaleCode);
+                gpt::launch_repack_sf(dn_scales, l->sfa_dn, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows,
+                                      flag, kNanScaleCode);
+            });
             l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
             l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
             GPT_CHECK(cudaMalloc(&l->w64, size_t(H) * 32 * sizeof(double)));
@@ -455,8 +481,12 @@ int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales
         const size_t sgu = gpt::sf_repacked_bytes(E, 2 * I, H / 32, gpt::kDecodeTileRows);
         const size_t sdn = gpt::sf_repacked_bytes(E, H, I / 32, gpt::kDecodeTileRows);
         uint8_t* sf = static_cast<uint8_t*>(g_pws_sf.get(sgu + sdn));
-        gpt::launch_repack_sf(gu_scales, sf, E, 2 * I, H / 32, nullptr, nullptr, gpt::kDecodeTileRows);
-        gpt::launch_repack_sf(dn_scales, sf + sgu, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows);
+        with_nan_scale_check("moe_batched", [&](int* flag) {
+            gpt::launch_repack_sf(gu_scales, sf, E, 2 * I, H / 32, nullptr, nullptr, gpt::kDecodeTileRows, flag,
+                                  kNanScaleCode);
+            gpt::launch_repack_sf(dn_scales, sf + sgu, E, H, I / 32, nullptr, nullptr, gpt::kDecodeTileRows, flag,
+                                  kNanScaleCode);
+        });
         const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
         const CUtensorMap td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
         const gpt::PrefillLayout L = gpt::prefill_layout(T, k, E, H, I);
@@ -716,6 +746,20 @@ int gptoss_ep_status(int E, int k, int H, int I, int world, int T_max, int* code
         int h = 0;
         GPT_CHECK(cudaMemcpy(&h, ws + L.off_misc + 256, sizeof(int), cudaMemcpyDeviceToHost));
         *code = h;
+    });
+}
+
+int gptoss_test_decode_epoch(int k, int H, int I, unsigned set_to, unsigned* previous) {
+    return guard([&] {
+        if (!tc_shape_ok(k, H, I)) throw std::runtime_error("test_decode_epoch: not a tensor-core decode shape");
+        const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
+        char* w = static_cast<char*>(g_dws.for_layout(L, k, H, I, nullptr));
+        unsigned* word = reinterpret_cast<unsigned*>(w + L.off_err + 256) + 4;   // grid-barrier word 4: the epoch
+        GPT_CHECK(cudaDeviceSynchronize());
+        unsigned prev = 0;
+        GPT_CHECK(cudaMemcpy(&prev, word, sizeof(prev), cudaMemcpyDeviceToHost));
+        GPT_CHECK(cudaMemcpy(word, &set_to, sizeof(set_to), cudaMemcpyHostToDevice));
+        if (previous) *previous = prev;
     });
 }
 

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
@@ -95,6 +96,61 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
+}
+
+// Reciprocal root-mean-square of a row from its sum of squares: the RMSNorm scale 1 / sqrt(mean(x^2) + eps) of
+// gptoss_ref/model.py:21-22. Every RMSNorm in this library (the stand-alone kernel, the routers, the fused decode
+// kernel) takes its scale from here, so they agree bit for bit given the same sum.
+__device__ __forceinline__ float rms_scale(float sum_sq, int n, float eps) {
+    return 1.0f / sqrtf(sum_sq / float(n) + eps);
+}
+
+// ---- Expert selection, shared by every router (stand-alone decode, fused decode, batched).
+//
+// Logits are fp64 and compared through a 64-bit unsigned key that preserves their order: a non-negative value keeps
+// its bits with the top bit set, a negative one is bit-inverted. NaN and lanes that hold no expert get key 0, which
+// no real logit reaches (-inf maps to 0x000FFFFFFFFFFFFF), so they can only be picked once every real logit is.
+__device__ __forceinline__ unsigned long long logit_order_key(double v, bool valid) {
+    const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(v));
+    if (!valid || (bits << 1) > 0xFFE0000000000000ull) return 0ull;          // NaN: exponent all ones, mantissa != 0
+    return (bits >> 63) ? ~bits : (bits | 0x8000000000000000ull);
+}
+
+// Top k of the 32 lane-held logits (lane e holds expert e; lanes with valid == false hold none). Each round the warp
+// takes the largest key with two 32-bit max reductions (high word, then low word among the lanes that hold that high
+// word) and the smallest expert id among the lanes holding the full key, so equal logits go to the lower id; the
+// winner leaves the race. Lane q < k receives the q-th pick (descending logit): its expert id and logit.
+__device__ __forceinline__ void warp_topk_logits(double v, bool valid, int k, int& pick_id, double& pick_logit) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long key = logit_order_key(v, valid);
+    unsigned id = valid ? unsigned(lane) : 32u + unsigned(lane);
+    pick_id = 0;
+    pick_logit = 0.0;
+    for (int q = 0; q < k; ++q) {
+        const unsigned hi = unsigned(key >> 32), lo = unsigned(key);
+        const unsigned best_hi = __reduce_max_sync(kFull, hi);
+        const unsigned best_lo = __reduce_max_sync(kFull, hi == best_hi ? lo : 0u);
+        const unsigned winner = __reduce_min_sync(kFull, hi == best_hi && lo == best_lo ? id : 0xFFFFFFFFu);
+        const double wv = __shfl_sync(kFull, v, int(winner & 31u));
+        if (lane == q) {
+            pick_id = int(winner);
+            pick_logit = wv;
+        }
+        if (id == winner) {
+            key = 0ull;
+            id = 32u + unsigned(lane);
+        }
+    }
+}
+
+// Gate weights of the k picks held in lanes 0..k-1 (descending, so lane 0 holds the largest): the softmax over the k
+// selected logits in fp32, as gptoss_ref/model.py:97-98 computes it. Lanes >= k return 0.
+__device__ __forceinline__ float warp_pick_softmax(double pick_logit, int k) {
+    const int lane = threadIdx.x & 31;
+    const float l = float(pick_logit);
+    const float lmax = __shfl_sync(kFull, l, 0);
+    const float e = lane < k ? expf(l - lmax) : 0.f;
+    return e / warp_sum(e);
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start its prologue, and wait for the previous

@@ -4,6 +4,8 @@
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <mutex>
+#include <stdexcept>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -11,38 +13,62 @@
 
 namespace gpt {
 
+// SM count of the current device, cached per device ordinal (a process may drive GPUs of different sizes).
 int num_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        GPT_CHECK(cudaGetDevice(&dev));
-        GPT_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
-    }
-    return n;
+    static std::mutex mu;
+    static int count[64] = {};
+    int dev = 0;
+    GPT_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("device ordinal out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!count[dev]) GPT_CHECK(cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev));
+    return count[dev];
 }
 
 namespace {
 
 // ---------------------------------------------------------------------------------------------------------------
-// RMSNorm: one CTA per row.
-__global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                       float* __restrict__ y, int n, float eps) {
-    __shared__ float red[32];
+// RMSNorm, one CTA of kNormThreads per row. Each warp adds the squares of a strided set of the row's float4 chunks
+// (scalars when the row is not 16-byte aligned); the eight warp sums meet in shared memory and every thread adds
+// them in warp order, so all threads hold the same total without a second reduction round; then each thread scales
+// the chunks it read.
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                               float* __restrict__ y, int n, float eps) {
+    __shared__ float warp_ss[kNormThreads / 32];
     const float* xr = x + size_t(blockIdx.x) * n;
     float* yr = y + size_t(blockIdx.x) * n;
+    const bool vec = (n & 3) == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(yr) |
+                                       reinterpret_cast<uintptr_t>(w)) & 15) == 0;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) red[0] = v;
+    if (vec) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        for (int c = threadIdx.x; c < (n >> 2); c += kNormThreads) {
+            const float4 v = x4[c];
+            ss = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, ss))));
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += kNormThreads) ss = fmaf(xr[i], xr[i], ss);
     }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) warp_ss[threadIdx.x >> 5] = ss;
     __syncthreads();
-    const float r = 1.0f / sqrtf(red[0] / float(n) + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * r * w[i];
+    float total = 0.f;
+#pragma unroll
+    for (int q = 0; q < kNormThreads / 32; ++q) total += warp_ss[q];
+    const float r = rms_scale(total, n, eps);
+    if (vec) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        const float4* w4 = reinterpret_cast<const float4*>(w);
+        float4* y4 = reinterpret_cast<float4*>(yr);
+        for (int c = threadIdx.x; c < (n >> 2); c += kNormThreads) {
+            const float4 v = x4[c], g = w4[c];
+            y4[c] = make_float4(v.x * r * g.x, v.y * r * g.y, v.z * r * g.z, v.w * r * g.w);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += kNormThreads) yr[i] = xr[i] * r * w[i];
+    }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -118,7 +144,7 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
         __syncthreads();
         float tot = 0.f;
         for (int w = 0; w < kRouterThreads / 32; ++w) tot += ssum[w];
-        const float rn = 1.0f / sqrtf(tot / float(H) + eps);
+        const float rn = rms_scale(tot, H, eps);
         for (int i = tid; i < H; i += kRouterThreads) {
             const float v = x_in[i] * rn * norm_w[i];
             hs[i] = v;
@@ -169,29 +195,15 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
     cluster_sync_all();
     if (r != 0 || warp != 0) return;
 
-    // Lane i holds expert i; lanes >= E and already-picked experts carry -inf and an id >= 32, so real experts win
-    // ties against them. NaN never wins.
-    double v = lane < E ? logits[lane] : -INFINITY;
-    if (v != v) v = -INFINITY;
-    int id = lane < E ? lane : 32 + lane;
-    float sel = -INFINITY;
-    int sel_id = 0;
-    for (int j = 0; j < k; ++j) {
-        double best = v;
-        int besti = id;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const double ob = __shfl_xor_sync(kFull, best, o);
-            const int oi = __shfl_xor_sync(kFull, besti, o);
-            if (ob > best || (ob == best && oi < besti)) { best = ob; besti = oi; }
-        }
-        if (lane == j) { sel = float(best); sel_id = besti; }
-        if (id == besti) { v = -INFINITY; id = 32 + lane; }
+    // warp 0 of CTA 0: top k of the E logits and the softmax over the picks (shared selection code)
+    int pick = 0;
+    double pick_logit = 0.0;
+    warp_topk_logits(lane < E ? logits[lane] : 0.0, lane < E, k, pick, pick_logit);
+    const float gate = warp_pick_softmax(pick_logit, k);
+    if (lane < k) {
+        ids[lane] = pick;
+        weights[lane] = gate;
     }
-    const float top = __shfl_sync(kFull, sel, 0);
-    const float p = lane < k ? expf(sel - top) : 0.f;
-    const float sum = warp_sum(p);
-    if (lane < k) { ids[lane] = sel_id; weights[lane] = p / sum; }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -392,10 +404,19 @@ void moe_simt_nb(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float
     const size_t smem_dn = size_t(k) * 32 * Gp * sizeof(float);
     const int grid_dn = std::max(1, std::min(sms * 2, (H / 2 + 7) / 8));
     auto kern = down_simt_kernel<NB, 4>;
-    static int smem_set = 0;                              // attribute calls stay out of CUDA-graph captures
-    if (int(smem_dn) > smem_set) {
-        GPT_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_dn)));
-        smem_set = int(smem_dn);
+    // The attribute is per device and set only when a larger plan first needs it (attribute calls stay out of
+    // CUDA-graph captures after the first eager call of a shape).
+    static std::mutex mu;
+    static int smem_set[64] = {};
+    {
+        int dev = 0;
+        GPT_CHECK(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= 64) throw std::runtime_error("moe down (simt): device ordinal out of range");
+        std::lock_guard<std::mutex> lock(mu);
+        if (int(smem_dn) > smem_set[dev]) {
+            GPT_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_dn)));
+            smem_set[dev] = int(smem_dn);
+        }
     }
     launch_pdl(kern, dim3(grid_dn), dim3(kSimtThreads), smem_dn, s, true, dn_blocks, dn_scales, dn_bias,
                (const float*)a, ids, weights, x_resid, k, H, I);
@@ -406,7 +427,7 @@ void moe_simt_nb(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float
 
 void launch_rmsnorm(const float* x, const float* w, float* y, int T, int n, float eps, cudaStream_t s) {
     require(T >= 1 && n >= 1, "rmsnorm: T and n must be positive");
-    rmsnorm_kernel<<<T, 1024, 0, s>>>(x, w, y, n, eps);
+    rmsnorm_kernel<<<T, kNormThreads, 0, s>>>(x, w, y, n, eps);
     check_launch("rmsnorm");
 }
 

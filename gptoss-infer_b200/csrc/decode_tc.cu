@@ -27,6 +27,7 @@
 // an error instead of hanging. The per-CTA stage lists are computed on the host once per shape (stream-K partition,
 // segment boundaries and which CTAs share each tile) and read by each CTA at start.
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <stdexcept>
@@ -156,6 +157,10 @@ __device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// The launch epoch that follows prev, skipping 0 (the tag of a zero-filled partial-sum word, which must never read
+// as current).
+__host__ __device__ __forceinline__ unsigned next_epoch(unsigned prev) { return prev == 0xFFFFFFFFu ? 1u : prev + 1u; }
+
 __device__ __forceinline__ double bf16lo(uint32_t w) { return double(__uint_as_float(w << 16)); }
 __device__ __forceinline__ double bf16hi(uint32_t w) { return double(__uint_as_float(w & 0xffff0000u)); }
 
@@ -247,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     pdl_launch_dependents();
     pdl_wait();
     // This launch's epoch (tags its split-tile partial sums): one more than the previous launch's, which that
-    // launch's last CTA out stored; never 0, the value of a zeroed word.
-    const unsigned ep = __ldcg(&j.gbar[4]) + 1u;
+    // launch's last CTA out stored; never 0, the value of a zeroed word: after 2^32 - 1 launches the count wraps to 1.
+    const unsigned ep = next_epoch(__ldcg(&j.gbar[4]));
     if (tid == 0 && s_n > cap) atomicCAS(j.err, 0, 100);    // host sized the stage list too small
     if (tid == 0) stamp<kTrace>(j, 123);
 #pragma unroll
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         if (j.norm_w) {
             float tot = 0.f;
             for (int w = 0; w < kThreads / 32; ++w) tot += aval[w];
-            rn = 1.0f / sqrtf(tot / float(H) + j.eps);
+            rn = rms_scale(tot, H, j.eps);
         }
 #pragma unroll
         for (int r = 0; r < kMaxX4; ++r) {
@@ -367,31 +372,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                     for (int w = 0; w < kThreads / 32; ++w) tt += red[w * 32 + lane];
                     v = tt + double(bias);
                 }
-                const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(v));
-                unsigned long long key = (bits >> 63) ? ~bits : (bits | (1ull << 63));
-                if ((bits & 0x7FFFFFFFFFFFFFFFull) > 0x7FF0000000000000ull || lane >= j.E) key = 0;   // NaN / unused
                 if (lane == 0) stamp<kTrace>(j, 120);
-                unsigned id = lane < j.E ? unsigned(lane) : 32u + lane;
-                float sel = -INFINITY;
                 int sel_id = 0;
-                for (int q = 0; q < j.k; ++q) {
-                    const unsigned hi = unsigned(key >> 32), lo = unsigned(key);
-                    const unsigned m1 = __reduce_max_sync(kFull, hi);
-                    const unsigned m2 = __reduce_max_sync(kFull, hi == m1 ? lo : 0u);
-                    const unsigned win = __reduce_min_sync(kFull, hi == m1 && lo == m2 ? id : 0xFFFFFFFFu);
-                    const double wv = __shfl_sync(kFull, v, int(win & 31u));
-                    if (lane == q) { sel = float(wv); sel_id = int(win); }
-                    if (id == win) { key = 0; id = 32u + lane; }
-                }
+                double sel_logit = 0.0;
+                warp_topk_logits(v, lane < j.E, j.k, sel_id, sel_logit);
                 if (lane == 0) stamp<kTrace>(j, 121);
-                const float top = __shfl_sync(kFull, sel, 0);
-                const float pz = lane < j.k ? expf(sel - top) : 0.f;
-                const float sum = warp_sum(pz);
+                const float gate = warp_pick_softmax(sel_logit, j.k);
                 if (lane == 0) stamp<kTrace>(j, 122);
                 if (lane < j.k) {
                     ids_s[lane] = sel_id;
-                    w_s[lane] = pz / sum;
-                    if (j.ids_out && c == 0) { j.ids_out[lane] = sel_id; j.w_out[lane] = pz / sum; }
+                    w_s[lane] = gate;
+                    if (j.ids_out && c == 0) { j.ids_out[lane] = sel_id; j.w_out[lane] = gate; }
                 }
             }
         } else if (tid < j.k) {
@@ -1009,19 +1000,20 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     // Programmatic dependent launch lets the next kernel on the stream start as this one's CTAs exit. If this
     // runtime refuses it together with a cooperative launch, the first launch on this device finds out and every
     // later one goes without it.
-    static int pdl_ok[64] = {};                              // 0 unknown, 1 accepted, -1 refused
+    static std::atomic<int> pdl_ok[64] = {};                 // 0 unknown, 1 accepted, -1 refused
     int dev = 0;
     GPT_CHECK(cudaGetDevice(&dev));
-    cfg.numAttrs = dev < 64 && pdl_ok[dev] >= 0 ? 2 : 1;
+    require(dev >= 0 && dev < 64, "moe (tc): device ordinal out of range");
+    cfg.numAttrs = pdl_ok[dev].load() >= 0 ? 2 : 1;
     auto kernel = a.trace ? moe_fused_kernel<true> : moe_fused_kernel<false>;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, *a.tmap_gu, *a.tmap_dn, j);
-    if (e != cudaSuccess && cfg.numAttrs == 2 && dev < 64 && pdl_ok[dev] == 0) {
+    if (e != cudaSuccess && cfg.numAttrs == 2 && pdl_ok[dev].load() == 0) {
         (void)cudaGetLastError();
-        pdl_ok[dev] = -1;
+        pdl_ok[dev].store(-1);
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, kernel, *a.tmap_gu, *a.tmap_dn, j);
-    } else if (e == cudaSuccess && cfg.numAttrs == 2 && dev < 64) {
-        pdl_ok[dev] = 1;
+    } else if (e == cudaSuccess && cfg.numAttrs == 2) {
+        pdl_ok[dev].store(1);
     }
     GPT_CHECK(e);
     check_launch("moe (tensor cores, fused)");

@@ -46,9 +46,10 @@ void launch_moe_decode_simt(const uint8_t* gu_blocks, const uint8_t* gu_scales, 
 // [mats][ceil(rows/128)][ceil(G/4)][512]; tile_rows = 192 or 256: [mats][ceil(rows/tile_rows)][ceil(G/4)][2][512]
 // (the tile's two 128-row parts side by side for each K chunk of 128; a 192-row tile's second part holds 64 rows).
 size_t sf_repacked_bytes(long long mats, int rows, int G, int tile_rows = 128);
-// With ids != nullptr, output matrix m is gathered from raw matrix ids[m] (m < mats).
+// With ids != nullptr, output matrix m is gathered from raw matrix ids[m] (m < mats). With nan_flag != nullptr, a
+// scale byte 0xFF (E8M0 NaN) stores nan_code into *nan_flag (device int, if it still holds 0).
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
-                      const int* ids = nullptr, int tile_rows = 128);
+                      const int* ids = nullptr, int tile_rows = 128, int* nan_flag = nullptr, int nan_code = 1);
 
 // Tensor-core decode MoE (decode_tc.cu): one persistent cooperative kernel per MoE layer. Weights are read in tiles
 // of kDecodeTileRows rows (TMA boxes of kDecodeTileRows rows x 128 bytes; scales repacked with that tile size).

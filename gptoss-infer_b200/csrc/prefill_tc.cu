@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __
             ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
         }
         ss = warp_sum(ss);
-        if (lane == 0) rn_s[warp] = g ? 1.0f / sqrtf(ss / float(H) + eps) : 1.f;
+        if (lane == 0) rn_s[warp] = g ? rms_scale(ss, H, eps) : 1.f;
     }
     __syncthreads();
     for (int i = tid * 4; i < nt * H; i += 512 * 4) {
@@ -152,27 +152,13 @@ __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __
             for (int p = 0; p < kRtParts; ++p) v += red[p][warp][lane];
             v += double(b[lane]);
         }
-        const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(v));
-        unsigned long long key = (bits >> 63) ? ~bits : (bits | (1ull << 63));
-        if ((bits & 0x7FFFFFFFFFFFFFFFull) > 0x7FF0000000000000ull || lane >= E) key = 0;   // NaN / unused
-        unsigned id = lane < E ? unsigned(lane) : 32u + lane;
-        float sel = -INFINITY;
         int sel_id = 0;
-        for (int q = 0; q < k; ++q) {
-            const unsigned hi = unsigned(key >> 32), lo = unsigned(key);
-            const unsigned m1 = __reduce_max_sync(kFull, hi);
-            const unsigned m2 = __reduce_max_sync(kFull, hi == m1 ? lo : 0u);
-            const unsigned win = __reduce_min_sync(kFull, hi == m1 && lo == m2 ? id : 0xFFFFFFFFu);
-            const double wv = __shfl_sync(kFull, v, int(win & 31u));
-            if (lane == q) { sel = float(wv); sel_id = int(win); }
-            if (id == win) { key = 0; id = 32u + lane; }
-        }
-        const float top = __shfl_sync(kFull, sel, 0);
-        const float pz = lane < k ? expf(sel - top) : 0.f;
-        const float sum = warp_sum(pz);
+        double sel_logit = 0.0;
+        warp_topk_logits(v, lane < E, k, sel_id, sel_logit);
+        const float gate = warp_pick_softmax(sel_logit, k);
         if (lane < k) {
             ids[size_t(t) * k + lane] = sel_id;
-            wts[size_t(t) * k + lane] = pz / sum;
+            wts[size_t(t) * k + lane] = gate;
         }
     }
 }

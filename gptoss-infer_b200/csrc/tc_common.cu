@@ -77,8 +77,10 @@ CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t
 namespace {
 // raw [mats][rows][G] E8M0 bytes -> [mats][RT][KT][halves][512] tcgen05 chunks (tiles of 128 * halves rows,
 // RT = ceil(rows / tile), KT = ceil(G/4)), zero padded. One thread per output word of 4 bytes (one row's 4 k-blocks).
+// A scale byte 0xFF (E8M0's NaN encoding) sets *nan_flag to nan_code when a flag is given (the first code set stays).
 __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, long long mats, int rows,
-                                 int G, int RT, int KT, int halves, int tile_rows, const int* __restrict__ ids) {
+                                 int G, int RT, int KT, int halves, int tile_rows, const int* __restrict__ ids,
+                                 int* nan_flag, int nan_code) {
     const long long words = mats * RT * KT * halves * 128;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
          i += (long long)gridDim.x * blockDim.x) {
@@ -100,6 +102,7 @@ __global__ void repack_sf_kernel(const uint8_t* __restrict__ raw, uint8_t* __res
                 const int g = kt * 4 + kb;
                 if (g < G) v |= uint32_t(src[g]) << (8 * kb);
             }
+            if (nan_flag && __vcmpeq4(v, 0xFFFFFFFFu)) atomicCAS(nan_flag, 0, nan_code);
         }
         reinterpret_cast<uint32_t*>(out)[i] = v;
     }
@@ -112,12 +115,13 @@ size_t sf_repacked_bytes(long long mats, int rows, int G, int tile_rows) {
 }
 
 void launch_repack_sf(const uint8_t* raw, uint8_t* out, long long mats, int rows, int G, cudaStream_t s,
-                      const int* ids, int tile_rows) {
+                      const int* ids, int tile_rows, int* nan_flag, int nan_code) {
     require(tile_rows == 128 || tile_rows == 192 || tile_rows == 256, "repack_sf: tiles of 128, 192 or 256 rows");
     const int halves = (tile_rows + 127) / 128, RT = (rows + tile_rows - 1) / tile_rows, KT = (G + 3) / 4;
     const long long words = mats * RT * KT * halves * 128;
     const int grid = int(std::min<long long>((words + 255) / 256, num_sms() * 8LL));
-    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, halves, tile_rows, ids);
+    repack_sf_kernel<<<std::max(1, grid), 256, 0, s>>>(raw, out, mats, rows, G, RT, KT, halves, tile_rows, ids,
+                                                        nan_flag, nan_code);
     check_launch("repack_sf");
 }
 

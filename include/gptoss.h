@@ -58,7 +58,8 @@ int gptoss_kernel_router(const void* W, const float* b, const float* x, int E, i
 /* x_resid += sum_e w[e] * (W2[ids[e]] swiglu(W1[ids[e]] x_norm + b1) + b2)   (reference gptoss.h:54-58)
  * gu_blocks uint8 [E, 2I, H/32, 16], gu_scales uint8 [E, 2I, H/32], gu_bias fp32 [E, 2I],
  * dn_blocks uint8 [E, H, I/32, 16], dn_scales uint8 [E, H, I/32], dn_bias fp32 [E, H]; gate/up rows interleaved
- * (even = glu, clamped above at limit; odd = linear, clamped to [-limit, limit]). */
+ * (even = glu, clamped above at limit; odd = linear, clamped to [-limit, limit]). On the tensor-core path (the
+ * default, for H % 64 == 0 and I % 64 == 0) an E8M0 scale byte 0xFF (NaN) of a selected expert returns -1. */
 int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
                       const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias, const float* x_norm,
                       const int32_t* ids, const float* weights, float* x_resid, int k, int H, int I, float alpha,
@@ -102,7 +103,9 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
  * (they must stay valid for the handle's lifetime), repacks the E8M0 scales once into the tcgen05 scale-factor
  * layout (device memory owned by the handle, 24.9 MB for gpt-oss-20b's 32 experts) and builds the TMA descriptors;
  * returns NULL on failure (gptoss_last_error). Needs H % 64 == 0, I % 64 == 0, 1 <= k <= 8, k <= E <= 32.
- * norm_w fp32 [H]; router_w bf16 [E,H]; router_b fp32 [E]; expert layouts as gptoss_kernel_moe. Synchronizes. */
+ * An E8M0 scale byte 0xFF (NaN) in any expert fails the creation, as the reference's loader refuses it
+ * (runtime/src/engine.cu:119-122). norm_w fp32 [H]; router_w bf16 [E,H]; router_b fp32 [E]; expert layouts as
+ * gptoss_kernel_moe. Synchronizes. */
 typedef struct gptoss_moe_layer gptoss_moe_layer;
 gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const void* router_w, const float* router_b,
                                           const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
@@ -133,8 +136,8 @@ int gptoss_moe_route_batched(const void* W, const float* b, const float* x, cons
 /* [extension] Batched (prefill) MoE on tensor cores: x_resid[t] += sum_s w[t][s] (W2[e] swiglu(W1[e] x_norm[t] + b1)
  * + b2) with e = ids[t][s], for T tokens (grouped GEMM over the experts: permute, tcgen05 block-scaled FP4 MMAs with
  * the activations split into 8 e2m1 residual terms, unpermute, slot-ordered combine). Layouts as gptoss_kernel_moe
- * with x_norm, ids, weights, x_resid of T rows; expert ids in 0..31; H and I multiples of 64; T <= 32768. Device
- * pointers; synchronizes. */
+ * with x_norm, ids, weights, x_resid of T rows; expert ids in 0..31; H and I multiples of 64; T <= 32768. An E8M0
+ * scale byte 0xFF (NaN) in the experts up to the largest id used returns -1. Device pointers; synchronizes. */
 int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
                               const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
                               const float* x_norm, const int32_t* ids, const float* weights, float* x_resid, int T,
@@ -155,7 +158,7 @@ int gptoss_moe_layer_experts_batched(gptoss_moe_layer* layer, const float* h, co
                                      float* x_resid, int T, int k, void* stream);
 
 /* [extension] Expert parallelism with dispatch and combine in the kernels over NVLink peer memory (no counterpart in
- * the reference; SURVEY's "EP layer call taking per-rank token shards").
+ * the reference, which runs every expert on one device: an EP layer call that takes one rank's shard of the tokens).
  *
  * Every rank (one GPU each) allocates one zeroed region of gptoss_ep_region_bytes() with gptoss_ep_region_alloc(),
  * exports it with gptoss_ipc_handle() (64 bytes), receives every other rank's handle (any host channel) and maps
@@ -202,6 +205,12 @@ int gptoss_trace_enable(void* device_buffer, long long bytes);
  * per_term is not NULL, stores the first two terms into per_term[2][n]. Device
  * pointers; synchronizes. */
 int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, int which);
+
+/* [extension] Test hook of the tensor-core decode path: on the current device, sets the launch-epoch word of the
+ * calling thread's decode workspace for shape (k, H, I) to set_to (storing the old value in *previous if not NULL).
+ * The next launch of that shape uses the epoch that follows set_to, which skips 0 when the count wraps. Synchronizes.
+ * For tests of the wrap-around; a decode loop never needs it. */
+int gptoss_test_decode_epoch(int k, int H, int I, unsigned set_to, unsigned* previous);
 
 /* [extension] Which decode MoE implementation gptoss_kernel_moe uses: 0 = SIMT (CUDA cores), 1 = tensor cores
  * (tcgen05 block-scaled MMA) where the shape allows it. Returns the previous setting, or -1. */

@@ -2,7 +2,9 @@
 
 Run here, where the reference is importable (it does not exist on the GPU box, so the outputs are committed):
 
-    GPTOSS_REF_DIR=/path/to/gptoss-infer/reference python tests/golden/make_golden.py
+    GPTOSS_REF_ROOT=/path/to/gptoss-infer python tests/golden/make_golden.py
+
+(GPTOSS_REF_ROOT defaults to a sibling checkout named `reference` next to this repository.)
 
 Fixtures (numpy .npz, small enough to commit):
   mxfp4_kat.npz     outputs of gptoss_ref.mxfp4.dequant / quantize on the inputs of the reference's own
@@ -26,7 +28,7 @@ import torch
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT / "gptoss-infer_b200"))
-sys.path.insert(0, os.environ.get("GPTOSS_REF_DIR", "/root/reference/reference"))
+sys.path.insert(0, str(Path(os.environ.get("GPTOSS_REF_ROOT", ROOT.parent / "reference")) / "reference"))
 
 from gptoss_ref import model as ref_model  # noqa: E402
 from gptoss_ref import mxfp4 as ref_mxfp4  # noqa: E402

@@ -211,3 +211,49 @@ def test_peer_ep_two_gpus_bit_identical_to_batched_forward(skew, split):
     for c in range(2):
         out = torch.cat([torch.from_numpy(got[r][c]) for r in range(world)])
         assert torch.equal(out, want)
+
+
+def test_peer_ep_bounded_wait_runs_out_and_next_call_is_clean():
+    """A cross-rank wait that nothing ends, on one GPU and without any fault: rank 0 of a world of 2 whose second
+    region is a second local allocation that no rank ever signals. Every expert-parallel barrier gives up after its
+    bound (about a second), gptoss_ep_status reports 60-62, all memory touched is valid, and the next normal call
+    (world 1, fresh regions) is bit-identical to the single-GPU batched forward."""
+    import ctypes
+    import time
+    lib = capi.load()
+    P = capi.ptr
+    t = _model(False)
+    x = synth.tokens(40, seed=15)
+    world, T_max, El = 2, 40, E8 // 2
+    ln, W, b = _router(t, "cuda")
+    L = _layer(lib, ln, W, b, _experts(t, "cuda", 0, El), El, 4)
+    nbytes = ctypes.c_longlong()
+    regions = []
+    try:
+        assert lib.gptoss_ep_region_bytes(E8, 4, 2880, 2880, world, T_max, ctypes.byref(nbytes)) == 0
+        for _ in range(world):
+            r = ctypes.c_void_p()
+            assert lib.gptoss_ep_region_alloc(nbytes, ctypes.byref(r)) == 0, lib.gptoss_last_error().decode()
+            regions.append(r.value)
+        peers = (ctypes.c_void_p * world)(*regions)
+        w64 = torch.empty(2880 * 32, dtype=torch.float64, device="cuda")
+        assert lib.gptoss_router_w64(P(W), E8, 2880, P(w64), None) == 0
+        xd = x.to("cuda").contiguous()
+        y = xd.clone()
+        t0 = time.time()
+        rc = lib.gptoss_ep_layer_forward(L, P(w64), P(b), P(ln), 1e-5, E8, 0, world, P(xd), P(y), 40, T_max, peers,
+                                         1, None)
+        assert rc == 0, lib.gptoss_last_error().decode()
+        code = ctypes.c_int()
+        assert lib.gptoss_ep_status(E8, 4, 2880, 2880, world, T_max, ctypes.byref(code)) == 0
+        waited = time.time() - t0
+        assert 60 <= code.value <= 62, code.value
+        assert waited < 60.0, waited
+    finally:
+        torch.cuda.synchronize()
+        for r in regions:
+            lib.gptoss_ep_region_free(r)
+        lib.gptoss_moe_layer_destroy(L)
+    want = _single_gpu_reference(t, x, "cuda")
+    for got in _peer_forward(lib, t, x, 0, 1, "cuda", T_max=64):
+        assert torch.equal(got, want)

@@ -330,3 +330,65 @@ def test_layer_create_rejects_bad_shapes(lib, config0):
     L = lib.gptoss_moe_layer_create(P(d["ln"]), 1e-5, P(d["W"]), P(d["b"]), *(P(e) for e in d["ex"]), 32, 9, 2880,
                                     2880, 1.702, 7.0)
     assert not L and b"k <= 8" in lib.gptoss_last_error()
+
+
+def test_layer_forward_epoch_wraps_past_zero(lib, config0):
+    """The decode kernel tags split-tile partial sums with a launch epoch kept in the workspace; epoch 0 is the tag of
+    a zero-filled word and must never be current. With the epoch word seeded just below the wrap, the launches run at
+    epochs 0xFFFFFFFF, 1 and 2, each bit-identical to an ordinary launch."""
+    import ctypes
+    d, g = config0
+    L = make_layer(lib, d)
+    try:
+        x = dev(g["x"][0])
+        want = x.clone()
+        ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(want), None, None))
+        torch.cuda.synchronize()
+        prev = ctypes.c_uint()
+        ok(lib, lib.gptoss_test_decode_epoch(4, 2880, 2880, 0xFFFFFFFE, ctypes.byref(prev)))
+        assert prev.value != 0
+        for _ in range(3):
+            out = x.clone()
+            ok(lib, lib.gptoss_moe_layer_forward(L, P(x), P(out), None, None))
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+        ok(lib, lib.gptoss_test_decode_epoch(4, 2880, 2880, 5, ctypes.byref(prev)))
+        assert prev.value == 2
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+
+
+@pytest.mark.parametrize("which", ["gate_up", "down"])
+def test_nan_scale_rejected(lib, config0, which):
+    """An E8M0 scale byte 0xFF (NaN) is refused wherever scales enter the tensor-core paths, as the reference's
+    loader refuses it (runtime/src/engine.cu:119-122): layer creation, the raw-weights decode entry point (for a
+    selected expert) and the batched entry point."""
+    d, _ = config0
+    ex = list(d["ex"])
+    i = 1 if which == "gate_up" else 4
+    bad = ex[i].clone()
+    bad[17, 123, 45] = 0xFF                               # expert 17
+    ex[i] = bad
+    L = lib.gptoss_moe_layer_create(P(d["ln"]), 1e-5, P(d["W"]), P(d["b"]), *(P(e) for e in ex), 32, 4, 2880, 2880,
+                                    1.702, 7.0)
+    assert not L and b"0xFF" in lib.gptoss_last_error()
+    x = torch.randn(2880, device=DEV)
+    out = torch.zeros(2880, device=DEV)
+    w = torch.full((4,), 0.25, device=DEV)
+    prev = lib.gptoss_set_moe_impl(1)
+    try:
+        ids_bad = torch.tensor([2, 17, 5, 9], dtype=torch.int32, device=DEV)
+        assert lib.gptoss_kernel_moe(*(P(e) for e in ex), P(x), P(ids_bad), P(w), P(out), 4, 2880, 2880,
+                                     1.702, 7.0) != 0
+        assert b"0xFF" in lib.gptoss_last_error()
+        ids_ok = torch.tensor([2, 16, 5, 9], dtype=torch.int32, device=DEV)   # expert 17 not selected: accepted
+        ok(lib, lib.gptoss_kernel_moe(*(P(e) for e in ex), P(x), P(ids_ok), P(w), P(out), 4, 2880, 2880, 1.702, 7.0))
+    finally:
+        lib.gptoss_set_moe_impl(prev)
+    xs = torch.randn(3, 2880, device=DEV)
+    ys = torch.zeros_like(xs)
+    ids3 = torch.tensor([[2, 17, 5, 9], [0, 1, 2, 3], [4, 5, 6, 7]], dtype=torch.int32, device=DEV)
+    w3 = torch.full((3, 4), 0.25, device=DEV)
+    assert lib.gptoss_kernel_moe_batched(*(P(e) for e in ex), P(xs), P(ids3), P(w3), P(ys), 3, 4, 2880, 2880, 1.702,
+                                         7.0) != 0
+    assert b"0xFF" in lib.gptoss_last_error()

@@ -1,45 +1,87 @@
-"""gptoss_kernel_moe_static_scratch (no device allocation during the call) against gptoss_kernel_moe.
+"""gptoss_kernel_moe_static_scratch: the MoE entry point for callers that cannot allocate device memory during the
+call (an engine that hands all its memory to its own budgeted allocator, or a decode loop that must not meet the
+implicit synchronization of cudaMalloc). Its scratch is a fixed device array in the library.
 
-Two calls in a row on the same residual stream (x_resid += MoE(x_norm) twice) through each entry point, at the
-real 20b layer shape, must agree within the MoE tolerance of this suite: allclose rtol 1e-4 / atol 1e-3 and
-max-abs <= 2e-5 * max|x_resid|. Shapes past the fixed scratch (k * I > 8 * 3072) must fail with -1 and a message.
+Checked through the C ABI, two calls in a row on the same residual stream (x_resid += MoE(x_norm) twice), at the
+real 20b layer shape:
+  * bit-identical to gptoss_kernel_moe on the CUDA-core path (the same kernels, only the scratch differs);
+  * against the float64 oracle (oracle/moe.py kernel_moe_f64, applied twice): rtol 1e-4 / atol 1e-3 (the
+    reference's runtime/tests/test_kernels.py:174 bound) and max-abs <= 2e-5 * max|x_resid|;
+  * against gptoss_kernel_moe on the tensor-core path with the same tolerance.
+Shapes past the fixed scratch (k * I > 8 * 3072) must fail with -1 and a message. This file is collected last, so a
+run that stops at the first failure has run every other test before it.
 """
 import numpy as np
 import pytest
 import torch
 
 from gptoss_b200 import capi, synth
+from oracle import moe as omoe
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 P = capi.ptr
+NAMES = ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks", "down_proj_scales",
+         "down_proj_bias")
 
 
-def _layer():
+@pytest.fixture(scope="module")
+def case():
     t = synth.moe_layer(seed=0)
     p = "model.layers.0.mlp.experts."
-    return [t[p + "gate_up_proj_blocks"].to(DEV), t[p + "gate_up_proj_scales"].to(DEV),
-            t[p + "gate_up_proj_bias"].float().to(DEV), t[p + "down_proj_blocks"].to(DEV),
-            t[p + "down_proj_scales"].to(DEV), t[p + "down_proj_bias"].float().to(DEV)]
-
-
-def test_static_scratch_matches_kernel_moe():
-    lib = capi.load()
-    ex = _layer()
+    host = [t[p + n] for n in NAMES]
+    ex = [h.to(DEV) for h in host]
+    ex[2], ex[5] = ex[2].float(), ex[5].float()
     g = torch.Generator().manual_seed(31)
-    x_norm = torch.randn(2880, generator=g).to(DEV)
-    ids = torch.tensor([3, 17, 8, 30], dtype=torch.int32, device=DEV)
-    w = torch.softmax(torch.randn(4, generator=g), 0).to(DEV)
-    x0 = torch.randn(2880, generator=g).to(DEV)
-    outs = []
-    for fn in (lib.gptoss_kernel_moe_static_scratch, lib.gptoss_kernel_moe):
-        xr = x0.clone()
-        for _ in range(2):
-            rc = fn(*(P(e) for e in ex), P(x_norm), P(ids), P(w), P(xr), 4, 2880, 2880, 1.702, 7.0)
-            assert rc == 0, lib.gptoss_last_error().decode()
-        outs.append(xr.cpu().numpy().astype(np.float64))
-    got, want = outs
-    assert np.isfinite(got).all()
+    x_norm = torch.randn(2880, generator=g)
+    ids = torch.tensor([3, 17, 8, 30], dtype=torch.int32)
+    w = torch.softmax(torch.randn(4, generator=g), 0)
+    x0 = torch.randn(2880, generator=g)
+    return host, ex, x_norm, ids, w, x0
+
+
+def run_twice(lib, fn, case):
+    _, ex, x_norm, ids, w, x0 = case
+    d_x, d_ids, d_w = x_norm.to(DEV), ids.to(DEV), w.to(DEV)
+    xr = x0.to(DEV).clone()
+    for _ in range(2):
+        rc = fn(*(P(e) for e in ex), P(d_x), P(d_ids), P(d_w), P(xr), 4, 2880, 2880, 1.702, 7.0)
+        assert rc == 0, lib.gptoss_last_error().decode()
+    return xr.cpu()
+
+
+def test_static_scratch_bitidentical_to_cuda_core_path(case):
+    lib = capi.load()
+    got = run_twice(lib, lib.gptoss_kernel_moe_static_scratch, case)
+    prev = lib.gptoss_set_moe_impl(0)
+    try:
+        want = run_twice(lib, lib.gptoss_kernel_moe, case)
+    finally:
+        lib.gptoss_set_moe_impl(prev)
+    assert torch.isfinite(got).all()
+    assert torch.equal(got, want)
+
+
+def test_static_scratch_matches_float64_oracle(case):
+    lib = capi.load()
+    got = run_twice(lib, lib.gptoss_kernel_moe_static_scratch, case).numpy().astype(np.float64)
+    host, _, x_norm, ids, w, x0 = case
+    arrs = [h.float().numpy() if h.dtype == torch.bfloat16 else h.numpy() for h in host]
+    want = x0.numpy().astype(np.float64)
+    for _ in range(2):
+        want = omoe.kernel_moe_f64(*arrs, x_norm.numpy(), ids.numpy(), w.numpy(), want)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
+    assert np.abs(got - want).max() <= 2e-5 * np.abs(want).max()
+
+
+def test_static_scratch_matches_tensor_core_path(case):
+    lib = capi.load()
+    got = run_twice(lib, lib.gptoss_kernel_moe_static_scratch, case).numpy().astype(np.float64)
+    prev = lib.gptoss_set_moe_impl(1)
+    try:
+        want = run_twice(lib, lib.gptoss_kernel_moe, case).numpy().astype(np.float64)
+    finally:
+        lib.gptoss_set_moe_impl(prev)
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
     assert np.abs(got - want).max() <= 2e-5 * np.abs(want).max()
 

@@ -1,26 +1,30 @@
 """Benchmark of the gpt-oss-20b MXFP4 MoE path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload moe-decode] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload moe-decode|prefill|ep] [--impl ours|reference]
 
-Workload "moe-decode" (BASELINE configs[0] stacked as in configs[1]): bs=1 decode through the 24 MoE layers of a
-20b-shaped random-init model: per step, one token x goes x <- x + MoE(RMSNorm(x)) through 24 distinct layers
+Default workload "moe-decode" (BASELINE configs[0] stacked as in configs[1]): bs=1 decode through the 24 MoE layers
+of a 20b-shaped random-init model: per step, one token x goes x <- x + MoE(RMSNorm(x)) through 24 distinct layers
 (router 2880->32, top-4, MXFP4 gate/up + clamped SwiGLU, MXFP4 down, weighted combine). 24 x 423 MB of expert
 weights are resident, far above the 126 MB L2, and each step reads 24 x 53,130,240 algorithmic bytes.
-
 Timed region: W untimed steps, then exactly K steps between a barrier + synchronize on both sides, CUDA events on
 the launching stream, max over ranks. With N > 1 every rank runs an independent replica (bs=1 decode does not
 shard): value = N * K * bytes / max time ("replicas only", scaling "weak").
 
-Workload "prefill": 2048 tokens x 1 MoE layer per step on one GPU through the batched forward (batched
-router, permute, grouped tcgen05 block-scaled FP4 GEMMs, combine) in a CUDA graph; replicas with N > 1.
+The same line carries, measured in the same run:
+  "ep"       configs[3] at the run's N: 8192 tokens (over all ranks) x 24 MoE layers per step, experts sharded over
+             the N ranks (placed by expected load), dispatch and combine inside the kernels over NVLink peer memory;
+             max over ranks (strong scaling). At N = 1 it is the one-GPU baseline of the same workload.
+  "prefill"  (N = 1) configs[2]: 2048 tokens x 1 MoE layer per step through the batched tensor-core path.
+  "ref_gpu"  (N = 1) the reference's own CUDA kernels (openvang/gptoss-infer runtime, built for sm_100a from its
+             sources into oracle/_ref/) against this library's, same ABI entry points, same inputs, same box.
 
-Workload "ep": 8192 tokens (over all ranks) x 24 MoE layers per step, the 32 experts of every layer
-sharded contiguously over the N ranks and the tokens split evenly; per layer, all-to-all dispatch and combine around
-each rank's local experts (gptoss_b200/ep.py). Strong scaling: value = 8192 / max-over-ranks step time.
+Workloads "prefill" and "ep" alone print their own line (metric of that workload).
 
---impl reference times the reference's own CPU algorithm for this path (the fp32 Reference.moe of
-openvang/gptoss-infer, restated in oracle/moe.py, dequantizing each selected expert per call as the reference does)
-on the host cores, on a bounded sample per step, and prints the same metric.
+--impl reference times the reference's own CPU implementation of this path: Reference.moe of gptoss_ref
+(openvang/gptoss-infer reference/gptoss_ref/model.py:92-105, fp32 torch, dequantizing each selected expert per call),
+staged into baseline/_ref/ by oracle/stage_reference.py, with torch using every host core; one token through one
+MoE layer per step, same metric, unit and config as this arm. Where the package is not staged it falls back to the
+numpy restatement in oracle/moe.py and says so ("kind": "port").
 """
 import argparse
 import json
@@ -39,24 +43,31 @@ EXPERT_BYTES = 8_294_400 + 518_400 + 4_147_200 + 259_200            # blocks + s
 LAYER_BYTES = K_TOP * EXPERT_BYTES + 184_320 + K_TOP * (5760 + 2880) * 2   # + router + bf16 biases = 53,130,240
 GATEUP_BYTES = K_TOP * (8_294_400 + 518_400 + 5760 * 4) + H * 4 + K_TOP * I * 4   # per launch, fp32 bias/in/out
 METRIC = "bs=1 decode MoE-layer HBM GB/s (20b-shaped, 24 layers)"
-REF_BUDGET_S = 90.0                  # timed seconds at most for the prefill / expert-parallel reference arms
 UNIT = "GB/s"
+PREFILL_METRIC = "prefill tok/s (2048 tokens x 1 MoE layer, Zipf s=1.1 routing)"
+EP_METRIC = "expert-parallel prefill tok/s (8192 tokens x 24 MoE layers, Zipf s=1.2 routing)"
+REF_BUDGET_S = 60.0                  # timed seconds at most for a CPU reference arm
+REF_STAGED = ROOT / "baseline" / "_ref" / "reference"
+REF_LIB = ROOT / "oracle" / "_ref" / "libgptoss_ref.so"
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="moe-decode", choices=["moe-decode", "prefill", "ep"])
     ap.add_argument("--tokens", type=int, default=None,
                     help="prefill: tokens per step (config 2: 2048); ep: tokens per step over all ranks (config 3: 8192)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="ep: dispatch/combine inside the kernels over peer memory, or NCCL all-to-all around them")
+    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="ep: experts placed on ranks by expected load (calibration batch) or in id order")
     ap.add_argument("--moe-impl", type=int, default=None, help="0 = SIMT, 1 = tensor cores (default: library's)")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="moe-decode: skip the ep / prefill / ref_gpu objects")
     return ap.parse_args()
 
 
@@ -113,22 +124,164 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------------- setup
-def dist_init():
-    import torch
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if ws > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-    return ws, rank, local
+class Ctx:
+    """One process per GPU: world size, rank, local rank, device, and the max-over-ranks helpers."""
+
+    def __init__(self):
+        import torch
+        self.ws = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.ws > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+        else:
+            torch.cuda.set_device(0)
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+
+    def barrier(self):
+        import torch
+        if self.ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, v):
+        import torch
+        if self.ws == 1:
+            return v
+        t = torch.tensor([float(v)], device=self.dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_list(self, v):
+        import torch
+        t = torch.tensor(v, dtype=torch.float64, device=self.dev)
+        if self.ws > 1:
+            torch.distributed.all_reduce(t)
+        return t.tolist()
+
+    def close(self):
+        if self.ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
 
 
+def peaks():
+    pk = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(pk.read_text()) if pk.exists() else {}
+
+
+def fp4_peak(lib, sustained):
+    """Dense FP4 (kind::mxf4) tensor peak of this GPU in TFLOP/s: measured live by the library's back-to-back MMA
+    microbenchmark when it has one, else 4 x the measured bf16 cuBLAS peak (dense FP4 runs at 4x the bf16 rate)."""
+    import ctypes
+    if hasattr(lib, "gptoss_selftest_mxf4_peak"):
+        tf = ctypes.c_double()
+        if lib.gptoss_selftest_mxf4_peak(ctypes.byref(tf)) == 0 and tf.value > 0:
+            return tf.value, "measured: back-to-back tcgen05.mma kind::mxf4 M=128 N=256 K=64 on every SM"
+    bf16 = peaks().get("bf16_tflops_sustained" if sustained else "bf16_tflops")
+    return (4.0 * bf16, "4 x measured bf16 cuBLAS (of measured)") if bf16 else (4.0 * 1590.0, "4 x fallback bf16")
+
+
+def ctypes_array(events):
+    import ctypes
+    return (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+
+
+# ------------------------------------------------------------------------------------------------------- configs
+def decode_config(ws, layers):
+    return {"workload": "moe-decode (configs[0] stacked x24, bs=1)", "layers": layers, "experts": E, "top_k": K_TOP,
+            "hidden": H, "intermediate": I, "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+            "l2": "inputs larger than L2: 24 distinct layers, 10.2 GB of experts"}
+
+
+def prefill_config(T, ws, counts=None):
+    c = {"workload": "prefill (configs[2])", "tokens": T, "experts": E, "top_k": K_TOP, "hidden": H,
+         "intermediate": I, "zipf_s": 1.1, "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+         "l2": "423 MB of experts per layer, larger than L2"}
+    if counts is not None:
+        c["expert_token_counts"] = counts
+    return c
+
+
+def ep_config(T, ws, layers):
+    return {"workload": "expert-parallel prefill (configs[3])", "tokens": T, "tokens_per_rank": T // ws,
+            "layers": layers, "experts": E, "experts_per_rank": E // ws, "top_k": K_TOP, "zipf_s": 1.2,
+            "parallelism": f"ep{ws} (experts) x dp{ws} (tokens)", "l2": "423 MB of experts per layer, larger than L2"}
+
+
+# ------------------------------------------------------------------------------------------------------- CPU reference
+class ReferenceMoE:
+    """The reference's CPU MoE: gptoss_ref's Reference.moe (fp32 torch, every selected expert dequantized per call)
+    when baseline/_ref holds the staged package, else oracle/moe.py's numpy restatement of it ("port")."""
+
+    def __init__(self, t, prefix="model.layers.0."):
+        import torch
+        self.cores = os.cpu_count()
+        self.prefix = prefix
+        if (REF_STAGED / "gptoss_ref" / "model.py").exists():
+            if str(REF_STAGED) not in sys.path:
+                sys.path.insert(0, str(REF_STAGED))
+            from gptoss_ref.config import GptOssConfig
+            from gptoss_ref.model import Reference, rms_norm
+            from gptoss_ref.weights import DictWeights
+            cfg = GptOssConfig.from_dict({
+                "vocab_size": 201088, "hidden_size": H, "intermediate_size": I, "num_hidden_layers": 1,
+                "num_attention_heads": 64, "num_key_value_heads": 8, "head_dim": 64, "num_local_experts": E,
+                "num_experts_per_tok": K_TOP, "sliding_window": 128, "rope_theta": 150000, "swiglu_limit": 7.0,
+                "rope_scaling": {"rope_type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                                 "truncate": False, "original_max_position_embeddings": 4096}})
+            self.ref = Reference(cfg, DictWeights({k.replace(prefix, "model.layers.0."): v for k, v in t.items()}),
+                                 threads=self.cores)
+            self.ln = t[prefix + "post_attention_layernorm.weight"].float()
+            self.norm = lambda x: rms_norm(x, self.ln, 1e-5)
+            self.kind = "reference"
+            self.what = (f"gptoss_ref Reference.moe (torch {torch.__version__} fp32, {torch.get_num_threads()} "
+                         f"threads, per-call MXFP4 dequant of every selected expert)")
+        else:
+            from gptoss_b200 import synth
+            from oracle import moe as omoe
+            self.omoe, self.tn = omoe, synth.to_numpy(t)
+            self.kind = "port"
+            self.what = "oracle/moe.py numpy restatement of Reference.moe (fp32, per-call MXFP4 dequant)"
+
+    def normed(self, x):
+        """RMSNorm (the reference's) of fp32 tokens x [T, H] (torch CPU tensor)."""
+        if self.kind == "reference":
+            return self.norm(x)
+        import torch
+        return torch.from_numpy(self.omoe.rms_norm(x.numpy(), self.tn[self.prefix + "post_attention_layernorm.weight"]))
+
+    def moe(self, h):
+        import torch
+        if self.kind == "reference":
+            with torch.inference_mode():
+                return self.ref.moe(0, h)
+        return self.omoe.moe(self.tn, self.prefix, h.numpy())
+
+
+def time_reference(rm, h, n_per_step, steps, warmup, budget_s):
+    """Runs rm.moe on slices of n_per_step tokens of h: min(warmup, 1) untimed, then up to `steps` timed within
+    budget_s seconds. Returns (seconds, tokens, steps timed)."""
+    n = h.shape[0]
+    for i in range(min(warmup, 1)):
+        rm.moe(h[:n_per_step])
+    t0 = time.perf_counter()
+    done = timed = 0
+    for i in range(steps):
+        j = (i * n_per_step) % max(1, n - n_per_step + 1)
+        rm.moe(h[j:j + n_per_step])
+        done += n_per_step
+        timed += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return time.perf_counter() - t0, done, timed
+
+
+# ------------------------------------------------------------------------------------------------------- decode
 def make_layers(n_layers, dev):
     """Layer 0 from synth seed 0 (the config-0 layer); the others drawn on the device with the same distributions."""
     import torch
@@ -152,101 +305,180 @@ def make_layers(n_layers, dev):
                 d[q + "_scales"] = torch.randint(120, 127, (E, rows, k // 32), device=dev, generator=g,
                                                  dtype=torch.uint8)
                 d[q + "_bias"] = (torch.randn(E, rows, device=dev, generator=g) * 0.01).bfloat16()
-        L = {
+        layers.append({
             "ln": d["post_attention_layernorm.weight"].float(),
             "W": d["mlp.router.weight"].contiguous(),
             "b": d["mlp.router.bias"].float(),
             "ex": [d["mlp.experts.gate_up_proj_blocks"], d["mlp.experts.gate_up_proj_scales"],
                    d["mlp.experts.gate_up_proj_bias"].float(), d["mlp.experts.down_proj_blocks"],
                    d["mlp.experts.down_proj_scales"], d["mlp.experts.down_proj_bias"].float()],
-        }
-        layers.append(L)
+        })
     return layers, t0
 
 
-# ------------------------------------------------------------------------------------------------------- cpu
-def cpu_moe_sample(t0, budget_s, token_seed=99):
-    """The reference's CPU algorithm (Reference.moe, fp32, per-call dequant) on one token of layer 0, repeated until
-    about budget_s seconds have passed. Returns (bytes_per_s, n_tokens, threads)."""
-    import numpy as np
-    from gptoss_b200 import synth
-    from oracle import moe as omoe
-    tn = synth.to_numpy(t0)
-    p = "model.layers.0."
-    x = synth.tokens(64, seed=token_seed).numpy()
-    h = omoe.rms_norm(x, tn[p + "post_attention_layernorm.weight"])
-    omoe.moe(tn, p, h[:1])                                        # cold run
-    n, t_start = 0, time.perf_counter()
-    while True:
-        omoe.moe(tn, p, h[n % 64: n % 64 + 1])
-        n += 1
-        el = time.perf_counter() - t_start
-        if el >= budget_s or n >= 64:
-            break
-    return LAYER_BYTES * n / el, n, os.cpu_count()
+def run_decode(args, ctx, lib):
+    import torch
+    from gptoss_b200 import capi
+    P = capi.ptr
+    ws, rank, dev = ctx.ws, ctx.rank, ctx.dev
+    if args.moe_impl is not None and lib.gptoss_set_moe_impl(args.moe_impl) < 0:
+        raise RuntimeError(lib.gptoss_last_error().decode())
+    layers, t0 = make_layers(args.layers, dev)
+    impl = args.moe_impl if args.moe_impl is not None else 1
+    handles = []
+    if impl == 1:
+        for L in layers:
+            hdl = lib.gptoss_moe_layer_create(P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]), E,
+                                              K_TOP, H, I, 1.702, 7.0)
+            if not hdl:
+                raise RuntimeError(lib.gptoss_last_error().decode())
+            handles.append(hdl)
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    X = torch.randn(args.steps + args.warmup, H, device=dev, generator=g)
+    stream = torch.cuda.current_stream()
+
+    def layer_call(li, x, sp, events):
+        if handles:
+            return lib.gptoss_moe_layer_forward(handles[li], P(x), P(x), sp, events)
+        L = layers[li]
+        return lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
+                                          P(x), E, K_TOP, H, I, 1.702, 7.0, sp, events)
+
+    def step(x, sp, events=None):
+        for li in range(len(layers)):
+            if layer_call(li, x, sp, events[li] if events else None) != 0:
+                raise RuntimeError(lib.gptoss_last_error().decode())
+
+    # One decode step (24 MoE layers) is captured once as a CUDA graph and replayed, as the reference engine does
+    # with its decode step (runtime/src/engine.cu:264-279): the host issues two operations per step, not 24+
+    # launches. The programmatic-dependent-launch edges between the layers' kernels are kept in the graph.
+    x_static = torch.empty(H, device=dev)
+    for i in range(args.warmup):                          # eager warm-up also sizes the library's workspaces
+        x_static.copy_(X[args.steps + i])
+        step(x_static, stream.cuda_stream)
+    ctx.barrier()
+    cap = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    x_static.copy_(X[0])
+    with torch.cuda.graph(graph, stream=cap):
+        step(x_static, cap.cuda_stream)
+    for i in range(3):
+        x_static.copy_(X[args.steps + (i % max(1, args.warmup))])
+        graph.replay()
+    ctx.barrier()
+
+    # ---- timed region: exactly K steps
+    with ClockSampler(ctx.local) as clocks:
+        ctx.barrier()
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0e.record(stream)
+        for i in range(args.steps):
+            x_static.copy_(X[i])
+            graph.replay()
+        t1e.record(stream)
+        ctx.barrier()
+    ms = ctx.max(t0e.elapsed_time(t1e))
+    value = ws * args.steps * args.layers * LAYER_BYTES / (ms / 1e3) / 1e9
+    # per layer: tensor cores = one fused launch; SIMT = rmsnorm + router + gate/up + down
+    gpu_launches = args.steps * args.layers * (1 if handles else 4)
+
+    # ---- per-kernel durations: a second graph of the same step with events around every layer's kernels
+    n_prof = min(args.steps, 100)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.layers)]
+    for quad in ev:                                       # torch creates the CUDA event at its first record
+        for e in quad:
+            e.record(stream)
+    torch.cuda.synchronize()
+    evh = [ctypes_array(e) for e in ev]
+    pgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(pgraph, stream=cap):
+        step(x_static, cap.cuda_stream, evh)
+    sums = [0.0, 0.0, 0.0]
+    ctx.barrier()
+    for i in range(n_prof):
+        x_static.copy_(X[i])
+        pgraph.replay()
+        torch.cuda.synchronize()
+        for q in ev:
+            sums[0] += q[0].elapsed_time(q[1])
+            sums[1] += q[1].elapsed_time(q[2])
+            sums[2] += q[2].elapsed_time(q[3])
+    nl = n_prof * args.layers
+    part_us = [v / nl * 1e3 for v in sums]
+    if handles:
+        # the timed region launches nothing but the fused kernel (one per layer) and one 11.5 KB copy per step, so
+        # its average launch duration is the timed region's time over its launches (an upper bound: it includes the
+        # gaps between launches); the event-bracketed figure is kept beside it
+        kernel_us = {"moe_fused_kernel": ms / args.steps / args.layers * 1e3,
+                     "moe_fused_kernel_event_bracketed": part_us[2]}
+        top_us, top_name, top_bytes = (ms / args.steps / args.layers * 1e3,
+                                       "moe_fused_kernel (RMSNorm + router + gate/up + down)", LAYER_BYTES)
+    else:
+        kernel_us = {"router+rmsnorm": part_us[0], "gate_up": part_us[1], "down+combine": part_us[2]}
+        top_us, top_name, top_bytes = part_us[1], "gateup_simt_kernel", GATEUP_BYTES
+    del evh
+
+    # ---- end to end through the public API: host x in, host x out, every step
+    xh = torch.randn(args.steps, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
+    yh = torch.empty(H).pin_memory()
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        x_static.copy_(xh[i], non_blocking=True)
+        graph.replay()
+        yh.copy_(x_static, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    ctx.barrier()
+    ms_e2e = ctx.max(e0.elapsed_time(e1))
+    e2e = ws * args.steps * args.layers * LAYER_BYTES / (ms_e2e / 1e3) / 1e9
+    del graph, pgraph
+    for hdl in handles:
+        lib.gptoss_moe_layer_destroy(hdl)
+    del layers
+    torch.cuda.empty_cache()
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        rm = ReferenceMoE(t0)
+        h = rm.normed(torch.randn(64, H, generator=torch.Generator().manual_seed(99)))
+        el, n, _ = time_reference(rm, h, 1, 64, 1, 15.0)
+        cpu = {"value": LAYER_BYTES * n / el / 1e9, "unit": UNIT, "cores": rm.cores, "kind": rm.kind,
+               "sample": f"{n} tokens x 1 MoE layer (config-0 layer) through {rm.what}"}
+
+    pk = peaks()
+    hbm = pk.get("hbm_gbs")
+    peak_src = "measured copy (MEASURED_PEAKS.json)" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    achieved = top_bytes / (top_us * 1e-6) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("moe_fused_kernel" if handles else "gateup_simt_kernel")
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init 20b-shaped MoE layers)",
+        "config": decode_config(ws, args.layers),
+        "moe_layers_tok_per_s": ws * args.steps / (ms / 1e3),
+        "us_per_moe_layer": ms / args.steps / args.layers * 1e3,
+        "moe_impl": "tensor cores (tcgen05 kind::mxf4)" if handles else "SIMT",
+        "kernel_us": kernel_us,
+        "roofline": {"bound": "hbm", "kernel": top_name, "achieved": achieved, "peak": hbm,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
+                     "frac_of_8TBs_nominal": achieved / 8000.0, "algorithmic_bytes_per_launch": top_bytes,
+                     "launch_us": top_us},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
+                "api": ("gptoss_moe_layer_forward" if handles else "gptoss_moe_block_async") +
+                       " x24 per token captured in one CUDA graph; host x copied in and out every step"},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks.summary(),
+    }
 
 
-# ------------------------------------------------------------------------------------------------------- main
-def run_reference(args):
-    """Reference arm: the reference's CPU implementation of this path, bounded sample per step."""
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    import numpy as np
-    from gptoss_b200 import synth
-    from oracle import moe as omoe
-    t0 = synth.moe_layer(seed=0)
-    tn = synth.to_numpy(t0)
-    p = "model.layers.0."
-    x = synth.tokens(64, seed=99).numpy()
-    h = omoe.rms_norm(x, tn[p + "post_attention_layernorm.weight"])
-    # A step is one token through one MoE layer, scaled down to a row slice of the selected experts when K is large,
-    # so the whole run stays within about two minutes. GB/s is per byte actually processed.
-    budget = 120.0
-    probe_t = time.perf_counter()
-    omoe.moe(tn, p, h[:1])
-    per_layer = time.perf_counter() - probe_t
-    frac = min(1.0, budget / max(1, args.steps + args.warmup) / max(per_layer, 1e-3))
-    _, ids, gate = omoe.router(h, tn[p + "mlp.router.weight"], tn[p + "mlp.router.bias"], K_TOP)
-    pe = p + "mlp.experts."
-
-    def step(i):
-        r = i % 64
-        out = np.zeros(H, np.float32)
-        nbytes = 0
-        for slot, e in enumerate(ids[r].tolist()):
-            rows_gu = max(2, int(2 * I * frac) // 2 * 2)
-            rows_dn = max(1, int(H * frac))
-            from oracle import mxfp4
-            w1 = mxfp4.dequant(tn[pe + "gate_up_proj_blocks"][e][:rows_gu], tn[pe + "gate_up_proj_scales"][e][:rows_gu])
-            a = omoe.swiglu(w1 @ h[r] + tn[pe + "gate_up_proj_bias"][e][:rows_gu])
-            w2 = mxfp4.dequant(tn[pe + "down_proj_blocks"][e][:rows_dn], tn[pe + "down_proj_scales"][e][:rows_dn])
-            out[:rows_dn] += gate[r, slot] * (w2[:, :a.shape[0]] @ a + tn[pe + "down_proj_bias"][e][:rows_dn])
-            nbytes += rows_gu * 90 * 17 + rows_dn * 90 * 17
-        return nbytes + int(184_320 * frac)
-
-    for i in range(args.warmup):
-        step(i)
-    t = time.perf_counter()
-    nbytes = sum(step(i) for i in range(args.steps))
-    el = time.perf_counter() - t
-    value = nbytes / el / 1e9
-    sample = (f"one token through one MoE layer per step, rows sliced to {frac:.4f} of each selected expert "
-              f"(numpy fp32, per-call MXFP4 dequant)")
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "moe-decode (configs[0] stacked x24, bs=1)", "layers": LAYERS},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
-
-
-PREFILL_METRIC = "prefill tok/s (2048 tokens x 1 MoE layer, Zipf s=1.1 routing)"
-
-
+# ------------------------------------------------------------------------------------------------------- prefill
 def prefill_flops(T):
     """Algorithmic FLOPs of one batched MoE layer: 2 * (T * k) * (2I * H + H * I)."""
     return 2.0 * T * K_TOP * (2 * I * H + H * I)
@@ -264,56 +496,13 @@ def prefill_inputs(T):
     return t, perm, x
 
 
-def run_prefill_reference(args):
-    """Reference arm for the prefill workload: Reference.moe (numpy fp32 restatement, per-call dequant) on a bounded
-    sample of the same tokens per step."""
-    rank = int(os.environ.get("RANK", "0"))
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    if rank != 0:
-        return
-    from gptoss_b200 import synth
-    from oracle import moe as omoe
-    t, _, x = prefill_inputs(args.tokens)
-    tn = synth.to_numpy(t)
-    p = "model.layers.0."
-    h = omoe.rms_norm(x.numpy(), tn[p + "post_attention_layernorm.weight"])
-    n_s = 64                                                   # tokens per step (a bounded sample)
-    omoe.moe(tn, p, h[:n_s])
-    el, done = 0.0, 0
-    for i in range(min(args.warmup, 1)):
-        omoe.moe(tn, p, h[:n_s])
-    t0 = time.perf_counter()
-    timed = 0
-    for i in range(args.steps):
-        omoe.moe(tn, p, h[(i * n_s) % args.tokens:(i * n_s) % args.tokens + n_s])
-        done += n_s
-        timed += 1
-        if time.perf_counter() - t0 > REF_BUDGET_S:               # bounded: the run ends within a few minutes
-            break
-    el = time.perf_counter() - t0
-    value = done / el
-    line = {"impl": "reference", "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
-            "steps": args.steps, "steps_timed": timed, "warmup": args.warmup, "ms_per_step": el / timed * 1e3,
-            "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "prefill (configs[2])", "tokens": args.tokens},
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{n_s} tokens per step through Reference.moe (numpy fp32, per-call MXFP4 "
-                                       f"dequant of every selected expert)"},
-            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
-
-
-def run_prefill(args):
+def run_prefill(args, ctx, lib, T, with_cpu):
     """Config 2 on one GPU (replicas with N > 1): per step x_resid = x + MoE(RMSNorm(x)) for T tokens through the
     prepared layer's batched forward (batched router, permute, grouped tcgen05 GEMMs, combine), one CUDA graph."""
     import torch
-    from gptoss_b200 import capi, synth
-    ws, rank, local = dist_init()
-    dev = torch.device("cuda", torch.cuda.current_device())
-    lib = capi.load()
+    from gptoss_b200 import capi
     P = capi.ptr
-    T = args.tokens
+    ws, dev = ctx.ws, ctx.dev
     t, perm, x_cpu = prefill_inputs(T)
     p = "model.layers.0."
     d = {k[len(p):]: v.to(dev) for k, v in t.items()}
@@ -328,12 +517,6 @@ def run_prefill(args):
     x = x_cpu.to(dev)
     y = torch.empty_like(x)
     stream = torch.cuda.current_stream()
-
-    def barrier():
-        if ws > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-
     # realised routing (per-expert token counts), from the library's own batched router
     ids = torch.empty(T, K_TOP, dtype=torch.int32, device=dev)
     wts = torch.empty(T, K_TOP, device=dev)
@@ -347,47 +530,39 @@ def run_prefill(args):
         if lib.gptoss_moe_layer_forward_batched(L, P(x), P(y), T, sp, events) != 0:
             raise RuntimeError(lib.gptoss_last_error().decode())
 
-    for _ in range(max(args.warmup, 1)):                 # eager warm-up also sizes the workspace
+    for _ in range(max(args.warmup, 3)):                 # eager warm-up also sizes the workspace
         step(stream.cuda_stream)
-    barrier()
+    ctx.barrier()
     cap = torch.cuda.Stream()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=cap):
         step(cap.cuda_stream)
     for _ in range(3):
         graph.replay()
-    barrier()
-    with ClockSampler(local) as clocks:
-        barrier()
+    ctx.barrier()
+    with ClockSampler(ctx.local) as clocks:
+        ctx.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
             graph.replay()
         e1.record(stream)
-        barrier()
-    ms = e0.elapsed_time(e1)
-    if ws > 1:
-        tt = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms = float(tt.item())
+        ctx.barrier()
+    ms = ctx.max(e0.elapsed_time(e1))
     step_s = ms / args.steps / 1e3
     value = ws * T / step_s
     # end to end: host x in (pinned), host result out, every step
     xh = x_cpu.pin_memory()
     yh = torch.empty_like(xh).pin_memory()
-    barrier()
+    ctx.barrier()
     e0.record(stream)
     for _ in range(args.steps):
         x.copy_(xh, non_blocking=True)
         graph.replay()
         yh.copy_(y, non_blocking=True)
     e1.record(stream)
-    barrier()
-    ms_e2e = e0.elapsed_time(e1)
-    if ws > 1:
-        tt = torch.tensor([ms_e2e], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms_e2e = float(tt.item())
+    ctx.barrier()
+    ms_e2e = ctx.max(e0.elapsed_time(e1))
     e2e = ws * T / (ms_e2e / args.steps / 1e3)
     # grouped GEMM durations: a second graph of the same step with events around the gate/up and down GEMM launches
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -400,7 +575,7 @@ def run_prefill(args):
         step(cap.cuda_stream, evh)
     gemm_ms = [0.0, 0.0]
     n_prof = min(args.steps, 50)
-    barrier()
+    ctx.barrier()
     for _ in range(n_prof):
         pgraph.replay()
         torch.cuda.synchronize()
@@ -408,139 +583,90 @@ def run_prefill(args):
         gemm_ms[1] += ev[2].elapsed_time(ev[3])
     gemm_us = [v / n_prof * 1e3 for v in gemm_ms]
     del graph, pgraph, evh
+    lib.gptoss_moe_layer_destroy(L)
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        from oracle import moe as omoe
-        tn = synth.to_numpy(t)
-        hn = omoe.rms_norm(x_cpu.numpy(), tn[p + "post_attention_layernorm.weight"])
-        n_s = 64
-        omoe.moe(tn, p, hn[:n_s])                             # cold run
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < 15.0 and reps < 4:
-            omoe.moe(tn, p, hn[reps * n_s:(reps + 1) * n_s])
-            reps += 1
-        el = time.perf_counter() - t0
-        cpu = {"value": reps * n_s / el, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{reps} x {n_s} tokens through Reference.moe (numpy fp32, per-call dequant of every "
-                         f"selected expert)"}
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    bf16 = peaks.get("bf16_tflops")
-    peak_fp4 = 4.0 * bf16 if bf16 else 4.0 * 1590.0
+    if with_cpu:
+        rm = ReferenceMoE(t)
+        hn = rm.normed(x_cpu[:256])
+        el, n, _ = time_reference(rm, hn, 64, 4, 1, 20.0)
+        cpu = {"value": n / el, "unit": "tok/s", "cores": rm.cores, "kind": rm.kind,
+               "sample": f"{n} tokens (64 per call) through {rm.what}"}
+    peak, peak_src = fp4_peak(lib, sustained=False)
     gemm_s = sum(gemm_us) / 1e6
     achieved = prefill_flops(T) / gemm_s / 1e12                  # algorithmic FLOPs of both grouped GEMMs
     traffic = None
     tj = ROOT / "profiles" / "traffic.json"
     if tj.exists():
         traffic = json.loads(tj.read_text()).get("grouped_gemm_kernel_prefill")
-    lib.gptoss_moe_layer_destroy(L)
-    if rank == 0:
-        line = {
-            "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "e2m1 x e2m1 (fp32 accumulate; activations as 8 residual terms)",
-            "data": "synthetic (seeded random-init 20b-shaped MoE layer, bf16 N(0,1) tokens)",
-            "config": {"workload": "prefill (configs[2])", "tokens": T, "experts": E, "top_k": K_TOP, "hidden": H,
-                       "intermediate": I, "zipf_s": 1.1, "expert_token_counts": counts,
-                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
-                       "l2": "423 MB of experts per layer, larger than L2"},
-            "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (gate/up + down launches of a step)",
-                         "achieved": achieved, "unit": "TFLOP/s", "peak": peak_fp4,
-                         "peak_source": "4 x measured burst bf16 cuBLAS (dense FP4 rate is 4x bf16); of measured",
-                         "frac": achieved / peak_fp4, "frac_of_9PF_nominal": achieved / 9000.0,
-                         "algorithmic_flops_per_step": prefill_flops(T), "gemm_us": gemm_us,
-                         "tensor_core_tflops_with_terms": 8 * achieved,
-                         "tensor_core_frac_with_terms": 8 * achieved / peak_fp4,
-                         "note": "each activation enters the MMA as 8 e2m1 terms, so the tensor cores execute 8x the "
-                                 "algorithmic FLOPs (plus M-tile padding)",
-                         "traffic": traffic},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
-                    "api": "gptoss_moe_layer_forward_batched in a CUDA graph; host tokens copied in and out"},
-            "gpu_launches": args.steps * 7,   # router, permute, 2 x (quantize, grouped GEMM), combine
-            "clocks": clocks.summary(),
-        }
-        print(json.dumps(line))
-    if ws > 1:
-        torch.distributed.destroy_process_group()
+    return {
+        "metric": PREFILL_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e2m1 x e2m1 (fp32 accumulate; activations as 8 residual terms)",
+        "data": "synthetic (seeded random-init 20b-shaped MoE layer, bf16 N(0,1) tokens)",
+        "config": prefill_config(T, ws, counts),
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (gate/up + down launches of a step)",
+                     "achieved": achieved, "unit": "TFLOP/s", "peak": peak, "peak_source": peak_src,
+                     "frac": achieved / peak, "frac_of_9PF_nominal": achieved / 9000.0,
+                     "algorithmic_flops_per_step": prefill_flops(T), "gemm_us": gemm_us,
+                     "tensor_core_tflops_with_terms": 8 * achieved,
+                     "tensor_core_frac_with_terms": 8 * achieved / peak,
+                     "note": "each activation enters the MMA as 8 e2m1 terms, so the tensor cores execute 8x the "
+                             "algorithmic FLOPs (plus M-tile padding)",
+                     "traffic": traffic},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                "api": "gptoss_moe_layer_forward_batched in a CUDA graph; host tokens copied in and out"},
+        "gpu_launches": args.steps * 7,   # router, permute, 2 x (quantize, grouped GEMM), combine
+        "clocks": clocks.summary(),
+    }
 
 
 # ------------------------------------------------------------------------------------------------ expert parallel
-EP_METRIC = "expert-parallel prefill tok/s (8192 tokens x 24 MoE layers, Zipf s=1.2 routing)"
+def ep_row_bytes():
+    """Bytes one (token, slot) row moves between ranks: its 8 activation terms written into the owner's A images
+    (12 K blocks of 256 x 8 terms x (128 B of e2m1 + 32 B of replicated scales)), and its fp32 result row back."""
+    kb = (H + 255) // 256
+    return kb * 8 * (128 + 32), H * 4
 
 
-def run_ep_reference(args):
-    """Reference arm for the expert-parallel workload: Reference.moe (numpy fp32 restatement, per-call dequant of
-    every selected expert) on the host cores, a bounded sample of tokens through one layer per step, reported as
-    tokens through all 24 layers per second."""
-    rank = int(os.environ.get("RANK", "0"))
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    if rank != 0:
-        return
-    import torch
-    from gptoss_b200 import synth
-    from oracle import moe as omoe
-    T = args.tokens
-    n_s = 32                                                    # tokens per step (a bounded sample)
-    t = {}
-    p = "model.layers.0."
-    ln, W, b = synth.ep_router(0)
-    t[p + "post_attention_layernorm.weight"], t[p + "mlp.router.weight"], t[p + "mlp.router.bias"] = ln, W.float(), b
-    ex = synth.ep_experts(0, 0, E, "cpu")
-    for n, v in zip(["gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
-                     "down_proj_scales", "down_proj_bias"], ex):
-        t[p + "mlp.experts." + n] = v
-    tn = synth.to_numpy(t)
-    x = torch.randn(T, H, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16).float().numpy()
-    h = omoe.rms_norm(x[:min(T, 8 * n_s)], ln.numpy())
-    for i in range(min(args.warmup, 1)):
-        omoe.moe(tn, p, h[:n_s])
-    done = 0
-    t0 = time.perf_counter()
-    timed = 0
-    for i in range(args.steps):
-        j = (i * n_s) % (len(h) - n_s + 1)
-        omoe.moe(tn, p, h[j:j + n_s])
-        done += n_s
-        timed += 1
-        if time.perf_counter() - t0 > REF_BUDGET_S:               # bounded: the run ends within a few minutes
-            break
-    el = time.perf_counter() - t0
-    value = done / el / LAYERS
-    line = {"impl": "reference", "metric": EP_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
-            "steps": args.steps, "steps_timed": timed, "warmup": args.warmup, "ms_per_step": el / timed * 1e3 * LAYERS,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "expert-parallel prefill (configs[3])", "tokens": T, "layers": LAYERS},
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{n_s} tokens per step through one layer of Reference.moe (numpy fp32, "
-                                       f"per-call MXFP4 dequant), scaled by 1/{LAYERS} layers"},
-            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
-
-
-def run_ep(args):
-    """Config 3: T tokens (over all ranks, T / N per rank) through 24 MoE layers per step, experts sharded
-    contiguously over the N ranks (32 / N each), tokens data-parallel. Per layer and rank: the library's batched
-    router on the rank's tokens, all-to-all dispatch of the (token, slot) rows to the experts' owners (NCCL over
-    NVLink), the local experts on tensor cores (gptoss_moe_layer_experts_batched, k = 1), reverse all-to-all and
-    slot-ordered combine (gptoss_b200/ep.py). Strong scaling: the total token count is fixed."""
+def run_ep(args, ctx, lib, T, with_cpu):
+    """Config 3: T tokens (over all ranks, T / N per rank) through 24 MoE layers per step, experts sharded over the
+    N ranks (E / N each; placed by expected load from a calibration batch unless --ep-placement contiguous), tokens
+    data-parallel. Per layer and rank: the library's batched router on the rank's tokens, dispatch of the (token,
+    slot) rows to the experts' owners, the local experts on tensor cores, combine back in slot order. Strong
+    scaling: the total token count is fixed."""
     import torch
     from gptoss_b200 import capi, ep, synth
-    ws, rank, local = dist_init()
-    dev = torch.device("cuda", torch.cuda.current_device())
-    lib = capi.load()
     P = capi.ptr
-    T = args.tokens
+    ws, rank, dev = ctx.ws, ctx.rank, ctx.dev
     if T % ws or E % ws:
         raise SystemExit(f"ep: {T} tokens and {E} experts must split evenly over {ws} ranks")
     Tl, El = T // ws, E // ws
-    group = None
     peer = args.ep_impl == "peer"
+    balanced = args.ep_placement == "balanced" and ws > 1
+    stream = torch.cuda.current_stream()
+    # expected per-expert loads of every layer: the library's router on a calibration batch (2048 tokens drawn with
+    # another seed than the benchmark's tokens), identical on every rank
+    xc = torch.randn(2048, H, generator=torch.Generator().manual_seed(123)).to(torch.bfloat16).float().to(dev)
+    placements, calib = [], []
+    for li in range(args.layers):
+        ln, W, b = (v.to(dev) for v in synth.ep_router(li))
+        ids = torch.empty(2048, K_TOP, dtype=torch.int32, device=dev)
+        w = torch.empty(2048, K_TOP, device=dev)
+        hc = torch.empty_like(xc)
+        if lib.gptoss_moe_route_batched(P(W), P(b), P(xc), P(ln), 1e-5, E, H, K_TOP, 2048, P(hc), P(ids), P(w),
+                                        stream.cuda_stream) != 0:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+        loads = torch.bincount(ids.flatten().long(), minlength=E).tolist()
+        calib.append(loads)
+        placements.append(ep.balanced_placement(loads, ws) if balanced else list(range(E)))
+    del xc, hc
     epg = ep.EpGroup(lib, E, K_TOP, H, I, rank, ws, Tl) if peer else None
     layers, handles = [], []
     for li in range(args.layers):
         ln, W, b = (v.to(dev) for v in synth.ep_router(li))
-        ex = synth.ep_experts(li, rank * El, (rank + 1) * El, dev)
+        W, b = ep.apply_placement(placements[li], W, b)
+        ex = synth.ep_experts_of(li, placements[li][rank * El:(rank + 1) * El], dev)
         hdl = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), El,
                                           K_TOP if peer else min(K_TOP, El), H, I, 1.702, 7.0)
         if not hdl:
@@ -548,353 +674,263 @@ def run_ep(args):
         handles.append(hdl)
         moe = (ep.PeerExpertParallelMoE(epg, hdl, W, b, ln) if peer else
                ep.ExpertParallelMoE(ep.gpu_route(lib, ln, W, b, E, K_TOP), ep.gpu_compute(lib, hdl), rank, ws, E,
-                                    K_TOP, H, group))
+                                    K_TOP, H, None))
         layers.append((ex, ln, W, b, moe))
-    g = torch.Generator().manual_seed(0)
-    x_all = torch.randn(T, H, generator=g).to(torch.bfloat16).float()
+    x_all = torch.randn(T, H, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16).float()
     x_cpu = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
     x0 = x_cpu.to(dev)
     x = torch.empty_like(x0)
-    stream = torch.cuda.current_stream()
-
-    def barrier():
-        if ws > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
 
     def step():
         x.copy_(x0)
         for L in layers:
             L[4].forward(x)
 
-    # realised routing of layer 0 over this rank's tokens (rows sent to each rank)
+    # realised routing of every layer over the benchmark's tokens: rows each rank receives, rows crossing ranks
+    h0 = torch.empty_like(x0)
     ids0 = torch.empty(Tl, K_TOP, dtype=torch.int32, device=dev)
     w0 = torch.empty(Tl, K_TOP, device=dev)
-    h0 = torch.empty_like(x0)
-    _, ln0, W0, b0, _ = layers[0]
-    if lib.gptoss_moe_route_batched(P(W0), P(b0), P(x0), P(ln0), 1e-5, E, H, K_TOP, Tl, P(h0), P(ids0), P(w0),
-                                    stream.cuda_stream) != 0:
-        raise RuntimeError(lib.gptoss_last_error().decode())
-    rows_to = torch.bincount(ids0.flatten().long() // El, minlength=ws)
-    if ws > 1:
-        torch.distributed.all_reduce(rows_to)
-    rows_to = rows_to.tolist()
+    recv = [0.0] * ws
+    cross_rows = 0.0
+    for li, (_, ln, W, b, _) in enumerate(layers):
+        if lib.gptoss_moe_route_batched(P(W), P(b), P(x0), P(ln), 1e-5, E, H, K_TOP, Tl, P(h0), P(ids0), P(w0),
+                                        stream.cuda_stream) != 0:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+        to = torch.bincount(ids0.flatten().long() // El, minlength=ws).tolist()
+        if li == 0:
+            rows0 = to
+        recv = [a + c for a, c in zip(recv, to)]
+        cross_rows += sum(c for r, c in enumerate(to) if r != rank)
+    recv = ctx.sum_list(recv)
+    rows0 = ctx.sum_list(rows0)
+    cross_rows = ctx.sum_list([cross_rows])[0]
     for _ in range(max(args.warmup, 3)):
         step()
-    barrier()
-    with ClockSampler(local) as clocks:
-        barrier()
+    ctx.barrier()
+    with ClockSampler(ctx.local) as clocks:
+        ctx.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
-        barrier()
-    ms = e0.elapsed_time(e1)
-    if ws > 1:
-        tt = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms = float(tt.item())
+        ctx.barrier()
+    ms = ctx.max(e0.elapsed_time(e1))
     step_s = ms / args.steps / 1e3
     value = T / step_s
     # end to end: this rank's host tokens in (pinned), host result out, every step
     xh = x_cpu.pin_memory()
     yh = torch.empty_like(xh).pin_memory()
-    barrier()
+    ctx.barrier()
     e0.record(stream)
     for _ in range(args.steps):
         x0.copy_(xh, non_blocking=True)
         step()
         yh.copy_(x, non_blocking=True)
     e1.record(stream)
-    barrier()
-    ms_e2e = e0.elapsed_time(e1)
-    if ws > 1:
-        tt = torch.tensor([ms_e2e], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms_e2e = float(tt.item())
+    ctx.barrier()
+    ms_e2e = ctx.max(e0.elapsed_time(e1))
     e2e = T / (ms_e2e / args.steps / 1e3)
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        from oracle import moe as omoe
+    if with_cpu:
         p = "model.layers.0."
         ex, ln, W, b, _ = layers[0]
-        t = {p + "post_attention_layernorm.weight": ln.cpu(), p + "mlp.router.weight": W.float().cpu(),
-             p + "mlp.router.bias": b.cpu()}
+        ln0, W0, b0 = synth.ep_router(0)
+        t = {p + "post_attention_layernorm.weight": ln0.to(torch.bfloat16), p + "mlp.router.weight": W0,
+             p + "mlp.router.bias": b0.to(torch.bfloat16)}
         for n, v in zip(["gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
-                         "down_proj_scales", "down_proj_bias"], ex):
-            t[p + "mlp.experts." + n] = v.cpu()
-        tn = synth.to_numpy(t)
-        hn = omoe.rms_norm(x_cpu.numpy(), tn[p + "post_attention_layernorm.weight"])
-        n_s = 32
-        omoe.moe(tn, p, hn[:n_s])                             # cold run
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < 15.0 and reps < 4:
-            omoe.moe(tn, p, hn[reps * n_s:(reps + 1) * n_s])
-            reps += 1
-        el = time.perf_counter() - t0
-        cpu = {"value": reps * n_s / el / args.layers, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{reps} x {n_s} tokens through layer 0 of Reference.moe (numpy fp32, per-call dequant), "
-                         f"scaled by 1/{args.layers} layers"}
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    bf16 = peaks.get("bf16_tflops_sustained")
-    peak_fp4 = 4.0 * bf16 if bf16 else 4.0 * 1400.0
+                         "down_proj_scales", "down_proj_bias"], synth.ep_experts(0, 0, E, "cpu")):
+            t[p + "mlp.experts." + n] = v
+        rm = ReferenceMoE(t)
+        hn = rm.normed(x_cpu[:128])
+        el, n, _ = time_reference(rm, hn, 32, 4, 1, 20.0)
+        cpu = {"value": n / el / args.layers, "unit": "tok/s", "cores": rm.cores, "kind": rm.kind,
+               "sample": f"{n} tokens (32 per call) through layer 0 with {rm.what}, scaled by 1/{args.layers} "
+                         f"layers"}
+    peak, peak_src = fp4_peak(lib, sustained=True)
     flops = prefill_flops(T) * args.layers
     achieved = flops / ws / step_s / 1e12
+    disp_b, comb_b = ep_row_bytes()
+    nvlink_bytes = cross_rows * (disp_b + comb_b)            # per step, all ranks together
     ep_status = epg.status() if peer else 0
     if peer:
         epg.close()
     for hdl in handles:
         lib.gptoss_moe_layer_destroy(hdl)
+    del layers
+    torch.cuda.empty_cache()
     if ep_status:
         raise RuntimeError(f"expert-parallel device check failed (code {ep_status})")
-    if rank == 0:
-        line = {
-            "metric": EP_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "e2m1 x e2m1 (fp32 accumulate; activations as 8 residual terms)",
-            "data": "synthetic (seeded random-init 20b-shaped MoE layers, bf16 N(0,1) tokens)",
-            "config": {"workload": "expert-parallel prefill (configs[3])", "tokens": T, "tokens_per_rank": Tl,
-                       "layers": args.layers, "experts": E, "experts_per_rank": El, "top_k": K_TOP, "zipf_s": 1.2,
-                       "layer0_rows_per_rank": rows_to, "parallelism": f"ep{ws} (experts) x dp{ws} (tokens)",
-                       "dispatch": ("inside the kernels: A terms and result rows stored into peer memory over "
-                                    "NVLink (gptoss_ep_layer_forward)" if peer else
-                                    "torch.distributed all_to_all_single (NCCL)") if ws > 1 else "none (one rank)",
-                       "l2": "423 MB of experts per layer, larger than L2"},
-            "roofline": {"bound": "tensor", "kernel": "whole expert-parallel step per GPU (grouped tcgen05 GEMMs, "
-                                                      "router, all-to-all)",
-                         "achieved": achieved, "unit": "TFLOP/s", "peak": peak_fp4,
-                         "peak_source": "4 x measured sustained bf16 (dense FP4 is 4x the bf16 rate)",
-                         "frac": achieved / peak_fp4, "algorithmic_flops_per_step": flops, "traffic": None},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
-                    "api": ("PeerExpertParallelMoE" if peer else "ExpertParallelMoE") +
-                           ".forward per layer; host tokens copied in and out every step"},
-            # peer: router, counts, permute, quantize, barrier, GEMM, quantize, GEMM, barrier, combine;
-            # nccl: w64, router, permute, 2 x (quantize, GEMM), combine
-            "gpu_launches": args.steps * args.layers * (10 if peer else 8),
-            "clocks": clocks.summary(),
-        }
-        print(json.dumps(line))
-    if ws > 1:
-        torch.distributed.destroy_process_group()
+    cfg = ep_config(T, ws, args.layers)
+    cfg.update({
+        "placement": ("by expected load: greedy over the per-expert counts of a 2048-token calibration batch "
+                      "(ep.balanced_placement), experts relabelled so each rank's range is balanced")
+        if balanced else "contiguous expert ids",
+        "dispatch": ("inside the kernels: A terms and result rows stored into peer memory over NVLink "
+                     "(gptoss_ep_layer_forward)" if peer else "torch.distributed all_to_all_single (NCCL)")
+        if ws > 1 else "none (one rank)"})
+    return {
+        "metric": EP_METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "e2m1 x e2m1 (fp32 accumulate; activations as 8 residual terms)",
+        "data": "synthetic (seeded random-init 20b-shaped MoE layers, bf16 N(0,1) tokens)",
+        "config": cfg,
+        "tok_per_s": value,
+        "rows_per_rank_layer0": rows0,
+        "rows_per_rank_all_layers": recv,
+        "max_over_mean_rows": max(recv) / (sum(recv) / ws),
+        "roofline": {"bound": "tensor", "kernel": "whole expert-parallel step per GPU (router, dispatch, grouped "
+                                                  "tcgen05 GEMMs, combine)",
+                     "achieved": achieved, "unit": "TFLOP/s", "peak": peak, "peak_source": peak_src,
+                     "frac": achieved / peak, "algorithmic_flops_per_step": flops, "traffic": None},
+        "nvlink": {"off_rank_rows_per_step": cross_rows, "bytes_per_step": nvlink_bytes,
+                   "GBps_all_ranks": nvlink_bytes / step_s / 1e9,
+                   "GBps_per_gpu": nvlink_bytes / ws / step_s / 1e9,
+                   "bytes_per_row": {"dispatch": disp_b, "combine": comb_b}},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                "api": ("PeerExpertParallelMoE" if peer else "ExpertParallelMoE") +
+                       ".forward per layer; host tokens copied in and out every step"},
+        # peer: router, counts, permute, quantize, barrier, GEMM, quantize, GEMM, barrier, combine;
+        # nccl: w64, router, permute, 2 x (quantize, GEMM), combine
+        "gpu_launches": args.steps * args.layers * (10 if peer else 8),
+        "clocks": clocks.summary(),
+    }
 
 
+# ------------------------------------------------------------------------------------------------ reference GPU bar
+def run_ref_gpu(ctx, lib):
+    """The reference's own CUDA kernels (openvang/gptoss-infer runtime/src/kernels.cu, built for sm_100a from its
+    sources by oracle/Makefile) against this library's, through the same C ABI entry points on the same inputs (the
+    config-0 layer, one token): host wall time of each synchronous call, median of 50 after 5 warm-up calls. The
+    reference allocates and frees its scratch inside gptoss_kernel_moe (runtime/src/capi.cpp:127-144), so its
+    figure includes that, as a caller sees it."""
+    import ctypes
+    import statistics
+    import torch
+    from gptoss_b200 import capi, synth
+    if not REF_LIB.exists():
+        return {"unavailable": "oracle/_ref/libgptoss_ref.so not built (reference sources absent at build time)"}
+    P = capi.ptr
+    ref = ctypes.CDLL(str(REF_LIB))
+    ref.gptoss_last_error.restype = ctypes.c_char_p
+    for lb in (ref,):
+        lb.gptoss_kernel_router.argtypes = capi.SIGNATURES["gptoss_kernel_router"][0]
+        lb.gptoss_kernel_moe.argtypes = capi.SIGNATURES["gptoss_kernel_moe"][0]
+    t = synth.moe_layer(seed=0)
+    p = "model.layers.0."
+    dev = ctx.dev
+    ex = [t[p + "mlp.experts." + n].to(dev) for n in ("gate_up_proj_blocks", "gate_up_proj_scales",
+                                                      "gate_up_proj_bias", "down_proj_blocks", "down_proj_scales",
+                                                      "down_proj_bias")]
+    ex[2], ex[5] = ex[2].float(), ex[5].float()
+    W, b = t[p + "mlp.router.weight"].to(dev), t[p + "mlp.router.bias"].float().to(dev)
+    x = synth.tokens(1, seed=8)[0].to(dev)
+    ids = torch.empty(4, dtype=torch.int32, device=dev)
+    w = torch.empty(4, device=dev)
+    out = torch.zeros(H, device=dev)
+
+    def timed(fn):
+        for _ in range(5):
+            assert fn() == 0
+        ts = []
+        for _ in range(50):
+            t0 = time.perf_counter()
+            assert fn() == 0
+            ts.append((time.perf_counter() - t0) * 1e6)
+        return statistics.median(ts)
+
+    res = {}
+    for name, lb in (("reference", ref), ("ours", lib)):
+        r_us = timed(lambda: lb.gptoss_kernel_router(P(W), P(b), P(x), E, H, K_TOP, P(ids), P(w)))
+        m_us = timed(lambda: lb.gptoss_kernel_moe(*(P(e) for e in ex), P(x), P(ids), P(w), P(out), K_TOP, H, I,
+                                                  1.702, 7.0))
+        res[name] = {"kernel_router_us": r_us, "kernel_moe_us": m_us}
+    res["moe_speedup"] = res["reference"]["kernel_moe_us"] / res["ours"]["kernel_moe_us"]
+    res["router_speedup"] = res["reference"]["kernel_router_us"] / res["ours"]["kernel_router_us"]
+    res["note"] = ("host wall time per synchronous ABI call (one token, config-0 layer, H = I = 2880, k = 4); ours "
+                   "is the raw-weights entry point (per-call scale gather), not the prepared layer")
+    return res
+
+
+# ------------------------------------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    """Reference arm: the reference's CPU implementation of this path on the host cores, rank 0 only, a bounded sample
+    per step, the same metric, unit and config as the GPU arm."""
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from gptoss_b200 import synth
+    if args.workload == "moe-decode":
+        t0 = synth.moe_layer(seed=0)
+        rm = ReferenceMoE(t0)
+        h = rm.normed(torch.randn(64, H, generator=torch.Generator().manual_seed(99)))
+        el, n, timed = time_reference(rm, h, 1, args.steps, args.warmup, REF_BUDGET_S)
+        value, unit, metric, cfg, scaling = LAYER_BYTES * n / el / 1e9, UNIT, METRIC, decode_config(ws, args.layers), \
+            "weak"
+        sample = f"one token through one MoE layer (config-0 layer) per step, {rm.what}"
+        ms = el / timed * 1e3
+    elif args.workload == "prefill":
+        t, _, x = prefill_inputs(args.tokens)
+        rm = ReferenceMoE(t)
+        h = rm.normed(x[:512])
+        el, n, timed = time_reference(rm, h, 64, args.steps, args.warmup, REF_BUDGET_S)
+        value, unit, metric, cfg, scaling = n / el, "tok/s", PREFILL_METRIC, prefill_config(args.tokens, ws), "weak"
+        sample = f"64 tokens per step through {rm.what}"
+        ms = el / timed * 1e3
+    else:
+        p = "model.layers.0."
+        ln0, W0, b0 = synth.ep_router(0)
+        t = {p + "post_attention_layernorm.weight": ln0.to(torch.bfloat16), p + "mlp.router.weight": W0,
+             p + "mlp.router.bias": b0.to(torch.bfloat16)}
+        for nm, v in zip(["gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+                          "down_proj_scales", "down_proj_bias"], synth.ep_experts(0, 0, E, "cpu")):
+            t[p + "mlp.experts." + nm] = v
+        rm = ReferenceMoE(t)
+        x = torch.randn(256, H, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16).float()
+        h = rm.normed(x)
+        el, n, timed = time_reference(rm, h, 32, args.steps, args.warmup, REF_BUDGET_S)
+        value, unit, metric, cfg, scaling = n / el / args.layers, "tok/s", EP_METRIC, \
+            ep_config(args.tokens, ws, args.layers), "strong"
+        sample = f"32 tokens per step through layer 0 with {rm.what}, scaled by 1/{args.layers} layers"
+        ms = el / timed * 1e3 * args.layers
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": ws, "steps": args.steps,
+            "steps_timed": timed, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": rm.cores, "kind": rm.kind, "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------------------------------------------------- main
 def main():
     args = parse()
     if args.tokens is None:
         args.tokens = 8192 if args.workload == "ep" else 2048
-    if args.workload == "ep":
-        return run_ep_reference(args) if args.impl == "reference" else run_ep(args)
-    if args.workload == "prefill":
-        return run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
     if args.impl == "reference":
         return run_reference(args)
-    import torch
     from gptoss_b200 import capi
-    ws, rank, local = dist_init()
-    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = Ctx()
     lib = capi.load()
-    if args.moe_impl is not None and lib.gptoss_set_moe_impl(args.moe_impl) < 0:
-        raise RuntimeError(lib.gptoss_last_error().decode())
-    P = capi.ptr
-    layers, t0 = make_layers(args.layers, dev)
-    impl = args.moe_impl if args.moe_impl is not None else 1
-    handles = []
-    if impl == 1:
-        for L in layers:
-            hdl = lib.gptoss_moe_layer_create(P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]), E,
-                                              K_TOP, H, I, 1.702, 7.0)
-            if not hdl:
-                raise RuntimeError(lib.gptoss_last_error().decode())
-            handles.append(hdl)
-    n_tok = args.steps + args.warmup
-    g = torch.Generator(device=dev).manual_seed(77 + rank)
-    X = torch.randn(n_tok, H, device=dev, generator=g)
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-
-    def layer_call(li, x, events):
-        if handles:
-            return lib.gptoss_moe_layer_forward(handles[li], P(x), P(x), sp, events)
-        L = layers[li]
-        return lib.gptoss_moe_block_async(P(x), P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]),
-                                          P(x), E, K_TOP, H, I, 1.702, 7.0, sp, events)
-
-    def step(x, events=None):
-        for li in range(len(layers)):
-            if layer_call(li, x, events) != 0:
-                raise RuntimeError(lib.gptoss_last_error().decode())
-
-    def barrier():
-        if ws > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-
-    # One decode step (24 MoE layers) is captured once as a CUDA graph and replayed, as the reference engine does
-    # with its decode step (runtime/src/engine.cu:264-279): the host issues two operations per step, not 72
-    # launches. The programmatic-dependent-launch edges between a layer's kernels are kept in the graph.
-    x_static = torch.empty(H, device=dev)
-    for i in range(args.warmup):                          # eager warm-up also sizes the library's workspaces
-        x_static.copy_(X[args.steps + i])
-        step(x_static)
-    barrier()
-    cap = torch.cuda.Stream()
-    graph = torch.cuda.CUDAGraph()
-    x_static.copy_(X[0])
-    with torch.cuda.graph(graph, stream=cap):
-        sp_cap = cap.cuda_stream
-        for li in range(len(layers)):
-            rc = (lib.gptoss_moe_layer_forward(handles[li], P(x_static), P(x_static), sp_cap, None) if handles else
-                  lib.gptoss_moe_block_async(P(x_static), P(layers[li]["ln"]), 1e-5, P(layers[li]["W"]),
-                                             P(layers[li]["b"]), *(P(e) for e in layers[li]["ex"]), P(x_static), E,
-                                             K_TOP, H, I, 1.702, 7.0, sp_cap, None))
-            assert rc == 0, lib.gptoss_last_error().decode()
-    for i in range(3):
-        x_static.copy_(X[args.steps + (i % max(1, args.warmup))])
-        graph.replay()
-    barrier()
-
-    # ---- timed region: exactly K steps
-    with ClockSampler(local) as clocks:
-        barrier()
-        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0e.record(stream)
-        for i in range(args.steps):
-            x_static.copy_(X[i])
-            graph.replay()
-        t1e.record(stream)
-        barrier()
-    ms = t0e.elapsed_time(t1e)
-    if ws > 1:
-        tt = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms = float(tt.item())
-    value = ws * args.steps * args.layers * LAYER_BYTES / (ms / 1e3) / 1e9
-    # per layer: tensor cores = one fused launch (RMSNorm, router, gate/up, down); SIMT = rmsnorm + router + gate/up
-    # + down
-    gpu_launches = args.steps * args.layers * (1 if handles else 4)
-
-    # ---- per-kernel durations: a second graph of the same step with events around the kernels of every layer
-    # (events[0..2] are recorded before the layer's kernels, events[3] after; with the SIMT path the events split
-    # router / gate-up / down). Launched on the same stream as the timed graph.
-    n_prof = min(args.steps, 100)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.layers)]
-    for quad in ev:                                       # torch creates the CUDA event at its first record
-        for e in quad:
-            e.record(stream)
-    torch.cuda.synchronize()
-    evh = [ctypes_array(e) for e in ev]
-    pgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(pgraph, stream=cap):
-        for li in range(len(layers)):
-            rc = (lib.gptoss_moe_layer_forward(handles[li], P(x_static), P(x_static), cap.cuda_stream, evh[li])
-                  if handles else
-                  lib.gptoss_moe_block_async(P(x_static), P(layers[li]["ln"]), 1e-5, P(layers[li]["W"]),
-                                             P(layers[li]["b"]), *(P(e) for e in layers[li]["ex"]), P(x_static), E,
-                                             K_TOP, H, I, 1.702, 7.0, cap.cuda_stream, evh[li]))
-            assert rc == 0, lib.gptoss_last_error().decode()
-    sums = [0.0, 0.0, 0.0]
-    barrier()
-    for i in range(n_prof):
-        x_static.copy_(X[i])
-        pgraph.replay()
-        torch.cuda.synchronize()
-        for q in ev:
-            sums[0] += q[0].elapsed_time(q[1])
-            sums[1] += q[1].elapsed_time(q[2])
-            sums[2] += q[2].elapsed_time(q[3])
-    nl = n_prof * args.layers
-    part_us = [v / nl * 1e3 for v in sums]
-    if handles:
-        # the timed region launches nothing but the fused kernel (one per layer) and one 11.5 KB copy per step, so
-        # its average launch duration is the timed region's time over its launches (an upper bound: it includes the
-        # gaps between launches); the event-bracketed figure above is kept beside it
-        kernel_us = {"moe_fused_kernel": ms / args.steps / args.layers * 1e3,
-                     "moe_fused_kernel_event_bracketed": part_us[2]}
-        top_us, top_name, top_bytes = (ms / args.steps / args.layers * 1e3,
-                                       "moe_fused_kernel (RMSNorm + router + gate/up + down)", LAYER_BYTES)
-    else:
-        kernel_us = {"router+rmsnorm": part_us[0], "gate_up": part_us[1], "down+combine": part_us[2]}
-        top_us, top_name, top_bytes = part_us[1], "gateup_simt_kernel", GATEUP_BYTES
-    del evh
-
-    # ---- end to end through the public API: host x in, host x out, every step
-    xh = torch.randn(args.steps, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
-    yh = torch.empty(H).pin_memory()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        x_static.copy_(xh[i], non_blocking=True)
-        graph.replay()
-        yh.copy_(x_static, non_blocking=True)
-        stream.synchronize()
-    e1.record(stream)
-    barrier()
-    ms_e2e = e0.elapsed_time(e1)
-    if ws > 1:
-        tt = torch.tensor([ms_e2e], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms_e2e = float(tt.item())
-    e2e = ws * args.steps * args.layers * LAYER_BYTES / (ms_e2e / 1e3) / 1e9
-    del graph, pgraph
-
-    cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        bps, n, cores = cpu_moe_sample(t0, budget_s=15.0)
-        cpu = {"value": bps / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{n} tokens x 1 MoE layer of the same workload (numpy fp32, per-call MXFP4 dequant, "
-                         f"{cores} host threads)"}
-
-    peaks = {}
-    pk = ROOT / "MEASURED_PEAKS.json"
-    if pk.exists():
-        peaks = json.loads(pk.read_text())
-    hbm = peaks.get("hbm_gbs")
-    peak_src = "measured" if hbm else "fallback"
-    hbm = hbm or 6650.0
-    achieved = top_bytes / (top_us * 1e-6) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("moe_fused_kernel" if handles else "gateup_simt_kernel")
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init 20b-shaped MoE layers)",
-            "config": {"workload": "moe-decode (configs[0] stacked x24, bs=1)", "layers": args.layers,
-                       "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
-                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
-                       "l2": "inputs larger than L2: 24 distinct layers, 10.2 GB of experts"},
-            "tok_per_s": ws * args.steps / (ms / 1e3),
-            "us_per_moe_layer": ms / args.steps / args.layers * 1e3,
-            "moe_impl": "tensor cores (tcgen05 kind::mxf4)" if handles else "SIMT",
-            "kernel_us": kernel_us,
-            "roofline": {"bound": "hbm", "kernel": top_name, "achieved": achieved, "peak": hbm,
-                         "peak_source": peak_src, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
-                         "frac_of_8TBs_nominal": achieved / 8000.0, "algorithmic_bytes_per_launch": top_bytes,
-                         "launch_us": top_us},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
-                    "api": ("gptoss_moe_layer_forward" if handles else "gptoss_moe_block_async") +
-                           " x24 per token captured in one CUDA graph; host x copied in and out every step"},
-            "gpu_launches": gpu_launches,
-            "clocks": clocks.summary(),
-        }
-        print(json.dumps(line))
-    for hdl in handles:
-        lib.gptoss_moe_layer_destroy(hdl)
-    if ws > 1:
-        torch.distributed.destroy_process_group()
-
-
-def ctypes_array(events):
-    import ctypes
-    arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
-    return arr
+    try:
+        first = ctx.rank == 0 and ctx.ws == 1 and not args.no_cpu_baseline
+        if args.workload == "ep":
+            line = run_ep(args, ctx, lib, args.tokens, first)
+        elif args.workload == "prefill":
+            line = run_prefill(args, ctx, lib, args.tokens, first)
+        else:
+            line = run_decode(args, ctx, lib)
+            if not args.no_extras:
+                line["ep"] = run_ep(args, ctx, lib, 8192, False)
+                if ctx.ws == 1:
+                    line["prefill"] = run_prefill(args, ctx, lib, 2048, False)
+                    line["ref_gpu"] = run_ref_gpu(ctx, lib)
+        if ctx.rank == 0:
+            print(json.dumps(line))
+    finally:
+        ctx.close()
 
 
 if __name__ == "__main__":

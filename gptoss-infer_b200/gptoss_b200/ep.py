@@ -194,6 +194,36 @@ class PeerExpertParallelMoE:
         return x
 
 
+def balanced_placement(loads, world):
+    """Expert placement by expected load: which expert each rank holds, E / world experts per rank.
+
+    loads[e] is expert e's expected row count (from routing statistics, e.g. a calibration batch). Greedy
+    longest-processing-time: experts in decreasing load, each to the rank with the fewest rows that still has room
+    (ties to the lower rank, equal loads to the lower expert id). Returns perm, a list of E expert ids: rank r holds
+    experts perm[r * El : (r + 1) * El], each rank's in ascending id order. Relabelling the model by perm (router rows
+    and expert weights; apply_placement) makes the contiguous ownership of the kernels balanced; the MoE output is
+    unchanged (the combine adds each token's slots in logit order, which a relabelling does not change; only exact
+    logit ties, which go to the lower id, could pick differently)."""
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    El = E // world
+    order = sorted(range(E), key=lambda e: (-float(loads[e]), e))
+    held = [[] for _ in range(world)]
+    rows = [0.0] * world
+    for e in order:
+        r = min((r for r in range(world) if len(held[r]) < El), key=lambda r: (rows[r], r))
+        held[r].append(e)
+        rows[r] += float(loads[e])
+    return [e for r in range(world) for e in sorted(held[r])]
+
+
+def apply_placement(perm, router_w, router_b):
+    """The router of the relabelled model: expert j of the new labelling is expert perm[j] of the old one."""
+    idx = torch.as_tensor(perm, dtype=torch.long, device=router_w.device)
+    return router_w[idx].contiguous(), router_b[idx].contiguous()
+
+
 def _ok(lib, rc):
     if rc != 0:
         raise RuntimeError(lib.gptoss_last_error().decode())

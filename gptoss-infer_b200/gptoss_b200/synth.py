@@ -102,8 +102,13 @@ def ep_experts(layer, e0, e1, device, H=H, I=I, scale_lo=120, scale_hi=126):
     """Experts e0..e1-1 of layer `layer` of the expert-parallel benchmark model, drawn on `device` expert by expert
     from a generator seeded by (layer, expert), so every split of the experts over ranks holds the same weights.
     Returns [gu_blocks, gu_scales, gu_bias fp32, dn_blocks, dn_scales, dn_bias fp32], experts stacked on dim 0."""
+    return ep_experts_of(layer, range(e0, e1), device, H, I, scale_lo, scale_hi)
+
+
+def ep_experts_of(layer, experts, device, H=H, I=I, scale_lo=120, scale_hi=126):
+    """ep_experts for any list of expert ids (stacked in the list's order): a rank's experts under a placement."""
     parts = [[] for _ in range(6)]
-    for e in range(e0, e1):
+    for e in experts:
         g = torch.Generator(device=device).manual_seed(1_000_003 * (layer + 1) + 7_919 * e)
         for j, (rows, k) in enumerate(((2 * I, H), (H, I))):
             parts[3 * j].append(torch.randint(0, 256, (rows, k // 32, 16), generator=g, device=device,

@@ -106,3 +106,46 @@ def test_ep_two_ranks_matches_single_process(force_rank0):
         out[r::world] = got[r]
     want = _reference(x_all, force_rank0, world)
     np.testing.assert_allclose(out, want, rtol=1e-12, atol=1e-12)
+
+
+def test_balanced_placement_properties():
+    """Expert placement by expected load: every expert placed once, E / world per rank, each rank's list ascending,
+    and on the benchmark's Zipf-skewed loads the busiest rank carries no more than the contiguous placement's."""
+    from gptoss_b200 import ep
+    g = torch.Generator().manual_seed(3)
+    for world in (1, 2, 4, 8):
+        loads = (torch.rand(32, generator=g) ** 4 * 1000).tolist()
+        perm = ep.balanced_placement(loads, world)
+        assert sorted(perm) == list(range(32))
+        El = 32 // world
+        ranks = [perm[r * El:(r + 1) * El] for r in range(world)]
+        assert all(r == sorted(r) for r in ranks)
+        busiest = max(sum(loads[e] for e in r) for r in ranks)
+        contiguous = max(sum(loads[r * El:(r + 1) * El]) for r in range(world))
+        assert busiest <= contiguous + 1e-9
+        # LPT bound: the busiest rank exceeds the mean by at most the largest single load
+        assert busiest <= sum(loads) / world + max(loads) + 1e-9
+    assert ep.balanced_placement([5, 1, 1, 5, 3, 3, 2, 2], 2) == [0, 1, 4, 6, 2, 3, 5, 7]
+
+
+def test_placement_relabelling_keeps_the_moe_output():
+    """Relabelling the experts (router rows and expert weights permuted together) leaves the batched MoE unchanged:
+    the float64 oracle on a relabelled tiny model equals the original's."""
+    import numpy as np
+    from gptoss_b200 import ep, synth
+    from oracle import moe as omoe
+    t = synth.moe_layer(seed=5, H=64, I=32, E=8)
+    p = "model.layers.0."
+    x = synth.tokens(12, seed=6, H=64).numpy()
+    perm = ep.balanced_placement([7, 1, 3, 3, 9, 2, 2, 5], 2)
+    W, b = ep.apply_placement(perm, t[p + "mlp.router.weight"], t[p + "mlp.router.bias"])
+    t2 = dict(t)
+    t2[p + "mlp.router.weight"], t2[p + "mlp.router.bias"] = W, b
+    for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+              "down_proj_scales", "down_proj_bias"):
+        t2[p + "mlp.experts." + n] = t[p + "mlp.experts." + n][perm]
+    tn, tn2 = synth.to_numpy(t), synth.to_numpy(t2)
+    h = omoe.rms_norm(x, tn[p + "post_attention_layernorm.weight"])
+    a = omoe.moe(tn, p, h)
+    b2 = omoe.moe(tn2, p, h)
+    np.testing.assert_allclose(b2, a, rtol=1e-6, atol=1e-7)

@@ -257,3 +257,18 @@ def test_peer_ep_bounded_wait_runs_out_and_next_call_is_clean():
     want = _single_gpu_reference(t, x, "cuda")
     for got in _peer_forward(lib, t, x, 0, 1, "cuda", T_max=64):
         assert torch.equal(got, want)
+
+
+def test_placement_relabelling_bit_identical_on_gpu():
+    """Expert placement by load relabels the experts (router rows and expert weights permuted together). The batched
+    forward adds each token's slots in logit order, which the relabelling keeps, so the result is bit-identical."""
+    t = _model(False)
+    perm = ep.balanced_placement([9, 1, 4, 4, 7, 2, 2, 5], 2)
+    W, b = ep.apply_placement(perm, t[PX + "mlp.router.weight"], t[PX + "mlp.router.bias"])
+    t2 = dict(t)
+    t2[PX + "mlp.router.weight"], t2[PX + "mlp.router.bias"] = W, b
+    for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+              "down_proj_scales", "down_proj_bias"):
+        t2[EX + n] = t[EX + n][perm].contiguous()
+    x = synth.tokens(40, seed=16)
+    assert torch.equal(_single_gpu_reference(t2, x, "cuda"), _single_gpu_reference(t, x, "cuda"))

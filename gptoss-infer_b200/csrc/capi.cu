@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "gptoss.h"
+#include "engine.h"
 #include "kernels.h"
 #include "tma.h"
 
@@ -124,6 +125,8 @@ struct DecodeWs {
 thread_local DecodeWs g_dws;
 
 bool tc_shape_ok(int k, int H, int I) { return k >= 1 && k <= 8 && H % 64 == 0 && I % 64 == 0 && H >= 64 && I >= 64; }
+// The tensor-core decode kernel also holds x in registers (H <= 3072).
+bool decode_tc_ok(int k, int H, int I) { return tc_shape_ok(k, H, I) && H <= 3072; }
 
 // Reads the device-side error word of the tensor-core kernels after a synchronization; on error the workspace's
 // counters are cleared so the next call starts clean.
@@ -204,6 +207,54 @@ struct gptoss_moe_layer {
     }
 };
 
+namespace gpt {
+
+size_t moe_layer_workspace_bytes(int k, int H, int I) { return decode_tc_layout(k, H, I).bytes; }
+
+// The fused decode kernel of a prepared layer with the given workspace (decode_tc_layout(k, H, I).bytes, zero-filled
+// before its first use, used by one stream at a time).
+void moe_layer_forward_ws(gptoss_moe_layer* l, const float* x, float* x_resid, cudaStream_t s, void* const* events,
+                          void* workspace) {
+    const DecodeTcLayout L = decode_tc_layout(l->k, l->H, l->I);
+    char* w = static_cast<char*>(workspace);
+    int* ids = reinterpret_cast<int*>(w + L.off_misc + ((size_t(l->H) * 4 + 127) & ~size_t(127)));
+    float* gw = reinterpret_cast<float*>(ids + 32);
+    auto rec = [&](int i) {
+        if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
+    };
+    rec(0);
+    rec(1);
+    rec(2);
+    DecodeTcArgs a{};
+    a.tmap_gu = &l->tg;
+    a.tmap_dn = &l->td;
+    a.sfa_gu = l->sfa_gu;
+    a.sfa_dn = l->sfa_dn;
+    a.sfa_by_slot = 0;
+    a.gu_bias = l->gu_bias;
+    a.dn_bias = l->dn_bias;
+    a.router_w = l->router_w;
+    a.router_b = l->router_b;
+    a.norm_w = l->norm_w;
+    a.eps = l->eps;
+    a.E = l->E;
+    a.x = x;
+    a.ids_out = ids;
+    a.w_out = gw;
+    a.x_resid = x_resid;
+    a.k = l->k;
+    a.H = l->H;
+    a.I = l->I;
+    a.alpha = l->alpha;
+    a.limit = l->limit;
+    a.workspace = w;
+    a.trace = g_trace;
+    launch_moe_decode_tc(a, s);
+    rec(3);
+}
+
+}  // namespace gpt
+
 namespace {
 // Workspace of the batched path, owned by the calling thread, one per device (grow-only).
 thread_local Scratch g_pws;
@@ -223,36 +274,88 @@ extern "C" {
 
 const char* gptoss_last_error(void) { return g_error.c_str(); }
 
-gptoss_engine* gptoss_create(const char* model_dir, int max_ctx, long long vram_budget_bytes) {
-    (void)model_dir; (void)max_ctx; (void)vram_budget_bytes;
-    guard([&] { not_built("gptoss_create"); });
-    return nullptr;
-}
-void gptoss_destroy(gptoss_engine* e) { (void)e; }
-int gptoss_vocab(const gptoss_engine*) { return -1; }
-int gptoss_position(const gptoss_engine*) { return -1; }
-long long gptoss_device_bytes(const gptoss_engine*) { return -1; }
-int gptoss_reset(gptoss_engine*) { return guard([] { not_built("gptoss_reset"); }); }
-int gptoss_use_graph(gptoss_engine*, int) { return guard([] { not_built("gptoss_use_graph"); }); }
-int gptoss_step(gptoss_engine*, int) { return guard([] { not_built("gptoss_step"); }); }
-int gptoss_logits(gptoss_engine*, float*) { return guard([] { not_built("gptoss_logits"); }); }
-int gptoss_prefill(gptoss_engine*, const int32_t*, int, const int32_t*, int, float*, int32_t*, float*) {
-    return guard([] { not_built("gptoss_prefill"); });
-}
-int gptoss_score(gptoss_engine*, const int32_t*, int, int, float*, int32_t*, float*, float*) {
-    return guard([] { not_built("gptoss_score"); });
-}
-int gptoss_set_position(gptoss_engine*, int) { return guard([] { not_built("gptoss_set_position"); }); }
-int gptoss_bench_steps(gptoss_engine*, int, int) { return guard([] { not_built("gptoss_bench_steps"); }); }
+// ---- engine (runtime/include/gptoss/gptoss.h:14-42): gpt::Engine in engine.cu
+struct gptoss_engine {
+    gpt::Engine impl;
+    gptoss_engine(const char* dir, int max_ctx, long long budget) : impl(dir, max_ctx, budget) {}
+};
 
-int gptoss_kernel_gemv_bf16(const void*, const float*, const float*, const float*, float*, int, int) {
-    return guard([] { not_built("gptoss_kernel_gemv_bf16"); });
+gptoss_engine* gptoss_create(const char* model_dir, int max_ctx, long long vram_budget_bytes) {
+    gptoss_engine* e = nullptr;
+    guard([&] {
+        if (!model_dir) throw std::runtime_error("create: null model_dir");
+        e = new gptoss_engine(model_dir, max_ctx, vram_budget_bytes);
+    });
+    return e;
 }
-int gptoss_kernel_rope_append(float*, const float*, const float*, int, void*, void*, int) {
-    return guard([] { not_built("gptoss_kernel_rope_append"); });
+void gptoss_destroy(gptoss_engine* e) { delete e; }
+int gptoss_vocab(const gptoss_engine* e) { return e ? e->impl.vocab() : -1; }
+int gptoss_position(const gptoss_engine* e) { return e ? e->impl.position() : -1; }
+long long gptoss_device_bytes(const gptoss_engine* e) { return e ? e->impl.device_bytes() : -1; }
+
+namespace {
+gpt::Engine& eng(gptoss_engine* e) {
+    if (!e) throw std::runtime_error("null engine");
+    return e->impl;
 }
-int gptoss_kernel_attention(const float*, const void*, const void*, const float*, int, int, int, float*) {
-    return guard([] { not_built("gptoss_kernel_attention"); });
+}  // namespace
+
+int gptoss_reset(gptoss_engine* e) { return guard([&] { eng(e).reset(); }); }
+int gptoss_use_graph(gptoss_engine* e, int on) { return guard([&] { eng(e).use_graph(on != 0); }); }
+int gptoss_step(gptoss_engine* e, int token) { return guard([&] { eng(e).step(token); }); }
+int gptoss_logits(gptoss_engine* e, float* out) {
+    return guard([&] {
+        if (!out) throw std::runtime_error("logits: null output");
+        eng(e).copy_logits(out);
+    });
+}
+int gptoss_prefill(gptoss_engine* e, const int32_t* tokens, int n, const int32_t* ids, int k, float* lp,
+                   int32_t* argmax, float* target_lp) {
+    return guard([&] {
+        if (!tokens) throw std::runtime_error("prefill: null tokens");
+        if (ids && (k < 0 || !lp || !argmax || !target_lp)) throw std::runtime_error("prefill: bad scoring arguments");
+        eng(e).prefill(tokens, n, ids, k, lp, argmax, target_lp);
+    });
+}
+int gptoss_score(gptoss_engine* e, const int32_t* ids, int k, int target, float* lp, int32_t* argmax,
+                 float* target_lp, float* lse) {
+    return guard([&] { eng(e).score(ids, k, target, lp, argmax, target_lp, lse); });
+}
+int gptoss_set_position(gptoss_engine* e, int pos) { return guard([&] { eng(e).set_position(pos); }); }
+int gptoss_bench_steps(gptoss_engine* e, int token, int n) { return guard([&] { eng(e).bench_steps(token, n); }); }
+int gptoss_generate_greedy(gptoss_engine* e, int token, int n, int32_t* out_tokens) {
+    return guard([&] { eng(e).greedy(token, n, out_tokens); });
+}
+int gptoss_kv_fill_random(gptoss_engine* e, int positions, unsigned long long seed) {
+    return guard([&] { eng(e).kv_fill_random(positions, seed); });
+}
+
+int gptoss_kernel_gemv_bf16(const void* W, const float* x, const float* bias, const float* resid, float* y, int N,
+                            int K) {
+    return guard([&] {
+        gpt::launch_gemv_bf16(W, x, nullptr, 0.f, bias, resid, y, N, K, nullptr, false);
+        sync_check("gemv_bf16");
+    });
+}
+
+int gptoss_kernel_rope_append(float* qkv, const float* cos_t, const float* sin_t, int pos, void* k_cache,
+                              void* v_cache, int window) {
+    return guard([&] {
+        if (pos < 0 || window < 0) throw std::runtime_error("rope_append: pos and window must be >= 0");
+        gpt::launch_rope_append(qkv, cos_t, sin_t, nullptr, pos, k_cache, v_cache, window, nullptr, false);
+        sync_check("rope_append");
+    });
+}
+
+int gptoss_kernel_attention(const float* q, const void* k_cache, const void* v_cache, const float* sinks, int pos,
+                            int window, int max_ctx, float* out) {
+    return guard([&] {
+        if (pos < 0 || window < 0) throw std::runtime_error("attention: pos and window must be >= 0");
+        if (window == 0 && pos >= max_ctx) throw std::runtime_error("attention: pos must be below max_ctx");
+        float* part = static_cast<float*>(g_scratch.get(gpt::attention_workspace_floats() * sizeof(float)));
+        gpt::launch_attention(q, k_cache, v_cache, sinks, nullptr, pos, window, part, out, nullptr, false);
+        sync_check("attention");
+    });
 }
 
 int gptoss_kernel_rmsnorm(const float* x, const float* w, float* y, int n, float eps) {
@@ -276,7 +379,7 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
                       float limit) {
     return guard([&] {
         if (k < 1 || k > 8) throw std::runtime_error("moe: k must be in 1..8");
-        if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
+        if (g_moe_impl == 1 && decode_tc_ok(k, H, I)) {
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
             void* ws = g_dws.for_layout(L, k, H, I, nullptr);
             moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
@@ -370,7 +473,7 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
         auto rec = [&](int i) {
             if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
         };
-        if (g_moe_impl == 1 && tc_shape_ok(k, H, I)) {
+        if (g_moe_impl == 1 && decode_tc_ok(k, H, I)) {
             // raw scales: the router runs first (its ids select which scales to repack), then the fused kernel
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
             char* tw = static_cast<char*>(g_dws.for_layout(L, k, H, I, s));
@@ -597,41 +700,7 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
         if (!l) throw std::runtime_error("moe_layer_forward: null layer");
         const gpt::DecodeTcLayout L = gpt::decode_tc_layout(l->k, l->H, l->I);
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        char* w = static_cast<char*>(g_dws.for_layout(L, l->k, l->H, l->I, s));
-        int* ids = reinterpret_cast<int*>(w + L.off_misc + ((size_t(l->H) * 4 + 127) & ~size_t(127)));
-        float* gw = reinterpret_cast<float*>(ids + 32);
-        auto rec = [&](int i) {
-            if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
-        };
-        rec(0);
-        rec(1);
-        rec(2);
-        gpt::DecodeTcArgs a{};
-        a.tmap_gu = &l->tg;
-        a.tmap_dn = &l->td;
-        a.sfa_gu = l->sfa_gu;
-        a.sfa_dn = l->sfa_dn;
-        a.sfa_by_slot = 0;
-        a.gu_bias = l->gu_bias;
-        a.dn_bias = l->dn_bias;
-        a.router_w = l->router_w;
-        a.router_b = l->router_b;
-        a.norm_w = l->norm_w;
-        a.eps = l->eps;
-        a.E = l->E;
-        a.x = x;
-        a.ids_out = ids;
-        a.w_out = gw;
-        a.x_resid = x_resid;
-        a.k = l->k;
-        a.H = l->H;
-        a.I = l->I;
-        a.alpha = l->alpha;
-        a.limit = l->limit;
-        a.workspace = w;
-        a.trace = g_trace;
-        gpt::launch_moe_decode_tc(a, s);
-        rec(3);
+        gpt::moe_layer_forward_ws(l, x, x_resid, s, events, g_dws.for_layout(L, l->k, l->H, l->I, s));
     });
 }
 

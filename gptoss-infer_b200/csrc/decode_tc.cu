@@ -59,13 +59,13 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColX = kRows;             // accumulator in columns [0, 256); x's scale chunks from 256 on
 constexpr int kTraceSlots = 160;
 constexpr int kMaxK = 8;
-constexpr int kMaxX4 = 8;                     // x is held as kMaxX4 float4 per thread: H <= 4 * kThreads * kMaxX4
-constexpr int kMaxGrid = 160;                 // CTAs (SMs) the router reduction is unrolled for
+constexpr int kMaxX4 = 4;                     // x is held as kMaxX4 float4 per thread: H <= 4 * kThreads * kMaxX4
+constexpr int kMaxGrid = 160;                 // CTAs (SMs) the stage tables and traces are sized for
 
 struct Layout {
     int NS, NSF, cap;                         // weight ring depth, TMEM scale ring depth, stage-list capacity
     uint32_t colSFB, colDSF;                  // TMEM columns of the weight-scale ring and of down's A-scale ring
-    int ring, xA, xSF, dA, dSF, hs, red, bars, misc, bytes;
+    int ring, xA, xSF, dA, dSF, red, bars, misc, bytes;
 };
 
 struct Job {
@@ -88,14 +88,14 @@ struct Job {
     Part gu, dn;
     const Stage* stab;                        // host-built stage lists of all CTAs
     const int* shdr;                          // [grid][4]: first entry, entries, gate/up entries
-    uint8_t* xq_img;                          // x's A terms [SPS_gu][NT*128] (written by all CTAs in phase 0)
-    uint8_t* xq_sf;                           // their scales [KT_gu][128] (rows 0-7 of each chunk)
     uint8_t* aq_img;                          // down's A terms [k][SPS_dn][NT*128]
     uint8_t* aq_sf;                           // down's A scales [k][KT_dn][128]
     float* x_resid;
     unsigned* gbar;                           // [5]: gate/up done, exits, router partials published, x blocks written,
                                               // the last launch's epoch
-    double* partials;                         // [grid][32] router partial sums
+    unsigned long long* logit_words;          // [32][2] router logit e as (epoch << 32) | high and low 32 bits
+    uint8_t* xq_img;                          // x's A terms [SPS_gu][NT*128] (quantized by the last CTAs in phase 0)
+    uint8_t* xq_sf;                           // their scales [KT_gu][128] (rows 0-7 of each chunk)
     int* err;
     long long* trace;                         // optional [grid][kTraceSlots] clock64 stamps
     Layout L;
@@ -191,14 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     float* red_s = reinterpret_cast<float*>(smem + j.L.red);                // [NT][kRows] accumulator rows 0..7
     uint64_t* fullB = reinterpret_cast<uint64_t*>(smem + j.L.bars);        // [NS] weight stage landed
     uint64_t* emptyB = fullB + NS;            // [NS] weight stage consumed by the MMAs
-    uint64_t* fullS = emptyB + NS;            // [0] gate/up's small operands
+    uint64_t* fullS = emptyB + NS;            // [0] x's terms in shared memory
     uint64_t* accF = fullS + 2;               // accumulator complete (one phase per segment)
     uint64_t* accE = accF + 1;                // accumulator read out (one phase per segment)
     uint64_t* fullD = accE + 1;               // [cap] down stage's A terms and scales loaded
-    float* hs = reinterpret_cast<float*>(smem + j.L.hs);     // h = RMSNorm(x) [H]
     uint32_t* holder = reinterpret_cast<uint32_t*>(smem + j.L.misc);
-    int* cnts = reinterpret_cast<int*>(holder + 2);          // [2] router partials published everywhere
-    double* red = reinterpret_cast<double*>(cnts + 6);       // [6][32] router sums
+    double* red = reinterpret_cast<double*>(holder + 8);     // [6][32] router sums
     int* ids_s = reinterpret_cast<int*>(red + 7 * 32);       // [8]
     float* w_s = reinterpret_cast<float*>(ids_s + kMaxK);    // [8]
     float* aval = w_s + kMaxK;                               // [kRows / 2] phase 0's per-warp sums of squares
@@ -207,14 +205,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, nc = gridDim.x;
     if (tid == 0) stamp<kTrace>(j, 0);
-    // this CTA's slice of the router weights: thread (expert = lane, o = warp) takes chunks cs0 + o, cs0 + o + 6, ...
-    // of 8 weights; the first is loaded before anything else (it does not depend on x)
-    const int H8 = j.H >> 3;
-    const int cs0 = int((long long)c * H8 / nc), cs1 = int((long long)(c + 1) * H8 / nc);
-    uint4 w_first = make_uint4(0u, 0u, 0u, 0u);
-    if (j.router_w && lane < j.E && cs0 + warp < cs1)
-        w_first = __ldg(reinterpret_cast<const uint4*>(j.router_w) + size_t(lane) * H8 + cs0 + warp);
-    const float bias = j.router_w && warp == 0 && lane < j.E ? __ldg(j.router_b + lane) : 0.f;
+    // Router CTAs: CTA c < E computes expert c's logit over all of K. Thread t holds the same elements of the router
+    // row as of x (float4 chunks t, t + kThreads, ...), widened to fp64 before the previous layer has finished (they
+    // do not depend on it).
+    const bool router_cta = j.router_w != nullptr && c < j.E;
+    double wd[kMaxX4][4];
+    double rbias = 0.0;
+#pragma unroll
+    for (int r = 0; r < kMaxX4; ++r) {
+        const int i = (tid + r * kThreads) * 4;
+        uint2 u = make_uint2(0u, 0u);
+        if (router_cta && i < j.H) u = __ldg(reinterpret_cast<const uint2*>(j.router_w + size_t(c) * j.H + i));
+        wd[r][0] = bf16lo(u.x);
+        wd[r][1] = bf16hi(u.x);
+        wd[r][2] = bf16lo(u.y);
+        wd[r][3] = bf16hi(u.y);
+    }
+    if (router_cta) rbias = double(__ldg(j.router_b + c));
     // the norm weights and x, kept in registers: thread t holds float4 chunks t, t + kThreads, ...
     float4 xv[kMaxX4], gv[kMaxX4];
 #pragma unroll
@@ -261,7 +268,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         const int i = (tid + r * kThreads) * 4;
         xv[r] = i < j.H ? *reinterpret_cast<const float4*>(j.x + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // ---------------------------------------------------------------- phase 0: RMSNorm, router, expert ids
+    // ---------------------------------------------------------------- phase 0: RMSNorm, router, x's terms
+    // Two publications between CTAs, made at the same time and awaited by different warps: router CTA c publishes
+    // logit c (fp64, exact bf16 x fp32 products summed in a fixed order, so every CTA reads the same values and
+    // picks the same experts) as two epoch-tagged 64-bit words that warp 0 of every CTA polls directly; and the 32-
+    // element blocks of x's 8 activation terms (gate/up's A operand) are quantized by the last CTAs, one block each,
+    // into global memory, counted on gbar[3], which the epilogue warps await and copy into shared memory. h =
+    // RMSNorm(x) and the router products stay in registers.
     {
         const int H = j.H;
         float ss = 0.f;
@@ -272,7 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         if (lane == 0) aval[warp] = ss;
         if (tid == 0) stamp<kTrace>(j, 124);
         __syncthreads();
-        if (tid == 0) stamp<kTrace>(j, 125);
         float rn = 1.f;
         if (j.norm_w) {
             float tot = 0.f;
@@ -280,118 +292,62 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             rn = rms_scale(tot, H, j.eps);
         }
 #pragma unroll
-        for (int r = 0; r < kMaxX4; ++r) {
-            const int i = (tid + r * kThreads) * 4;
-            if (i < H) {
-                float4 v = xv[r];
-                if (j.norm_w) {
-                    v.x = v.x * rn * gv[r].x; v.y = v.y * rn * gv[r].y; v.z = v.z * rn * gv[r].z; v.w = v.w * rn * gv[r].w;
-                }
-                *reinterpret_cast<float4*>(hs + i) = v;
+        for (int r = 0; r < kMaxX4; ++r)
+            if (j.norm_w) {
+                xv[r].x = xv[r].x * rn * gv[r].x; xv[r].y = xv[r].y * rn * gv[r].y;
+                xv[r].z = xv[r].z * rn * gv[r].z; xv[r].w = xv[r].w * rn * gv[r].w;
             }
-        }
-        __syncthreads();
         if (tid == 0) stamp<kTrace>(j, 84);
-        double acc = 0.0;
-        if (j.router_w) {
-            for (int cc = cs0 + warp; cc < cs1; cc += kThreads / 32) {
-                if (lane < j.E) {
-                    const uint4 u = cc == cs0 + warp
-                                        ? w_first
-                                        : __ldg(reinterpret_cast<const uint4*>(j.router_w) + size_t(lane) * H8 + cc);
-                    const float4 h0 = *reinterpret_cast<const float4*>(hs + cc * 8);
-                    const float4 h1 = *reinterpret_cast<const float4*>(hs + cc * 8 + 4);
-                    acc = fma(bf16lo(u.x), double(h0.x), acc); acc = fma(bf16hi(u.x), double(h0.y), acc);
-                    acc = fma(bf16lo(u.y), double(h0.z), acc); acc = fma(bf16hi(u.y), double(h0.w), acc);
-                    acc = fma(bf16lo(u.z), double(h1.x), acc); acc = fma(bf16hi(u.z), double(h1.y), acc);
-                    acc = fma(bf16lo(u.w), double(h1.z), acc); acc = fma(bf16hi(u.w), double(h1.w), acc);
-                }
+        if (router_cta) {
+            double acc = 0.0;
+#pragma unroll
+            for (int r = 0; r < kMaxX4; ++r) {
+                acc = fma(wd[r][0], double(xv[r].x), acc);
+                acc = fma(wd[r][1], double(xv[r].y), acc);
+                acc = fma(wd[r][2], double(xv[r].z), acc);
+                acc = fma(wd[r][3], double(xv[r].w), acc);
             }
-        }
-        red[warp * 32 + lane] = acc;
-        __syncthreads();
-        if (warp >= 3) {
-            // this CTA's share of x's 32-blocks -> A terms in global memory (warps 5, 4, 3, while warp 0 publishes
-            // the router sums), published on their own counter, which the epilogue checks before reading x's terms
-            const int nb = H / 32, b0 = int((long long)c * nb / nc), b1 = int((long long)(c + 1) * nb / nc);
-            for (int g = b0 + (kThreads / 32 - 1 - warp); g < b1; g += 3)
-                quantize_block_terms_warp32<NT>(hs[g * 32 + lane], j.xq_img + (g / 8) * kA, g % 8,
-                                                j.xq_sf + (g / 4) * kSF8, g % 4, true);
-            asm volatile("bar.sync 2, 96;" ::: "memory");
-            if (warp == 3 && lane == 0) red_add_release(&j.gbar[3], 1u);
-        }
-        if (warp == 0) {
-            if (j.router_w) {
+            acc = warp_sum(acc);
+            if (lane == 0) red[warp] = acc;
+            __syncthreads();
+            if (tid == 0) {
                 double t = 0.0;
-                for (int w = 0; w < kThreads / 32; ++w) t += red[w * 32 + lane];
-                j.partials[size_t(c) * 32 + lane] = t;
-            }
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) {
-                atomicAdd(&j.gbar[2], 1u);
+                for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+                const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(t + rbias));
+                st_relaxed64(j.logit_words + 2 * c, (static_cast<unsigned long long>(ep) << 32) | (bits >> 32));
+                st_relaxed64(j.logit_words + 2 * c + 1, (static_cast<unsigned long long>(ep) << 32) | (bits & 0xFFFFFFFFull));
                 stamp<kTrace>(j, 85);
             }
-            // every CTA's partial sums and x blocks published (bounded wait; the launch is cooperative)
-            bool done = false;
-            for (uint32_t i = 0; i < tc::kSpinLimit && !done; ++i) {
-                done = __shfl_sync(kFull, lane == 0 ? ld_acquire(&j.gbar[2]) >= unsigned(nc) : false, 0);
-                if (!done) __nanosleep(20);
-            }
-            if (lane == 0) {
-                if (!done) atomicCAS(j.err, 0, 10);
-                cnts[2] = done;
-                stamp<kTrace>(j, 86);
+        }
+        // x's blocks: block g is quantized by CTA nc - 1 - (g % nc), in the 8 lanes whose registers hold it (float4
+        // round r = g / (kThreads / 8), threads 8 (g % (kThreads / 8)) ..+7), which write its terms into global memory
+        // and count it on gbar[3]
+        {
+            const int nb = H / 32, per_round = kThreads / 8;
+#pragma unroll
+            for (int r = 0; r < kMaxX4; ++r) {
+                const int g = r * per_round + tid / 8;
+                if (g < nb && nc - 1 - (g % nc) == c) {          // uniform over the 8 lanes of the group
+                    const int sub8 = tid & 7;
+                    const float v[4] = {xv[r].x, xv[r].y, xv[r].z, xv[r].w};
+                    uint8_t* img = j.xq_img + size_t(g / 8) * kA + 2 * sub8;
+                    uint8_t* sf = j.xq_sf + size_t(g / 4) * kSF8 + (g & 3);
+                    const int q = g & 7;
+                    const unsigned grp = 0xFFu << (lane & 24);
+                    quantize_block_digits_lanes8_masked(v, grp, [&](int t, uint32_t half, uint32_t scale) {
+                        *reinterpret_cast<uint16_t*>(img + t * 128 + ((q ^ (t & 7)) << 4)) = uint16_t(half);
+                        // the scale byte goes to all four lane-quadrant copies of the term's row (lane sub8 < 4:
+                        // copy sub8)
+                        if (sub8 < 4) sf[t * 16 + sub8 * 4] = uint8_t(scale);
+                    });
+                    __syncwarp(grp);
+                    if (sub8 == 0) red_add_release(&j.gbar[3], 1u);
+                }
             }
         }
-        __syncthreads();
-        if (j.router_w) {
-            // every CTA adds all partial sums in the same order: thread (w, e) takes CTAs w, w + 6, ... (all its
-            // loads issued together), then warp 0 adds the six sums
-            double t = 0.0;
-            if (cnts[2]) {
-                constexpr int kPer = (kMaxGrid + kThreads / 32 - 1) / (kThreads / 32);
-                double v[kPer];
-#pragma unroll
-                for (int u = 0; u < kPer; ++u) {
-                    const int cc = warp + u * (kThreads / 32);
-                    v[u] = cc < nc ? __ldcg(&j.partials[size_t(cc) * 32 + lane]) : 0.0;
-                }
-#pragma unroll
-                for (int u = 0; u < kPer; ++u) t += v[u];
-            }
-            red[warp * 32 + lane] = t;
-            __syncthreads();
-            if (tid == 0) stamp<kTrace>(j, 87);
-            if (warp == 0) {
-                // top k on order-preserving 64-bit keys of the fp64 logits (integer warp reductions; ties to the
-                // lower id; NaN, picked experts and lanes >= E get key 0 and never win while a real logit is left)
-                double v = 0.0;
-                if (lane < j.E) {
-                    double tt = 0.0;
-                    for (int w = 0; w < kThreads / 32; ++w) tt += red[w * 32 + lane];
-                    v = tt + double(bias);
-                }
-                if (lane == 0) stamp<kTrace>(j, 120);
-                int sel_id = 0;
-                double sel_logit = 0.0;
-                warp_topk_logits(v, lane < j.E, j.k, sel_id, sel_logit);
-                if (lane == 0) stamp<kTrace>(j, 121);
-                const float gate = warp_pick_softmax(sel_logit, j.k);
-                if (lane == 0) stamp<kTrace>(j, 122);
-                if (lane < j.k) {
-                    ids_s[lane] = sel_id;
-                    w_s[lane] = gate;
-                    if (j.ids_out && c == 0) { j.ids_out[lane] = sel_id; j.w_out[lane] = gate; }
-                }
-            }
-        } else if (tid < j.k) {
-            ids_s[tid] = j.ids_in[tid];
-            w_s[tid] = j.w_in[tid];
-        }
-        if (tid == 0) stamp<kTrace>(j, 88);
+        if (tid == 0) stamp<kTrace>(j, 126);
     }
-    tc::fence_proxy_async_smem();             // h's shared memory becomes the TMA ring from here on
+    tc::fence_proxy_async_smem();             // x's terms (generic stores) are read by the MMAs (async proxy)
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -401,7 +357,43 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
     auto part_of = [&](const Stage& st) -> const Part& { return st.mode == sk::kGateUp ? j.gu : j.dn; };
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- producer (converged warp, elected lane)
+        // ---------------------------------------------------------------- expert ids, then the TMA producer
+        if (j.router_w) {
+            // lane e polls logit e's two words until both carry this launch's epoch (bounded)
+            unsigned long long w0 = 0, w1 = 0;
+            bool done = false;
+            for (uint32_t i = 0; i < tc::kSpinLimit && !done; ++i) {
+                if (lane < j.E) {
+                    w0 = ld_relaxed64(j.logit_words + 2 * lane);
+                    w1 = ld_relaxed64(j.logit_words + 2 * lane + 1);
+                }
+                done = __all_sync(kFull, lane >= j.E || (unsigned(w0 >> 32) == ep && unsigned(w1 >> 32) == ep));
+                if (!done) __nanosleep(20);
+            }
+            if (!done && lane == 0) atomicCAS(j.err, 0, 10);
+            const double v = __longlong_as_double(static_cast<long long>((w0 << 32) | (w1 & 0xFFFFFFFFull)));
+            if (lane == 0) stamp<kTrace>(j, 120);
+            int sel_id = 0;
+            double sel_logit = 0.0;
+            warp_topk_logits(v, lane < j.E, j.k, sel_id, sel_logit);
+            if (lane == 0) stamp<kTrace>(j, 121);
+            const float gate = warp_pick_softmax(sel_logit, j.k);
+            if (lane == 0) stamp<kTrace>(j, 122);
+            if (lane < j.k) {
+                ids_s[lane] = sel_id;
+                w_s[lane] = gate;
+                if (j.ids_out && c == 0) { j.ids_out[lane] = sel_id; j.w_out[lane] = gate; }
+            }
+            if (lane == 0) stamp<kTrace>(j, 127);
+        } else if (lane < j.k) {
+            ids_s[lane] = j.ids_in[lane];
+            w_s[lane] = j.w_in[lane];
+        }
+        // ids and gate weights are in shared memory: release the MMA and epilogue warps, which sleep in named
+        // barrier 3 meanwhile (a spinning wait there would compete with this warp's shuffles and reductions)
+        __syncwarp();
+        asm volatile("bar.arrive 3, %0;" ::"n"(kThreads) : "memory");
+        if (lane == 0) stamp<kTrace>(j, 88);
         if (tc::elect_one()) {
             stamp<kTrace>(j, 89);
             tc::prefetch_tmap(&tm_gu);
@@ -465,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         // slot it % NSF) before the stage's data is waited for, then the weight scales (4 chunks from the ring slot:
         // 2 K chunks x 2 row halves, 8 TMEM columns per K chunk) into weight-scale slot it % NSF, up to 4 MMAs and
         // one commit.
+        asm volatile("bar.sync 3, %0;" ::"n"(kThreads) : "memory");   // expert ids known (warp 0)
         if (tc::elect_one()) {
             bool ok = nst == 0 || tc::mbar_wait(&fullS[0], 0, j.err, 6);
             // Gate/up stages: x's scale chunks (first use of each K chunk), the weight scales, 4 MMAs, commits.
@@ -563,11 +556,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         // ---------------------------------------------------------------- epilogue warps 2..5
         const int et = tid - 64;                    // 0..127
 
-        // x's terms and scales (written by all CTAs in phase 0, counted on gbar[3]), with asynchronous 16-byte copies.
+        // x's terms and scales (quantized by the last CTAs in phase 0, counted on gbar[3]), with asynchronous 16-byte
+        // copies; then the expert ids from warp 0
         {
             if (et == 0) {
                 bool done = false;
-                for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) done = ld_acquire(&j.gbar[3]) >= unsigned(nc);
+                for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
+                    done = ld_acquire(&j.gbar[3]) >= unsigned(j.H / 32);
+                    if (!done) __nanosleep(32);
+                }
                 if (!done) atomicCAS(j.err, 0, 13);
             }
             epi_sync();
@@ -576,11 +573,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                 if (x < n1) tc::cp_async16(xA + 16 * x, j.xq_img + 16 * x);
                 else tc::cp_async16(xSF + 16 * (x - n1), j.xq_sf + 16 * (x - n1));
             }
-            if (et == 0) stamp<kTrace>(j, 126);
             tc::cp_async_wait_all();
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&fullS[0]);
             if (et == 0) stamp<kTrace>(j, 80);
+            asm volatile("bar.sync 3, %0;" ::"n"(kThreads) : "memory");   // expert ids known (warp 0)
+            if (et == 0) stamp<kTrace>(j, 78);
         }
         // After the CTA's last gate/up epilogue: count it on the grid barrier; once every CTA has finished gate/up
         // (bounded wait), one thread loads each down stage's A terms and scales with two bulk copies completing on
@@ -798,11 +796,6 @@ Layout make_layout(int NS, int cap, int cap_dn, const Part& gu, int H) {
     L.xSF = o; o += (gu.KT * kSF8 + 1023) & ~1023;
     L.dA = o; o += cap_dn * kA;
     L.dSF = o; o += cap_dn * 2 * kSF8;
-    L.hs = H * 4 <= NS * kSlot ? L.ring : -1;   // h is read only in phase 0, before the ring's first stage
-    if (L.hs < 0) {
-        L.hs = o;
-        o += (H * 4 + 15) & ~15;
-    }
     L.red = o; o += NT * kRows * 4;
     L.bars = o; o += (2 * NS + 4 + cap) * 8;
     o = (o + 15) & ~15;
@@ -879,19 +872,19 @@ DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     L.RT_gu = (2 * I + TR - 1) / TR;
     L.RT_dn = (H + TR - 1) / TR;
     size_t o = 0;
-    L.off_partials = o; o += al(size_t(256) * 32 * 8);
     L.off_xq_img = o; o += al(size_t(L.SPS_gu) * NT * 128);
     L.off_xq_sf = o; o += al(size_t(L.KT_gu) * fz::kSF8);
     L.off_aq_img = o; o += al(size_t(k) * L.SPS_dn * NT * 128);
     L.off_aq_sf = o; o += al(size_t(k) * L.KT_dn * fz::kSF8);
     L.off_part_gu = o; o += al(size_t(k) * L.RT_gu * sk::kMaxContrib * TR * 8);
     L.off_part_dn = o; o += al(size_t(L.RT_dn) * sk::kMaxContrib * TR * 8);
+    L.off_logits = o; o += al(size_t(32) * 16);              // epoch-tagged router logits
     L.off_err = o; o += 1024;                                // error word, then the grid barrier at +256
     L.off_sfa_gu = o; o += al(sf_repacked_bytes(k, 2 * I, H / 32, TR));
     L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32, TR));
     L.off_misc = o; o += al(size_t(H) * 4 + 256);
     L.bytes = o;
-    L.zero_bytes_from = L.off_part_gu;                        // partial sums (epoch 0), error word, grid barrier
+    L.zero_bytes_from = L.off_part_gu;                        // tagged partial sums and logits, error word, barrier
     L.zero_bytes_to = L.off_err + 1024;
     return L;
 }
@@ -916,9 +909,9 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     using namespace fz;
     require(a.k >= 1 && a.k <= kMaxK, "moe (tc): k must be in 1..8");
     require(a.H % 64 == 0 && a.I % 64 == 0, "moe (tc): H and I must be multiples of 64");
-    require(a.H <= 4 * kThreads * kMaxX4, "moe (tc): H too large for the register-held x");
+    require(a.H <= 4 * kThreads * kMaxX4, "moe (tc): H must be at most 3072 (x is held in registers)");
     require(!a.router_w || (a.E >= a.k && a.E <= 32), "moe (tc): router needs k <= E <= 32");
-    require(num_sms() <= kMaxGrid, "moe (tc): more SMs than the router reduction is written for");
+    require(num_sms() <= kMaxGrid, "moe (tc): more SMs than the stage tables are written for");
     const DecodeTcLayout W = decode_tc_layout(a.k, a.H, a.I);
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
     Job j{};
@@ -962,14 +955,14 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     d.UT = a.k * d.UK;
     d.total = (long long)d.n_tiles * d.UT;
     d.partial = reinterpret_cast<unsigned long long*>(ws + W.off_part_dn);
-    j.xq_img = ws + W.off_xq_img;
-    j.xq_sf = ws + W.off_xq_sf;
     j.aq_img = ws + W.off_aq_img;
     j.aq_sf = ws + W.off_aq_sf;
     j.x_resid = a.x_resid;
     j.err = reinterpret_cast<int*>(ws + W.off_err);
     j.gbar = reinterpret_cast<unsigned*>(ws + W.off_err + 256);
-    j.partials = reinterpret_cast<double*>(ws + W.off_partials);
+    j.logit_words = reinterpret_cast<unsigned long long*>(ws + W.off_logits);
+    j.xq_img = ws + W.off_xq_img;
+    j.xq_sf = ws + W.off_xq_sf;
     j.trace = a.trace;
 
     // One CTA per SM, all resident (cooperative launch); the stage lists come from the per-shape table.

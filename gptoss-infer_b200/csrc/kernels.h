@@ -7,6 +7,8 @@
 #include <cstddef>
 #include <cstdint>
 
+struct gptoss_moe_layer;
+
 namespace gpt {
 
 int num_sms();
@@ -59,7 +61,7 @@ constexpr int kDecodeTileRows = 256;
 // (the partial-sum words carry the launch epoch and the grid barrier resets itself afterwards).
 struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
-    size_t off_partials, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_err;
+    size_t off_logits, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
 };
 DecodeTcLayout decode_tc_layout(int k, int H, int I);
@@ -166,5 +168,26 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
 // and decodes them back into out [n]; per_term (optional, [2][n]) receives the first two terms. Synchronizes.
 void selftest_terms(const float* x, int n, float* out, float* per_term, int which, void* scratch, size_t bytes,
                     cudaStream_t s);
+
+// Decode step around the MoE (decode_step.cu). pdl: launch with programmatic dependent launch (the kernels wait for
+// the previous kernel's memory before reading their inputs). d_pos (device int) overrides pos when not null.
+void launch_gemv_bf16(const void* W, const float* x, const float* norm_w, float eps, const float* bias,
+                      const float* resid, float* y, int N, int K, cudaStream_t s, bool pdl);
+void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, const int* d_pos, int pos, void* k_cache,
+                        void* v_cache, int window, cudaStream_t s, bool pdl);
+size_t attention_workspace_floats();
+void launch_attention(const float* q, const void* k_cache, const void* v_cache, const float* sinks, const int* d_pos,
+                      int pos, int window, float* part, float* out, cudaStream_t s, bool pdl);
+void launch_embed(const void* table, const int* d_token, float* x, int H, cudaStream_t s, bool pdl);
+void launch_increment(int* p, cudaStream_t s, bool pdl);
+size_t score_workspace_bytes();   // zero-filled before the first use (its counter resets itself)
+void launch_score(const float* logits, int V, void* work, const int* ids, int k, int target, float* lp, int* argmax,
+                  float* target_lp, float* lse, int* next_token, cudaStream_t s, bool pdl);
+
+// The fused decode kernel of a prepared layer (capi.cu) with a caller-owned workspace of
+// moe_layer_workspace_bytes(k, H, I), zero-filled before its first use and used by one stream at a time.
+size_t moe_layer_workspace_bytes(int k, int H, int I);
+void moe_layer_forward_ws(gptoss_moe_layer* l, const float* x, float* x_resid, cudaStream_t s, void* const* events,
+                          void* workspace);
 
 }  // namespace gpt

@@ -215,6 +215,45 @@ __device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8]
     }
 }
 
+// quantize_block_digits_lanes4 with eight lanes per block, four elements each (lane `sub8` = 0..7 of an aligned
+// 8-lane group holds elements 4 sub8 .. 4 sub8 + 3): the same terms, scales and digits, so the same bits. emit(t,
+// half, scale) receives the lane's 16 bits of term t's codes (element 4 sub8 + i in bits 4i..4i+3), which are bytes
+// 2 sub8 and 2 sub8 + 1 of the block's 16 code bytes. `mask` names the lanes that call (whole aligned 8-lane groups).
+template <class Emit>
+__device__ __forceinline__ void quantize_block_digits_lanes8_masked(const float (&v)[4], unsigned mask, Emit&& emit) {
+    constexpr int kOff = 4 * 299593;                            // 4 (8^7 - 1) / 7
+    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 4));
+    const int k = fixed_schedule_k0(amax);
+    const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+    uint32_t w0 = 0, w1 = 0;
+    int Rp[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t code;
+        const float q0 = round_e2m1_code(v[i] * inv, code);
+        w0 |= code << (4 * i);
+        const float r = fmaf(-q0, sc, v[i]);                    // exact
+        Rp[i] = __float2int_rn((r * inv) * 1048576.f) + kOff;    // in 0 .. 2^20 + kOff
+        const uint32_t u1 = uint32_t(Rp[i]) >> 18;               // top digit + 4, 0..8
+        w1 |= (u1 < 4 ? 12u - u1 : u1 - 4u) << (4 * i);
+    }
+    emit(0, w0, uint32_t(k + 127));
+    emit(1, (k - 1 >= -127) ? w1 : 0u, uint32_t(max(k - 1 + 127, 0)));
+#pragma unroll
+    for (int t = 2; t < 8; ++t) {
+        const int kt = k + 2 - 3 * t, j = 7 - t;
+        uint32_t u = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) u |= ((uint32_t(Rp[i]) >> (3 * j)) & 7u) << (4 * i);
+        const uint32_t hi = ((u >> 2) & 0x1111u) * 0xFu;
+        const uint32_t w = (u & 0x3333u & hi) | ((0x8888u | ((~u & 0x3333u) + 0x1111u)) & ~hi & 0xFFFFu);
+        emit(t, kt >= -127 ? w : 0u, uint32_t(max(kt + 127, 0)));
+    }
+}
+
 // Same image format and first term as quantize_block_terms_cvt, with the later terms' scales fixed instead of
 // taken from each residual's maximum: term 0 keeps the block's maximum within 6 * 2^k0, so its rounding error is at
 // most 2^k0 (the e2m1 grid step is 2 between 4 and 6); term 1 uses k0 - 2 (|y| <= 4), and from then on every

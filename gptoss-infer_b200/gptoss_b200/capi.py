@@ -62,6 +62,8 @@ SIGNATURES = {
     "gptoss_score": ([P, P, I32, I32, P, P, P, P], I32),
     "gptoss_set_position": ([P, I32], I32),
     "gptoss_bench_steps": ([P, I32, I32], I32),
+    "gptoss_generate_greedy": ([P, I32, I32, P], I32),
+    "gptoss_kv_fill_random": ([P, I32, ctypes.c_ulonglong], I32),
 }
 
 _lib = None

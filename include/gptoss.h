@@ -21,8 +21,12 @@ typedef struct gptoss_engine gptoss_engine;
 
 /* ---- Engine lifecycle and decode (reference gptoss.h:14-42) ------------------------------------------------ */
 
-/* Loads the checkpoint in model_dir onto the current CUDA device; returns NULL on failure (reference gptoss.h:14-17).
- * vram_budget_bytes > 0 caps the engine's own device allocations. */
+/* Loads the checkpoint in model_dir (config.json, optional generation_config.json, safetensors with Hugging Face
+ * names, MXFP4 experts) onto the current CUDA device; returns NULL on failure (reference gptoss.h:14-17).
+ * vram_budget_bytes > 0 caps the engine's own device allocations. Geometry: 64 query heads, 8 key/value heads, head
+ * dim 64, hidden and intermediate multiples of 64 with hidden <= 3072, k <= E <= 32, k <= 8 (gpt-oss-20b and -120b).
+ * A step runs embed, 24 x (RMSNorm + QKV GEMV, RoPE + fp16 KV append, split-K attention with sinks and sliding
+ * window, O GEMV + residual, the fused tensor-core MoE), final RMSNorm + LM head, captured once as a CUDA graph. */
 gptoss_engine* gptoss_create(const char* model_dir, int max_ctx, long long vram_budget_bytes);
 void gptoss_destroy(gptoss_engine* e);                                   /* reference gptoss.h:18 */
 const char* gptoss_last_error(void);                                     /* reference gptoss.h:19 */
@@ -39,6 +43,13 @@ int gptoss_score(gptoss_engine* e, const int32_t* ids, int k, int target, float*
                  float* target_lp, float* lse);                          /* reference gptoss.h:36-38 */
 int gptoss_set_position(gptoss_engine* e, int pos);                      /* reference gptoss.h:40-41 */
 int gptoss_bench_steps(gptoss_engine* e, int token, int n);              /* reference gptoss.h:42 */
+/* [extension] Greedy decode of n tokens from `token`: each step's argmax is found on the device and fed to the next
+ * step without a host round trip; out_tokens (host, n entries, may be NULL) receives the generated tokens. Advances
+ * the position by n. */
+int gptoss_generate_greedy(gptoss_engine* e, int token, int n, int32_t* out_tokens);
+/* [extension] Benchmarking: fills every layer's fp16 KV cache for positions 0 .. positions-1 with deterministic
+ * N(0, 1) values (seeded) and sets the position to `positions`, standing in for a prefilled context. */
+int gptoss_kv_fill_random(gptoss_engine* e, int positions, unsigned long long seed);
 
 /* ---- Kernel entry points (reference gptoss.h:44-58). Device pointers; each call synchronizes. ------------- */
 

@@ -20,7 +20,7 @@ SUITE = STAGED / "runtime_tests" / "test_kernels.py"
 LIB = ROOT / "gptoss-infer_b200" / "lib" / "libgptoss.so"
 
 # the reference's test functions whose entry points are implemented here
-IMPLEMENTED = ["test_rmsnorm", "test_router", "test_moe_real_shape"]
+IMPLEMENTED = ["test_gemv_bf16", "test_rmsnorm", "test_rope_append", "test_attention", "test_router", "test_moe_real_shape"]
 
 if not SUITE.exists() or not (STAGED / "reference" / "gptoss_ref" / "model.py").exists():
     pytest.skip("the reference's kernel tests are not staged (python oracle/stage_reference.py)",

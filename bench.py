@@ -56,7 +56,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode", "prefill", "ep"])
+    ap.add_argument("--workload", default="moe-decode", choices=["moe-decode", "prefill", "ep", "decode"])
     ap.add_argument("--tokens", type=int, default=None,
                     help="prefill: tokens per step (config 2: 2048); ep: tokens per step over all ranks (config 3: 8192)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -68,6 +68,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="moe-decode: skip the ep / prefill / ref_gpu objects")
+    ap.add_argument("--decode-tokens", type=int, default=128, help="decode: greedy tokens per timed run (configs[1]: 128)")
+    ap.add_argument("--decode-reps", type=int, default=3, help="decode: timed runs (median reported)")
     return ap.parse_args()
 
 
@@ -799,6 +801,121 @@ def run_ep(args, ctx, lib, T, with_cpu):
     }
 
 
+# ------------------------------------------------------------------------------------------------ full decode step
+DECODE_V = 201088
+DECODE_BYTES_PER_TOKEN = 3_705_753_600     # 24 x (QKV + O + router + 4 experts) + LM head, bf16 / MXFP4 as stored
+
+
+def write_20b_checkpoint(d, layers=LAYERS, seed=0):
+    """A random-init gpt-oss-20b-shaped checkpoint in the Hugging Face safetensors layout, one shard per
+    layer plus one for the embeddings, norm and LM head, with model.safetensors.index.json and config.json.
+    Attention and LM head bf16 N(0, 0.02), sinks N(0, 1), RMSNorm weights 1 + N(0, 0.02), embeddings N(0, 1), MoE as
+    configs[0] (blocks uniform over all codes, scales uniform 120..126, biases N(0, 0.01), router N(0, 0.02) / bias
+    N(0, 0.01)). Drawn on the GPU from a seeded generator, written from host memory."""
+    import torch
+    from safetensors.torch import save_file
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    n = lambda *s, std=1.0: (torch.randn(*s, device="cuda", generator=g) * std).to(torch.bfloat16).cpu()
+    u8 = lambda lo, hi, *s: torch.randint(lo, hi, s, device="cuda", generator=g, dtype=torch.uint8).cpu()
+    index = {}
+    top = {"model.embed_tokens.weight": n(DECODE_V, H), "lm_head.weight": n(DECODE_V, H, std=0.02),
+           "model.norm.weight": (1 + torch.randn(H, device="cuda", generator=g) * 0.02).to(torch.bfloat16).cpu()}
+    save_file(top, str(d / "model-top.safetensors"))
+    index.update({k: "model-top.safetensors" for k in top})
+    del top
+    for l in range(layers):
+        p = f"model.layers.{l}."
+        t = {p + "input_layernorm.weight": (1 + torch.randn(H, device="cuda", generator=g) * 0.02).to(torch.bfloat16).cpu(),
+             p + "post_attention_layernorm.weight": (1 + torch.randn(H, device="cuda", generator=g) * 0.02).to(torch.bfloat16).cpu(),
+             p + "self_attn.q_proj.weight": n(4096, H, std=0.02), p + "self_attn.q_proj.bias": n(4096, std=0.02),
+             p + "self_attn.k_proj.weight": n(512, H, std=0.02), p + "self_attn.k_proj.bias": n(512, std=0.02),
+             p + "self_attn.v_proj.weight": n(512, H, std=0.02), p + "self_attn.v_proj.bias": n(512, std=0.02),
+             p + "self_attn.o_proj.weight": n(H, 4096, std=0.02), p + "self_attn.o_proj.bias": n(H, std=0.02),
+             p + "self_attn.sinks": n(64), p + "mlp.router.weight": n(E, H, std=0.02), p + "mlp.router.bias": n(E, std=0.01)}
+        for name, rows, kk in (("gate_up_proj", 2 * I, H), ("down_proj", H, I)):
+            q = p + "mlp.experts." + name
+            t[q + "_blocks"] = u8(0, 256, E, rows, kk // 32, 16)
+            t[q + "_scales"] = u8(120, 127, E, rows, kk // 32)
+            t[q + "_bias"] = n(E, rows, std=0.01)
+        f = f"model-layer{l:02d}.safetensors"
+        save_file(t, str(d / f))
+        index.update({k: f for k in t})
+        del t
+    (d / "model.safetensors.index.json").write_text(json.dumps({"weight_map": index}))
+    cfg = {"num_hidden_layers": layers, "hidden_size": H, "intermediate_size": I, "vocab_size": DECODE_V,
+           "num_local_experts": E, "num_experts_per_tok": K_TOP, "sliding_window": 128, "num_attention_heads": 64,
+           "num_key_value_heads": 8, "head_dim": 64, "max_position_embeddings": 131072, "rms_norm_eps": 1e-5,
+           "swiglu_limit": 7.0, "rope_theta": 150000,
+           "layer_types": ["sliding_attention" if l % 2 == 0 else "full_attention" for l in range(layers)],
+           "rope_scaling": {"rope_type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                            "truncate": False, "original_max_position_embeddings": 4096}}
+    (d / "config.json").write_text(json.dumps(cfg))
+
+
+def run_decode_step(args, ctx, lib, context=4096, new_tokens=128, reps=3):
+    """bs=1 greedy decode of `new_tokens` tokens of the 20b-shaped random-init model through the engine
+    entry points (gptoss_create on the written checkpoint, gptoss_kv_fill_random for the 4096-position fp16 context,
+    gptoss_generate_greedy: argmax on the device, no host round trip per token). Timed through the API (host clock
+    around the synchronous call, which covers every kernel of every step), median of `reps` runs after a warm-up
+    that also captures the step graph."""
+    import shutil
+    import statistics
+    import tempfile
+    t0 = time.time()
+    d = Path(tempfile.mkdtemp(prefix="gptoss20b_", dir=os.environ.get("GPTOSS_BENCH_TMP", "/tmp")))
+    try:
+        write_20b_checkpoint(d, args.layers)
+        t_write = time.time() - t0
+        t1 = time.time()
+        e = lib.gptoss_create(str(d).encode(), context + new_tokens + 64, 0)
+        if not e:
+            raise RuntimeError(lib.gptoss_last_error().decode())
+        t_load = time.time() - t1
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    import ctypes
+    import numpy as np
+    try:
+        dev_bytes = lib.gptoss_device_bytes(e)
+        out = np.zeros(new_tokens, np.int32)
+
+        def run():
+            if lib.gptoss_kv_fill_random(e, context, 11) != 0:
+                raise RuntimeError(lib.gptoss_last_error().decode())
+            t = time.perf_counter()
+            if lib.gptoss_generate_greedy(e, 1, new_tokens, out.ctypes.data) != 0:
+                raise RuntimeError(lib.gptoss_last_error().decode())
+            return time.perf_counter() - t
+
+        run()                                               # warm-up: eager first step, graph capture
+        with ClockSampler(ctx.local) as clocks:
+            times = [run() for _ in range(reps)]
+        sec = statistics.median(times)
+        tok_s = new_tokens / sec
+        kv_bytes = 12 * (context + new_tokens // 2) * 2048 + 12 * 128 * 2048
+        pk = peaks()
+        hbm = pk.get("hbm_gbs") or 6650.0
+        achieved = (DECODE_BYTES_PER_TOKEN + kv_bytes) * tok_s / 1e9
+        return {
+            "metric": "bs=1 decode tok/s (20b-shaped, greedy, 4096-position fp16 KV context)",
+            "value": tok_s, "unit": "tok/s", "higher_is_better": True, "new_tokens": new_tokens, "reps": reps,
+            "ms_per_token": sec / new_tokens * 1e3, "run_seconds": times,
+            "config": {"workload": "configs[1]: 24 layers, hidden 2880, vocab 201088, 64/8 heads, window 128 on even "
+                                   "layers, MoE as configs[0]", "context": context, "kv": "fp16 N(0,1) (seeded)",
+                       "sampling": "greedy (argmax on the device)"},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (GEMVs, attention, fused MoE, LM head)",
+                         "algorithmic_bytes_per_token": DECODE_BYTES_PER_TOKEN + kv_bytes, "achieved": achieved,
+                         "unit": "GB/s", "peak": hbm, "frac": achieved / hbm,
+                         "frac_of_8TBs_nominal": achieved / 8000.0},
+            "api": "gptoss_create + gptoss_kv_fill_random + gptoss_generate_greedy (one CUDA graph per step)",
+            "setup_s": {"write_checkpoint": t_write, "gptoss_create": t_load}, "device_bytes": dev_bytes,
+            "first_tokens": out[:8].tolist(),
+            "clocks": clocks.summary(),
+        }
+    finally:
+        lib.gptoss_destroy(e)
+
+
 # ------------------------------------------------------------------------------------------------ reference GPU bar
 def run_ref_gpu(ctx, lib):
     """The reference's own CUDA kernels (openvang/gptoss-infer runtime/src/kernels.cu, built for sm_100a from its
@@ -920,6 +1037,8 @@ def main():
             line = run_ep(args, ctx, lib, args.tokens, first)
         elif args.workload == "prefill":
             line = run_prefill(args, ctx, lib, args.tokens, first)
+        elif args.workload == "decode":
+            line = run_decode_step(args, ctx, lib, new_tokens=args.decode_tokens, reps=args.decode_reps)
         else:
             line = run_decode(args, ctx, lib)
             if not args.no_extras:
@@ -927,6 +1046,7 @@ def main():
                 if ctx.ws == 1:
                     line["prefill"] = run_prefill(args, ctx, lib, 2048, False)
                     line["ref_gpu"] = run_ref_gpu(ctx, lib)
+                    line["decode"] = run_decode_step(args, ctx, lib)
         if ctx.rank == 0:
             print(json.dumps(line))
     finally:

@@ -58,7 +58,8 @@ def build(force=False, verbose=False):
                 print(log, file=sys.stderr)
     objs = [BUILD / (s.stem + ".o") for s in srcs]
     if force or jobs or not LIB.exists():
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda", "-lcublas",
+               "-Xlinker", "-rpath,/usr/local/cuda/lib64"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

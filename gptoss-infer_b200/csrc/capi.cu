@@ -704,6 +704,20 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
     });
 }
 
+int gptoss_selftest_mxf4_peak(double* tflops) {
+    return guard([&] {
+        if (!tflops) throw std::runtime_error("selftest_mxf4_peak: null output");
+        int* err = static_cast<int*>(g_flag.get(sizeof(int)));
+        GPT_CHECK(cudaMemset(err, 0, sizeof(int)));
+        const double t = gpt::selftest_mxf4_peak(err);
+        sync_check("selftest_mxf4_peak");
+        int h = 0;
+        GPT_CHECK(cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (h) throw std::runtime_error("selftest_mxf4_peak: a wait gave up");
+        *tflops = t;
+    });
+}
+
 int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, int which) {
     return guard([&] {
         const size_t bytes = size_t(n / 256 + 1) * gpt::kDecodeTerms * 128 + size_t(n / 128 + 1) * 512;

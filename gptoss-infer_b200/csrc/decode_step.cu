@@ -149,64 +149,53 @@ __global__ void __launch_bounds__(256) rope_append_kernel(float* qkv, const floa
 
 // ---------------------------------------------------------------------------------------------------- attention
 // Keys visible to the query at `pos`: positions first .. pos, n = min(pos + 1, window) with a window, pos + 1
-// without; position p lives in cache slot p % window (window) or p. Grid (8 key/value heads, kSplits): CTA (h, s)
-// takes positions [first + s L, first + (s + 1) L), L = ceil(n / kSplits), in chunks of kChunk keys staged in shared
-// memory (keys and values, fp16, 16-byte loads), and keeps a running softmax for its 8 query heads: m (max score),
-// l (sum of exp(score - m)) and acc[8][64] (sum of exp(score - m) v). Scores are q . k / 8 in fp32. The partials
-// (m, l, acc) go to `part`; attention_combine_kernel merges the splits with the head's sink logit (one more
-// softmax column that carries no value) and writes out = acc / l.
+// without; position p lives in cache slot p % window (window) or p. A CTA owns one key/value head (8 query heads,
+// GQA) and a contiguous range [k0, k1) of the visible keys (split-K over kSplits ranges), walks it in chunks of
+// kChunk keys staged in shared memory (keys and values, fp16, 16-byte loads) and keeps a running softmax per query
+// head: m (max score), l (sum of exp(score - m)) and acc[64] (sum of exp(score - m) v). Scores are q . k / 8 in
+// fp32. The partials (m, l, acc) of all ranges are merged with the head's sink logit (one more softmax column that
+// carries no value): M = max(sink, m_s), l = exp(sink - M) + sum l_s exp(m_s - M), out = sum acc_s exp(m_s - M) / l.
 constexpr int kSplits = 18, kChunk = 128, kAttnThreads = 256;
 constexpr int kKvRow = kHeadDim * 2 + 16;                       // staged key/value row: 128 bytes + 16 of padding
 
-__global__ void __launch_bounds__(kAttnThreads) attention_partial_kernel(const float* __restrict__ q,
-                                                                         const __half* __restrict__ kc,
-                                                                         const __half* __restrict__ vc,
-                                                                         const int* d_pos, int pos_arg, int window,
-                                                                         float* __restrict__ part) {
-    __shared__ __align__(16) uint8_t ks[kChunk * kKvRow];
-    __shared__ __align__(16) uint8_t vs[kChunk * kKvRow];
-    __shared__ float qs[kGroup][kHeadDim];
-    __shared__ float ps[kGroup][kChunk];                        // exp(score - m_new) of the chunk
-    __shared__ float cm[kGroup], cl[kGroup], scale_old[kGroup];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.x, sp = blockIdx.y;
-    pdl_wait();
-    pdl_launch_dependents();
-    const int pos = d_pos ? *d_pos : pos_arg;
-    const int n = window > 0 ? min(pos + 1, window) : pos + 1;
-    const int first = pos + 1 - n;
-    const int L = (n + kSplits - 1) / kSplits;
-    const int k0 = min(n, sp * L), k1 = min(n, k0 + L);
-    for (int i = tid; i < kGroup * kHeadDim; i += kAttnThreads) qs[i / kHeadDim][i % kHeadDim] = q[h * kGroup * kHeadDim + i];
+struct AttnShared {
+    __align__(16) uint8_t ks[kChunk * kKvRow];
+    __align__(16) uint8_t vs[kChunk * kKvRow];
+    float qs[kGroup][kHeadDim];                                 // the 8 query heads (rotated)
+    float ps[kGroup][kChunk];                                   // scores, then exp(score - m_new) of the chunk
+    float cm[kGroup], cl[kGroup], scale_old[kGroup];
+};
+
+// Running softmax over visible keys [k0, k1) for the 8 query heads in sh.qs (all kAttnThreads threads call; sh.qs
+// written and visible). load_kv(kk, part16, kw, vw) returns the 16-byte pieces part16 of the key and value at
+// visible index kk. Thread (query head = warp, lane) ends with acc = dims 2 lane, 2 lane + 1 of that head.
+template <class LoadKV>
+__device__ __forceinline__ float2 attend_keys(AttnShared& sh, int k0, int k1, LoadKV&& load_kv) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, qh = warp;
     if (tid < kGroup) {
-        cm[tid] = -INFINITY;
-        cl[tid] = 0.f;
+        sh.cm[tid] = -INFINITY;
+        sh.cl[tid] = 0.f;
     }
-    // thread (qh = tid / 32, d pair = lane) owns acc[qh][2 lane .. 2 lane + 1]
-    const int qh = warp;
     float2 acc = make_float2(0.f, 0.f);
     __syncthreads();
     for (int c0 = k0; c0 < k1; c0 += kChunk) {
         const int len = min(kChunk, k1 - c0);
-        // stage the chunk's keys and values: 8 threads per 128-byte row
-        for (int i = tid; i < len * 8; i += kAttnThreads) {
+        for (int i = tid; i < len * 8; i += kAttnThreads) {       // 8 threads per 128-byte row
             const int kk = i >> 3, part16 = i & 7;
-            const int p = first + c0 + kk;
-            const size_t slot = window > 0 ? size_t(p % window) : size_t(p);
-            const size_t off = (slot * kKvHeads + h) * kHeadDim * 2 + part16 * 16;
-            *reinterpret_cast<uint4*>(ks + kk * kKvRow + part16 * 16) =
-                ldg_stream(reinterpret_cast<const uint8_t*>(kc) + off);
-            *reinterpret_cast<uint4*>(vs + kk * kKvRow + part16 * 16) =
-                ldg_stream(reinterpret_cast<const uint8_t*>(vc) + off);
+            uint4 kw, vw;
+            load_kv(c0 + kk, part16, kw, vw);
+            *reinterpret_cast<uint4*>(sh.ks + kk * kKvRow + part16 * 16) = kw;
+            *reinterpret_cast<uint4*>(sh.vs + kk * kKvRow + part16 * 16) = vw;
         }
         __syncthreads();
         // scores: an 8-lane group per key (each lane 8 dims), 4 keys per warp pass; the group's partial dots for the
-        // 8 query heads are reduced so that lane j of the group ends with head j's score
+        // 8 query heads are reduced so that lane j of the group ends with head j's dot (bit 2 of the lane picks heads
+        // 4-7, bit 1 the upper pair, bit 0 the upper head)
         for (int kb = warp * 4; kb < len; kb += (kAttnThreads / 32) * 4) {
             const int kk = kb + (lane >> 3), sub = lane & 7;
             float d[kGroup];
             if (kk < len) {
-                const uint4 u = *reinterpret_cast<const uint4*>(ks + kk * kKvRow + sub * 16);
+                const uint4 u = *reinterpret_cast<const uint4*>(sh.ks + kk * kKvRow + sub * 16);
                 const uint32_t w[4] = {u.x, u.y, u.z, u.w};
                 float kv[8];
 #pragma unroll
@@ -219,115 +208,363 @@ __global__ void __launch_bounds__(kAttnThreads) attention_partial_kernel(const f
                 for (int g = 0; g < kGroup; ++g) {
                     float t = 0.f;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) t = fmaf(qs[g][sub * 8 + e], kv[e], t);
+                    for (int e = 0; e < 8; ++e) t = fmaf(sh.qs[g][sub * 8 + e], kv[e], t);
                     d[g] = t;
                 }
             } else {
 #pragma unroll
                 for (int g = 0; g < kGroup; ++g) d[g] = 0.f;
             }
-            // reduce-scatter over the 8 lanes: after the three steps lane `sub` holds the full dot of head `sub`
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
                 const bool up = sub & 4;
-                const float send = up ? d[g] : d[g + 4];
-                const float recv = __shfl_xor_sync(kFull, send, 4);
+                const float recv = __shfl_xor_sync(kFull, up ? d[g] : d[g + 4], 4);
                 d[g] = (up ? d[g + 4] : d[g]) + recv;
             }
 #pragma unroll
             for (int g = 0; g < 2; ++g) {
                 const bool up = sub & 2;
-                const float send = up ? d[g] : d[g + 2];
-                const float recv = __shfl_xor_sync(kFull, send, 2);
+                const float recv = __shfl_xor_sync(kFull, up ? d[g] : d[g + 2], 2);
                 d[g] = (up ? d[g + 2] : d[g]) + recv;
             }
             {
                 const bool up = sub & 1;
-                const float send = up ? d[0] : d[1];
-                const float recv = __shfl_xor_sync(kFull, send, 1);
+                const float recv = __shfl_xor_sync(kFull, up ? d[0] : d[1], 1);
                 d[0] = (up ? d[1] : d[0]) + recv;
             }
-            // lane sub now holds the full dot of query head sub (bit 2 picked heads 4-7, bit 1 the upper pair, bit 0
-            // the upper head); the score is the dot scaled by 1 / sqrt(64)
-            if (kk < len) ps[sub][kk] = d[0] * 0.125f;
+            if (kk < len) sh.ps[sub][kk] = d[0] * 0.125f;          // scale 1 / sqrt(64)
         }
         __syncthreads();
         // per query head (warp qh): chunk max, new running max, exp, chunk sum
         {
             float m = -INFINITY;
-            for (int kk = lane; kk < len; kk += 32) m = fmaxf(m, ps[qh][kk]);
+            for (int kk = lane; kk < len; kk += 32) m = fmaxf(m, sh.ps[qh][kk]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
-            const float m_old = cm[qh], m_new = fmaxf(m_old, m);
-            float s = 0.f;
+            const float m_old = sh.cm[qh], m_new = fmaxf(m_old, m);
+            float ssum = 0.f;
             for (int kk = lane; kk < len; kk += 32) {
-                const float e = expf(ps[qh][kk] - m_new);
-                ps[qh][kk] = e;
-                s += e;
+                const float e = expf(sh.ps[qh][kk] - m_new);
+                sh.ps[qh][kk] = e;
+                ssum += e;
             }
-            s = warp_sum(s);
+            ssum = warp_sum(ssum);
             __syncwarp();
             if (lane == 0) {
                 const float a = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-                scale_old[qh] = a;
-                cl[qh] = cl[qh] * a + s;
-                cm[qh] = m_new;
+                sh.scale_old[qh] = a;
+                sh.cl[qh] = sh.cl[qh] * a + ssum;
+                sh.cm[qh] = m_new;
             }
         }
         __syncwarp();
-        // acc = acc * exp(m_old - m_new) + sum_k p v (thread: head qh, dims 2 lane .. 2 lane + 1)
+        // acc = acc exp(m_old - m_new) + sum_k p v
         {
-            const float a = scale_old[qh];
+            const float a = sh.scale_old[qh];
             acc.x *= a;
             acc.y *= a;
             for (int kk = 0; kk < len; ++kk) {
-                const float p = ps[qh][kk];
-                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(vs + kk * kKvRow + lane * 4));
+                const float p = sh.ps[qh][kk];
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(sh.vs + kk * kKvRow + lane * 4));
                 acc.x = fmaf(p, v.x, acc.x);
                 acc.y = fmaf(p, v.y, acc.y);
             }
         }
         __syncthreads();                                        // the chunk buffers are refilled next
     }
-    const size_t base = (size_t(h) * kSplits + sp) * kGroup;
-    float* pm = part;
-    float* pl = part + kKvHeads * kSplits * kGroup;
-    float* pa = part + 2 * kKvHeads * kSplits * kGroup;
-    if (lane == 0) {
-        pm[base + qh] = cm[qh];
-        pl[base + qh] = cl[qh];
-    }
-    *reinterpret_cast<float2*>(pa + (base + qh) * kHeadDim + 2 * lane) = acc;
+    return acc;
 }
 
-// One CTA per key/value head, one warp per query head: merges the kSplits partials with the sink column.
-__global__ void __launch_bounds__(kAttnThreads) attention_combine_kernel(const float* __restrict__ part,
-                                                                         const float* __restrict__ sinks,
-                                                                         float* __restrict__ out) {
-    const int h = blockIdx.x, qh = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
-    pdl_launch_dependents();
-    const int head = h * kGroup + qh;
-    const float* pm = part;
-    const float* pl = part + kKvHeads * kSplits * kGroup;
-    const float* pa = part + 2 * kKvHeads * kSplits * kGroup;
+// Partials of `kSplits` ranges for (query row r, kv head h): m, l at [(r * 8 + h) * kSplits + s][8], acc after them.
+struct AttnPartials {
+    float* base;
+    size_t rows;                                                 // query rows the buffer holds
+    __device__ __forceinline__ size_t idx(int r, int h, int s) const {
+        return ((size_t(r) * kKvHeads + h) * kSplits + s) * kGroup;
+    }
+    __device__ __forceinline__ float* m() const { return base; }
+    __device__ __forceinline__ float* l() const { return base + rows * kKvHeads * kSplits * kGroup; }
+    __device__ __forceinline__ float* acc() const { return base + 2 * rows * kKvHeads * kSplits * kGroup; }
+};
+
+__device__ __forceinline__ void store_partials(const AttnShared& sh, const AttnPartials& P, int r, int h, int s,
+                                               float2 acc) {
+    const int qh = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t b = P.idx(r, h, s) + qh;
+    if (lane == 0) {
+        P.m()[b] = sh.cm[qh];
+        P.l()[b] = sh.cl[qh];
+    }
+    *reinterpret_cast<float2*>(P.acc() + b * kHeadDim + 2 * lane) = acc;
+}
+
+// Warp qh of the calling CTA merges row r / head h's partials with the sink into out (the 64 query heads' rows).
+__device__ __forceinline__ void merge_partials(const AttnPartials& P, int r, int h, const float* sinks, float* out) {
+    const int qh = threadIdx.x >> 5, lane = threadIdx.x & 31, head = h * kGroup + qh;
     const float sink = sinks[head];
     float M = sink;
-    for (int s = 0; s < kSplits; ++s) M = fmaxf(M, pm[(size_t(h) * kSplits + s) * kGroup + qh]);
+    for (int s = 0; s < kSplits; ++s) M = fmaxf(M, __ldcg(P.m() + P.idx(r, h, s) + qh));
     float l = expf(sink - M);
     float2 o = make_float2(0.f, 0.f);
     for (int s = 0; s < kSplits; ++s) {
-        const size_t b = (size_t(h) * kSplits + s) * kGroup + qh;
-        const float m = pm[b];
-        if (m == -INFINITY) continue;                           // a split with no keys
+        const size_t b = P.idx(r, h, s) + qh;
+        const float m = __ldcg(P.m() + b);
+        if (m == -INFINITY) continue;                           // a range with no keys
         const float a = expf(m - M);
-        l = fmaf(pl[b], a, l);
-        const float2 v = *reinterpret_cast<const float2*>(pa + b * kHeadDim + 2 * lane);
+        l = fmaf(__ldcg(P.l() + b), a, l);
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(P.acc() + b * kHeadDim + 2 * lane));
         o.x = fmaf(v.x, a, o.x);
         o.y = fmaf(v.y, a, o.y);
     }
     const float inv = 1.f / l;
     *reinterpret_cast<float2*>(out + size_t(head) * kHeadDim + 2 * lane) = make_float2(o.x * inv, o.y * inv);
+}
+
+__device__ __forceinline__ void visible_range(int pos, int window, int sp, int& first, int& n, int& k0, int& k1) {
+    n = window > 0 ? min(pos + 1, window) : pos + 1;
+    first = pos + 1 - n;
+    const int L = (n + kSplits - 1) / kSplits;
+    k0 = min(n, sp * L);
+    k1 = min(n, k0 + L);
+}
+
+__device__ __forceinline__ void load_cache_kv(const __half* kc, const __half* vc, int h, int p, int window, int part16,
+                                              uint4& kw, uint4& vw) {
+    const size_t slot = window > 0 ? size_t(p % window) : size_t(p);
+    const size_t off = (slot * kKvHeads + h) * kHeadDim * 2 + part16 * 16;
+    kw = ldg_stream(reinterpret_cast<const uint8_t*>(kc) + off);
+    vw = ldg_stream(reinterpret_cast<const uint8_t*>(vc) + off);
+}
+
+// The ABI's attention for one query whose key and value are already in the cache: grid (8 kv heads, kSplits).
+__global__ void __launch_bounds__(kAttnThreads) attention_partial_kernel(const float* __restrict__ q,
+                                                                         const __half* __restrict__ kc,
+                                                                         const __half* __restrict__ vc,
+                                                                         const int* d_pos, int pos_arg, int window,
+                                                                         float* __restrict__ part) {
+    __shared__ AttnShared sh;
+    const int h = blockIdx.x, sp = blockIdx.y, tid = threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int pos = d_pos ? *d_pos : pos_arg;
+    int first, n, k0, k1;
+    visible_range(pos, window, sp, first, n, k0, k1);
+    for (int i = tid; i < kGroup * kHeadDim; i += kAttnThreads) sh.qs[i / kHeadDim][i % kHeadDim] = q[h * kGroup * kHeadDim + i];
+    const float2 acc = attend_keys(sh, k0, k1, [&](int kk, int part16, uint4& kw, uint4& vw) {
+        load_cache_kv(kc, vc, h, first + kk, window, part16, kw, vw);
+    });
+    store_partials(sh, AttnPartials{part, 1}, 0, h, sp, acc);
+}
+
+// One CTA per key/value head, one warp per query head: merges the partials with the sinks.
+__global__ void __launch_bounds__(kAttnThreads) attention_combine_kernel(const float* __restrict__ part,
+                                                                         const float* __restrict__ sinks,
+                                                                         float* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    merge_partials(AttnPartials{const_cast<float*>(part), 1}, 0, blockIdx.x, sinks, out);
+}
+
+// RoPE pair i of a head row x (in registers of the caller): (x1, x2) -> (x1 c - x2 s, x2 c + x1 s), rounded per op.
+__device__ __forceinline__ float2 rotate_pair(float x1, float x2, float c, float s) {
+    return make_float2(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)), __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+}
+
+// The attention of one decode step in one launch (the engine's path): CTA (h, s) rotates its 8 query heads from the
+// raw QKV output itself; the CTA whose key range holds the new position also rotates that position's key, rounds key
+// and value to fp16, stores them into the cache and uses those values for the position (the cache is read through
+// the non-coherent path, which need not see this kernel's own stores). The last CTA of each key/value head to finish
+// (a per-head counter, reset by that CTA) merges the head's partials with the sinks.
+__global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const float* __restrict__ qkv,
+                                                                      const float* __restrict__ cos_t,
+                                                                      const float* __restrict__ sin_t,
+                                                                      __half* kc, __half* vc,
+                                                                      const float* __restrict__ sinks,
+                                                                      const int* d_pos, int window,
+                                                                      float* part, unsigned* counters, float* out) {
+    __shared__ AttnShared sh;
+    __shared__ __align__(16) __half newk[kHeadDim], newv[kHeadDim];
+    __shared__ bool last;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int h = blockIdx.x, sp = blockIdx.y;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int pos = *d_pos;
+    int first, n, k0, k1;
+    visible_range(pos, window, sp, first, n, k0, k1);
+    const bool holds_new = k0 <= n - 1 && n - 1 < k1;
+    {
+        const int j = tid >> 5, i = lane;                        // query head h*8 + j, rotary pair i
+        const float c = cos_t[size_t(pos) * kPairs + i], sn = sin_t[size_t(pos) * kPairs + i];
+        const float* base = qkv + (h * kGroup + j) * kHeadDim;
+        const float2 r = rotate_pair(base[i], base[i + kPairs], c, sn);
+        sh.qs[j][i] = r.x;
+        sh.qs[j][i + kPairs] = r.y;
+        if (holds_new && j == 0) {
+            const float* kb = qkv + (kHeads + h) * kHeadDim;
+            const float2 rk = rotate_pair(kb[i], kb[i + kPairs], c, sn);
+            newk[i] = __float2half_rn(rk.x);
+            newk[i + kPairs] = __float2half_rn(rk.y);
+        } else if (holds_new && j == 1) {
+            const float* vb = qkv + (kHeads + kKvHeads + h) * kHeadDim;
+            newv[i] = __float2half_rn(vb[i]);
+            newv[i + kPairs] = __float2half_rn(vb[i + kPairs]);
+        }
+    }
+    __syncthreads();
+    if (holds_new && tid < 16) {                                // the new position's key and value into the cache
+        const size_t slot = window > 0 ? size_t(pos % window) : size_t(pos);
+        const size_t off = (slot * kKvHeads + h) * kHeadDim * 2;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(tid < 8 ? newk : newv) + (tid & 7) * 16;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(tid < 8 ? kc : vc) + off + (tid & 7) * 16;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+    const float2 acc = attend_keys(sh, k0, k1, [&](int kk, int part16, uint4& kw, uint4& vw) {
+        if (kk == n - 1) {
+            kw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(newk) + part16 * 16);
+            vw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(newv) + part16 * 16);
+        } else {
+            load_cache_kv(kc, vc, h, first + kk, window, part16, kw, vw);
+        }
+    });
+    const AttnPartials P{part, 1};
+    store_partials(sh, P, 0, h, sp, acc);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(counters + h, 1u) == unsigned(kSplits - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    merge_partials(P, 0, h, sinks, out);
+    if (tid == 0) counters[h] = 0;
+}
+
+// ---------------------------------------------------------------------------------------------------- prefill
+// Attention of a batch of n consecutive positions p0 .. p0 + n - 1 of one sequence (prefill), grid (8 kv heads,
+// kSplits, rows of this chunk). Query row r (position p0 + r0 + r) was rotated in place in qkv; the batch's own keys
+// and values (rotated, rounded to fp16) are in kvb [n][2][8][64] and are read from there, older positions from the
+// cache (a sliding-window cache may already have been overwritten by the batch's later positions, so the batch is
+// appended to the cache only after its attention).
+__global__ void __launch_bounds__(kAttnThreads) attention_prefill_kernel(const float* __restrict__ qkv, int r0,
+                                                                         const __half* __restrict__ kvb,
+                                                                         const __half* __restrict__ kc,
+                                                                         const __half* __restrict__ vc, int p0,
+                                                                         int window, float* __restrict__ part,
+                                                                         size_t part_rows) {
+    __shared__ AttnShared sh;
+    const int h = blockIdx.x, sp = blockIdx.y, r = blockIdx.z, tid = threadIdx.x;
+    const int row = r0 + r, pos = p0 + row;
+    int first, n, k0, k1;
+    visible_range(pos, window, sp, first, n, k0, k1);
+    for (int i = tid; i < kGroup * kHeadDim; i += kAttnThreads)
+        sh.qs[i / kHeadDim][i % kHeadDim] = qkv[size_t(row) * kQkv + h * kGroup * kHeadDim + i];
+    const float2 acc = attend_keys(sh, k0, k1, [&](int kk, int part16, uint4& kw, uint4& vw) {
+        const int p = first + kk;
+        if (p >= p0) {
+            const uint8_t* b = reinterpret_cast<const uint8_t*>(kvb) + (size_t(p - p0) * 2 * kKvHeads + h) * kHeadDim * 2;
+            kw = *reinterpret_cast<const uint4*>(b + part16 * 16);
+            vw = *reinterpret_cast<const uint4*>(b + kKvHeads * kHeadDim * 2 + part16 * 16);
+        } else {
+            load_cache_kv(kc, vc, h, p, window, part16, kw, vw);
+        }
+    });
+    store_partials(sh, AttnPartials{part, part_rows}, r, h, sp, acc);
+}
+
+// grid (8 kv heads, rows of the chunk): merges each row's partials into out[r0 + r][4096].
+__global__ void __launch_bounds__(kAttnThreads) attention_prefill_merge_kernel(const float* part, size_t part_rows,
+                                                                               int r0, const float* __restrict__ sinks,
+                                                                               float* out) {
+    const int r = blockIdx.y;
+    merge_partials(AttnPartials{const_cast<float*>(part), part_rows}, r, blockIdx.x, sinks,
+                   out + size_t(r0 + r) * kHeads * kHeadDim);
+}
+
+// Per batch row t (position p0 + t): qkv += bias; q and k rotated in place; the rotated k and the v rounded to fp16
+// into kvb[t] ([2][8][64]). One CTA per row, one thread per rotary pair (72 heads x 32 pairs) and per v pair.
+__global__ void __launch_bounds__(256) prefill_qkv_rope_kernel(float* qkv, const float* __restrict__ bias,
+                                                               const float* __restrict__ cos_t,
+                                                               const float* __restrict__ sin_t, int p0, __half* kvb) {
+    const int t = blockIdx.x, pos = p0 + t;
+    float* row = qkv + size_t(t) * kQkv;
+    __half* kv = kvb + size_t(t) * 2 * kKvHeads * kHeadDim;
+    for (int p = threadIdx.x; p < (kHeads + kKvHeads) * kPairs; p += blockDim.x) {
+        const int head = p / kPairs, i = p % kPairs;
+        float* base = row + head * kHeadDim;
+        const float x1 = base[i] + bias[head * kHeadDim + i], x2 = base[i + kPairs] + bias[head * kHeadDim + i + kPairs];
+        const float2 r = rotate_pair(x1, x2, cos_t[size_t(pos) * kPairs + i], sin_t[size_t(pos) * kPairs + i]);
+        base[i] = r.x;
+        base[i + kPairs] = r.y;
+        if (head >= kHeads) {
+            const int kh = head - kHeads;
+            kv[kh * kHeadDim + i] = __float2half_rn(r.x);
+            kv[kh * kHeadDim + i + kPairs] = __float2half_rn(r.y);
+        }
+    }
+    for (int i = threadIdx.x; i < kKvHeads * kHeadDim; i += blockDim.x) {
+        const int c = (kHeads + kKvHeads) * kHeadDim + i;
+        const float v = row[c] + bias[c];
+        row[c] = v;
+        kv[kKvHeads * kHeadDim + i] = __float2half_rn(v);
+    }
+}
+
+// Appends batch rows [t0, n) of kvb to the cache (positions p0 + t; slot p % window or p). One thread per 16 bytes.
+__global__ void prefill_append_kernel(const __half* __restrict__ kvb, int t0, int n, int p0, int window, __half* kc,
+                                      __half* vc) {
+    const size_t per_row = 2 * kKvHeads * kHeadDim * 2 / 16;    // 16-byte pieces per row (k then v)
+    const size_t total = size_t(n - t0) * per_row;
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int t = t0 + int(i / per_row), piece = int(i % per_row);
+        const int p = p0 + t;
+        const size_t slot = window > 0 ? size_t(p % window) : size_t(p);
+        const bool is_v = piece >= int(per_row / 2);
+        const int pp = is_v ? piece - int(per_row / 2) : piece;
+        const uint4 w = reinterpret_cast<const uint4*>(kvb + size_t(t) * 2 * kKvHeads * kHeadDim)[piece];
+        reinterpret_cast<uint4*>((is_v ? vc : kc) + slot * kKvHeads * kHeadDim)[pp] = w;
+    }
+}
+
+// Row-wise split for the tensor-core projections: y = RMSNorm(x; g) (g null: y = x), hi = bf16(y), lo = bf16(y -
+// hi), so hi + lo carries 16 significant bits of y. One CTA per row.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ x, int K, const float* __restrict__ g,
+                                                         float eps, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    __shared__ float part[8];
+    const float* xr = x + size_t(blockIdx.x) * K;
+    float r = 1.f;
+    if (g) {
+        float ss = 0.f;
+        for (int i = threadIdx.x * 4; i < K; i += 1024) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            ss = fmaf(v.w, v.w, fmaf(v.z, v.z, fmaf(v.y, v.y, fmaf(v.x, v.x, ss))));
+        }
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += part[w];
+        r = rms_scale(tot, K, eps);
+    }
+    for (int i = threadIdx.x; i < K; i += 256) {
+        const float y = g ? xr[i] * r * g[i] : xr[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(y);
+        hi[size_t(blockIdx.x) * K + i] = h;
+        lo[size_t(blockIdx.x) * K + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+    }
+}
+
+// x[t][i] += b[i] for n rows.
+__global__ void add_bias_rows_kernel(float* x, const float* __restrict__ b, int n, int K) {
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < size_t(n) * K; i += size_t(gridDim.x) * blockDim.x)
+        x[i] += b[i % K];
+}
+
+// x[t] = embed[tokens[t]] for n tokens.
+__global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ tokens, float* x,
+                                  int H) {
+    const size_t t = size_t(tokens[blockIdx.x]);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) x[size_t(blockIdx.x) * H + i] = __bfloat162float(table[t * H + i]);
 }
 
 // ---------------------------------------------------------------------------------------------------- misc
@@ -481,7 +718,20 @@ void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, cons
                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), window);
 }
 
-size_t attention_workspace_floats() { return size_t(ds::kKvHeads) * ds::kSplits * ds::kGroup * (2 + ds::kHeadDim); }
+// partials (m, l, acc) of every (head, split), then 8 per-head counters (zero-filled before the first use)
+size_t attention_workspace_floats() {
+    return size_t(ds::kKvHeads) * ds::kSplits * ds::kGroup * (2 + ds::kHeadDim) + 16;
+}
+
+void launch_attention_step(const float* qkv, const float* cos_t, const float* sin_t, void* k_cache, void* v_cache,
+                           const float* sinks, const int* d_pos, int window, float* part, float* out, cudaStream_t s,
+                           bool pdl) {
+    require(window >= 0, "attention: window must be >= 0");
+    unsigned* counters = reinterpret_cast<unsigned*>(part + (attention_workspace_floats() - 16));
+    ds::launch(ds::attention_step_kernel, dim3(ds::kKvHeads, ds::kSplits), dim3(ds::kAttnThreads), 0, s, pdl, qkv,
+               cos_t, sin_t, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), sinks, d_pos, window, part,
+               counters, out);
+}
 
 void launch_attention(const float* q, const void* k_cache, const void* v_cache, const float* sinks, const int* d_pos,
                       int pos, int window, float* part, float* out, cudaStream_t s, bool pdl) {
@@ -490,6 +740,60 @@ void launch_attention(const float* q, const void* k_cache, const void* v_cache, 
                static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), d_pos, pos, window, part);
     ds::launch(ds::attention_combine_kernel, dim3(ds::kKvHeads), dim3(ds::kAttnThreads), 0, s, pdl,
                static_cast<const float*>(part), sinks, out);
+}
+
+size_t prefill_attention_floats(int rows) {
+    return size_t(rows) * ds::kKvHeads * ds::kSplits * ds::kGroup * (2 + ds::kHeadDim);
+}
+
+void launch_prefill_qkv_rope(float* qkv, const float* bias, const float* cos_t, const float* sin_t, int p0, int n,
+                             void* kvb, cudaStream_t s) {
+    ds::prefill_qkv_rope_kernel<<<n, 256, 0, s>>>(qkv, bias, cos_t, sin_t, p0, static_cast<__half*>(kvb));
+    check_launch("prefill qkv rope");
+}
+
+void launch_prefill_attention(const float* qkv, const void* kvb, const void* k_cache, const void* v_cache,
+                              const float* sinks, int p0, int n, int window, float* part, int part_rows, float* out,
+                              cudaStream_t s) {
+    for (int r0 = 0; r0 < n; r0 += part_rows) {
+        const int rows = std::min(part_rows, n - r0);
+        ds::attention_prefill_kernel<<<dim3(ds::kKvHeads, ds::kSplits, rows), ds::kAttnThreads, 0, s>>>(
+            qkv, r0, static_cast<const __half*>(kvb), static_cast<const __half*>(k_cache),
+            static_cast<const __half*>(v_cache), p0, window, part, size_t(part_rows));
+        check_launch("prefill attention");
+        ds::attention_prefill_merge_kernel<<<dim3(ds::kKvHeads, rows), ds::kAttnThreads, 0, s>>>(
+            part, size_t(part_rows), r0, sinks, out);
+        check_launch("prefill attention merge");
+    }
+}
+
+void launch_prefill_append(const void* kvb, int p0, int n, int window, void* k_cache, void* v_cache, cudaStream_t s) {
+    const int t0 = window > 0 ? std::max(0, n - window) : 0;  // a window cache keeps only the last `window`
+    if (t0 >= n) return;
+    const size_t pieces = size_t(n - t0) * 2 * ds::kKvHeads * ds::kHeadDim * 2 / 16;
+    const int grid = int(std::min<size_t>((pieces + 255) / 256, size_t(num_sms()) * 8));
+    ds::prefill_append_kernel<<<std::max(1, grid), 256, 0, s>>>(static_cast<const __half*>(kvb), t0, n, p0, window,
+                                                               static_cast<__half*>(k_cache), static_cast<__half*>(v_cache));
+    check_launch("prefill append");
+}
+
+void launch_split_rows(const float* x, int n, int K, const float* norm_w, float eps, void* hi, void* lo, cudaStream_t s) {
+    require(K % 4 == 0, "split_rows: K must be a multiple of 4");
+    ds::split_rows_kernel<<<n, 256, 0, s>>>(x, K, norm_w, eps, static_cast<__nv_bfloat16*>(hi),
+                                            static_cast<__nv_bfloat16*>(lo));
+    check_launch("split rows");
+}
+
+void launch_add_bias_rows(float* x, const float* b, int n, int K, cudaStream_t s) {
+    const size_t total = size_t(n) * K;
+    const int grid = int(std::min<size_t>((total + 255) / 256, size_t(num_sms()) * 8));
+    ds::add_bias_rows_kernel<<<std::max(1, grid), 256, 0, s>>>(x, b, n, K);
+    check_launch("add bias rows");
+}
+
+void launch_embed_rows(const void* table, const int* tokens, float* x, int n, int H, cudaStream_t s) {
+    ds::embed_rows_kernel<<<n, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(table), tokens, x, H);
+    check_launch("embed rows");
 }
 
 void launch_embed(const void* table, const int* d_token, float* x, int H, cudaStream_t s, bool pdl) {

@@ -3,8 +3,8 @@
 // Per step (token in device memory, position in device memory, so one captured graph serves every step):
 //   x = embed[token]
 //   per layer: qkv = Wqkv RMSNorm(x; ln1) + bqkv            (GEMV with the norm fused in front)
-//              RoPE on q and k, k and v appended to the fp16 cache
-//              attn = attention(q, cache, sinks, window)      (split-K partials + combine)
+//              attn = attention(RoPE(q), cache + RoPE(k), v)   (one launch: RoPE, fp16 cache append, split-K
+//                                                              partials, merge with the sinks by the last CTA)
 //              x += Wo attn + bo                               (GEMV with the residual fused)
 //              x += MoE(RMSNorm(x; ln2))                       (the fused tensor-core decode MoE kernel)
 //   logits = lm_head RMSNorm(x; norm); position += 1
@@ -347,6 +347,7 @@ Engine::Engine(const std::string& dir, int max_ctx, long long vram_budget) : cfg
         qkv_ = static_cast<float*>(alloc(size_t(QD + 2 * KVD) * 4));
         attn_ = static_cast<float*>(alloc(size_t(QD) * 4));
         part_ = static_cast<float*>(alloc(attention_workspace_floats() * 4));
+        GPT_CHECK(cudaMemset(part_, 0, attention_workspace_floats() * 4));
         logits_ = static_cast<float*>(alloc(size_t(V) * 4));
         score_work_ = alloc(score_workspace_bytes());
         GPT_CHECK(cudaMemset(score_work_, 0, score_workspace_bytes()));
@@ -371,6 +372,7 @@ Engine::Engine(const std::string& dir, int max_ctx, long long vram_budget) : cfg
 
 Engine::~Engine() {
     if (graph_) cudaGraphExecDestroy(graph_);
+    if (cublas_) cublasDestroy(cublas_);
     for (Layer& L : layers_)
         if (L.moe) gptoss_moe_layer_destroy(L.moe);
     for (void* p : allocs_) cudaFree(p);
@@ -390,8 +392,7 @@ void Engine::forward(cudaStream_t s, bool pdl) {
     launch_embed(embed_, token_, x_, H, s, pdl);
     for (const Layer& L : layers_) {
         launch_gemv_bf16(L.wqkv, x_, L.ln1, cfg_.eps, L.bqkv, nullptr, qkv_, QD + 2 * KVD, H, s, pdl);
-        launch_rope_append(qkv_, cos_, sin_, pos_d_, 0, L.kc, L.vc, L.window, s, pdl);
-        launch_attention(qkv_, L.kc, L.vc, L.sinks, pos_d_, 0, L.window, part_, attn_, s, pdl);
+        launch_attention_step(qkv_, cos_, sin_, L.kc, L.vc, L.sinks, pos_d_, L.window, part_, attn_, s, pdl);
         launch_gemv_bf16(L.wo, attn_, nullptr, 0.f, L.bo, x_, x_, H, QD, s, pdl);
         moe_layer_forward_ws(L.moe, x_, x_, s, nullptr, moe_ws_);
     }
@@ -472,7 +473,8 @@ void Engine::score(const int* ids, int k, int target, float* lp, int* argmax, fl
     if (lse) *lse = tail[1];
 }
 
-void Engine::prefill(const int* tokens, int n, const int* ids, int k, float* lp, int* argmax, float* target_lp) {
+void Engine::prefill_stepwise(const int* tokens, int n, const int* ids, int k, float* lp, int* argmax,
+                              float* target_lp) {
     if (n <= 0) throw std::runtime_error("prefill: n must be positive");
     if (pos_ + n > max_ctx_) throw std::runtime_error("context is full");
     for (int p = 0; p < n; ++p) {
@@ -481,6 +483,117 @@ void Engine::prefill(const int* tokens, int n, const int* ids, int k, float* lp,
             score(ids + size_t(p) * k, k, tokens[p + 1], lp + size_t(p) * k, argmax + p, target_lp + p, nullptr);
     }
     GPT_CHECK(cudaStreamSynchronize(stream_));
+}
+
+void* Engine::scratch(size_t i, size_t bytes) {
+    if (pre_.size() <= i) pre_.resize(i + 1, {nullptr, 0});
+    auto& b = pre_[i];
+    if (b.second < bytes) {
+        if (b.first) {
+            GPT_CHECK(cudaFree(b.first));
+            bytes_ -= (long long)b.second;
+            allocs_.erase(std::find(allocs_.begin(), allocs_.end(), b.first));
+            b = {nullptr, 0};
+        }
+        b.first = alloc(bytes);
+        b.second = bytes;
+    }
+    return b.first;
+}
+
+// out[rows][n_out] (= or +=) x W^T for x = hi + lo (bf16 rows, K wide) and W bf16 [n_out][K]: two cuBLAS bf16 GEMMs
+// with fp32 accumulation, so the activations keep 16 significant bits while the weights stay as stored.
+void Engine::project(const void* W, int n_out, int K, const void* hi, const void* lo, int rows, float* out,
+                     bool accumulate) {
+    const float one = 1.f, zero = 0.f;
+    for (int pass = 0; pass < 2; ++pass) {
+        const float* beta = pass == 0 && !accumulate ? &zero : &one;
+        const cublasStatus_t st = cublasGemmEx(cublas_, CUBLAS_OP_T, CUBLAS_OP_N, n_out, rows, K, &one, W, CUDA_R_16BF,
+                                               K, pass == 0 ? hi : lo, CUDA_R_16BF, K, beta, out, CUDA_R_32F, n_out,
+                                               CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        if (st != CUBLAS_STATUS_SUCCESS) throw std::runtime_error("prefill: cublasGemmEx failed (" + std::to_string(int(st)) + ")");
+    }
+}
+
+// Batched prefill (gptoss.h: the same distributions as n single steps), layer-major as the fp32 reference runs a
+// batch (gptoss_ref/model.py:107-125): per layer, the n rows' QKV projection on tensor cores, RoPE and fp16 rounding
+// of the new keys and values, causal attention of every row (sinks, window), the batch appended to the cache, the O
+// projection plus residual, and the MoE of all n rows through the batched grouped-GEMM path; then the final norm and
+// the LM head for the rows that are scored (tensor cores, in chunks) and for the last row (the decode GEMV, whose
+// logits the next step's score and gptoss_logits read).
+void Engine::prefill(const int* tokens, int n, const int* ids, int k, float* lp, int* argmax, float* target_lp) {
+    if (n <= 0) throw std::runtime_error("prefill: n must be positive");
+    if (pos_ + n > max_ctx_) throw std::runtime_error("context is full");
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= cfg_.vocab) throw std::runtime_error("prefill: token id out of range");
+    if (ids) {
+        if (k < 0 || k > score_cap_) throw std::runtime_error("prefill: k out of range");
+        for (long long i = 0; i < (long long)(n - 1) * k; ++i)
+            if (ids[i] < 0 || ids[i] >= cfg_.vocab) throw std::runtime_error("prefill: id out of range");
+    }
+    if (n == 1) return prefill_stepwise(tokens, n, ids, k, lp, argmax, target_lp);
+    if (greedy_graph_) {                                          // the next step captures the plain step graph
+        greedy_graph_ = false;
+        if (graph_) { cudaGraphExecDestroy(graph_); graph_ = nullptr; }
+    }
+    if (!cublas_) {
+        if (cublasCreate(&cublas_) != CUBLAS_STATUS_SUCCESS) throw std::runtime_error("prefill: cublasCreate failed");
+    }
+    if (cublasSetStream(cublas_, stream_) != CUBLAS_STATUS_SUCCESS) throw std::runtime_error("prefill: cublasSetStream");
+    const int H = cfg_.hidden, V = cfg_.vocab;
+    const int QD = cfg_.heads * cfg_.head_dim, QKV = QD + 2 * cfg_.kv_heads * cfg_.head_dim;
+    const int p0 = pos_;
+    constexpr int kPartRows = 64, kLogitRows = 32;
+    float* X = static_cast<float*>(scratch(0, size_t(n) * H * 4));
+    const int Kmax = std::max(H, QD);
+    void* hi = scratch(1, size_t(n) * Kmax * 2);
+    void* lo = scratch(2, size_t(n) * Kmax * 2);
+    float* Q = static_cast<float*>(scratch(3, size_t(n) * QKV * 4));
+    void* kvb = scratch(4, size_t(n) * 2 * cfg_.kv_heads * cfg_.head_dim * 2);
+    float* A = static_cast<float*>(scratch(5, size_t(n) * QD * 4));
+    float* part = static_cast<float*>(scratch(6, prefill_attention_floats(kPartRows) * 4));
+    int* tok_d = static_cast<int*>(scratch(7, size_t(n) * 4));
+    cudaStream_t s = stream_;
+    GPT_CHECK(cudaMemcpyAsync(tok_d, tokens, size_t(n) * 4, cudaMemcpyHostToDevice, s));
+    launch_embed_rows(embed_, tok_d, X, n, H, s);
+    for (const Layer& L : layers_) {
+        launch_split_rows(X, n, H, L.ln1, cfg_.eps, hi, lo, s);
+        project(L.wqkv, QKV, H, hi, lo, n, Q, false);
+        launch_prefill_qkv_rope(Q, L.bqkv, cos_, sin_, p0, n, kvb, s);
+        launch_prefill_attention(Q, kvb, L.kc, L.vc, L.sinks, p0, n, L.window, part, kPartRows, A, s);
+        launch_prefill_append(kvb, p0, n, L.window, L.kc, L.vc, s);
+        launch_split_rows(A, n, QD, nullptr, 0.f, hi, lo, s);
+        project(L.wo, H, QD, hi, lo, n, X, true);
+        launch_add_bias_rows(X, L.bo, n, H, s);
+        if (gptoss_moe_layer_forward_batched(L.moe, X, X, n, s, nullptr) != 0)
+            throw std::runtime_error(std::string("prefill moe: ") + gptoss_last_error());
+    }
+    if (ids && n > 1) {
+        const int rows = n - 1;
+        float* LG = static_cast<float*>(scratch(8, size_t(kLogitRows) * V * 4));
+        int* ids_d = static_cast<int*>(scratch(9, size_t(rows) * std::max(k, 1) * 4));
+        float* lp_d = static_cast<float*>(scratch(10, size_t(rows) * (std::max(k, 0) + 1) * 4));
+        int* am_d = static_cast<int*>(scratch(11, size_t(rows) * 4));
+        float* tl_d = lp_d + size_t(rows) * k;
+        if (k) GPT_CHECK(cudaMemcpyAsync(ids_d, ids, size_t(rows) * k * 4, cudaMemcpyHostToDevice, s));
+        for (int c0 = 0; c0 < rows; c0 += kLogitRows) {
+            const int rc = std::min(kLogitRows, rows - c0);
+            launch_split_rows(X + size_t(c0) * H, rc, H, norm_, cfg_.eps, hi, lo, s);
+            project(lm_head_, V, H, hi, lo, rc, LG, false);
+            for (int r = 0; r < rc; ++r) {
+                const int t = c0 + r;
+                launch_score(LG + size_t(r) * V, V, score_work_, ids_d + size_t(t) * k, k, tokens[t + 1],
+                             lp_d + size_t(t) * k, am_d + t, tl_d + t, nullptr, nullptr, s, false);
+            }
+        }
+        if (k) GPT_CHECK(cudaMemcpyAsync(lp, lp_d, size_t(rows) * k * 4, cudaMemcpyDeviceToHost, s));
+        GPT_CHECK(cudaMemcpyAsync(argmax, am_d, size_t(rows) * 4, cudaMemcpyDeviceToHost, s));
+        GPT_CHECK(cudaMemcpyAsync(target_lp, tl_d, size_t(rows) * 4, cudaMemcpyDeviceToHost, s));
+    }
+    // the last row's logits, through the decode path's LM head
+    launch_gemv_bf16(lm_head_, X + size_t(n - 1) * H, norm_, cfg_.eps, nullptr, nullptr, logits_, V, H, s, false);
+    GPT_CHECK(cudaStreamSynchronize(s));
+    set_position(p0 + n);
 }
 
 void Engine::bench_steps(int token, int n) {

@@ -2,6 +2,7 @@
 // gptoss_score, gptoss_prefill, ...): a gpt-oss checkpoint (config.json + safetensors, Hugging Face names) on one
 // GPU, one token per step.
 #pragma once
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -44,6 +45,8 @@ class Engine {
     void bench_steps(int token, int n);
     void greedy(int token, int n, int* out_tokens);
     void kv_fill_random(int positions, unsigned long long seed);
+    // n single steps (the reference's prefill) instead of the batched path, for comparisons
+    void prefill_stepwise(const int* tokens, int n, const int* ids, int k, float* lp, int* argmax, float* target_lp);
 
   private:
     struct Layer {
@@ -64,6 +67,8 @@ class Engine {
     void forward(cudaStream_t s, bool pdl);
     void capture();
     void run_step();
+    void* scratch(size_t i, size_t bytes);     // grow-only buffers of the batched prefill, counted in device_bytes
+    void project(const void* W, int n_out, int K, const void* hi, const void* lo, int rows, float* out, bool accumulate);
 
     ModelConfig cfg_;
     int max_ctx_ = 0, pos_ = 0;
@@ -83,6 +88,8 @@ class Engine {
     int* score_i_ = nullptr;                    // [score_cap_] ids, then argmax
     int *token_ = nullptr, *pos_d_ = nullptr, *next_token_ = nullptr;
     void* moe_ws_ = nullptr;                    // the MoE kernel's workspace, owned by this engine
+    cublasHandle_t cublas_ = nullptr;           // the batched prefill's projections (created at its first use)
+    std::vector<std::pair<void*, size_t>> pre_; // batched prefill buffers
     int score_cap_ = 1 << 16;
 };
 

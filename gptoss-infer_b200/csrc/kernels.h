@@ -175,7 +175,12 @@ void launch_gemv_bf16(const void* W, const float* x, const float* norm_w, float 
                       const float* resid, float* y, int N, int K, cudaStream_t s, bool pdl);
 void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, const int* d_pos, int pos, void* k_cache,
                         void* v_cache, int window, cudaStream_t s, bool pdl);
-size_t attention_workspace_floats();
+size_t attention_workspace_floats();   // zero-filled before the first use of launch_attention_step
+// RoPE of the raw QKV output, the new position's key and value into the cache, attention and the merge of the
+// split partials, in one launch (qkv is not modified).
+void launch_attention_step(const float* qkv, const float* cos_t, const float* sin_t, void* k_cache, void* v_cache,
+                           const float* sinks, const int* d_pos, int window, float* part, float* out, cudaStream_t s,
+                           bool pdl);
 void launch_attention(const float* q, const void* k_cache, const void* v_cache, const float* sinks, const int* d_pos,
                       int pos, int window, float* part, float* out, cudaStream_t s, bool pdl);
 void launch_embed(const void* table, const int* d_token, float* x, int H, cudaStream_t s, bool pdl);
@@ -189,5 +194,24 @@ void launch_score(const float* logits, int V, void* work, const int* ids, int k,
 size_t moe_layer_workspace_bytes(int k, int H, int I);
 void moe_layer_forward_ws(gptoss_moe_layer* l, const float* x, float* x_resid, cudaStream_t s, void* const* events,
                           void* workspace);
+
+// Measured dense kind::mxf4 tensor rate of the current device in TFLOP/s (tc_common.cu; err_dev: a zeroed device
+// int that records a wait that gave up).
+double selftest_mxf4_peak(int* err_dev);
+
+// Batched prefill of n consecutive positions p0.. of one sequence (decode_step.cu): QKV bias + RoPE in place and the
+// rotated k / v rounded to fp16 into kvb [n][2][8][64]; attention of every row (older positions from the cache, the
+// batch's own from kvb; part holds prefill_attention_floats(part_rows)); the batch appended to the cache afterwards;
+// row splits into bf16 hi + lo (after an optional RMSNorm) for the tensor-core projections.
+size_t prefill_attention_floats(int rows);
+void launch_prefill_qkv_rope(float* qkv, const float* bias, const float* cos_t, const float* sin_t, int p0, int n,
+                             void* kvb, cudaStream_t s);
+void launch_prefill_attention(const float* qkv, const void* kvb, const void* k_cache, const void* v_cache,
+                              const float* sinks, int p0, int n, int window, float* part, int part_rows, float* out,
+                              cudaStream_t s);
+void launch_prefill_append(const void* kvb, int p0, int n, int window, void* k_cache, void* v_cache, cudaStream_t s);
+void launch_split_rows(const float* x, int n, int K, const float* norm_w, float eps, void* hi, void* lo, cudaStream_t s);
+void launch_add_bias_rows(float* x, const float* b, int n, int K, cudaStream_t s);
+void launch_embed_rows(const void* table, const int* tokens, float* x, int n, int H, cudaStream_t s);
 
 }  // namespace gpt

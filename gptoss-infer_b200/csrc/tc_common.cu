@@ -210,6 +210,82 @@ __global__ void __launch_bounds__(128) mxf4_selftest_kernel(const __grid_constan
 }
 }  // namespace
 
+// Dense kind::mxf4 tensor rate of this GPU: every CTA (one per SM) issues `iters` x 4 back-to-back M = 128, N = 256,
+// K = 64 block-scaled MMAs into one TMEM accumulator from shared-memory operands (zero e2m1 codes, every E8M0 scale
+// 2^0: the operands' values do not change the rate) and commits once; the host times the launch with events.
+__global__ void __launch_bounds__(128) mxf4_peak_kernel(int iters, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;                                      // 128 rows x 128 bytes (256 values of K)
+    uint8_t* sB = sA + 128 * 128;                            // 256 rows x 128 bytes
+    uint8_t* sSF = sB + 256 * 128;                           // 6 scale chunks of 512 bytes: A (2), B (2 x 2)
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sSF + 6 * 512);
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    for (int i = tid; i < (128 + 256) * 128 / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(sA)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < 6 * 512 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(sSF)[i] = 0x7F7F7F7Fu;
+    if (tid == 0) {
+        tc::mbar_init(bar, 1);
+        tc::fence_barrier_init();
+    }
+    tc::fence_proxy_async_smem();
+    if (warp == 0) {
+        tc::tmem_alloc(holder, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tm = *holder, tm_sfa = tm + 256, tm_sfb = tm + 264;
+    if (tid == 0) {
+        for (int kt = 0; kt < 2; ++kt) {
+            tc::tmem_cp_sf(tm_sfa + 4 * kt, tc::desc_sf_chunk(tc::smem_u32(sSF + kt * 512)));
+            for (int hh = 0; hh < 2; ++hh)
+                tc::tmem_cp_sf(tm_sfb + 8 * kt + 4 * hh, tc::desc_sf_chunk(tc::smem_u32(sSF + (2 + 2 * kt + hh) * 512)));
+        }
+        for (int it = 0; it < iters; ++it) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t sf_id = 2u * uint32_t(u & 1), q = uint32_t(u >> 1);
+                tc::mma_mxf4(tm, tc::desc_sw128(tc::smem_u32(sA + u * 32)), tc::desc_sw128(tc::smem_u32(sB + u * 32)),
+                             tc::idesc_mxf4(128, 256, sf_id, sf_id), (tm_sfa + 4 * q) | (sf_id << 30),
+                             (tm_sfb + 8 * q) | (sf_id << 30), it > 0 || u > 0);
+            }
+        }
+        tc::mma_commit(bar);
+    }
+    __syncwarp();
+    tc::mbar_wait(bar, 0, err, 1);
+    tc::tc_fence_after();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tm, 512);
+}
+
+double selftest_mxf4_peak(int* err_dev) {
+    const int sms = num_sms();
+    const int smem = 1024 + (128 + 256) * 128 + 6 * 512 + 64;
+    GPT_CHECK(cudaFuncSetAttribute(mxf4_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cudaEvent_t e0, e1;
+    GPT_CHECK(cudaEventCreate(&e0));
+    GPT_CHECK(cudaEventCreate(&e1));
+    const int iters = 4096;
+    mxf4_peak_kernel<<<sms, 128, smem>>>(64, err_dev);             // warm-up
+    check_launch("mxf4_peak");
+    GPT_CHECK(cudaEventRecord(e0));
+    mxf4_peak_kernel<<<sms, 128, smem>>>(iters, err_dev);
+    check_launch("mxf4_peak");
+    GPT_CHECK(cudaEventRecord(e1));
+    GPT_CHECK(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    GPT_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    const double flops = 2.0 * 128 * 256 * 64 * 4.0 * iters * sms;
+    return flops / (double(ms) * 1e-3) / 1e12;
+}
+
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                         const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
                         cudaStream_t s) {

@@ -203,6 +203,11 @@ int gptoss_ep_status(int E, int k, int H, int I, int world, int T_max, int* code
 int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                               const uint8_t* b_scales, float* d, int N, int K);
 
+/* [extension] Measures this GPU's dense block-scaled FP4 tensor rate (tcgen05.mma kind::mxf4, M = 128, N = 256,
+ * K = 64, back to back on every SM, timed with CUDA events on the legacy default stream) and stores it in *tflops
+ * (TFLOP/s). The denominator of the batched path's roofline. Synchronizes. */
+int gptoss_selftest_mxf4_peak(double* tflops);
+
 /* [extension] Pipeline tracing of the tensor-core decode kernel (profiling aid). With a device buffer of at least
  * 160 * 160 int64 installed, every later gptoss_moe_layer_forward stores, per CTA, up to 160 clock64 stamps of its
  * phases (the slot list is at the trace stamp helper in decode_tc.cu; unused slots keep their old contents). NULL

@@ -134,7 +134,7 @@ def test_engine_graph_eager_prefill_greedy_and_score(lib, ckpt):
         eager = engine_logits(lib, e, TOKENS)
         assert np.array_equal(graph, eager)
         assert lib.gptoss_use_graph(e, 1) == 0
-        # prefill with scoring = steps + score
+        # batched prefill with scoring: the same distributions as the steps (the engine's tolerance for two paths)
         assert lib.gptoss_reset(e) == 0
         n, k = len(TOKENS), 3
         ids = np.array([[1, 2, 3]] * (n - 1), np.int32)
@@ -144,14 +144,15 @@ def test_engine_graph_eager_prefill_greedy_and_score(lib, ckpt):
         tok = np.array(TOKENS, np.int32)
         assert lib.gptoss_prefill(e, tok.ctypes.data, n, ids.ctypes.data, k, lp.ctypes.data, am.ctypes.data,
                                   tlp.ctypes.data) == 0, lib.gptoss_last_error().decode()
+        assert lib.gptoss_position(e) == n
         for p in range(n - 1):
             ls = graph[p].astype(np.float64) - np.logaddexp.reduce(graph[p].astype(np.float64))
             assert am[p] == int(np.argmax(graph[p]))
-            np.testing.assert_allclose(lp[p], ls[[1, 2, 3]], rtol=1e-5, atol=1e-5)
-            np.testing.assert_allclose(tlp[p], ls[TOKENS[p + 1]], rtol=1e-5, atol=1e-5)
+            np.testing.assert_allclose(lp[p], ls[[1, 2, 3]], rtol=1e-3, atol=2e-3)
+            np.testing.assert_allclose(tlp[p], ls[TOKENS[p + 1]], rtol=1e-3, atol=2e-3)
         buf = np.empty(V, np.float32)
         assert lib.gptoss_logits(e, buf.ctypes.data) == 0
-        assert np.array_equal(buf, graph[-1])
+        close_logits(buf, graph[-1])
         # score of the current logits
         one = np.array([7, 8], np.int32)
         lp2 = np.zeros(2, np.float32)
@@ -173,6 +174,39 @@ def test_engine_graph_eager_prefill_greedy_and_score(lib, ckpt):
         assert out.tolist() == chain[1:]
         # errors: out-of-range token, full context
         assert lib.gptoss_step(e, V) != 0 and b"token" in lib.gptoss_last_error()
+    finally:
+        lib.gptoss_destroy(e)
+
+
+def close_logits(got, want):
+    """Two paths of the engine: top-1 agreement, KL(want || got) <= 1e-5, max |difference| <= 2e-3 max |want|."""
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    assert int(np.argmax(got)) == int(np.argmax(want))
+    lw, lg = want - np.logaddexp.reduce(want), got - np.logaddexp.reduce(got)
+    assert float(np.sum(np.exp(lw) * (lw - lg))) <= 1e-5
+    assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()
+
+
+def test_engine_batched_prefill_then_decode(lib, ckpt):
+    """A batched prefill longer than the sliding window (12 positions, window 4: the batch's own keys are attended
+    before it is appended to the window cache), after two single steps, then three decode steps: every logits vector
+    matches the all-steps path, and the reference's n-step loop semantics (positions, cache) carry over."""
+    d, _ = ckpt
+    e = create(lib, d)
+    try:
+        want = engine_logits(lib, e, TOKENS + [9, 10, 11])
+        assert lib.gptoss_reset(e) == 0
+        got = list(engine_logits(lib, e, TOKENS[:2]))
+        tok = np.array(TOKENS[2:], np.int32)
+        assert lib.gptoss_prefill(e, tok.ctypes.data, len(tok), None, 0, None, None, None) == 0, \
+            lib.gptoss_last_error().decode()
+        buf = np.empty(V, np.float32)
+        assert lib.gptoss_logits(e, buf.ctypes.data) == 0
+        got.append(buf.copy())
+        got.extend(engine_logits(lib, e, [9, 10, 11]))
+        idx = [0, 1, len(TOKENS) - 1, len(TOKENS), len(TOKENS) + 1, len(TOKENS) + 2]
+        for g_, i in zip(got, idx):
+            close_logits(g_, want[i])
     finally:
         lib.gptoss_destroy(e)
 

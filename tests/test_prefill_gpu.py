@@ -148,3 +148,55 @@ def test_layer_forward_batched_matches_decode_and_oracle():
         _check(dec, want)
     finally:
         lib.gptoss_moe_layer_destroy(L)
+
+
+def test_layer_forward_batched_config2_2048_zipf():
+    """configs[2] at full size: 2048 bf16 N(0,1) tokens, router bias skewed towards Zipf s=1.1 (per-expert row counts
+    from a few tens to the 2048 cap, so every M-tile shape occurs). The whole batch runs through the prepared layer;
+    the expert ids of every token equal the float64 ranking (except near-ties), 48 sampled rows (the most and least
+    loaded experts' tokens included) meet the float64 oracle's bound, and two runs are bit-identical."""
+    lib = capi.load()
+    T = 2048
+    t = synth.moe_layer(seed=0)
+    synth.zipf_router_bias(t, s=1.1, beta=1.0, seed=7)
+    x = torch.randn(T, 2880, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16).float()
+    d = {k_: v.to(DEV) for k_, v in t.items()}
+    ln = d[PX + "post_attention_layernorm.weight"].float()
+    W, b = d[PX + "mlp.router.weight"], d[PX + "mlp.router.bias"].float()
+    ex = [e.to(DEV) for e in _experts(t)]
+    L = lib.gptoss_moe_layer_create(P(ln), 1e-5, P(W), P(b), *(P(e) for e in ex), 32, 4, 2880, 2880, 1.702, 7.0)
+    assert L, lib.gptoss_last_error().decode()
+    try:
+        xb = x.to(DEV).contiguous()
+        outs = []
+        for _ in range(2):
+            y = xb.clone()
+            _ok(lib, lib.gptoss_moe_layer_forward_batched(L, P(xb), P(y), T, None, None))
+            torch.cuda.synchronize()
+            outs.append(y.cpu().numpy())
+        assert np.array_equal(outs[0], outs[1])
+    finally:
+        lib.gptoss_moe_layer_destroy(L)
+    xn = x.numpy()
+    h = omoe.rms_norm(xn, t[PX + "post_attention_layernorm.weight"].float().numpy())
+    logits = h.astype(np.float64) @ t[PX + "mlp.router.weight"].float().numpy().astype(np.float64).T + \
+        t[PX + "mlp.router.bias"].float().numpy().astype(np.float64)
+    ids = omoe.topk_ids(logits, 4)
+    ties = omoe.near_tie_rows(logits, 4)
+    counts = np.bincount(ids.reshape(-1), minlength=32)
+    assert counts.max() > 8 * max(1, counts.min()), counts          # the routing is skewed
+    # the library's own ids for the whole batch
+    dh = torch.from_numpy(h).to(DEV).contiguous()
+    gid = torch.empty(T, 4, dtype=torch.int32, device=DEV)
+    gw = torch.empty(T, 4, device=DEV)
+    _ok(lib, lib.gptoss_kernel_router_batched(P(W), P(b), P(dh), 32, 2880, 4, T, P(gid), P(gw)))
+    assert np.array_equal(gid.cpu().numpy()[~ties], ids[~ties])
+    hot, cold = int(np.argmax(counts)), int(np.argmin(np.where(counts > 0, counts, T * 4)))
+    rows = set(np.random.default_rng(3).choice(T, 40, replace=False).tolist())
+    rows |= set(np.nonzero((ids == cold).any(1))[0][:4].tolist()) | set(np.nonzero((ids == hot).any(1))[0][:4].tolist())
+    rows = np.array(sorted(r for r in rows if not ties[r]))
+    sel = np.take_along_axis(logits[rows], ids[rows], 1)
+    w = np.exp(sel - sel[:, :1])
+    w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+    want = _oracle(_experts(t), h[rows], ids[rows].astype(np.int32), w, xn[rows])
+    _check(outs[0][rows], want)

@@ -71,3 +71,14 @@ def test_activation_terms_roundtrip(which):
     even = {0.25: 0.0, 0.75: 1.0, 1.25: 1.0, 1.75: 2.0, 2.5: 2.0, 3.5: 4.0, 5.0: 4.0}
     want_tie = np.sign(x.numpy()[tie]) * np.array([even[float(v)] for v in y[tie]]) * scale[tie]
     assert np.array_equal(got[tie], want_tie.astype(np.float32))
+
+
+def test_mxf4_peak_is_plausible():
+    """The measured dense kind::mxf4 rate (the batched path's roofline denominator) lies between a quarter of and
+    just above NVIDIA's nominal dense FP4 figure for B200 (9 PFLOP/s)."""
+    import ctypes
+    from gptoss_b200 import capi
+    lib = capi.load()
+    tf = ctypes.c_double()
+    assert lib.gptoss_selftest_mxf4_peak(ctypes.byref(tf)) == 0, lib.gptoss_last_error().decode()
+    assert 2250.0 < tf.value < 10000.0, tf.value

@@ -199,4 +199,11 @@ def test_layer_forward_batched_config2_2048_zipf():
     w = np.exp(sel - sel[:, :1])
     w = (w / w.sum(1, keepdims=True)).astype(np.float32)
     want = _oracle(_experts(t), h[rows], ids[rows].astype(np.int32), w, xn[rows])
-    _check(outs[0][rows], want)
+    got = np.asarray(outs[0][rows], np.float64)
+    # The skewed routing gives rows of magnitude ~1e3; fp32 accumulation error scales with the terms, so the
+    # absolute part of the element-wise bound is taken relative to the largest output (1e-6 of it; 1e-3 at 1e3).
+    scale = np.abs(want).max()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6 * scale)
+    assert np.abs(got - want).max() <= 2e-5 * scale
+    assert np.linalg.norm(got - want) <= 2e-5 * np.linalg.norm(want)

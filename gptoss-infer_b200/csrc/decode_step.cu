@@ -28,38 +28,19 @@ __device__ __forceinline__ float bf16_hi_f(uint32_t w) { return __uint_as_float(
 
 // ---------------------------------------------------------------------------------------------------- GEMV
 // y[n] = sum_k W[n][k] x'[k] (+ bias[n]) (+ resid[n]), W bf16 [N][K] (K % 8 == 0), x' = x or RMSNorm(x; g, eps).
-// CTA c owns the contiguous rows [c R, (c + 1) R). When the matrix fits well inside L2 (l2_prefetch), the CTA first
-// asks L2 to prefetch its rows (bulk prefetches of up to 256 KB) and only then waits for the previous kernel
-// (programmatic dependent launch): the weights do not depend on it and stream in while it finishes. Every CTA then
-// stages x' (fp32) in shared memory (computing the norm itself when g is given). A warp takes kRows rows at a time;
-// lane l reads the rows' 16-byte chunks l, l + 32, ... (all loads of a row group issued before the FMAs) and
-// accumulates in packed fp32 pairs; warp_sum ends each row.
+// Every CTA stages x' (fp32) in shared memory (computing the norm itself when g is given: one read of x from L2).
+// A warp takes kRows rows at a time; lane l reads the rows' 16-byte chunks l, l + 32, ... with streaming loads (all
+// loads of a row group issued before the FMAs) and accumulates in packed fp32 pairs; warp_sum ends each row.
 constexpr int kGemvThreads = 256, kRows = 2, kChunksInFlight = 8;
-
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ W,
                                                                     const float* __restrict__ x,
                                                                     const float* __restrict__ g, float eps,
                                                                     const float* __restrict__ bias,
-                                                                    const float* resid, float* y, int N, int K,
-                                                                    int rows_per_cta, int l2_prefetch) {
+                                                                    const float* resid, float* y, int N, int K) {
     extern __shared__ float xs[];                               // [K]
     __shared__ float part[kGemvThreads / 32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int r_begin = min(N, int(blockIdx.x) * rows_per_cta), r_end = min(N, r_begin + rows_per_cta);
-    if (l2_prefetch && tid == 0 && r_end > r_begin) {
-        const char* p = reinterpret_cast<const char*>(W) + size_t(r_begin) * K * 2;
-        size_t left = size_t(r_end - r_begin) * K * 2;           // a multiple of 16 (K % 8 == 0)
-        while (left) {
-            const uint32_t n = uint32_t(left < (256u << 10) ? left : (256u << 10));
-            prefetch_l2_bulk(p, n);
-            p += n;
-            left -= n;
-        }
-    }
     pdl_wait();                                                 // x comes from the previous kernel
     if (g) {
         float ss = 0.f;
@@ -87,7 +68,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_b
     pdl_launch_dependents();
     const int K8 = K >> 3;
     const uint4* Wv = reinterpret_cast<const uint4*>(W);
-    for (int row0 = r_begin + warp * kRows; row0 < r_end; row0 += (kGemvThreads / 32) * kRows) {
+    const int gw = blockIdx.x * (kGemvThreads / 32) + warp, nw = gridDim.x * (kGemvThreads / 32);
+    for (int row0 = gw * kRows; row0 < N; row0 += nw * kRows) {
         float2 acc[kRows];
 #pragma unroll
         for (int r = 0; r < kRows; ++r) acc[r] = make_float2(0.f, 0.f);
@@ -98,8 +80,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_b
 #pragma unroll
                 for (int q = 0; q < kChunksInFlight; ++q) {
                     const int c = c0 + lane + 32 * q;
-                    u[r][q] = row0 + r < r_end && c < K8 ? ldg_stream(Wv + size_t(row0 + r) * K8 + c)
-                                                         : make_uint4(0u, 0u, 0u, 0u);
+                    u[r][q] = row0 + r < N && c < K8 ? ldg_stream(Wv + size_t(row0 + r) * K8 + c)
+                                                     : make_uint4(0u, 0u, 0u, 0u);
                 }
 #pragma unroll
             for (int q = 0; q < kChunksInFlight; ++q) {
@@ -122,7 +104,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_b
         for (int r = 0; r < kRows; ++r) {
             const float v = warp_sum(acc[r].x + acc[r].y);
             const int row = row0 + r;
-            if (lane == 0 && row < r_end) {
+            if (lane == 0 && row < N) {
                 float o = v;
                 if (bias) o += bias[row];
                 if (resid) o += resid[row];                     // resid may alias y: read before the write
@@ -723,15 +705,10 @@ void launch_gemv_bf16(const void* W, const float* x, const float* norm_w, float 
             set[dev] = int(smem);
         }
     }
-    // rows in contiguous per-CTA ranges, two CTAs per SM; a matrix that fits comfortably in L2 (the attention
-    // projections) is prefetched into L2 by its CTAs before they wait for the previous kernel
-    const size_t bytes = size_t(N) * size_t(K) * 2;
-    const int grid = std::max(1, std::min(num_sms() * 2, (N + ds::kRows - 1) / ds::kRows));
-    int rows = (N + grid - 1) / grid;
-    rows = (rows + ds::kRows - 1) / ds::kRows * ds::kRows;
+    const int warps_needed = (N + ds::kRows - 1) / ds::kRows;
+    const int grid = std::max(1, std::min(num_sms() * 2, (warps_needed + 7) / 8));
     ds::launch(ds::gemv_bf16_kernel, dim3(grid), dim3(ds::kGemvThreads), smem, s, pdl,
-               static_cast<const __nv_bfloat16*>(W), x, norm_w, eps, bias, resid, y, N, K, rows,
-               bytes <= (size_t(48) << 20) ? 1 : 0);
+               static_cast<const __nv_bfloat16*>(W), x, norm_w, eps, bias, resid, y, N, K);
 }
 
 void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, const int* d_pos, int pos, void* k_cache,

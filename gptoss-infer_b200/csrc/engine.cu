@@ -373,6 +373,7 @@ Engine::Engine(const std::string& dir, int max_ctx, long long vram_budget) : cfg
 Engine::~Engine() {
     if (graph_) cudaGraphExecDestroy(graph_);
     if (cublas_) cublasDestroy(cublas_);
+    if (pinned_) cudaFreeHost(pinned_);
     for (Layer& L : layers_)
         if (L.moe) gptoss_moe_layer_destroy(L.moe);
     for (void* p : allocs_) cudaFree(p);
@@ -612,22 +613,21 @@ void Engine::greedy(int token, int n, int* out_tokens) {
         greedy_graph_ = true;
         if (graph_) { cudaGraphExecDestroy(graph_); graph_ = nullptr; }
     }
-    GPT_CHECK(cudaMemcpyAsync(token_, &token, sizeof(int), cudaMemcpyHostToDevice, stream_));
-    int* pinned = nullptr;
-    GPT_CHECK(cudaMallocHost(&pinned, size_t(std::max(n, 1)) * sizeof(int)));
-    try {
-        for (int i = 0; i < n; ++i) {
-            run_step();
-            ++pos_;
-            GPT_CHECK(cudaMemcpyAsync(pinned + i, token_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
-        }
-        GPT_CHECK(cudaStreamSynchronize(stream_));
-        if (out_tokens) std::memcpy(out_tokens, pinned, size_t(n) * sizeof(int));
-    } catch (...) {
-        cudaFreeHost(pinned);
-        throw;
+    if (pinned_n_ < n) {                                          // grow-only pinned buffer for the tokens
+        if (pinned_) GPT_CHECK(cudaFreeHost(pinned_));
+        pinned_ = nullptr;
+        pinned_n_ = 0;
+        GPT_CHECK(cudaMallocHost(&pinned_, size_t(std::max(n, 1)) * sizeof(int)));
+        pinned_n_ = n;
     }
-    cudaFreeHost(pinned);
+    GPT_CHECK(cudaMemcpyAsync(token_, &token, sizeof(int), cudaMemcpyHostToDevice, stream_));
+    for (int i = 0; i < n; ++i) {
+        run_step();
+        ++pos_;
+        GPT_CHECK(cudaMemcpyAsync(pinned_ + i, token_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    }
+    GPT_CHECK(cudaStreamSynchronize(stream_));
+    if (out_tokens) std::memcpy(out_tokens, pinned_, size_t(n) * sizeof(int));
 }
 
 void Engine::kv_fill_random(int positions, unsigned long long seed) {

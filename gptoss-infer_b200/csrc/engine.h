@@ -90,6 +90,8 @@ class Engine {
     void* moe_ws_ = nullptr;                    // the MoE kernel's workspace, owned by this engine
     cublasHandle_t cublas_ = nullptr;           // the batched prefill's projections (created at its first use)
     std::vector<std::pair<void*, size_t>> pre_; // batched prefill buffers
+    int* pinned_ = nullptr;                     // host tokens of a greedy decode
+    int pinned_n_ = 0;
     int score_cap_ = 1 << 16;
 };
 

@@ -3,6 +3,7 @@
 // returning (runtime/src/capi.cpp:34-37).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -179,6 +180,17 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
 }
 
 int g_moe_impl = 1;                   // 0: SIMT decode MoE, 1: tensor cores where the shape allows
+std::atomic<int> g_prefill_terms{8};   // e2m1 terms per activation in the batched MoE
+std::atomic<int> g_prefill_pack{-1};   // -1: by batch size, 0: stacked, 1: packed
+
+// The batched MoE's term plan: the packed plan (16 tokens a tile, one MMA per K step) where experts average at most
+// kPackRowsPerExpert rows, the stacked plan (128 tokens a tile, one MMA per term) above.
+constexpr long long kPackRowsPerExpert = 32;
+void set_term_plan(gpt::PrefillArgs& a) {
+    a.terms = g_prefill_terms.load();
+    const int pk = g_prefill_pack.load();
+    a.pack = pk >= 0 ? pk : ((long long)a.T * a.k <= kPackRowsPerExpert * a.E ? 1 : 0);
+}
 long long* g_trace = nullptr;          // device buffer for pipeline traces, installed by gptoss_trace_enable
 
 [[noreturn]] void not_built(const char* what) {
@@ -615,6 +627,7 @@ int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales
         a.limit = limit;
         a.workspace = ws;
         a.trace = g_trace;
+        set_term_plan(a);
         gpt::launch_moe_batched(a, nullptr);
         sync_check("moe_batched");
         check_prefill_error(ws, L);
@@ -655,6 +668,7 @@ int gptoss_moe_layer_forward_batched(gptoss_moe_layer* l, const float* x, float*
         a.workspace = ws;
         a.trace = g_trace;
         a.events = events;
+        set_term_plan(a);
         gpt::launch_moe_batched(a, s);
     });
 }
@@ -689,6 +703,7 @@ int gptoss_moe_layer_experts_batched(gptoss_moe_layer* l, const float* h, const 
         a.limit = l->limit;
         a.workspace = ws;
         a.trace = g_trace;
+        set_term_plan(a);
         gpt::launch_moe_batched(a, s);
     });
 }
@@ -817,6 +832,7 @@ int gptoss_ep_layer_forward(gptoss_moe_layer* l, const double* router_w64, const
         a.epoch = epoch;
         a.local_ws = g_ews.get(L.local_bytes);
         a.trace = g_trace;
+        a.terms = g_prefill_terms.load();
         gpt::launch_ep_layer(a, static_cast<cudaStream_t>(stream));
     });
 }
@@ -844,6 +860,22 @@ int gptoss_test_decode_epoch(int k, int H, int I, unsigned set_to, unsigned* pre
         GPT_CHECK(cudaMemcpy(word, &set_to, sizeof(set_to), cudaMemcpyHostToDevice));
         if (previous) *previous = prev;
     });
+}
+
+int gptoss_set_prefill_terms(int terms) {
+    if (terms < 1 || terms > 8) {
+        g_error = "gptoss_set_prefill_terms: terms must be 1 .. 8";
+        return -1;
+    }
+    return g_prefill_terms.exchange(terms);
+}
+
+int gptoss_set_prefill_packing(int mode) {
+    if (mode < -1 || mode > 1) {
+        g_error = "gptoss_set_prefill_packing: mode must be -1 (by batch size), 0 (stacked) or 1 (packed)";
+        return -2;
+    }
+    return g_prefill_pack.exchange(mode);
 }
 
 int gptoss_set_moe_impl(int impl) {

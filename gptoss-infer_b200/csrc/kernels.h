@@ -122,6 +122,8 @@ struct PrefillArgs {
     void* workspace;              // prefill_layout(T, k, E, H, I).bytes
     long long* trace = nullptr;   // optional: grouped GEMM wait totals per CTA, [160][160], slots 64 * mode + i
     void* const* events = nullptr;   // optional: 4 cudaEvent_t around the gate/up and the down grouped GEMM
+    int terms = 8;                // e2m1 terms per activation (8: exact to 2^-21 of each block's scale)
+    int pack = 0;                 // 0: terms stacked as MMAs on 128-token tiles; 1: packed as rows, 16 tokens a tile
 };
 void launch_moe_batched(const PrefillArgs& a, cudaStream_t s);
 
@@ -154,6 +156,7 @@ struct EpArgs {
     unsigned epoch;               // the same on every rank for one layer call; increases from 1
     void* local_ws;               // ep_layout(...).local_bytes
     long long* trace = nullptr;
+    int terms = 8;                // as PrefillArgs (always stacked)
 };
 void launch_ep_layer(const EpArgs& a, cudaStream_t s);
 

@@ -6,18 +6,24 @@
 //   1. router_batched_kernel: RMSNorm (optional) and the router for 8 tokens per CTA; logits accumulated in fp64
 //      from exact products in a fixed order, top k with ties to the lower id, softmax over the k. Writes h (fp32).
 //   2. permute_kernel (one CTA): the (token, slot) pairs sorted by expert, then token, into "rows"; the rows of each
-//      expert cut into M tiles of 128; pos_of[(token, slot)] = 128 * tile + row in the tile.
-//   3. quantize_h_kernel: every token's h split once into NT = 8 e2m1 residual terms with E8M0 scales per 32 values
-//      (exact to 2^-24 of each block's maximum) and written into the A images of the k tiles that hold it. An A
-//      "piece" is one term of one 256-wide K block of one M tile: 128 rows x 128 bytes in the 128-byte-swizzled
-//      layout shared memory wants, followed by its two scale chunks - one bulk copy.
+//      expert cut into M tiles of 128 / P rows; pos_of[(token, slot)] = 128 * tile + P * (row in the tile).
+//   3. quantize_h_kernel: every token's h split once into nt (default NT = 8) e2m1 terms with E8M0 scales per 32
+//      values (8 terms: exact to 2^-21 of each block's scale) and written into the A images of the k tiles that hold
+//      it. An A "slot" is 128 rows x 128 bytes of one 256-wide K block of one M tile, in the 128-byte-swizzled layout
+//      shared memory wants, followed by its scale chunks - one bulk copy.
 //   4. grouped_gemm_kernel (persistent, one CTA per SM), gate/up: tiles of (M tile, 256 weight rows); the weights
 //      are the MMA's B operand straight from the checkpoint layout (TMA boxes of 256 rows x 128 bytes). Per K block
-//      the 8 terms are 8 MMAs of M = 128 tokens, N = 256, K = 64 x 4 (tcgen05.mma kind::mxf4) into the SAME TMEM
-//      accumulator, so the tensor core adds the terms and one B tile serves 8 x 128 token-terms. Epilogue: bias,
-//      clamped SwiGLU, and the activations quantized into the down projection's A pieces (terms, scales) in place.
-//   5. grouped_gemm_kernel, down: the same mainloop; epilogue w * (y + b2) -> the (token, slot) result row.
-//   6. combine_kernel: x_resid[t] += sum over slots in slot order (deterministic).
+//      the S slots are S MMAs of M = 128 rows, N = 256, K = 64 x 4 (tcgen05.mma kind::mxf4) into the SAME TMEM
+//      accumulator. Epilogue: bias, clamped SwiGLU -> activations.
+//   5. quantize_act_kernel: the activations into the down projection's A slots, as step 3.
+//   6. grouped_gemm_kernel, down: the same mainloop; epilogue w * (y + b2) -> the (token, slot) result row.
+//   7. combine_kernel: x_resid[t] += sum over slots in slot order (deterministic).
+//
+// Term plan (nt terms, S slots, P rows per token; S P >= nt). Stacked (P = 1, S = nt): row r of a tile is one token,
+// slot i holds its term S - 1 - i, and the tensor core adds the terms in the accumulator; one B tile serves
+// nt x 128 token-terms. Packed (P = 8, S = 1): row P j + t holds term t of the tile's token j (rows t >= nt zero),
+// 16 tokens per tile, and the epilogue adds each token's P rows (lanes) - an expert with few rows (small batches)
+// then costs one MMA per K step instead of nt on a mostly empty tile.
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -33,7 +39,8 @@
 namespace gpt {
 namespace pf {
 
-constexpr int NT = 8;                          // terms per token
+constexpr int NT = 8;                          // most terms per token (the exact default)
+constexpr int kPackRows = 8;                   // rows per token in the packed plan
 constexpr int kTileM = 128;                    // tokens (rows of one expert) per M tile = the MMA's M
 constexpr int kRows = kDecodeTileRows;         // weight rows per N tile (the MMA's N)
 constexpr int kEpiWarps = 8;                   // two per TMEM lane quadrant, 128 columns each
@@ -41,7 +48,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 producer, warp 1 MMA is
 constexpr int kImg = kTileM * 128;             // one term's A image for a 256-wide K block (16 KB)
 constexpr int kSFA = 4096;                     // its scales, replicated per lane quadrant (tcgen05.cp 128x256b source)
 constexpr int kTermA = kImg + kSFA;            // 20 KB
-constexpr int kPT = 2;                         // terms per A piece (one barrier wait per 8 MMAs)
+constexpr int kPT = 2;                         // slots per A piece (one barrier wait per 8 MMAs)
 constexpr int kPieceA = kPT * kTermA;
 constexpr int kBImg = kRows * 128;             // B tile for a 256-wide K block (32 KB)
 constexpr int kPieceB = kBImg + 4 * 512;       // + its scale chunks (2 K chunks x 2 row halves)
@@ -51,7 +58,6 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColSFA = kRows;            // 8 columns per term, 16 per A slot
 constexpr uint32_t kColSFB = kRows + 16 * NSA; // 16 columns per B slot
 static_assert(kColSFB + 16 * NSB <= kTmemCols, "TMEM budget");
-static_assert(NT % kPT == 0, "terms per piece");
 constexpr int kRtTok = 14;                     // tokens per router CTA (2048 tokens: 147 CTAs, one wave)
 
 // ------------------------------------------------------------------------------------------------ router (batched)
@@ -166,12 +172,13 @@ __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __
 // ------------------------------------------------------------------------------------------------ permute
 // One CTA of 1024 threads. Thread i owns tokens [i * per, (i + 1) * per); its per-expert counts are scanned over the
 // threads (expert e by warp e), giving every (token, slot) its row: experts in id order, tokens ascending within an
-// expert. Rows of expert e are cut into M tiles of kTileM rows: tiles[m] = (expert, first row, rows), and
-// pos_of[t * k + s] = kTileM * (tile) + (row within the tile), or -1 for an invalid id.
-__global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ ids, int T, int k, int E,
+// expert. Rows of expert e are cut into M tiles of kTileM / P rows: tiles[m] = (expert, first row, rows), and
+// pos_of[t * k + s] = kTileM * (tile) + P * (row within the tile), or -1 for an invalid id.
+__global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ ids, int T, int k, int E, int P,
                                                        int* __restrict__ pos_of, int* __restrict__ tok_of,
                                                        int* __restrict__ slot_of, int4* __restrict__ tiles,
                                                        int* __restrict__ n_tiles, int* __restrict__ err) {
+    const int TM = kTileM / P;
     extern __shared__ unsigned short cnt_raw[];
     unsigned short (*cnt)[1024] = reinterpret_cast<unsigned short (*)[1024]>(cnt_raw);   // [32][1024]
     __shared__ int total[32], base[33], tile0[32];
@@ -212,7 +219,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ i
         for (int e = 0; e < 32; ++e) {
             base[e] = acc;
             tile0[e] = m;
-            for (int r = 0; r < total[e]; r += kTileM) tiles[m++] = make_int4(e, acc + r, min(kTileM, total[e] - r), 0);
+            for (int r = 0; r < total[e]; r += TM) tiles[m++] = make_int4(e, acc + r, min(TM, total[e] - r), 0);
             acc += total[e];
         }
         base[32] = acc;
@@ -229,17 +236,18 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ i
             const int r = cnt[e][tid];
             const int row = base[e] + r;
             cnt[e][tid] = (unsigned short)(r + 1);
-            pos_of[size_t(t) * k + s] = (tile0[e] + r / kTileM) * kTileM + r % kTileM;
+            pos_of[size_t(t) * k + s] = (tile0[e] + r / TM) * kTileM + (r % TM) * P;
             tok_of[row] = t;
             slot_of[row] = s;
         }
 }
 
 // ------------------------------------------------------------------------------------------------ A images
-// A images: per (M tile, K block) the NT terms in DESCENDING order (term NT - 1 first), each kTermA bytes: the
-// 128 x 128-byte image in the 128-byte swizzle, then its scales. Pieces of kPT consecutive terms are one bulk copy.
-__device__ __forceinline__ uint8_t* a_term(uint8_t* img, int m, int KB, int kb, int t) {
-    return img + ((size_t(m) * KB + kb) * NT + (NT - 1 - t)) * kTermA;
+// A images: per (M tile, K block) S slots of kTermA bytes each: the 128 x 128-byte image in the 128-byte swizzle,
+// then its scales. Slot i holds the rows' terms P (S - 1 - i) .. P (S - 1 - i) + P - 1 (DESCENDING: the smallest
+// first). A piece of up to kPT consecutive slots is one bulk copy.
+__device__ __forceinline__ uint8_t* a_slot(uint8_t* img, int m, int KB, int kb, int S, int i) {
+    return img + ((size_t(m) * KB + kb) * S + i) * kTermA;
 }
 
 // Term t's 16-byte unit of block g (0..7 within the K block) in row r (128-byte swizzle).
@@ -261,11 +269,18 @@ __device__ __forceinline__ void tmem_cp_128x256b(uint32_t tmem_col, uint64_t sde
     asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(tmem_col), "l"(sdesc) : "memory");
 }
 
+struct TermPlan {
+    int nt;                                    // terms per token (1 .. NT)
+    int S;                                     // A slots per (M tile, K block)
+    int P;                                     // rows per token (1 or kPackRows); tokens per tile = kTileM / P
+};
+
 // One warp quantizes 8 blocks (K block kb, 4 lanes per 32-value block) of the source row `src` once and writes the
-// terms into the A terms of `nd` destination rows (pos = 128 * tile + row in the tile; negative = none).
+// terms into the A slots of `nd` destination tokens (pos = 128 * tile + P * (token in the tile); negative = none):
+// term t to row pos % 128 + t % P of slot S - 1 - t / P.
 template <int MaxD>                                 // destinations the caller may pass (nd <= MaxD <= 8)
 __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ src, int K, int kb, const int (&pos)[8],
-                                                    int nd, int KB, uint8_t* const (&img)[8]) {
+                                                    int nd, int KB, uint8_t* const (&img)[8], const TermPlan tp) {
     const int lane = threadIdx.x & 31, sub = lane & 3, gl = lane >> 2;
     const int g = kb * 8 + gl;
     const bool valid = g * 32 < K;
@@ -285,18 +300,17 @@ __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ sr
     // gathered once and every later word is a bytewise saturating subtraction (saturating step by step equals
     // clamping the total, the amounts only grow).
     const int wsel = (lane >> 2) & 1, qsel = lane & 3;
-    // Per destination, once: where this lane's code word and scale word of term NT - 1 go (the terms follow in
-    // descending order, kTermA apart).
-    uint8_t* pw[MaxD];
-    uint8_t* ps[MaxD];
+    // Per destination, once: its (M tile, K block) slot 0 and first row.
+    uint8_t* base[MaxD];
+    int row0[MaxD];
 #pragma unroll
     for (int s = 0; s < MaxD; ++s) {
         const bool on = s < nd && pos[s] >= 0;
-        const int ps_ = on ? pos[s] : 0, m = ps_ / kTileM, r = ps_ % kTileM;
-        uint8_t* piece = a_term(img[s], m, KB, kb, NT - 1);
-        pw[s] = on ? piece + a_unit_off(r, gl) + sub * 4 : nullptr;
-        ps[s] = on ? piece + a_sf_off(r, 4 * wsel, qsel) : nullptr;
+        const int ps_ = on ? pos[s] : 0;
+        base[s] = on ? a_slot(img[s], ps_ / kTileM, KB, kb, tp.S, 0) : nullptr;
+        row0[s] = ps_ % kTileM;
     }
+    const int n_emit = tp.S * tp.P;
     uint32_t sw0 = 0, sw = 0;
     quantize_block_digits_lanes4(v8, [&](int term, uint32_t word, uint32_t scale) {
         if (term == 0) {
@@ -310,14 +324,17 @@ __device__ __forceinline__ void quantize_row_kblock(const float* __restrict__ sr
         } else {
             sw = __vsubus4(sw, 0x03030303u);
         }
-        const size_t toff = size_t(NT - 1 - term) * kTermA;
+        if (term >= n_emit) return;
+        const int slot = tp.S - 1 - term / tp.P, dr = term % tp.P;
 #pragma unroll
         for (int s = 0; s < MaxD; ++s) {
-            if (!pw[s]) continue;
-            if (valid) *reinterpret_cast<uint32_t*>(pw[s] + toff) = word;
-            if (lane < 8) *reinterpret_cast<uint32_t*>(ps[s] + toff) = sw;
+            if (!base[s]) continue;
+            uint8_t* piece = base[s] + size_t(slot) * kTermA;
+            const int r = row0[s] + dr;
+            if (valid) *reinterpret_cast<uint32_t*>(piece + a_unit_off(r, gl) + sub * 4) = word;
+            if (lane < 8) *reinterpret_cast<uint32_t*>(piece + a_sf_off(r, 4 * wsel, qsel)) = sw;
         }
-    });
+    }, tp.nt);
 }
 
 // Image bases by rank (expert parallelism: index = the rank that owns the row's expert, the peer's mapping of its
@@ -330,7 +347,8 @@ struct ImgBases {
 // to the k tiles that hold it (pos_of; dest_of = the owning rank, or null for one rank).
 __global__ void __launch_bounds__(256) quantize_h_kernel(const float* __restrict__ h, int T, int H, int k,
                                                          const int* __restrict__ pos_of, const int* __restrict__ dest_of,
-                                                         int KB, const __grid_constant__ ImgBases imgs) {
+                                                         int KB, const __grid_constant__ ImgBases imgs,
+                                                         const TermPlan tp) {
     const long long items = (long long)T * KB;
     const long long warps = (long long)gridDim.x * (blockDim.x / 32);
     for (long long w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < items; w += warps) {
@@ -342,31 +360,32 @@ __global__ void __launch_bounds__(256) quantize_h_kernel(const float* __restrict
             pos[s] = s < k ? pos_of[size_t(t) * k + s] : -1;
             img[s] = imgs.p[(s < k && dest_of) ? (dest_of[size_t(t) * k + s] & 7) : 0];
         }
-        quantize_row_kblock<8>(h + size_t(t) * H, H, kb, pos, k, KB, img);
+        quantize_row_kblock<8>(h + size_t(t) * H, H, kb, pos, k, KB, img, tp);
     }
     if (dest_of) __threadfence_system();                    // expert parallel: stores into peers' regions
 }
 
-// Down A terms from the activations act [rows][I] (rows in tile order): work item (tile m, row j, K block kb).
+// Down A terms from the activations act [rows][I] (rows in tile order): work item (tile m, token j, K block kb).
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ act, int I,
                                                            const int4* __restrict__ tiles,
                                                            const int* __restrict__ n_tiles, int KB,
-                                                           uint8_t* __restrict__ img) {
-    const long long items = (long long)(*n_tiles) * kTileM * KB;
+                                                           uint8_t* __restrict__ img, const TermPlan tp) {
+    const int TM = kTileM / tp.P;
+    const long long items = (long long)(*n_tiles) * TM * KB;
     const long long warps = (long long)gridDim.x * (blockDim.x / 32);
     for (long long w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < items; w += warps) {
         const int kb = int(w % KB);
-        const int jm = int(w / KB), j = jm % kTileM, m = jm / kTileM;
+        const int jm = int(w / KB), j = jm % TM, m = jm / TM;
         const int4 tl = tiles[m];
         if (j >= tl.z) continue;
         int pos[8];
         uint8_t* im[8];
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-            pos[s] = s == 0 ? m * kTileM + j : -1;
+            pos[s] = s == 0 ? m * kTileM + j * tp.P : -1;
             im[s] = img;
         }
-        quantize_row_kblock<1>(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, im);
+        quantize_row_kblock<1>(act + size_t(tl.y + j) * I, I, kb, pos, 1, KB, im, tp);
     }
 }
 
@@ -375,7 +394,8 @@ struct GemmJob {
     int mode;                                  // 0: gate/up (SwiGLU -> down A pieces), 1: down (w (y + b) -> out_ts)
     int K, N;                                  // reduction length, weight rows of one expert
     int UK, KB, KT, RT;                        // K / 64, 256-wide K blocks, 128-wide K chunks, 256-row N tiles
-    const uint8_t* a_img;                      // [tiles][KB][NT] terms, descending
+    const uint8_t* a_img;                      // [tiles][KB][S] slots, descending terms
+    int S, P;                                  // term plan: slots per (tile, K block), rows per token
     const uint8_t* b_sf;                       // [E][RT][KT][2][512]
     const int4* tiles;
     const int* n_tiles;
@@ -417,6 +437,30 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
+}
+
+// Packed plan: a token's kPackRows term rows are 8 aligned lanes (q = lane % 8 = the term). A reduce-scatter over
+// the three lane bits leaves lane q with the token's sums of columns 16 q .. 16 q + 15 (112 shuffles; every column is
+// added once, in an order fixed by the lanes, so the result is deterministic).
+__device__ __forceinline__ void pack_reduce_scatter(const float (&sums)[128], int q, float (&out)[16]) {
+    static_assert(kPackRows == 8, "three lane bits");
+    float r1[64], r2[32];
+    const bool b2 = q & 4, b1 = q & 2, b0 = q & 1;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {                 // r1[i] = column 64 b2 + i
+        const float keep = b2 ? sums[64 + i] : sums[i], send = b2 ? sums[i] : sums[64 + i];
+        r1[i] = keep + __shfl_xor_sync(kFull, send, 4);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {                 // r2[i] = column 64 b2 + 32 b1 + i
+        const float keep = b1 ? r1[32 + i] : r1[i], send = b1 ? r1[i] : r1[32 + i];
+        r2[i] = keep + __shfl_xor_sync(kFull, send, 2);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {                 // out[i] = column 16 q + i
+        const float keep = b0 ? r2[16 + i] : r2[i], send = b0 ? r2[i] : r2[16 + i];
+        out[i] = keep + __shfl_xor_sync(kFull, send, 1);
+    }
 }
 
 // Persistent: CTA c takes output tiles c, c + grid, ... of (M tile m, N tile nt) = (tau / RT, tau % RT), so the CTAs
@@ -475,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             tc::prefetch_tmap(&tm_b);
             bool ok = true;
             int ia = 0, ib = 0;
+            const int npc = (j.S + kPT - 1) / kPT;
             long long wA = 0, wB = 0;
             long long* twA = j.trace && c < 160 ? &wA : nullptr;
             long long* twB = j.trace && c < 160 ? &wB : nullptr;
@@ -483,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 const int e = j.tiles[m].x;
                 for (int s0 = 0; s0 < j.KB && ok; s0 += kSeg) {
                     const int s1 = min(j.KB, s0 + kSeg);
-                    for (int pc = 0; pc < NT / kPT && ok; ++pc)
+                    for (int pc = 0; pc < npc && ok; ++pc)
                         for (int kb = s0; kb < s1; ++kb) {
                             if (pc == 0) {
                                 const int nkq = min(2, j.KT - 2 * kb);
@@ -497,13 +542,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                                              nkq * 1024, &fullB[sb]);
                                 ++ib;
                             }
-                            const int sa = ia % NSA;
+                            const int sa = ia % NSA, nw = min(kPT, j.S - kPT * pc);
                             if (ia >= NSA) ok = twait(&emptyA[sa], uint32_t(ia / NSA - 1) & 1u, j.err, 32, twA);
                             if (!ok) break;
-                            tc::mbar_arrive_expect_tx(&fullA[sa], uint32_t(kPieceA));
+                            tc::mbar_arrive_expect_tx(&fullA[sa], uint32_t(nw * kTermA));
                             tc::bulk_g2s(ringA + sa * kPieceA,
-                                         a_term(const_cast<uint8_t*>(j.a_img), m, j.KB, kb, NT - 1 - kPT * pc),
-                                         kPieceA, &fullA[sa]);
+                                         a_slot(const_cast<uint8_t*>(j.a_img), m, j.KB, kb, j.S, kPT * pc),
+                                         nw * kTermA, &fullA[sa]);
                             ++ia;
                         }
                 }
@@ -520,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         if (lane == 0) {
             bool ok = true;
             int ia = 0, ib = 0, seg = 0;
+            const int npc = (j.S + kPT - 1) / kPT;
             long long wA = 0, wB = 0, wE = 0, t_start = clock64();
             const bool trc = j.trace && c < 160;
             const uint32_t idesc0 = tc::idesc_mxf4(128, kRows, 0, 0), idesc2 = tc::idesc_mxf4(128, kRows, 2, 2);
@@ -527,8 +573,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 for (int s0 = 0; s0 < j.KB && ok; s0 += kSeg, ++seg) {
                     const int s1 = min(j.KB, s0 + kSeg);
                     if (seg > 0) ok = twait(accE, uint32_t(seg - 1) & 1u, j.err, 33, trc ? &wE : nullptr);
-                    for (int pc = 0; pc < NT / kPT && ok; ++pc)
+                    for (int pc = 0; pc < npc && ok; ++pc)
                         for (int kb = s0; kb < s1; ++kb) {
+                            const int nw = min(kPT, j.S - kPT * pc);
                             const int nu = min(4, j.UK - 4 * kb), nkq = (nu + 1) / 2;
                             const int sb = (ib + kb - s0) % NSB;
                             const uint8_t* pb = ringB + sb * kPieceB;
@@ -546,8 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                             ok = twait(&fullA[sa], uint32_t(ia / NSA) & 1u, j.err, 35, trc ? &wA : nullptr);
                             if (!ok) break;
                             tc::tc_fence_after();
-#pragma unroll
-                            for (int w = 0; w < kPT; ++w) {
+                            for (int w = 0; w < nw; ++w) {
                                 const uint8_t* pa = ringA + sa * kPieceA + w * kTermA;
                                 const uint32_t csfa = tmem + kColSFA + 16 * sa + 8 * w;
                                 tmem_cp_128x256b(csfa, desc_sfa_128x256b(tc::smem_u32(pa + kImg)));
@@ -561,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                             }
                             tc::mma_commit(&emptyA[sa]);
                             ++ia;
-                            if (pc == NT / kPT - 1) tc::mma_commit(&emptyB[sb]);
+                            if (pc == npc - 1) tc::mma_commit(&emptyB[sb]);
                         }
                     ib += s1 - s0;
                     if (ok) tc::mma_commit(accF);
@@ -620,9 +666,55 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             const long long te0 = clock64();
             const int e = tl.x;
             const float* bb = j.bias + size_t(e) * j.N;
-            const bool live = row_t < tl.z;
             const int n0 = nt * kRows + 128 * hc;
-            if (j.mode == 0 && live) {
+            if (j.P > 1) {
+                // packed plan: lane q (= row % 8, the term) of the token's 8 lanes ends with the token's sums of
+                // columns 16 q .. 16 q + 15 and stores them
+                const int tok_t = row_t / kPackRows, q = row_t % kPackRows;
+                float r[16];
+                pack_reduce_scatter(sums, q, r);
+                const int nb = n0 + 16 * q;
+                if (tok_t < tl.z && j.mode == 0) {
+                    const int ab = nt * (kRows / 2) + 64 * hc + 8 * q;     // activations ab .. ab + 7
+                    float* arow = j.act + size_t(tl.y + tok_t) * j.I;
+                    if (ab < j.I) {
+                        float o[8];
+#pragma unroll
+                        for (int d = 0; d < 8; ++d) {
+                            const int n = min(nb + 2 * d, j.N - 2);           // I % 64 == 0: never clamped
+                            const float gv = fminf(r[2 * d] + __ldg(bb + n), j.limit);
+                            const float lv = fminf(fmaxf(r[2 * d + 1] + __ldg(bb + (n + 1)), -j.limit), j.limit);
+                            o[d] = __fdividef(gv, 1.f + __expf(-j.alpha * gv)) * (lv + 1.f);
+                        }
+                        if (ab + 7 < j.I) {
+                            *reinterpret_cast<float4*>(arow + ab) = make_float4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<float4*>(arow + ab + 4) = make_float4(o[4], o[5], o[6], o[7]);
+                        } else {
+                            for (int d = 0; d < 8; ++d)
+                                if (ab + d < j.I) arow[ab + d] = o[d];
+                        }
+                    }
+                } else if (tok_t < tl.z && j.mode == 1 && nb < j.N) {
+                    const int row = tl.y + tok_t, t = j.tok_of[row], s = j.slot_of[row];
+                    const float w = j.wts[size_t(t) * j.k + s];
+                    float* orow = j.out_ts + (size_t(t) * j.k + s) * j.N;
+                    if (nb + 16 <= j.N) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            float4 o;
+                            o.x = w * (r[i] + __ldg(bb + (nb + i)));
+                            o.y = w * (r[i + 1] + __ldg(bb + (nb + i + 1)));
+                            o.z = w * (r[i + 2] + __ldg(bb + (nb + i + 2)));
+                            o.w = w * (r[i + 3] + __ldg(bb + (nb + i + 3)));
+                            *reinterpret_cast<float4*>(orow + nb + i) = o;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (nb + i < j.N) orow[nb + i] = w * (r[i] + __ldg(bb + (nb + i)));
+                    }
+                }
+            } else if (j.mode == 0 && row_t < tl.z) {
                 // columns n0 .. n0 + 127 = 64 (gate, up) pairs = activations 64 (2 nt + hc) .. + 63
                 const int a0 = nt * (kRows / 2) + 64 * hc;
                 float* arow = j.act + size_t(tl.y + row_t) * j.I + a0;
@@ -643,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                                 if (a0 + i + d < j.I) arow[i + d] = o[d];
                     }
                 }
-            } else if (j.mode == 1 && live && n0 < j.N) {
+            } else if (j.mode == 1 && row_t < tl.z && n0 < j.N) {
                 const int row = tl.y + row_t;
                 float w;
                 float* orow;
@@ -902,7 +994,11 @@ PrefillLayout prefill_layout(int T, int k, int E, int H, int I) {
     PrefillLayout L{};
     auto al = [](size_t b) { return (b + 1023) & ~size_t(1023); };
     const long long rows = (long long)T * k;
-    L.max_tiles = int((rows + pf::kTileM - 1) / pf::kTileM) + E;
+    // Sized for either term plan: tiles of 16 rows (packed) and, per (tile, K block), NT slots of 128-row tiles
+    // (stacked; at least the packed plan's tiles x 1 slot).
+    const int tiles_stacked = int((rows + pf::kTileM - 1) / pf::kTileM) + E;
+    L.max_tiles = int((rows + pf::kTileM / pf::kPackRows - 1) / (pf::kTileM / pf::kPackRows)) + E;
+    const size_t img_slots = size_t(tiles_stacked) * pf::NT;
     L.KB_gu = (H + 255) / 256;
     L.KB_dn = (I + 255) / 256;
     size_t o = 0;
@@ -914,8 +1010,8 @@ PrefillLayout prefill_layout(int T, int k, int E, int H, int I) {
     L.off_slot_of = o; o += al(size_t(rows) * 4);
     L.off_tiles = o; o += al(size_t(L.max_tiles) * 16);
     L.off_misc = o; o += 1024;                              // [0] tile count, [64] error word
-    L.off_img_gu = o; o += al(size_t(L.max_tiles) * L.KB_gu * pf::NT * pf::kTermA);
-    L.off_img_dn = o; o += al(size_t(L.max_tiles) * L.KB_dn * pf::NT * pf::kTermA);
+    L.off_img_gu = o; o += al(img_slots * L.KB_gu * pf::kTermA);
+    L.off_img_dn = o; o += al(img_slots * L.KB_dn * pf::kTermA);
     L.off_out = o; o += al(size_t(rows) * std::max(H, I) * 4);   // activations, then the (token, slot) results
     L.off_w64 = o; o += al(size_t(H) * 32 * 8);
     L.bytes = o;
@@ -957,6 +1053,8 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
     require(a.k >= 1 && a.k <= 8 && a.k <= a.E && a.E <= 32, "moe_batched: needs 1 <= k <= 8 and k <= E <= 32");
     require(a.H % 64 == 0 && a.I % 64 == 0, "moe_batched: H and I must be multiples of 64");
     require(a.T <= 32768, "moe_batched: at most 32768 tokens per call");
+    require(a.terms >= 1 && a.terms <= NT && (a.pack == 0 || a.pack == 1), "moe_batched: bad term plan");
+    const TermPlan tp = a.pack ? TermPlan{a.terms, 1, kPackRows} : TermPlan{a.terms, a.terms, 1};
     const PrefillLayout L = prefill_layout(a.T, a.k, a.E, a.H, a.I);
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
     int* pos_of = reinterpret_cast<int*>(ws + L.off_pos_of);
@@ -982,11 +1080,12 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
             done[dev] = true;
         }
     }
-    permute_kernel<<<1, 1024, 32 * 1024 * 2, s>>>(a.ids, a.T, a.k, a.E, pos_of, tok_of, slot_of, tiles, n_tiles, err);
+    permute_kernel<<<1, 1024, 32 * 1024 * 2, s>>>(a.ids, a.T, a.k, a.E, tp.P, pos_of, tok_of, slot_of, tiles, n_tiles,
+                                                  err);
     check_launch("moe_batched permute");
     ImgBases ib{};
     for (int r = 0; r < 8; ++r) ib.p[r] = img_gu;
-    quantize_h_kernel<<<sms * 8, 256, 0, s>>>(a.h, a.T, a.H, a.k, pos_of, nullptr, L.KB_gu, ib);
+    quantize_h_kernel<<<sms * 8, 256, 0, s>>>(a.h, a.T, a.H, a.k, pos_of, nullptr, L.KB_gu, ib, tp);
     check_launch("moe_batched quantize");
     for (int pass = 0; pass < 2; ++pass) {
         const bool gu = pass == 0;
@@ -1000,6 +1099,8 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
         g.KT = (K + 127) / 128;
         g.RT = (N + kRows - 1) / kRows;
         g.a_img = gu ? img_gu : img_dn;
+        g.S = tp.S;
+        g.P = tp.P;
         g.b_sf = gu ? a.sf_gu : a.sf_dn;
         g.tiles = tiles;
         g.n_tiles = n_tiles;
@@ -1024,7 +1125,7 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
         check_launch("moe_batched grouped gemm");
         rec(2 * pass + 1);
         if (gu) {
-            quantize_act_kernel<<<sms * 8, 256, 0, s>>>(out, a.I, tiles, n_tiles, L.KB_dn, img_dn);
+            quantize_act_kernel<<<sms * 8, 256, 0, s>>>(out, a.I, tiles, n_tiles, L.KB_dn, img_dn, tp);
             check_launch("moe_batched quantize act");
         }
     }
@@ -1068,6 +1169,8 @@ void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
     require(a.T >= 0 && a.T <= a.T_max && a.T_max <= 32768, "ep: 0 <= T <= T_max <= 32768");
     require(a.k >= 1 && a.k <= 8 && a.E <= 32 && a.rank >= 0 && a.rank < a.world, "ep: bad k, E or rank");
     require(a.H % 64 == 0 && a.I % 64 == 0, "ep: H and I must be multiples of 64");
+    require(a.terms >= 1 && a.terms <= NT, "ep: terms must be 1 .. 8");
+    const TermPlan tp{a.terms, a.terms, 1};                  // stacked: the peers' row metadata is per row
     const EpLayout L = ep_layout(a.T_max, a.k, a.E, a.world, a.H, a.I);
     uint8_t* ws = static_cast<uint8_t*>(a.local_ws);
     float* h = reinterpret_cast<float*>(ws + L.off_h);
@@ -1117,7 +1220,7 @@ void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
     if (a.T > 0) {
         ImgBases ib{};
         for (int r = 0; r < kMaxRanks; ++r) ib.p[r] = r < a.world ? d.base[r] + L.off_img : nullptr;
-        quantize_h_kernel<<<sms * 8, 256, 0, s>>>(h, a.T, a.H, a.k, pos_of, dest_of, L.KB_gu, ib);
+        quantize_h_kernel<<<sms * 8, 256, 0, s>>>(h, a.T, a.H, a.k, pos_of, dest_of, L.KB_gu, ib, tp);
         check_launch("ep dispatch");
     }
     ep_barrier_kernel<<<1, 32, 0, s>>>(d, 1);
@@ -1134,6 +1237,8 @@ void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
         g.KT = (K + 127) / 128;
         g.RT = (N + kRows - 1) / kRows;
         g.a_img = gu ? own + L.off_img : img_dn;
+        g.S = tp.S;
+        g.P = tp.P;
         g.b_sf = gu ? a.sf_gu : a.sf_dn;
         g.tiles = tiles;
         g.n_tiles = n_tiles;
@@ -1150,7 +1255,7 @@ void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
         grouped_gemm_kernel<<<sms, kThreads, kGemmSmem, s>>>(gu ? *a.tmap_gu : *a.tmap_dn, g);
         check_launch("ep grouped gemm");
         if (gu) {
-            quantize_act_kernel<<<sms * 8, 256, 0, s>>>(act, a.I, tiles, n_tiles, L.KB_dn, img_dn);
+            quantize_act_kernel<<<sms * 8, 256, 0, s>>>(act, a.I, tiles, n_tiles, L.KB_dn, img_dn, tp);
             check_launch("ep quantize act");
         }
     }

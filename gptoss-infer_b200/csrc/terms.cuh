@@ -173,12 +173,16 @@ __device__ __forceinline__ int fixed_schedule_k0(float amax) {
 // with scale 2^k_t: term 1 (top digit) has k_1 = k - 1 and term t = 2..7 has k_t = k + 2 - 3t (digit 7 - t). The
 // represented value is exact up to the rint: |error| <= 2^(k - 21). Terms whose scale would fall below 2^-127 (blocks
 // under about 2^-105) are left zero. emit(t, word, scale) as quantize_block_terms_lanes4.
+//
+// Fewer terms: with `nt` < 8 the remainder is rounded once to the grid of the last kept digit (R = rint(r 2^(20 - s))
+// 2^s, s = 3 (8 - nt); nt = 1 keeps term 0 alone), so terms 0 .. nt - 1 are the nearest nt-term value (|error| <=
+// 2^(k + 3 - 3 nt) for nt >= 2, 2^k for nt = 1) and the later terms' codes are all zero.
 __device__ __forceinline__ uint32_t balanced_digit_code(uint32_t u) {     // u = digit + 4 in 0..7 -> e2m1 code
     return (0x32109ABCu >> (4 * u)) & 0xFu;
 }
 
 template <class Emit>
-__device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8], Emit&& emit) {
+__device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8], Emit&& emit, int nt = 8) {
     constexpr int kOff = 4 * 299593;                            // 4 (8^7 - 1) / 7
     float amax = 0.f;
 #pragma unroll
@@ -187,6 +191,9 @@ __device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8]
     amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
     const int k = fixed_schedule_k0(amax);
     const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+    // grid of the last kept digit: 2^s units of 2^(k - 20); nt = 1 keeps no digit (scale 0 makes R = 0)
+    const int sh = 3 * (8 - max(2, min(8, nt)));
+    const float gscale = nt <= 1 ? 0.f : exp2i_exact(20 - sh);
     uint32_t w0 = 0, w1 = 0;
     int Rp[8];
 #pragma unroll
@@ -195,7 +202,7 @@ __device__ __forceinline__ void quantize_block_digits_lanes4(const float (&v)[8]
         const float q0 = round_e2m1_code(v[i] * inv, code);
         w0 |= code << (4 * i);
         const float r = fmaf(-q0, sc, v[i]);                    // exact
-        Rp[i] = __float2int_rn((r * inv) * 1048576.f) + kOff;    // in 0 .. 2^20 + kOff
+        Rp[i] = __float2int_rn((r * inv) * gscale) * (1 << sh) + kOff;   // in 0 .. 2^20 + kOff
         const uint32_t u1 = uint32_t(Rp[i]) >> 18;               // top digit + 4, 0..8
         w1 |= (u1 < 4 ? 12u - u1 : u1 - 4u) << (4 * i);
     }

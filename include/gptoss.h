@@ -146,7 +146,8 @@ int gptoss_moe_route_batched(const void* W, const float* b, const float* x, cons
 
 /* [extension] Batched (prefill) MoE on tensor cores: x_resid[t] += sum_s w[t][s] (W2[e] swiglu(W1[e] x_norm[t] + b1)
  * + b2) with e = ids[t][s], for T tokens (grouped GEMM over the experts: permute, tcgen05 block-scaled FP4 MMAs with
- * the activations split into 8 e2m1 residual terms, unpermute, slot-ordered combine). Layouts as gptoss_kernel_moe
+ * the activations split into e2m1 terms - 8 unless gptoss_set_prefill_terms says otherwise - unpermute,
+ * slot-ordered combine). Layouts as gptoss_kernel_moe
  * with x_norm, ids, weights, x_resid of T rows; expert ids in 0..31; H and I multiples of 64; T <= 32768. An E8M0
  * scale byte 0xFF (NaN) in the experts up to the largest id used returns -1. Device pointers; synchronizes. */
 int gptoss_kernel_moe_batched(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
@@ -231,6 +232,19 @@ int gptoss_test_decode_epoch(int k, int H, int I, unsigned set_to, unsigned* pre
 /* [extension] Which decode MoE implementation gptoss_kernel_moe uses: 0 = SIMT (CUDA cores), 1 = tensor cores
  * (tcgen05 block-scaled MMA) where the shape allows it. Returns the previous setting, or -1. */
 int gptoss_set_moe_impl(int impl);
+
+/* [extension] Activation terms of the batched (prefill) MoE, for every later batched and expert-parallel call in the
+ * process: each 32-value block of the tensor-core operand is the sum of `terms` e2m1 terms under E8M0 scales, the
+ * nearest such sum. 8 (the default) is exact to 2^-21 of each block's scale and meets the float64 bound of the
+ * reference's tests; fewer terms run fewer MMAs at a larger error (measured per count in the tests and the bench).
+ * Returns the previous count, or -1 (terms outside 1 .. 8). */
+int gptoss_set_prefill_terms(int terms);
+
+/* [extension] Tile plan of the batched MoE: 1 = packed (a token's terms are 8 rows of a 128-row tile, 16 tokens per
+ * tile: one MMA per K step for experts with few rows), 0 = stacked (128 tokens per tile, one MMA per term), -1 (the
+ * default) = packed while the experts average at most 32 rows (T * k <= 32 * E). Both give the same results within
+ * the float64 bound. Returns the previous mode, or -2 (mode outside -1 .. 1). */
+int gptoss_set_prefill_packing(int mode);
 
 #ifdef __cplusplus
 }

@@ -4,7 +4,9 @@ combine by all-to-all, the local experts by the batched tensor-core path with k 
 Every row's expert computation and the slot-ordered combine are the operations of the single-GPU batched forward
 (gptoss_moe_layer_forward_batched, the batched form of gptoss_ref/model.py:100-104), so the expert-parallel result
 must be bit-identical to it: on one GPU (no collective), and over two GPUs with NCCL (skipped with fewer GPUs),
-including a step where one rank receives no rows.
+including a step where one rank receives no rows. The expert-parallel kernels use the stacked tile plan (a token's
+activation terms as successive MMAs on one accumulator row); the packed plan adds the same terms in another order
+(equal within the float64 bound, not bit for bit), so every test here runs the batched path in the stacked plan.
 """
 import datetime
 import os
@@ -18,6 +20,14 @@ from gptoss_b200 import capi, ep, synth
 
 pytestmark = pytest.mark.gpu
 PX = "model.layers.0."
+
+
+@pytest.fixture(autouse=True)
+def stacked_plan():
+    lib = capi.load()
+    prev = lib.gptoss_set_prefill_packing(0)
+    yield
+    lib.gptoss_set_prefill_packing(prev)
 EX = PX + "mlp.experts."
 E8 = 8
 
@@ -109,6 +119,7 @@ def _worker(rank, world, port, skew, x, q):
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
     try:
         lib = capi.load()
+        lib.gptoss_set_prefill_packing(0)              # a fresh process: the stacked plan, as the parent's reference
         t = _model(skew)
         y = _ep_forward(lib, t, x[rank::world], rank, world, dev)
         q.put((rank, y.numpy()))
@@ -181,6 +192,7 @@ def _peer_worker(rank, world, port, skew, x, split, q):
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
     try:
         lib = capi.load()
+        lib.gptoss_set_prefill_packing(0)
         t = _model(skew)
         lo, hi = split[rank], split[rank + 1]
         outs = _peer_forward(lib, t, x[lo:hi], rank, world, dev, T_max=40)

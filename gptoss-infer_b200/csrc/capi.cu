@@ -719,6 +719,20 @@ int gptoss_moe_layer_forward(gptoss_moe_layer* l, const float* x, float* x_resid
     });
 }
 
+int gptoss_selftest_mxf4_mma_ns(int n, double* ns) {
+    return guard([&] {
+        if (!ns) throw std::runtime_error("selftest_mxf4_mma_ns: null output");
+        int* err = static_cast<int*>(g_flag.get(sizeof(int)));
+        GPT_CHECK(cudaMemset(err, 0, sizeof(int)));
+        const double t = gpt::selftest_mxf4_mma_ns(n, err);
+        sync_check("selftest_mxf4_mma_ns");
+        int h = 0;
+        GPT_CHECK(cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (h) throw std::runtime_error("selftest_mxf4_mma_ns: a wait gave up");
+        *ns = t;
+    });
+}
+
 int gptoss_selftest_mxf4_peak(double* tflops) {
     return guard([&] {
         if (!tflops) throw std::runtime_error("selftest_mxf4_peak: null output");

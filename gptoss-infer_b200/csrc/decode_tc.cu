@@ -2,17 +2,18 @@
 //
 // Operands. B = expert weights straight from the checkpoint layout: TMA boxes of 256 rows x 128 bytes of K (256
 // e2m1 values) with the 128-byte swizzle, one 32 KB box per pipeline stage; their E8M0 scales repacked once into
-// 512-byte tcgen05 chunks ([tile][K chunk][half]). A = the activation vector split into NT = 8 e2m1 residual terms,
-// each with its own E8M0 scale per 32 elements (x equals their sum to 2^-24 of each block's maximum): 8 rows of
+// 512-byte tcgen05 chunks ([tile][K chunk][half]). A = the activation vector split into NT = 8 e2m1 terms, each
+// with its own E8M0 scale per 32 elements (the integer digit split of terms.cuh: the vector equals their sum to
+// 2^-21 of each block's scale, below 2^-22 of the block's maximum): 8 rows of
 // 128 bytes per 256 values of K, read as M = 128 rows through a descriptor whose 8-row groups all start at the same
 // address. One tcgen05.mma kind::mxf4 (M = 128, N = 256, K = 64) therefore consumes 8 KB of weights; the tensor core
 // performs the MXFP4 dequantization, accumulator rows 0..7 hold the 8 terms' dot products and the epilogue adds them.
 //
 // Phases of every CTA (all 148 resident, one per SM):
-//   0. RMSNorm of x (every CTA, into shared memory) and the router split over the grid: each CTA computes the
-//      router's partial dot products over its slice of K (fp64, exact products) and publishes them; after a
-//      counting barrier every CTA adds all partial sums in the same fixed order (so all CTAs pick the same experts),
-//      takes the top k (ties to the lower id) and the softmax over the k.
+//   0. RMSNorm of x (every CTA, in registers); router CTA c < E computes logit c over all of K (fp64, exact products
+//      summed in a fixed order) and publishes it; warp 0 of every CTA reads the E logits, takes the top k (ties to
+//      the lower id) and the softmax over the k, so all CTAs pick the same experts. The last CTAs quantize x's
+//      32-value blocks into its terms in global memory (gate/up's A operand), counted on a grid-wide word.
 //   1. Gate/up stream-K GEMV; the CTA finishing a 256-row tile applies bias, the clamped SwiGLU (rows 2j glu, 2j+1
 //      linear) and the slot's gate weight, and writes the tile's 128 activations as down's A terms (global memory).
 //   2. Down stream-K GEMV over K' = k * I: the k experts' rows form one long GEMV because A carries the gate
@@ -101,11 +102,12 @@ struct Job {
     Layout L;
 };
 
-// Trace slots per CTA: 0 start, 123 stage list copied, 124/125 sum of squares, 84 h in shared memory, 85 router
-// partials published, 86 all partials published, 87 partial sums added, 120 logits, 121 top k, 122 softmax, 88 ids
-// known, 1 phase 0 done, 89 producer start, 2+i producer issues stage i, 126 scale copies issued, 127+p x terms pass
-// p, 80 small operands in shared memory, 34+i MMA warp sees stage i landed, 96+i its MMAs issued, 66+g epilogue
-// finished segment g, 81 grid barrier passed, 83 down's A terms in shared memory, 82 end.
+// Trace slots per CTA: 0 start, 123 previous layer complete, 124 sum of squares, 84 h, 85 router logit published,
+// 126 x blocks quantized, 1 phase 0 done, 120 logits read, 121 top k, 122 softmax, 127 ids in shared memory, 88 ids
+// released to the other warps, 89 producer start, 2+i producer issues stage i, 80 x's terms in shared memory, 78
+// epilogue warps see the ids, 34+i MMA warp sees stage i landed, 96+i its MMAs issued, 66+g epilogue read segment g,
+// 132+g its split partial sums added, 140+g its down terms written, 131 gate/up done (counted on the grid barrier),
+// 81 grid barrier passed, 83 down's A terms loaded, 82 end.
 // Tracing is a compile-time choice: the untraced kernel carries no stamp code at all (branches over it in the
 // single-thread issue loops measurably slowed them).
 template <bool kTrace>
@@ -320,8 +322,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
             }
         }
         // x's blocks: block g is quantized by CTA nc - 1 - (g % nc), in the 8 lanes whose registers hold it (float4
-        // round r = g / (kThreads / 8), threads 8 (g % (kThreads / 8)) ..+7), which write its terms into global memory
-        // and count it on gbar[3]
+        // round r = g / (kThreads / 8), threads 8 (g % (kThreads / 8)) ..+7), which write its terms into global memory.
+        // The CTA counts its blocks on gbar[3] with one release after the barrier that ends phase 0 (an epilogue
+        // thread, below): a release per block here would hold that barrier, and warp 0's wait for the expert ids
+        // behind it, until the stores were acknowledged.
         {
             const int nb = H / 32, per_round = kThreads / 8;
 #pragma unroll
@@ -340,14 +344,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                         // copy sub8)
                         if (sub8 < 4) sf[t * 16 + sub8 * 4] = uint8_t(scale);
                     });
-                    __syncwarp(grp);
-                    if (sub8 == 0) red_add_release(&j.gbar[3], 1u);
                 }
             }
         }
         if (tid == 0) stamp<kTrace>(j, 126);
     }
-    tc::fence_proxy_async_smem();             // x's terms (generic stores) are read by the MMAs (async proxy)
+    tc::fence_proxy_async_smem();             // phase 0's generic shared-memory accesses before the TMA's writes
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -560,6 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
         // copies; then the expert ids from warp 0
         {
             if (et == 0) {
+                // this CTA's x blocks (every thread's stores precede the phase-0 barrier): nc - 1 - c = g % nc
+                const int nb = j.H / 32, r0 = nc - 1 - c;
+                if (r0 < nb) red_add_release(&j.gbar[3], unsigned((nb - r0 + nc - 1) / nc));
                 bool done = false;
                 for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
                     done = ld_acquire(&j.gbar[3]) >= unsigned(j.H / 32);
@@ -744,11 +749,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
                     const float lv = fminf(fmaxf(lin, -j.limit), j.limit);
                     const float act = __fdividef(gv, 1.f + __expf(-j.alpha * gv)) * (lv + 1.f) * w_s[s];
                     {                                // the tile's four 32-element blocks, one per epilogue warp
+                        static_assert(NT == 8, "the digit split makes 8 terms");
                         const int gb = rt * (kRows / 64) + (warp - 2);
-                        quantize_block_terms_warp32<NT>(act,
-                                                        j.aq_img + (size_t(s) * j.dn.SPS + gb / 8) * kA, gb % 8,
-                                                        j.aq_sf + (size_t(s) * j.dn.KT + gb / 4) * kSF8, gb % 4,
-                                                        gb * 32 < j.I);
+                        quantize_block_digits_warp32(act, j.aq_img + (size_t(s) * j.dn.SPS + gb / 8) * kA, gb % 8,
+                                                     j.aq_sf + (size_t(s) * j.dn.KT + gb / 4) * kSF8, gb % 4,
+                                                     gb * 32 < j.I);
                     }
 
                     if (et == 0 && st.seg < 8) stamp<kTrace>(j, 140 + st.seg);
@@ -779,8 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fused_kernel(const __grid_con
 }
 
 // Shared-memory plan: NS ring slots (a 32 KB weight box and its 2 KB of scales each), x's terms and scales, down's A
-// terms and scales per down stage, h (fp32; inside the ring, which phase 0 does not use yet), the accumulator's 8
-// term rows, barriers, and the small per-CTA state. TMEM: the accumulator in columns [0, 256), x's scale chunks, then
+// terms and scales per down stage, the accumulator's 8 term rows, barriers, and the small per-CTA state. TMEM: the accumulator in columns [0, 256), x's scale chunks, then
 // a ring of NSF weight-scale slots (16 columns each) and of down's A-scale slots (8 columns each).
 Layout make_layout(int NS, int cap, int cap_dn, const Part& gu, int H) {
     Layout L{};

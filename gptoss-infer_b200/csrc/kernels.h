@@ -201,6 +201,7 @@ void moe_layer_forward_ws(gptoss_moe_layer* l, const float* x, float* x_resid, c
 // Measured dense kind::mxf4 tensor rate of the current device in TFLOP/s (tc_common.cu; err_dev: a zeroed device
 // int that records a wait that gave up).
 double selftest_mxf4_peak(int* err_dev);
+double selftest_mxf4_mma_ns(int n, int* err_dev);
 
 // Batched prefill of n consecutive positions p0.. of one sequence (decode_step.cu): QKV bias + RoPE in place and the
 // rotated k / v rounded to fp16 into kvb [n][2][8][64]; attention of every row (older positions from the cache, the

@@ -593,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                             ok = twait(&fullA[sa], uint32_t(ia / NSA) & 1u, j.err, 35, trc ? &wA : nullptr);
                             if (!ok) break;
                             tc::tc_fence_after();
-                            for (int w = 0; w < nw; ++w) {
+                            auto slot_mmas = [&](int w) {
                                 const uint8_t* pa = ringA + sa * kPieceA + w * kTermA;
                                 const uint32_t csfa = tmem + kColSFA + 16 * sa + 8 * w;
                                 tmem_cp_128x256b(csfa, desc_sfa_128x256b(tc::smem_u32(pa + kImg)));
@@ -604,6 +604,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                                                  (csfa + 4 * q) | (sfid << 30), (csfb + 8 * q) | (sfid << 30),
                                                  !(pc == 0 && w == 0 && kb == s0 && u == 0));
                                 }
+                            };
+                            if (nw == kPT) {                     // a full piece (the common case), unrolled
+#pragma unroll
+                                for (int w = 0; w < kPT; ++w) slot_mmas(w);
+                            } else {
+                                for (int w = 0; w < nw; ++w) slot_mmas(w);
                             }
                             tc::mma_commit(&emptyA[sa]);
                             ++ia;

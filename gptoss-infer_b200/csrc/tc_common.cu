@@ -210,10 +210,10 @@ __global__ void __launch_bounds__(128) mxf4_selftest_kernel(const __grid_constan
 }
 }  // namespace
 
-// Dense kind::mxf4 tensor rate of this GPU: every CTA (one per SM) issues `iters` x 4 back-to-back M = 128, N = 256,
+// Dense kind::mxf4 tensor rate of this GPU: every CTA (one per SM) issues `iters` x 4 back-to-back M = 128, N = n,
 // K = 64 block-scaled MMAs into one TMEM accumulator from shared-memory operands (zero e2m1 codes, every E8M0 scale
 // 2^0: the operands' values do not change the rate) and commits once; the host times the launch with events.
-__global__ void __launch_bounds__(128) mxf4_peak_kernel(int iters, int* err) {
+__global__ void __launch_bounds__(128) mxf4_peak_kernel(int iters, int n, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;                                      // 128 rows x 128 bytes (256 values of K)
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(128) mxf4_peak_kernel(int iters, int* err) {
             for (int u = 0; u < 4; ++u) {
                 const uint32_t sf_id = 2u * uint32_t(u & 1), q = uint32_t(u >> 1);
                 tc::mma_mxf4(tm, tc::desc_sw128(tc::smem_u32(sA + u * 32)), tc::desc_sw128(tc::smem_u32(sB + u * 32)),
-                             tc::idesc_mxf4(128, 256, sf_id, sf_id), (tm_sfa + 4 * q) | (sf_id << 30),
+                             tc::idesc_mxf4(128, n, sf_id, sf_id), (tm_sfa + 4 * q) | (sf_id << 30),
                              (tm_sfb + 8 * q) | (sf_id << 30), it > 0 || u > 0);
             }
         }
@@ -263,7 +263,9 @@ __global__ void __launch_bounds__(128) mxf4_peak_kernel(int iters, int* err) {
     if (warp == 0) tc::tmem_dealloc(tm, 512);
 }
 
-double selftest_mxf4_peak(int* err_dev) {
+// Nanoseconds per M = 128, N = n, K = 64 kind::mxf4 MMA issued back to back on one SM (every SM busy).
+double selftest_mxf4_mma_ns(int n, int* err_dev) {
+    require(n % 8 == 0 && n >= 8 && n <= 256, "selftest_mxf4_mma_ns: n must be a multiple of 8 in 8..256");
     const int sms = num_sms();
     const int smem = 1024 + (128 + 256) * 128 + 6 * 512 + 64;
     GPT_CHECK(cudaFuncSetAttribute(mxf4_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -271,10 +273,10 @@ double selftest_mxf4_peak(int* err_dev) {
     GPT_CHECK(cudaEventCreate(&e0));
     GPT_CHECK(cudaEventCreate(&e1));
     const int iters = 4096;
-    mxf4_peak_kernel<<<sms, 128, smem>>>(64, err_dev);             // warm-up
+    mxf4_peak_kernel<<<sms, 128, smem>>>(64, n, err_dev);          // warm-up
     check_launch("mxf4_peak");
     GPT_CHECK(cudaEventRecord(e0));
-    mxf4_peak_kernel<<<sms, 128, smem>>>(iters, err_dev);
+    mxf4_peak_kernel<<<sms, 128, smem>>>(iters, n, err_dev);
     check_launch("mxf4_peak");
     GPT_CHECK(cudaEventRecord(e1));
     GPT_CHECK(cudaEventSynchronize(e1));
@@ -282,8 +284,12 @@ double selftest_mxf4_peak(int* err_dev) {
     GPT_CHECK(cudaEventElapsedTime(&ms, e0, e1));
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
-    const double flops = 2.0 * 128 * 256 * 64 * 4.0 * iters * sms;
-    return flops / (double(ms) * 1e-3) / 1e12;
+    return double(ms) * 1e6 / (4.0 * iters);
+}
+
+double selftest_mxf4_peak(int* err_dev) {
+    const double ns = selftest_mxf4_mma_ns(256, err_dev);
+    return 2.0 * 128 * 256 * 64 * num_sms() / (ns * 1e-9) / 1e12;
 }
 
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
@@ -334,14 +340,20 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
 
 namespace {
 // One warp per 8 blocks: quantize x into residual terms with the chosen quantizer (0 = comparisons, 1 = converters,
-// 2 = fixed scale schedule with fp32 rounding, 3 = the same computed by a whole warp per block).
+// 2 = fixed scale schedule with fp32 rounding, 3 = the same computed by a whole warp per block, 4 = the integer digit
+// split computed by a whole warp per block).
 __global__ void terms_quantize_kernel(const float* x, int n, uint8_t* img, uint8_t* sf, int which) {
     const int lane = threadIdx.x & 31, sub = lane & 3;
-    if (which == 3) {                                        // one block per warp, one element per lane
+    if (which == 3 || which == 4) {                          // one block per warp, one element per lane
         const int warps = gridDim.x * (blockDim.x / 32), w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-        for (int g = w; g < n / 32; g += warps)
-            quantize_block_terms_warp32<kDecodeTerms>(x[g * 32 + lane], img + (g / 8) * (kDecodeTerms * 128), g % 8,
-                                                      sf + (g / 4) * 512, g % 4, true);
+        for (int g = w; g < n / 32; g += warps) {
+            if (which == 3)
+                quantize_block_terms_warp32<kDecodeTerms>(x[g * 32 + lane], img + (g / 8) * (kDecodeTerms * 128),
+                                                          g % 8, sf + (g / 4) * 512, g % 4, true);
+            else
+                quantize_block_digits_warp32(x[g * 32 + lane], img + (g / 8) * (kDecodeTerms * 128), g % 8,
+                                             sf + (g / 4) * 512, g % 4, true);
+        }
         return;
     }
     const int g = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 8 + (lane >> 2);
@@ -380,6 +392,7 @@ __global__ void terms_decode_kernel(const uint8_t* img, const uint8_t* sf, int n
 void selftest_terms(const float* x, int n, float* out, float* per_term, int which, void* scratch, size_t bytes,
                     cudaStream_t s) {
     require(n % 256 == 0 && n > 0, "selftest_terms: n must be a positive multiple of 256");
+    require(which >= 0 && which <= 4, "selftest_terms: which must be 0 .. 4");
     const size_t img_bytes = size_t(n / 256) * kDecodeTerms * 128, sf_bytes = size_t(n / 128) * 512;
     require(bytes >= img_bytes + sf_bytes, "selftest_terms: scratch too small");
     uint8_t* img = static_cast<uint8_t*>(scratch);

@@ -261,6 +261,47 @@ __device__ __forceinline__ void quantize_block_digits_lanes8_masked(const float 
     }
 }
 
+// One 32-element block, one element per lane (lane l holds element l), into the 8 terms of
+// quantize_block_digits_lanes4 (the same codes and scales) in the image format of quantize_block_terms_warp32<8>.
+// Each lane builds its element's 8 codes as one 32-bit word (term t in nibble t), then three shuffle-and-select
+// steps transpose the 8 x 8 nibble matrix of each aligned 8-lane group, after which lane l holds term (l % 8)'s codes
+// of elements 8 (l / 8) .. + 7: every lane stores one code word and one scale byte. There is no per-term dependency
+// chain (the digits come from one integer), unlike the residual form.
+__device__ __forceinline__ void quantize_block_digits_warp32(float v, uint8_t* img_stage, int q, uint8_t* sf_chunk,
+                                                            int kb, bool active) {
+    constexpr int kOff = 4 * 299593;                            // 4 (8^7 - 1) / 7
+    const int lane = threadIdx.x & 31;
+    const float amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(fabsf(v))));
+    const int k = fixed_schedule_k0(amax);
+    const float inv = exp2i_exact(-k), sc = exp2i_exact(k);
+    uint32_t code0;
+    const float q0 = round_e2m1_code(v * inv, code0);
+    const float r = fmaf(-q0, sc, v);                           // exact
+    const uint32_t R = uint32_t(__float2int_rn((r * inv) * 1048576.f) + kOff);
+    const uint32_t u1 = R >> 18;                                // top digit + 4, 0..8
+    uint32_t w = code0 | ((u1 < 4 ? 12u - u1 : u1 - 4u) << 4);
+    uint32_t keep = 0xFu | (k - 1 >= -127 ? 0xF0u : 0u);       // terms whose scale would fall below 2^-127: zero
+#pragma unroll
+    for (int t = 2; t < 8; ++t) {
+        w |= balanced_digit_code((R >> (3 * (7 - t))) & 7u) << (4 * t);
+        if (k + 2 - 3 * t >= -127) keep |= 0xFu << (4 * t);
+    }
+    w &= keep;
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) {                          // swap the off-diagonal m x m nibble blocks
+        const uint32_t lo = m == 4 ? 0x0000FFFFu : (m == 2 ? 0x00FF00FFu : 0x0F0F0F0Fu);
+        const uint32_t y = __shfl_xor_sync(kFull, w, m);
+        w = (lane & m) ? ((w & ~lo) | ((y & ~lo) >> (4 * m))) : ((w & lo) | ((y & lo) << (4 * m)));
+    }
+    const int t = lane & 7;
+    const int kt = t == 0 ? k : (t == 1 ? k - 1 : k + 2 - 3 * t);
+    if (active) {
+        *reinterpret_cast<uint32_t*>(img_stage + t * 128 + (((q ^ t) << 4) | ((lane >> 3) * 4))) = w;
+        // the scale byte in all four 4-byte groups of the term's 16-byte row, as quantize_block_terms_warp32
+        sf_chunk[t * 16 + (lane >> 3) * 4 + kb] = uint8_t(max(kt + 127, 0));
+    }
+}
+
 // Same image format and first term as quantize_block_terms_cvt, with the later terms' scales fixed instead of
 // taken from each residual's maximum: term 0 keeps the block's maximum within 6 * 2^k0, so its rounding error is at
 // most 2^k0 (the e2m1 grid step is 2 between 4 and 6); term 1 uses k0 - 2 (|y| <= 4), and from then on every

@@ -209,6 +209,11 @@ int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, 
  * (TFLOP/s). The denominator of the batched path's roofline. Synchronizes. */
 int gptoss_selftest_mxf4_peak(double* tflops);
 
+/* [extension] The same measurement for M = 128, N = n, K = 64 (n a multiple of 8 in 8..256): nanoseconds per MMA
+ * issued back to back on one SM, every SM busy. How the MMA's cost depends on N (the decode kernels' operand choice).
+ * Synchronizes. */
+int gptoss_selftest_mxf4_mma_ns(int n, double* ns);
+
 /* [extension] Pipeline tracing of the tensor-core decode kernel (profiling aid). With a device buffer of at least
  * 160 * 160 int64 installed, every later gptoss_moe_layer_forward stores, per CTA, up to 160 clock64 stamps of its
  * phases (the slot list is at the trace stamp helper in decode_tc.cu; unused slots keep their old contents). NULL
@@ -217,10 +222,10 @@ int gptoss_trace_enable(void* device_buffer, long long bytes);
 
 /* [extension] Self-test of the activation quantizer of the tensor-core path: splits x[n] (n % 256 == 0) into e2m1
  * residual terms with per-32 E8M0 scales (which = 0: comparison rounding, 1: the hardware converters, 2: the
- * fixed scale schedule with fp32 rounding that the decode kernel uses, 3: the same computed by a whole warp per
- * block), decodes the terms back into out[n], and, if
- * per_term is not NULL, stores the first two terms into per_term[2][n]. Device
- * pointers; synchronizes. */
+ * fixed scale schedule with fp32 rounding, 3: the same computed by a whole warp per block, 4: the integer digit
+ * split - one rounding, then the remainder's balanced octal digits - computed by a whole warp per block, as the
+ * decode kernel's activations use it), decodes the terms back into out[n], and, if per_term is not NULL, stores the
+ * first two terms into per_term[2][n]. Device pointers; synchronizes. */
 int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, int which);
 
 /* [extension] Test hook of the tensor-core decode path: on the current device, sets the launch-epoch word of the

@@ -40,7 +40,7 @@ def test_mxf4_gemm_selftest(N, K):
     assert np.linalg.norm(got - want) <= 1e-6 * np.linalg.norm(want)
 
 
-@pytest.mark.parametrize("which", [0, 1, 2, 3])
+@pytest.mark.parametrize("which", [0, 1, 2, 3, 4])
 def test_activation_terms_roundtrip(which):
     """x -> 16 e2m1 residual terms -> decoded sum: within 2^-22 of each 32-block's maximum (fp32 rounding of the sum
     included), and the first term equals the reference quantizer's rounding of x (oracle/mxfp4.quantize: the same
@@ -82,3 +82,19 @@ def test_mxf4_peak_is_plausible():
     tf = ctypes.c_double()
     assert lib.gptoss_selftest_mxf4_peak(ctypes.byref(tf)) == 0, lib.gptoss_last_error().decode()
     assert 2250.0 < tf.value < 10000.0, tf.value
+
+
+def test_mxf4_mma_cost_by_n():
+    """Time per M = 128, K = 64 kind::mxf4 MMA for N = 8 .. 256 (printed with pytest -s): positive, at most the N = 256
+    time plus a little for every N, and the N = 256 figure consistent with the measured peak."""
+    import ctypes
+    lib = capi.load()
+    ns = {}
+    for n in (8, 16, 32, 64, 128, 256):
+        v = ctypes.c_double()
+        assert lib.gptoss_selftest_mxf4_mma_ns(n, ctypes.byref(v)) == 0, lib.gptoss_last_error().decode()
+        ns[n] = v.value
+    print("ns per MMA by N:", {n: round(t, 2) for n, t in ns.items()})
+    assert all(t > 0 for t in ns.values())
+    assert all(ns[n] <= 1.1 * ns[256] for n in ns)
+    assert lib.gptoss_selftest_mxf4_mma_ns(12, ctypes.byref(ctypes.c_double())) != 0

@@ -153,6 +153,37 @@ __device__ __forceinline__ float warp_pick_softmax(double pick_logit, int k) {
     return e / warp_sum(e);
 }
 
+// Thread-block clusters: this CTA's rank, a barrier over every thread of the cluster (release / acquire, so shared
+// memory written before it is visible to the other CTAs after it), and distributed shared memory accesses to the
+// same variable in CTA `cta` of the cluster.
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local_ptr, unsigned cta) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local_ptr));
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(cta));
+    return ra;
+}
+__device__ __forceinline__ void dsmem_store_f64(double* local_ptr, unsigned cta, double v) {
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(dsmem_addr(local_ptr, cta)), "d"(v) : "memory");
+}
+__device__ __forceinline__ double dsmem_load_f64(const double* local_ptr, unsigned cta) {
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(dsmem_addr(local_ptr, cta)) : "memory");
+    return v;
+}
+__device__ __forceinline__ float dsmem_load_f32(const float* local_ptr, unsigned cta) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(dsmem_addr(local_ptr, cta)) : "memory");
+    return v;
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its prologue, and wait for the previous
 // kernel's memory to be visible. Both are no-ops when the launch did not opt in.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

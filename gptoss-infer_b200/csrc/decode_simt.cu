@@ -102,23 +102,6 @@ __global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks, const u
 // id (runtime/src/kernels.cu:307-324 states the same rule).
 constexpr int kRouterCluster = 8, kRouterThreads = 256, kRouterPerCta = 4;
 
-__device__ __forceinline__ void dsmem_store_f64(double* local_ptr, unsigned cta, double v) {
-    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local_ptr));
-    uint32_t ra;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(cta));
-    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(ra), "d"(v) : "memory");
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ unsigned cluster_rank() {
-    unsigned r;
-    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
 __device__ __forceinline__ double bf16_lo_d(uint32_t w) { return double(__uint_as_float(w << 16)); }
 __device__ __forceinline__ double bf16_hi_d(uint32_t w) { return double(__uint_as_float(w & 0xffff0000u)); }
 

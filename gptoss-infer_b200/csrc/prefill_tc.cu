@@ -52,7 +52,7 @@ constexpr int kPT = 2;                         // slots per A piece (one barrier
 constexpr int kPieceA = kPT * kTermA;
 constexpr int kBImg = kRows * 128;             // B tile for a 256-wide K block (32 KB)
 constexpr int kPieceB = kBImg + 4 * 512;       // + its scale chunks (2 K chunks x 2 row halves)
-constexpr int kSeg = 2;                        // K blocks per accumulation segment
+constexpr int kSeg = 2;                        // K blocks per accumulation segment (stacked plan)
 constexpr int NSA = 3, NSB = kSeg + 1;         // ring slots: A pieces, B pieces
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColSFA = kRows;            // 8 columns per term, 16 per A slot
@@ -69,78 +69,103 @@ __global__ void router_w64_kernel(const __nv_bfloat16* __restrict__ W, int E, in
     }
 }
 
-// kRtTok tokens per CTA, 512 threads: RMSNorm (warp w < kRtTok on token w), h in shared memory (fp32), then thread
-// (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp, kp + 16, ... for the CTA's tokens, chunk by chunk of
-// K: the chunk's twelve weight loads per thread are issued first, the CTA widens the chunk's h values to fp64 once
-// (exact; widening at every FMA kept the conversion pipe saturated), then each load serves all the tokens; the 16
-// partial sums (stored over h, which is dead by then) are added in order and warp w picks token w's top k on
-// order-preserving integer keys of the fp64 logits.
+// kRtTok tokens per cluster of KS CTAs (KS = 1, 2, 4 or 8: the grid is token groups x KS, cluster dims (KS, 1, 1)),
+// 512 threads per CTA. CTA q of a cluster owns the K slice [q SW, (q + 1) SW), SW = router_slice(H, KS):
+//   1. the sums of squares of its tokens over the slice (warp w < kRtTok on token w); the cluster's KS partial sums
+//      are added in rank order (distributed shared memory), so every CTA of the cluster has the same RMSNorm scale;
+//   2. h over the slice (fp32, x * rn * g as RMSNorm computes it) into shared memory and h_out;
+//   3. thread (e = tid % 32, kp = tid / 32) accumulates expert e over k = kp, kp + 16, ... of the slice, chunk by
+//      chunk of K: the chunk's twelve weight loads per thread are issued first, the CTA widens the chunk's h values to
+//      fp64 once (exact; widening at every FMA kept the conversion pipe saturated), then each load serves all tokens;
+//   4. the 16 partial sums (stored over h, which is dead by then) are added in order; CTA 0 of the cluster adds the
+//      KS slices' sums in rank order and warp w picks token w's top k on order-preserving integer keys of the fp64
+//      logits.
+// Small batches use several CTAs per token group (KS > 1), so that the router is spread over the GPU instead of
+// running through K on a few SMs; KS = 1 is one CTA per group over all of K.
 constexpr int kRtParts = 16;
 static_assert(kRtTok <= 16, "one top-k warp per token");
 constexpr int kRtAhead = 12;                   // weight loads in flight per router thread
 constexpr int kRtChunk = kRtAhead * kRtParts;  // K values widened to fp64 at a time (192)
-// Router shared memory: h (fp32, [kRtTok][H]; the partial sums go over it after the FMAs), then one chunk of h
-// widened to fp64 ([kRtTok][kRtChunk]).
-__host__ __device__ constexpr int router_chunk_off(int H) {
-    return ((kRtTok * H * 4 > kRtParts * kRtTok * 32 * 8 ? kRtTok * H * 4 : kRtParts * kRtTok * 32 * 8) + 15) & ~15;
+constexpr int kRtMaxSplit = 8;                 // CTAs per token group at most (a portable cluster size)
+// Router shared memory: h (fp32, [kRtTok][SW]; the partial sums go over it after the FMAs), one chunk of h widened to
+// fp64 ([kRtTok][kRtChunk]), the slice's logit sums ([kRtTok][32] fp64) and sums of squares ([kRtTok] fp32).
+__host__ __device__ constexpr int router_slice(int H, int KS) { return ((H / 4 + KS - 1) / KS) * 4; }
+__host__ __device__ constexpr int router_chunk_off(int H, int KS) {
+    return ((kRtTok * router_slice(H, KS) * 4 > kRtParts * kRtTok * 32 * 8 ? kRtTok * router_slice(H, KS) * 4
+                                                                             : kRtParts * kRtTok * 32 * 8) + 15) & ~15;
 }
-__host__ __device__ constexpr int router_smem_bytes(int H) { return router_chunk_off(H) + kRtTok * kRtChunk * 8; }
+__host__ __device__ constexpr int router_sum_off(int H, int KS) { return router_chunk_off(H, KS) + kRtTok * kRtChunk * 8; }
+__host__ __device__ constexpr int router_smem_bytes(int H, int KS) {
+    return router_sum_off(H, KS) + kRtTok * 32 * 8 + kRtTok * 4;
+}
 __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __restrict__ W64, const float* __restrict__ b,
                                                              const float* __restrict__ x, const float* __restrict__ g,
-                                                             float eps, int T, int E, int H, int k,
+                                                             float eps, int T, int E, int H, int k, int KS,
                                                              float* __restrict__ h_out, int* __restrict__ ids,
                                                              float* __restrict__ wts) {
     extern __shared__ __align__(16) uint8_t rt_smem[];
-    float* hs = reinterpret_cast<float*>(rt_smem);           // [kRtTok][H]
+    const int SW = router_slice(H, KS);
+    float* hs = reinterpret_cast<float*>(rt_smem);           // [kRtTok][SW]
     double (*red)[kRtTok][32] = reinterpret_cast<double (*)[kRtTok][32]>(rt_smem);   // [kRtParts]: after the FMAs
+    double* hc = reinterpret_cast<double*>(rt_smem + router_chunk_off(H, KS));       // [kRtTok][kRtChunk]
+    double (*csum)[32] = reinterpret_cast<double (*)[32]>(rt_smem + router_sum_off(H, KS));   // [kRtTok][32]
+    float* ssp = reinterpret_cast<float*>(rt_smem + router_sum_off(H, KS) + kRtTok * 32 * 8);   // [kRtTok]
     __shared__ float rn_s[kRtTok];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int t0 = blockIdx.x * kRtTok, nt = min(kRtTok, T - t0);
+    const unsigned q = KS > 1 ? cluster_rank() : 0u;
+    const int t0 = (blockIdx.x / KS) * kRtTok, nt = min(kRtTok, T - t0);
+    const int k0 = min(H, int(q) * SW), k1 = min(H, k0 + SW), w = k1 - k0;
     if (warp < nt) {
         float ss = 0.f;
         const float* xr = x + size_t(t0 + warp) * H;
-        for (int i = lane * 4; i < H; i += 128) {
+        for (int i = k0 + lane * 4; i < k1; i += 128) {
             const float4 v = *reinterpret_cast<const float4*>(xr + i);
             ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
         }
         ss = warp_sum(ss);
-        if (lane == 0) rn_s[warp] = g ? rms_scale(ss, H, eps) : 1.f;
+        if (lane == 0) ssp[warp] = ss;
+    }
+    if (KS > 1) cluster_sync_all();
+    else __syncthreads();
+    if (warp < nt && lane == 0) {
+        float tot = 0.f;
+        for (int r = 0; r < KS; ++r) tot += KS > 1 ? dsmem_load_f32(ssp + warp, unsigned(r)) : ssp[warp];
+        rn_s[warp] = g ? rms_scale(tot, H, eps) : 1.f;
     }
     __syncthreads();
-    for (int i = tid * 4; i < nt * H; i += 512 * 4) {
-        const int tb = i / H, kk = i - tb * H;
-        float4 v = *reinterpret_cast<const float4*>(x + size_t(t0) * H + i);
+    for (int i = tid * 4; i < nt * w; i += 512 * 4) {        // w % 4 == 0: a float4 never crosses a token
+        const int tb = i / w, kk = k0 + (i - tb * w);
+        float4 v = *reinterpret_cast<const float4*>(x + size_t(t0 + tb) * H + kk);
         if (g) {
             const float4 gg = *reinterpret_cast<const float4*>(g + kk);
             const float r = rn_s[tb];
             v.x = v.x * r * gg.x; v.y = v.y * r * gg.y; v.z = v.z * r * gg.z; v.w = v.w * r * gg.w;
         }
-        if (h_out) *reinterpret_cast<float4*>(h_out + size_t(t0) * H + i) = v;
-        *reinterpret_cast<float4*>(hs + i) = v;
+        if (h_out) *reinterpret_cast<float4*>(h_out + size_t(t0 + tb) * H + kk) = v;
+        *reinterpret_cast<float4*>(hs + tb * SW + (kk - k0)) = v;
     }
-    for (int i = nt * H + tid; i < kRtTok * H; i += 512) hs[i] = 0.f;
+    for (int i = nt * SW + tid; i < kRtTok * SW; i += 512) hs[i] = 0.f;
     __syncthreads();
     const int e = lane, kp = warp;
     double acc[kRtTok];
 #pragma unroll
     for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = 0.0;
-    double* hc = reinterpret_cast<double*>(rt_smem + router_chunk_off(H));   // [kRtTok][kRtChunk]
-    for (int c0 = 0; c0 < H; c0 += kRtChunk) {
+    for (int c0 = k0; c0 < k1; c0 += kRtChunk) {
         double wk[kRtAhead];
 #pragma unroll
         for (int u = 0; u < kRtAhead; ++u) {
             const int kk = c0 + kp + u * kRtParts;
-            wk[u] = kk < H ? W64[size_t(kk) * 32 + e] : 0.0;
+            wk[u] = kk < k1 ? W64[size_t(kk) * 32 + e] : 0.0;
         }
         for (int i = tid; i < kRtTok * kRtChunk; i += 512) {
             const int tb = i / kRtChunk, jj = i - tb * kRtChunk;
-            hc[i] = c0 + jj < H ? double(hs[tb * H + c0 + jj]) : 0.0;
+            hc[i] = c0 + jj < k1 ? double(hs[tb * SW + (c0 - k0) + jj]) : 0.0;
         }
         __syncthreads();
 #pragma unroll
         for (int u = 0; u < kRtAhead; ++u) {
             const int jj = kp + u * kRtParts;
-            if (c0 + jj < H) {
+            if (c0 + jj < k1) {
 #pragma unroll
                 for (int tb = 0; tb < kRtTok; ++tb) acc[tb] = fma(wk[u], hc[tb * kRtChunk + jj], acc[tb]);
             }
@@ -152,10 +177,17 @@ __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __
     for (int tb = 0; tb < kRtTok; ++tb) red[kp][tb][e] = acc[tb];
     __syncthreads();
     if (warp < nt) {
+        double v = 0.0;
+        for (int p = 0; p < kRtParts; ++p) v += red[p][warp][lane];
+        csum[warp][lane] = v;
+    }
+    if (KS > 1) cluster_sync_all();
+    else __syncthreads();
+    if (q == 0 && warp < nt) {
         const int t = t0 + warp;
         double v = 0.0;
         if (lane < E) {
-            for (int p = 0; p < kRtParts; ++p) v += red[p][warp][lane];
+            for (int r = 0; r < KS; ++r) v += KS > 1 ? dsmem_load_f64(&csum[warp][lane], unsigned(r)) : csum[warp][lane];
             v += double(b[lane]);
         }
         int sel_id = 0;
@@ -167,6 +199,7 @@ __global__ void __launch_bounds__(512, 1) router_batched_kernel(const double* __
             wts[size_t(t) * k + lane] = gate;
         }
     }
+    if (KS > 1) cluster_sync_all();                          // the slices' sums stay until CTA 0 has read them
 }
 
 // ------------------------------------------------------------------------------------------------ permute
@@ -396,6 +429,7 @@ struct GemmJob {
     int UK, KB, KT, RT;                        // K / 64, 256-wide K blocks, 128-wide K chunks, 256-row N tiles
     const uint8_t* a_img;                      // [tiles][KB][S] slots, descending terms
     int S, P;                                  // term plan: slots per (tile, K block), rows per token
+    int seg;                                   // K blocks per accumulation segment (kSeg; KB when S == 1)
     const uint8_t* b_sf;                       // [E][RT][KT][2][512]
     const int4* tiles;
     const int* n_tiles;
@@ -474,6 +508,9 @@ __device__ __forceinline__ void pack_reduce_scatter(const float (&sums)[128], in
 // smallest (NT - 1) to the largest (0), each over the segment's K blocks (whose B pieces stay resident), so the small
 // terms are added while D is still small; after each segment the epilogue warps add D into fp32 registers and D
 // restarts from zero. Term 0, the only term of full magnitude, then meets at most 4 kSeg MMAs per accumulator.
+// In the packed plan every accumulator row holds one term of one token, as in the decode kernel, and its B pieces are
+// used once each (one slot per K block): the whole K range is one segment (j.seg = KB), so the MMAs stop for the
+// epilogue's read of TMEM once per tile instead of every kSeg K blocks.
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_b,
                                                                    const __grid_constant__ GemmJob j) {
     extern __shared__ uint8_t smem_raw[];
@@ -526,8 +563,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             for (int tau = c; tau < n_tiles && ok; tau += nc) {
                 const int m = tau / j.RT, nt = tau % j.RT;
                 const int e = j.tiles[m].x;
-                for (int s0 = 0; s0 < j.KB && ok; s0 += kSeg) {
-                    const int s1 = min(j.KB, s0 + kSeg);
+                for (int s0 = 0; s0 < j.KB && ok; s0 += j.seg) {
+                    const int s1 = min(j.KB, s0 + j.seg);
                     for (int pc = 0; pc < npc && ok; ++pc)
                         for (int kb = s0; kb < s1; ++kb) {
                             if (pc == 0) {
@@ -570,8 +607,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             const bool trc = j.trace && c < 160;
             const uint32_t idesc0 = tc::idesc_mxf4(128, kRows, 0, 0), idesc2 = tc::idesc_mxf4(128, kRows, 2, 2);
             for (int tau = c; tau < n_tiles && ok; tau += nc) {
-                for (int s0 = 0; s0 < j.KB && ok; s0 += kSeg, ++seg) {
-                    const int s1 = min(j.KB, s0 + kSeg);
+                for (int s0 = 0; s0 < j.KB && ok; s0 += j.seg, ++seg) {
+                    const int s1 = min(j.KB, s0 + j.seg);
                     if (seg > 0) ok = twait(accE, uint32_t(seg - 1) & 1u, j.err, 33, trc ? &wE : nullptr);
                     for (int pc = 0; pc < npc && ok; ++pc)
                         for (int kb = s0; kb < s1; ++kb) {
@@ -646,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 #pragma unroll
             for (int i = 0; i < 128; ++i) sums[i] = 0.f;
             bool ok = true;
-            for (int s0 = 0; s0 < j.KB; s0 += kSeg, ++seg) {
+            for (int s0 = 0; s0 < j.KB; s0 += j.seg, ++seg) {
                 // One thread polls the accumulator barrier; the other epilogue warps sleep in a named barrier.
                 if (warp == 2 && lane == 0)
                     epi_flag[seg & 1] = (ok && twait(accF, uint32_t(seg) & 1u, j.err, 36, trc ? &wF : nullptr)) ? 1 : 0;
@@ -1030,12 +1067,22 @@ void launch_router_w64(const void* W, int E, int H, double* W64, cudaStream_t s)
     check_launch("router_w64");
 }
 
+// CTAs per token group of the batched router: as many (up to kRtMaxSplit, a power of two) as keep the grid within one
+// wave of SMs.
+static int router_split(int T) {
+    const int groups = (T + pf::kRtTok - 1) / pf::kRtTok, sms = num_sms();
+    int KS = 1;
+    while (KS < pf::kRtMaxSplit && groups * KS * 2 <= sms) KS *= 2;
+    return KS;
+}
+
 void launch_router_batched(const double* W64, const float* b, const float* x, const float* norm_w, float eps, int T,
                            int E, int H, int k, float* h_out, int* ids, float* wts, cudaStream_t s) {
     require(T >= 1, "router_batched: T must be positive");
     require(H % 8 == 0 && H >= 8, "router_batched: H must be a positive multiple of 8");
     require(k >= 1 && k <= 8 && k <= E && E <= 32, "router_batched: needs 1 <= k <= 8 and k <= E <= 32");
-    const int smem = pf::router_smem_bytes(H);
+    const int KS = router_split(T);
+    const int smem = pf::router_smem_bytes(H, KS);
     require(smem <= 220 * 1024, "router_batched: H too large");
     static std::mutex mu;
     static std::map<int, int> done;
@@ -1048,8 +1095,20 @@ void launch_router_batched(const double* W64, const float* b, const float* x, co
             done[dev] = smem;
         }
     }
-    pf::router_batched_kernel<<<(T + pf::kRtTok - 1) / pf::kRtTok, 512, smem, s>>>(W64, b, x, norm_w, eps, T, E, H, k,
-                                                                                   h_out, ids, wts);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(((T + pf::kRtTok - 1) / pf::kRtTok) * KS);
+    cfg.blockDim = dim3(512);
+    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(KS);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = KS > 1 ? 1 : 0;
+    GPT_CHECK(cudaLaunchKernelEx(&cfg, pf::router_batched_kernel, W64, b, x, norm_w, eps, T, E, H, k, KS, h_out, ids,
+                                 wts));
     check_launch("router_batched");
 }
 
@@ -1107,6 +1166,7 @@ void launch_moe_batched(const PrefillArgs& a, cudaStream_t s) {
         g.a_img = gu ? img_gu : img_dn;
         g.S = tp.S;
         g.P = tp.P;
+        g.seg = tp.S == 1 ? g.KB : kSeg;          // one slot per K block: B pieces are used once, any segment fits
         g.b_sf = gu ? a.sf_gu : a.sf_dn;
         g.tiles = tiles;
         g.n_tiles = n_tiles;
@@ -1245,6 +1305,7 @@ void launch_ep_layer(const EpArgs& a, cudaStream_t s) {
         g.a_img = gu ? own + L.off_img : img_dn;
         g.S = tp.S;
         g.P = tp.P;
+        g.seg = tp.S == 1 ? g.KB : kSeg;          // one slot per K block: B pieces are used once, any segment fits
         g.b_sf = gu ? a.sf_gu : a.sf_dn;
         g.tiles = tiles;
         g.n_tiles = n_tiles;

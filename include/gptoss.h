@@ -247,7 +247,7 @@ int gptoss_set_prefill_terms(int terms);
 
 /* [extension] Tile plan of the batched MoE: 1 = packed (a token's terms are 8 rows of a 128-row tile, 16 tokens per
  * tile: one MMA per K step for experts with few rows), 0 = stacked (128 tokens per tile, one MMA per term), -1 (the
- * default) = packed while the experts average at most 32 rows (T * k <= 32 * E). Both give the same results within
+ * default) = packed while the experts average at most 64 rows (T * k <= 64 * E). Both give the same results within
  * the float64 bound. Returns the previous mode, or -2 (mode outside -1 .. 1). */
 int gptoss_set_prefill_packing(int mode);
 

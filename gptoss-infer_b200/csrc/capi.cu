@@ -125,6 +125,12 @@ struct DecodeWs {
 };
 thread_local DecodeWs g_dws;
 
+// Decode MoE implementation: 0 SIMT, 1 tensor cores (the row-job kernel where its shape conditions hold, else the
+// stream-K kernel), 2 tensor cores with the stream-K kernel only.
+int g_moe_impl = 1;
+int decode_plan() { return g_moe_impl == 2 ? 1 : 0; }
+bool moe_impl_tc() { return g_moe_impl == 1 || g_moe_impl == 2; }
+
 bool tc_shape_ok(int k, int H, int I) { return k >= 1 && k <= 8 && H % 64 == 0 && I % 64 == 0 && H >= 64 && I >= 64; }
 // The tensor-core decode kernel also holds x in registers (H <= 3072).
 bool decode_tc_ok(int k, int H, int I) { return tc_shape_ok(k, H, I) && H <= 3072; }
@@ -158,9 +164,12 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
     // experts' rows are ever read.
     const CUtensorMap tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, 32, 128, gpt::kDecodeTileRows);
     const CUtensorMap td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, 32, 128, gpt::kDecodeTileRows);
+    const CUtensorMap td64 = gpt::make_tmap_u8_swz_3d(dn_blocks, I / 2, H, 32, 64, gpt::kDecodeTileRows, 64);
     gpt::DecodeTcArgs a{};
     a.tmap_gu = &tg;
     a.tmap_dn = &td;
+    a.tmap_dn64 = &td64;
+    a.plan = decode_plan();
     a.sfa_gu = reinterpret_cast<uint8_t*>(w + L.off_sfa_gu);
     a.sfa_dn = reinterpret_cast<uint8_t*>(w + L.off_sfa_dn);
     a.sfa_by_slot = 1;
@@ -179,7 +188,6 @@ void moe_tc_raw(const uint8_t* gu_blocks, const uint8_t* gu_scales, const float*
     gpt::launch_moe_decode_tc(a, s);
 }
 
-int g_moe_impl = 1;                   // 0: SIMT decode MoE, 1: tensor cores where the shape allows
 std::atomic<int> g_prefill_terms{8};   // e2m1 terms per activation in the batched MoE
 std::atomic<int> g_prefill_pack{-1};   // -1: by batch size, 0: stacked, 1: packed
 
@@ -212,6 +220,7 @@ struct gptoss_moe_layer {
     uint8_t* sfa_dn = nullptr;
     double* w64 = nullptr;                     // router weights as fp64 [H][32] for the batched router
     CUtensorMap tg, td;
+    CUtensorMap td64;                          // down blocks in 64-byte boxes (the row-job decode kernel)
     ~gptoss_moe_layer() {
         if (sfa_gu) cudaFree(sfa_gu);
         if (sfa_dn) cudaFree(sfa_dn);
@@ -240,6 +249,8 @@ void moe_layer_forward_ws(gptoss_moe_layer* l, const float* x, float* x_resid, c
     DecodeTcArgs a{};
     a.tmap_gu = &l->tg;
     a.tmap_dn = &l->td;
+    a.tmap_dn64 = &l->td64;
+    a.plan = decode_plan();
     a.sfa_gu = l->sfa_gu;
     a.sfa_dn = l->sfa_dn;
     a.sfa_by_slot = 0;
@@ -391,7 +402,7 @@ int gptoss_kernel_moe(const uint8_t* gu_blocks, const uint8_t* gu_scales, const 
                       float limit) {
     return guard([&] {
         if (k < 1 || k > 8) throw std::runtime_error("moe: k must be in 1..8");
-        if (g_moe_impl == 1 && decode_tc_ok(k, H, I)) {
+        if (moe_impl_tc() && decode_tc_ok(k, H, I)) {
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
             void* ws = g_dws.for_layout(L, k, H, I, nullptr);
             moe_tc_raw(gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, x_norm, ids, weights, x_resid, k,
@@ -485,7 +496,7 @@ int gptoss_moe_block_async(const float* x, const float* norm_w, float eps, const
         auto rec = [&](int i) {
             if (events) GPT_CHECK(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(events[i]), s, cudaEventRecordExternal));
         };
-        if (g_moe_impl == 1 && decode_tc_ok(k, H, I)) {
+        if (moe_impl_tc() && decode_tc_ok(k, H, I)) {
             // raw scales: the router runs first (its ids select which scales to repack), then the fused kernel
             const gpt::DecodeTcLayout L = gpt::decode_tc_layout(k, H, I);
             char* tw = static_cast<char*>(g_dws.for_layout(L, k, H, I, s));
@@ -521,6 +532,15 @@ int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, 
     });
 }
 
+int gptoss_selftest_mxf4_gemm_swizzle(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
+                                      const uint8_t* b_scales, float* d, int N, int K, int a_swizzle) {
+    return guard([&] {
+        const size_t bytes = size_t(1) << 22;
+        void* scratch = g_scratch.get(bytes);
+        gpt::selftest_mxf4_gemm(a_blocks, a_scales, b_blocks, b_scales, d, N, K, scratch, bytes, nullptr, a_swizzle);
+    });
+}
+
 gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const void* router_w, const float* router_b,
                                           const uint8_t* gu_blocks, const uint8_t* gu_scales, const float* gu_bias,
                                           const uint8_t* dn_blocks, const uint8_t* dn_scales, const float* dn_bias,
@@ -542,6 +562,7 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
             });
             l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
             l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
+            l->td64 = gpt::make_tmap_u8_swz_3d(dn_blocks, I / 2, H, E, 64, gpt::kDecodeTileRows, 64);
             GPT_CHECK(cudaMalloc(&l->w64, size_t(H) * 32 * sizeof(double)));
             gpt::launch_router_w64(router_w, E, H, l->w64, nullptr);
             sync_check("moe_layer_create");
@@ -893,8 +914,8 @@ int gptoss_set_prefill_packing(int mode) {
 }
 
 int gptoss_set_moe_impl(int impl) {
-    if (impl != 0 && impl != 1) {
-        g_error = "gptoss_set_moe_impl: impl must be 0 (SIMT) or 1 (tensor cores)";
+    if (impl < 0 || impl > 2) {
+        g_error = "gptoss_set_moe_impl: impl must be 0 (SIMT), 1 (tensor cores) or 2 (tensor cores, stream-K kernel)";
         return -1;
     }
     const int prev = g_moe_impl;

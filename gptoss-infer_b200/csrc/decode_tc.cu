@@ -887,6 +887,9 @@ DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     L.off_sfa_gu = o; o += al(sf_repacked_bytes(k, 2 * I, H / 32, TR));
     L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32, TR));
     L.off_misc = o; o += al(size_t(H) * 4 + 256);
+    L.off_rows = o;
+    L.rows_bytes = size_t(k) * L.RT_gu * H * 4;
+    o += al(L.rows_bytes);
     L.bytes = o;
     L.zero_bytes_from = L.off_part_gu;                        // tagged partial sums and logits, error word, barrier
     L.zero_bytes_to = L.off_err + 1024;
@@ -911,6 +914,10 @@ void set_fused_smem(int bytes) {
 
 void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s) {
     using namespace fz;
+    if (a.tmap_dn64 && a.plan == 0 && decode_rows_ok(a.k, a.H, a.I, a.router_w ? a.E : 0)) {
+        launch_moe_decode_rows(a, s);
+        return;
+    }
     require(a.k >= 1 && a.k <= kMaxK, "moe (tc): k must be in 1..8");
     require(a.H % 64 == 0 && a.I % 64 == 0, "moe (tc): H and I must be multiples of 64");
     require(a.H <= 4 * kThreads * kMaxX4, "moe (tc): H must be at most 3072 (x is held in registers)");

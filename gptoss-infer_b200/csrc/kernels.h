@@ -63,6 +63,7 @@ struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
     size_t off_logits, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
+    size_t off_rows, rows_bytes;   // the row-job kernel's partial output vectors [k * RT_gu][H] fp32
 };
 DecodeTcLayout decode_tc_layout(int k, int H, int I);
 
@@ -89,8 +90,20 @@ struct DecodeTcArgs {
     float alpha, limit;
     void* workspace;              // decode_tc_layout(k, H, I).bytes
     long long* trace = nullptr;   // optional pipeline trace: [num_sms][160] clock64 stamps
+    const CUtensorMap* tmap_dn64 = nullptr;   // down blocks [E][H][I/2] bytes in boxes of 256 rows x 64 bytes (64-byte
+                                              // swizzle): enables the row-job kernel
+    int plan = 0;                 // 0: the row-job kernel where it applies, else stream-K; 1: stream-K only
 };
+// Launches the row-job kernel (decode_rows.cu) when a.tmap_dn64 is set, a.plan == 0 and decode_rows_ok holds, else
+// the stream-K kernel (decode_tc.cu).
 void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
+
+// Row-job decode MoE (decode_rows.cu): G = k * ceil(2I / 256) CTAs, CTA c owns 256 gate/up rows of one selected expert
+// over all of K and the down K-slice of their 128 activations; one reduction of the G partial vectors at the end.
+// Needs G <= the SM count (and G >= E when the kernel runs the router).
+int decode_rows_jobs(int k, int I);
+bool decode_rows_ok(int k, int H, int I, int E_router);
+void launch_moe_decode_rows(const DecodeTcArgs& a, cudaStream_t s);
 
 // Batched (prefill) MoE on tensor cores (prefill_tc.cu). Workspace layout for T tokens.
 struct PrefillLayout {
@@ -161,10 +174,11 @@ struct EpArgs {
 void launch_ep_layer(const EpArgs& a, cudaStream_t s);
 
 // Single-CTA tcgen05 kind::mxf4 GEMM, D[128][N] = dequant(A)[128][K] . dequant(B)[N][K]^T, from raw MXFP4 arrays
-// (checkpoint layout). Pins the layout conventions of the tensor-core kernels. Synchronizes.
+// (checkpoint layout). Pins the layout conventions of the tensor-core kernels. A is loaded by TMA with the 128-byte
+// swizzle (128-byte boxes of K) or the 64-byte swizzle (64-byte boxes, a_swizzle = 64). Synchronizes.
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                         const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
-                        cudaStream_t s);
+                        cudaStream_t s, int a_swizzle = 128);
 
 // Quantizes x [n] into kDecodeTerms e2m1 residual terms (which = 0: comparison quantizer, 1: converter quantizer,
 // 2: fixed scale schedule with fp32 rounding, 3: the same with one warp per block)

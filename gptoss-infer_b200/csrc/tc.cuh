@@ -176,6 +176,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 // K-major operand in the 128-byte swizzled layout: 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) { return smem_desc(saddr, 16, 1024, 2); }
 
+// K-major operand in the 64-byte swizzled layout (64-byte rows: 64 bytes of K per row, 8-row atoms of 512 bytes; 16-byte
+// chunk j of row r at chunk position j ^ ((r / 2) % 4)), as a TMA box of 64-byte rows with the 64-byte swizzle writes
+// it. One MMA reads 32 bytes of K per row, so MMA j of a 64-byte row starts 32*j bytes in.
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr) { return smem_desc(saddr, 16, 512, 4); }
+
 // The same layout with all 8-row groups at one address (stride 0): an 8-row operand (1 KB per 128 bytes of K) read as
 // M = 128 rows, rows r and r + 8 identical; the accumulator rows repeat with period 8.
 __device__ __forceinline__ uint64_t desc_sw128_rows8(uint32_t saddr) { return smem_desc(saddr, 16, 0, 2); }
@@ -226,6 +231,25 @@ __device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, float* v) {
                  : "r"(taddr));
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Warp reads 32 lanes (its quadrant) x 16 / 32 consecutive fp32 columns: thread t gets lane (quadrant*32 + t).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 

@@ -37,11 +37,18 @@ EncodeTiled encoder() {
 }
 }  // namespace
 
-CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
-                               uint32_t box_rows) {
+namespace {
+CUtensorMapSwizzle swizzle_mode(uint32_t swizzle_bytes) {
+    require(swizzle_bytes == 64 || swizzle_bytes == 128, "TMA swizzle must be 64 or 128 bytes");
+    return swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+}
+}  // namespace
+
+CUtensorMap make_tmap_u8_swz(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                             uint32_t box_rows, uint32_t swizzle_bytes) {
     require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
     require(row_bytes % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
-    require(box_bytes <= 128 && box_bytes % 16 == 0 && box_rows >= 1 && box_rows <= 256, "bad TMA box");
+    require(box_bytes <= swizzle_bytes && box_bytes % 16 == 0 && box_rows >= 1 && box_rows <= 256, "bad TMA box");
     CUtensorMap m;
     std::memset(&m, 0, sizeof(m));
     const cuuint64_t dims[2] = {row_bytes, rows};
@@ -49,17 +56,22 @@ CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t ro
     const cuuint32_t box[2] = {box_bytes, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_mode(swizzle_bytes),
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
     return m;
 }
 
-CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
-                                  uint32_t box_bytes, uint32_t box_rows) {
+CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                               uint32_t box_rows) {
+    return make_tmap_u8_swz(base, row_bytes, rows, box_bytes, box_rows, 128);
+}
+
+CUtensorMap make_tmap_u8_swz_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
+                                uint32_t box_bytes, uint32_t box_rows, uint32_t swizzle_bytes) {
     require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
     require(row_bytes % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
-    require(box_bytes <= 128 && box_bytes % 16 == 0 && box_rows >= 1 && box_rows <= 256, "bad TMA box");
+    require(box_bytes <= swizzle_bytes && box_bytes % 16 == 0 && box_rows >= 1 && box_rows <= 256, "bad TMA box");
     CUtensorMap m;
     std::memset(&m, 0, sizeof(m));
     const cuuint64_t dims[3] = {row_bytes, rows, mats};
@@ -67,10 +79,15 @@ CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t
     const cuuint32_t box[3] = {box_bytes, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_mode(swizzle_bytes),
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3d) failed: " + std::to_string(int(r)));
     return m;
+}
+
+CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
+                                  uint32_t box_bytes, uint32_t box_rows) {
+    return make_tmap_u8_swz_3d(base, row_bytes, rows, mats, box_bytes, box_rows, 128);
 }
 
 // ---------------------------------------------------------------------------------------------------- SF repack
@@ -131,7 +148,7 @@ __global__ void __launch_bounds__(128) mxf4_selftest_kernel(const __grid_constan
                                                             const uint8_t* __restrict__ sfa,
                                                             const uint8_t* __restrict__ bimg,
                                                             const uint8_t* __restrict__ sfb, float* __restrict__ out,
-                                                            int N, int K, int* err) {
+                                                            int N, int K, int a64, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = (K + 255) / 256, KT = (K + 127) / 128, nB = N > 128 ? 2 : 1;
@@ -162,7 +179,12 @@ __global__ void __launch_bounds__(128) mxf4_selftest_kernel(const __grid_constan
             const int kt0 = 2 * s, nkt = min(2, KT - kt0);
             const uint32_t bytes = 16384 + N * 128 + nkt * 512 + nkt * nB * 512;
             tc::mbar_arrive_expect_tx(&bars[s], bytes);
-            tc::tma_load_2d(sA + s * 16384, &tmA, s * 128, 0, &bars[s]);
+            if (a64) {                           // two 64-byte-wide boxes per stage, one per K chunk of 128
+                tc::tma_load_2d(sA + s * 16384, &tmA, s * 128, 0, &bars[s]);
+                tc::tma_load_2d(sA + s * 16384 + 8192, &tmA, s * 128 + 64, 0, &bars[s]);
+            } else {
+                tc::tma_load_2d(sA + s * 16384, &tmA, s * 128, 0, &bars[s]);
+            }
             tc::bulk_g2s(sB + s * N * 128, bimg + size_t(s) * N * 128, N * 128, &bars[s]);
             tc::bulk_g2s(sSFA + kt0 * 512, sfa + size_t(kt0) * 512, nkt * 512, &bars[s]);
             tc::bulk_g2s(sSFB + kt0 * nB * 512, sfb + size_t(kt0) * nB * 512, nkt * nB * 512, &bars[s]);
@@ -181,7 +203,8 @@ __global__ void __launch_bounds__(128) mxf4_selftest_kernel(const __grid_constan
                 for (int j = 0; j < 2; ++j) {
                     const int kk = kt * 128 + j * 64;
                     if (kk >= K) break;
-                    const uint64_t ad = tc::desc_sw128(tc::smem_u32(sA + s * 16384 + (kt2 * 2 + j) * 32));
+                    const uint64_t ad = a64 ? tc::desc_sw64(tc::smem_u32(sA + s * 16384 + kt2 * 8192 + j * 32))
+                                            : tc::desc_sw128(tc::smem_u32(sA + s * 16384 + (kt2 * 2 + j) * 32));
                     const uint64_t bd = tc::desc_sw128(tc::smem_u32(sB + s * N * 128 + (kt2 * 2 + j) * 32));
                     const uint32_t sf_id = 2u * j;
                     tc::mma_mxf4(tm_d, ad, bd, tc::idesc_mxf4(128, N, sf_id, sf_id), (tm_sfa + 4 * kt) | (sf_id << 30),
@@ -294,7 +317,8 @@ double selftest_mxf4_peak(int* err_dev) {
 
 void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                         const uint8_t* b_scales, float* d, int N, int K, void* scratch, size_t scratch_bytes,
-                        cudaStream_t s) {
+                        cudaStream_t s, int a_swizzle) {
+    require(a_swizzle == 64 || a_swizzle == 128, "selftest: A's swizzle must be 64 or 128 bytes");
     require(N % 8 == 0 && N >= 8 && N <= 256, "selftest: N must be a multiple of 8 in 8..256");
     require(K % 64 == 0 && K >= 64 && K <= 1024, "selftest: K must be a multiple of 64 in 64..1024");
     const int S = (K + 255) / 256, KT = (K + 127) / 128, nB = N > 128 ? 2 : 1, G = K / 32;
@@ -327,10 +351,10 @@ void selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const 
     GPT_CHECK(cudaMemcpy(d_sfb, sfb.data(), sfb.size(), cudaMemcpyHostToDevice));
     GPT_CHECK(cudaMemset(d_err, 0, sizeof(int)));
     launch_repack_sf(a_scales, d_sfa, 1, 128, G, s);
-    const CUtensorMap tmA = make_tmap_u8_sw128(a_blocks, K / 2, 128, 128, 128);
+    const CUtensorMap tmA = make_tmap_u8_swz(a_blocks, K / 2, 128, uint32_t(a_swizzle), 128, uint32_t(a_swizzle));
     const size_t smem = 1024 + size_t(S) * 16384 + size_t(S) * N * 128 + KT * 512 + KT * nB * 512 + (S + 1) * 8 + 16;
     GPT_CHECK(cudaFuncSetAttribute(mxf4_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    mxf4_selftest_kernel<<<1, 128, smem, s>>>(tmA, d_sfa, d_img, d_sfb, d, N, K, d_err);
+    mxf4_selftest_kernel<<<1, 128, smem, s>>>(tmA, d_sfa, d_img, d_sfb, d, N, K, a_swizzle == 64 ? 1 : 0, d_err);
     check_launch("mxf4 selftest");
     GPT_CHECK(cudaStreamSynchronize(s));
     int herr = 0;

@@ -18,4 +18,11 @@ CUtensorMap make_tmap_u8_sw128(const void* base, uint64_t row_bytes, uint64_t ro
 CUtensorMap make_tmap_u8_sw128_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
                                   uint32_t box_bytes, uint32_t box_rows);
 
+// The same maps with a 64- or 128-byte swizzle (box_bytes <= swizzle_bytes): a 64-byte box of K lands in shared
+// memory as 64-byte rows in the 64-byte swizzled K-major layout (8-row atoms of 512 bytes).
+CUtensorMap make_tmap_u8_swz(const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                             uint32_t box_rows, uint32_t swizzle_bytes);
+CUtensorMap make_tmap_u8_swz_3d(const void* base, uint64_t row_bytes, uint64_t rows, uint64_t mats,
+                                uint32_t box_bytes, uint32_t box_rows, uint32_t swizzle_bytes);
+
 }  // namespace gpt

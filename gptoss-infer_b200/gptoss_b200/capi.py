@@ -47,6 +47,7 @@ SIGNATURES = {
     "gptoss_trace_enable": ([P, I64], I32),
     "gptoss_selftest_terms": ([P, I32, P, P, I32], I32),
     "gptoss_selftest_mxf4_gemm": ([P, P, P, P, P, I32, I32], I32),
+    "gptoss_selftest_mxf4_gemm_swizzle": ([P, P, P, P, P, I32, I32, I32], I32),
     "gptoss_selftest_mxf4_peak": ([P], I32),
     "gptoss_selftest_mxf4_mma_ns": ([I32, P], I32),
     "gptoss_moe_layer_create": ([P, F32, P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32], P),

@@ -203,6 +203,10 @@ int gptoss_ep_status(int E, int k, int H, int I, int world, int T_max, int* code
  * K % 64 == 0, 64 <= K <= 1024. Device pointers; synchronizes. */
 int gptoss_selftest_mxf4_gemm(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
                               const uint8_t* b_scales, float* d, int N, int K);
+/* [extension] The same with A loaded by TMA in the 64-byte swizzled layout (64-byte boxes of K, a_swizzle = 64; the
+ * layout of the decode kernel's down-projection slices) or the 128-byte one (a_swizzle = 128). */
+int gptoss_selftest_mxf4_gemm_swizzle(const uint8_t* a_blocks, const uint8_t* a_scales, const uint8_t* b_blocks,
+                                      const uint8_t* b_scales, float* d, int N, int K, int a_swizzle);
 
 /* [extension] Measures this GPU's dense block-scaled FP4 tensor rate (tcgen05.mma kind::mxf4, M = 128, N = 256,
  * K = 64, back to back on every SM, timed with CUDA events on the legacy default stream) and stores it in *tflops
@@ -234,8 +238,10 @@ int gptoss_selftest_terms(const float* x, int n, float* out, float* per_term, in
  * For tests of the wrap-around; a decode loop never needs it. */
 int gptoss_test_decode_epoch(int k, int H, int I, unsigned set_to, unsigned* previous);
 
-/* [extension] Which decode MoE implementation gptoss_kernel_moe uses: 0 = SIMT (CUDA cores), 1 = tensor cores
- * (tcgen05 block-scaled MMA) where the shape allows it. Returns the previous setting, or -1. */
+/* [extension] Which decode MoE implementation gptoss_kernel_moe, the prepared layers and the engine use: 0 = SIMT
+ * (CUDA cores), 1 = tensor cores (tcgen05 block-scaled MMA) where the shape allows it: the row-job kernel (one CTA
+ * per 256 gate/up rows of a selected expert, k * ceil(2I / 256) CTAs, at most the SM count) and otherwise the stream-K
+ * kernel (one CTA per SM); 2 = tensor cores with the stream-K kernel only. Returns the previous setting, or -1. */
 int gptoss_set_moe_impl(int impl);
 
 /* [extension] Activation terms of the batched (prefill) MoE, for every later batched and expert-parallel call in the

@@ -153,10 +153,12 @@ def small_shape_case(seed=9):
     return [gu_b, gu_s, gu_bias, dn_b, dn_s, dn_bias, x, ids, weights], resid, H, I, k
 
 
-def test_moe_tensor_cores_alternating_shapes(lib):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_moe_tensor_cores_alternating_shapes(lib, impl):
     """Two shapes alternating on one thread share its decode workspace, whose launch-to-launch state (barrier words,
     launch epoch, epoch-tagged partial sums) sits at shape-dependent offsets: every call must give the result the
-    shape gives alone (bit-identical), and the small shape must meet the float64 bound."""
+    shape gives alone (bit-identical), and the small shape must meet the float64 bound. impl 1: the row-job kernel
+    (where the shape allows it), 2: the stream-K kernel."""
     cases = [real_shape_case(), small_shape_case()]
     dev_cases = [([t.to(DEV).contiguous() for t in args], resid.to(DEV), H, I, k) for args, resid, H, I, k in cases]
 
@@ -166,7 +168,7 @@ def test_moe_tensor_cores_alternating_shapes(lib):
         ok(lib, lib.gptoss_kernel_moe(*(P(t) for t in d), P(out), k, H, I, 1.702, 7.0))
         return out.cpu()
 
-    prev = lib.gptoss_set_moe_impl(1)
+    prev = lib.gptoss_set_moe_impl(impl)
     try:
         alone = [run(0), run(0), run(1), run(1)]
         assert torch.equal(alone[0], alone[1]) and torch.equal(alone[2], alone[3])
@@ -181,7 +183,7 @@ def test_moe_tensor_cores_alternating_shapes(lib):
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
 
 
-@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("impl", [0, 1, 2])
 def test_moe_real_shape(lib, impl):
     args, resid, H, I, k = real_shape_case()
     want = omoe.kernel_moe_f64(*[a.numpy() for a in args[:6]], args[6].numpy(), args[7].numpy(), args[8].numpy(),
@@ -236,7 +238,7 @@ def config0():
     return d, g
 
 
-@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("impl", [0, 1, 2])
 def test_config0_block_vs_reference_golden(lib, config0, impl):
     """RMSNorm -> router -> MoE for each of the 4 golden tokens, against Reference.moe's own output."""
     d, g = config0
@@ -261,6 +263,14 @@ def test_config0_block_vs_reference_golden(lib, config0, impl):
         lib.gptoss_set_moe_impl(prev)
 
 
+@pytest.fixture(params=[1, 2], ids=["rows", "streamk"])
+def tc_impl(lib, request):
+    """The tensor-core decode kernel a prepared layer runs: 1 = the row-job kernel, 2 = the stream-K kernel."""
+    prev = lib.gptoss_set_moe_impl(request.param)
+    yield request.param
+    lib.gptoss_set_moe_impl(prev)
+
+
 def make_layer(lib, d, E=32, k=4):
     L = lib.gptoss_moe_layer_create(P(d["ln"]), 1e-5, P(d["W"]), P(d["b"]), *(P(e) for e in d["ex"]), E, k, 2880, 2880,
                                     1.702, 7.0)
@@ -268,7 +278,7 @@ def make_layer(lib, d, E=32, k=4):
     return L
 
 
-def test_layer_forward_config0_vs_reference_golden(lib, config0):
+def test_layer_forward_config0_vs_reference_golden(lib, config0, tc_impl):
     """Prepared layer (fused RMSNorm + router + tensor-core GEMVs) on the 4 golden tokens: x + Reference.moe(h)."""
     d, g = config0
     L = make_layer(lib, d)
@@ -284,7 +294,7 @@ def test_layer_forward_config0_vs_reference_golden(lib, config0):
         lib.gptoss_moe_layer_destroy(L)
 
 
-def test_layer_forward_is_deterministic_and_in_place(lib, config0):
+def test_layer_forward_is_deterministic_and_in_place(lib, config0, tc_impl):
     d, g = config0
     L = make_layer(lib, d)
     try:
@@ -300,7 +310,7 @@ def test_layer_forward_is_deterministic_and_in_place(lib, config0):
         lib.gptoss_moe_layer_destroy(L)
 
 
-def test_traced_kernel_matches_untraced(lib, config0):
+def test_traced_kernel_matches_untraced(lib, config0, tc_impl):
     """gptoss_trace_enable switches to the traced instantiation of the decode kernel (clock64 stamps compiled in):
     its results are bit-identical to the untraced kernel's, and it writes its stamps (slot 0 = start, slot 82 = end,
     per CTA)."""
@@ -332,7 +342,7 @@ def test_layer_create_rejects_bad_shapes(lib, config0):
     assert not L and b"k <= 8" in lib.gptoss_last_error()
 
 
-def test_layer_forward_epoch_wraps_past_zero(lib, config0):
+def test_layer_forward_epoch_wraps_past_zero(lib, config0, tc_impl):
     """The decode kernel tags split-tile partial sums with a launch epoch kept in the workspace; epoch 0 is the tag of
     a zero-filled word and must never be current. With the epoch word seeded just below the wrap, the launches run at
     epochs 0xFFFFFFFF, 1 and 2, each bit-identical to an ordinary launch."""

@@ -17,9 +17,11 @@ DEV = "cuda"
 P = capi.ptr
 
 
-@pytest.mark.parametrize("N,K", [(8, 64), (8, 576), (16, 1024), (64, 512), (128, 256), (256, 256), (24, 320),
-                                 (192, 512)])
-def test_mxf4_gemm_selftest(N, K):
+@pytest.mark.parametrize("N,K,swz", [(8, 64, 128), (8, 576, 128), (16, 1024, 128), (64, 512, 128), (128, 256, 128),
+                                     (256, 256, 128), (24, 320, 128), (192, 512, 128), (8, 64, 64), (8, 128, 64),
+                                     (8, 576, 64), (16, 1024, 64), (256, 320, 64)])
+def test_mxf4_gemm_selftest(N, K, swz):
+    """swz: A loaded with the 128-byte swizzle (128-byte boxes of K) or the 64-byte one (64-byte boxes)."""
     lib = capi.load()
     g = torch.Generator().manual_seed(N * 1000 + K)
     a_b = torch.randint(0, 256, (128, K // 32, 16), generator=g, dtype=torch.uint8)
@@ -28,7 +30,7 @@ def test_mxf4_gemm_selftest(N, K):
     b_s = torch.randint(110, 140, (N, K // 32), generator=g, dtype=torch.uint8)
     d = [t.to(DEV).contiguous() for t in (a_b, a_s, b_b, b_s)]
     out = torch.full((128, N), float("nan"), device=DEV)
-    rc = lib.gptoss_selftest_mxf4_gemm(*(P(t) for t in d), P(out), N, K)
+    rc = lib.gptoss_selftest_mxf4_gemm_swizzle(*(P(t) for t in d), P(out), N, K, swz)
     assert rc == 0, lib.gptoss_last_error().decode()
     A = mxfp4.dequant(a_b.numpy(), a_s.numpy()).astype(np.float64)
     B = mxfp4.dequant(b_b.numpy(), b_s.numpy()).astype(np.float64)

@@ -221,7 +221,9 @@ struct gptoss_moe_layer {
     double* w64 = nullptr;                     // router weights as fp64 [H][32] for the batched router
     CUtensorMap tg, td;
     CUtensorMap td64;                          // down blocks in 64-byte boxes (the row-job decode kernel)
+    uint8_t* dn_img = nullptr;                 // the row-job kernel's pre-packed down stages
     ~gptoss_moe_layer() {
+        if (dn_img) cudaFree(dn_img);
         if (sfa_gu) cudaFree(sfa_gu);
         if (sfa_dn) cudaFree(sfa_dn);
         if (w64) cudaFree(w64);
@@ -251,6 +253,7 @@ void moe_layer_forward_ws(gptoss_moe_layer* l, const float* x, float* x_resid, c
     a.tmap_dn = &l->td;
     a.tmap_dn64 = &l->td64;
     a.plan = decode_plan();
+    a.dn_img = l->dn_img;
     a.sfa_gu = l->sfa_gu;
     a.sfa_dn = l->sfa_dn;
     a.sfa_by_slot = 0;
@@ -563,6 +566,10 @@ gptoss_moe_layer* gptoss_moe_layer_create(const float* norm_w, float eps, const 
             l->tg = gpt::make_tmap_u8_sw128_3d(gu_blocks, H / 2, 2 * I, E, 128, gpt::kDecodeTileRows);
             l->td = gpt::make_tmap_u8_sw128_3d(dn_blocks, I / 2, H, E, 128, gpt::kDecodeTileRows);
             l->td64 = gpt::make_tmap_u8_swz_3d(dn_blocks, I / 2, H, E, 64, gpt::kDecodeTileRows, 64);
+            if (gpt::decode_rows_ok(k, H, I, E)) {    // the row-job kernel's down stages, one bulk copy each
+                GPT_CHECK(cudaMalloc(&l->dn_img, gpt::down_jobs_bytes(E, H, I)));
+                gpt::launch_pack_down_jobs(dn_blocks, l->sfa_dn, l->dn_img, E, H, I, nullptr);
+            }
             GPT_CHECK(cudaMalloc(&l->w64, size_t(H) * 32 * sizeof(double)));
             gpt::launch_router_w64(router_w, E, H, l->w64, nullptr);
             sync_check("moe_layer_create");

@@ -91,6 +91,7 @@ struct Job {
     const float* dn_bias;                     // [E][H]
     float alpha, limit;
     float* part;                              // [G][H] partial output vectors
+    const uint8_t* dn_img;                    // pre-packed down stages [E][RT][NP][kSlot], or null (TMA boxes)
     uint8_t* xq_img;                          // x's terms [SPS][NT*128]
     uint8_t* xq_sf;                           // their scales [KT_gu][128]
     float* x_resid;
@@ -378,6 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
                     tc::tma_load_3d(dst, &tm_gu, it * 128, rt * kRows, e, &fullB[slot]);
                     tc::bulk_g2s(dst + kGu, j.sf_gu + ((size_t(mat) * j.RT + rt) * j.KT_gu + 2 * it) * 1024,
                                  uint32_t(nkt * 1024), &fullB[slot]);
+                } else if (j.dn_img) {                  // down, pre-packed: the stage's two boxes and scales at once
+                    const int p = it - j.SPS;
+                    tc::mbar_arrive_expect_tx(&fullB[slot], uint32_t(kSlot));
+                    tc::bulk_g2s(dst, j.dn_img + ((size_t(e) * j.RT + rt) * j.NP + p) * kSlot, uint32_t(kSlot),
+                                 &fullB[slot]);
                 } else {                                // down: row boxes d0, d0 + 1, K bytes [64 rt, +64)
                     const int d0 = 2 * (it - j.SPS), nb = min(2, j.RD - d0);
                     tc::mbar_arrive_expect_tx(&fullB[slot], uint32_t(nb * (kDn + 1024)));
@@ -393,18 +399,29 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer (one lane of warp 1)
+        // One thread issues every tcgen05 operation; its cost per operation bounds the stage rate (the tensor pipe
+        // itself needs ~55 cycles per M = 128, N = 8 MMA and ~47 per scale copy), so every descriptor is a base
+        // computed once plus a byte offset / 16 (shared-memory addresses stay below 256 KB: the 14-bit start field
+        // never carries), and the common stages are fully unrolled.
         if (tc::elect_one()) {
             bool ok = true;
             int slot = 0, f = 0;
-            uint32_t ph = 0;
+            uint32_t ph = 0, so = 0;                 // ring slot, its phase, its byte offset
             auto advance = [&]() {
+                so += kSlot;
                 if (++slot == NS) {
                     slot = 0;
+                    so = 0;
                     ph ^= 1u;
                 }
                 if (++f == NSF) f = 0;
             };
-            // gate/up: per stage the weight scales (nkt K chunks x 2 halves), then per unit of K = 64 one MMA per half
+            const uint64_t dA128 = tc::desc_sw128(tc::smem_u32(ring)), dA64 = tc::desc_sw64(tc::smem_u32(ring));
+            const uint64_t dBx = tc::desc_sw128(tc::smem_u32(xA)), dBd = tc::desc_sw128(tc::smem_u32(dA));
+            const uint64_t dSFw = tc::desc_sf_chunk(tc::smem_u32(ring)), dSFx = tc::desc_sf_chunk8(tc::smem_u32(xSF));
+            constexpr uint32_t id0 = tc::idesc_mxf4(128, NT, 0, 0), id2 = tc::idesc_mxf4(128, NT, 2, 2);
+            const uint32_t colXs = tmem + j.L.colXs;
+            // gate/up: per stage x's and the weights' scale chunks, then per unit of K = 64 one MMA per 128-row half
             for (int it = 0; it < j.SPS && ok; ++it, advance()) {
                 const int nu = min(4, j.UK - 4 * it), nkt = (nu + 1) / 2;
                 if (it == 0) ok = tc::mbar_wait(fullS, 0, j.err, 6);
@@ -412,38 +429,44 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
                 if (!ok) break;
                 tc::tc_fence_after();
                 if (it < 32) stamp<kTrace>(j, 34 + it);
-                const uint8_t* wslot = ring + slot * kSlot;
                 const uint32_t col = tmem + j.L.colW + 16u * uint32_t(f);
-                for (int q = 0; q < nkt; ++q)            // x's scale chunks of this stage
-                    tc::tmem_cp_sf(tmem + j.L.colXs + 4 * (2 * it + q),
-                                   tc::desc_sf_chunk8(tc::smem_u32(xSF + (2 * it + q) * kSF8)));
-                for (int x = 0; x < 2 * nkt; ++x)
-                    tc::tmem_cp_sf(col + 4 * x, tc::desc_sf_chunk(tc::smem_u32(wslot + kGu + x * 512)));
-                const uint8_t* xa = xA + it * kA;
-                auto one = [&](int u) {
-                    const uint32_t sf = 2u * uint32_t(u & 1), q = uint32_t(u >> 1);
-                    const uint64_t bd = tc::desc_sw128(tc::smem_u32(xa + u * 32));
-                    const uint32_t sfb = (tmem + j.L.colXs + 4u * uint32_t(2 * it + int(q))) | (sf << 30);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        tc::mma_mxf4(tmem + kColGu + 8u * h, tc::desc_sw128(tc::smem_u32(wslot + h * 16384 + u * 32)),
-                                     bd, tc::idesc_mxf4(128, NT, sf, sf), (col + 4u * (2u * q + h)) | (sf << 30), sfb,
-                                     it > 0 || u > 0);
-                };
+                const uint64_t aB = dA128 + (so >> 4), bB = dBx + uint64_t(it) * (kA >> 4),
+                               sfw = dSFw + ((so + kGu) >> 4), sfx = dSFx + uint64_t(2 * it) * (kSF8 >> 4);
+                const uint32_t cx = colXs + 8u * uint32_t(it);
                 if (nu == 4) {
+                    tc::tmem_cp_sf(cx, sfx);
+                    tc::tmem_cp_sf(cx + 4, sfx + (kSF8 >> 4));
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) one(u);
+                    for (int x = 0; x < 4; ++x) tc::tmem_cp_sf(col + 4 * x, sfw + 32 * x);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint32_t sfb = (cx + 4u * (u >> 1)) | ((u & 1) ? (2u << 30) : 0u);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            tc::mma_mxf4(tmem + kColGu + 8u * h, aB + 1024 * h + 2 * u, bB + 2 * u, (u & 1) ? id2 : id0,
+                                         (col + 4u * (2u * (u >> 1) + h)) | ((u & 1) ? (2u << 30) : 0u), sfb,
+                                         it > 0 || u > 0);
+                    }
                 } else {
-                    for (int u = 0; u < nu; ++u) one(u);
+                    for (int q = 0; q < nkt; ++q) tc::tmem_cp_sf(cx + 4 * q, sfx + q * (kSF8 >> 4));
+                    for (int x = 0; x < 2 * nkt; ++x) tc::tmem_cp_sf(col + 4 * x, sfw + 32 * x);
+                    for (int u = 0; u < nu; ++u) {
+                        const uint32_t sfhi = (u & 1) ? (2u << 30) : 0u;
+                        for (int h = 0; h < 2; ++h)
+                            tc::mma_mxf4(tmem + kColGu + 8u * h, aB + 1024 * h + 2 * u, bB + 2 * u, (u & 1) ? id2 : id0,
+                                         (col + 4u * (2u * (u >> 1) + h)) | sfhi, (cx + 4u * (u >> 1)) | sfhi,
+                                         it > 0 || u > 0);
+                    }
                 }
                 tc::mma_commit(&emptyB[slot]);
             }
             tc::mma_commit(accF);                    // (also when a wait gave up: the epilogue is not held)
             // down: the job's activations (down's operand, written by the epilogue warps) against every row box
             ok = ok && tc::mbar_wait(dReady, 0, j.err, 9);
+            const uint32_t cds = tmem + j.L.colDs;
             if (ok) {
                 tc::tc_fence_after();
-                tc::tmem_cp_sf(tmem + j.L.colDs, tc::desc_sf_chunk8(tc::smem_u32(dSF)));
+                tc::tmem_cp_sf(cds, tc::desc_sf_chunk8(tc::smem_u32(dSF)));
             }
             // Down stage p: row boxes 2p, 2p + 1 (rows [512 p, +512)); its accumulators are committed to accD[p] so the
             // epilogue reads them out while the next stages stream.
@@ -454,22 +477,31 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
                 if (!ok) break;
                 tc::tc_fence_after();
                 if (j.SPS + p < 32) stamp<kTrace>(j, 34 + j.SPS + p);
-                const uint8_t* wslot = ring + slot * kSlot;
                 const uint32_t col = tmem + j.L.colW + 16u * uint32_t(f);
+                const uint64_t aB = dA64 + (so >> 4), sfw = dSFw + ((so + 2 * kDn) >> 4);
+                const uint32_t acc = tmem + kColDn + 32u * uint32_t(p);
                 const int nb = min(2, j.RD - 2 * p);
-                for (int b = 0; b < nb; ++b) {
-                    const int d = 2 * p + b, nh = d * kRows + 128 < j.H ? 2 : 1;
-                    for (int h = 0; h < nh; ++h)
-                        tc::tmem_cp_sf(col + 4 * (2 * b + h),
-                                       tc::desc_sf_chunk(tc::smem_u32(wslot + 2 * kDn + b * 1024 + h * 512)));
-                    for (int u = 0; u < nu_dn; ++u) {
-                        const uint32_t sf = 2u * uint32_t(u);
-                        const uint64_t bd = tc::desc_sw128(tc::smem_u32(dA + u * 32));
-                        for (int h = 0; h < nh; ++h)
-                            tc::mma_mxf4(tmem + kColDn + 16u * d + 8u * h,
-                                         tc::desc_sw64(tc::smem_u32(wslot + b * kDn + h * 8192 + u * 32)), bd,
-                                         tc::idesc_mxf4(128, NT, sf, sf), (col + 4u * (2 * b + h)) | (sf << 30),
-                                         (tmem + j.L.colDs) | (sf << 30), u > 0);
+                if (nb == 2 && (2 * p + 1) * kRows + 128 < j.H && nu_dn == 2) {   // the common stage, unrolled
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) tc::tmem_cp_sf(col + 4 * x, sfw + 32 * x);
+#pragma unroll
+                    for (int b = 0; b < 2; ++b)
+#pragma unroll
+                        for (int u = 0; u < 2; ++u)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h)
+                                tc::mma_mxf4(acc + 16u * b + 8u * h, aB + (b * kDn + h * 8192) / 16 + 2 * u, dBd + 2 * u,
+                                             u ? id2 : id0, (col + 4u * (2 * b + h)) | (u ? (2u << 30) : 0u),
+                                             cds | (u ? (2u << 30) : 0u), u > 0);
+                } else {
+                    for (int b = 0; b < nb; ++b) {
+                        const int d = 2 * p + b, nh = d * kRows + 128 < j.H ? 2 : 1;
+                        for (int h = 0; h < nh; ++h) tc::tmem_cp_sf(col + 4 * (2 * b + h), sfw + 64 * b + 32 * h);
+                        for (int u = 0; u < nu_dn; ++u)
+                            for (int h = 0; h < nh; ++h)
+                                tc::mma_mxf4(acc + 16u * b + 8u * h, aB + (b * kDn + h * 8192) / 16 + 2 * u, dBd + 2 * u,
+                                             u ? id2 : id0, (col + 4u * (2 * b + h)) | (u ? (2u << 30) : 0u),
+                                             cds | (u ? (2u << 30) : 0u), u > 0);
                     }
                 }
                 tc::mma_commit(&emptyB[slot]);
@@ -693,10 +725,62 @@ Layout make_layout(int NS, int SPS, int KT_gu, int RD) {
     return L;
 }
 
+
+// Pre-packed down stages: for expert e, job rt (activations [128 rt, +128)) and stage p (row boxes 2p, 2p + 1), the
+// shared-memory image of the stage exactly as the TMA path lands it: box b (256 rows x 64 bytes, the 64-byte swizzle:
+// 16-byte chunk ch of row r at chunk position ch ^ ((r / 2) % 4)) at b * 16 KB, then box b's two scale chunks (the
+// layer's repacked chunks of row tile 2p + b, K chunk rt) at 32 KB + b * 1 KB. Rows past H and bytes past I / 2 are
+// zero. One thread per 16 bytes of output.
+__global__ void pack_down_jobs_kernel(const uint8_t* __restrict__ blocks, const uint8_t* __restrict__ sf_rep,
+                                      uint8_t* __restrict__ out, int E, int H, int I, int RT, int NP, int RT_dn,
+                                      int KT_dn) {
+    const long long per_stage = kSlot / 16, total = (long long)E * RT * NP * per_stage;
+    const int row_bytes = I / 2;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int w = int(i % per_stage);
+        long long st = i / per_stage;
+        const int p = int(st % NP);
+        st /= NP;
+        const int rt = int(st % RT);
+        const int e = int(st / RT);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (w < 2 * kDn / 16) {                              // weight bytes
+            const int b = w / (kDn / 16), o = (w % (kDn / 16)) * 16;
+            const int r = o / 64, pos = (o % 64) / 16, ch = pos ^ ((r >> 1) & 3);
+            const int row = (2 * p + b) * kRows + r, col = 64 * rt + 16 * ch;
+            if (row < H && col < row_bytes)
+                v = *reinterpret_cast<const uint4*>(blocks + ((size_t(e) * H + row) * row_bytes + col));
+        } else {                                             // scale chunks
+            const int o = (w - 2 * kDn / 16) * 16, b = o / 1024, d = 2 * p + b;
+            if (d < RT_dn)
+                v = *reinterpret_cast<const uint4*>(sf_rep + ((size_t(e) * RT_dn + d) * KT_dn + rt) * 1024 + o % 1024);
+        }
+        reinterpret_cast<uint4*>(out)[i] = v;
+    }
+}
+
 }  // namespace rj
 
 // ---------------------------------------------------------------------------------------------------- host API
 int decode_rows_jobs(int k, int I) { return k * ((2 * I + rj::kRows - 1) / rj::kRows); }
+
+size_t down_jobs_bytes(int E, int H, int I) {
+    const int RT = (2 * I + rj::kRows - 1) / rj::kRows, RD = (H + rj::kRows - 1) / rj::kRows;
+    return size_t(E) * RT * ((RD + 1) / 2) * rj::kSlot;
+}
+
+void launch_pack_down_jobs(const uint8_t* dn_blocks, const uint8_t* sf_dn_repacked, uint8_t* out, int E, int H, int I,
+                           cudaStream_t s) {
+    require(H % 64 == 0 && I % 64 == 0, "pack_down_jobs: H and I must be multiples of 64");
+    const int RT = (2 * I + rj::kRows - 1) / rj::kRows, RD = (H + rj::kRows - 1) / rj::kRows;
+    const int RT_dn = (H + kDecodeTileRows - 1) / kDecodeTileRows, KT_dn = (I / 32 + 3) / 4;
+    const long long n16 = (long long)down_jobs_bytes(E, H, I) / 16;
+    const int grid = int(std::min<long long>((n16 + 255) / 256, num_sms() * 16LL));
+    rj::pack_down_jobs_kernel<<<std::max(1, grid), 256, 0, s>>>(dn_blocks, sf_dn_repacked, out, E, H, I, RT,
+                                                                (RD + 1) / 2, RT_dn, KT_dn);
+    check_launch("pack_down_jobs");
+}
 
 bool decode_rows_ok(int k, int H, int I, int E_router) {
     const int G = decode_rows_jobs(k, I);
@@ -761,6 +845,11 @@ void launch_moe_decode_rows(const DecodeTcArgs& a, cudaStream_t s) {
     j.alpha = a.alpha;
     j.limit = a.limit;
     j.part = reinterpret_cast<float*>(ws + W.off_rows);
+#ifdef GPTOSS_NO_DOWN_IMAGE
+    j.dn_img = nullptr;                     // (A/B builds: the TMA path of the down stages)
+#else
+    j.dn_img = a.dn_img;
+#endif
     j.xq_img = ws + W.off_xq_img;
     j.xq_sf = ws + W.off_xq_sf;
     j.x_resid = a.x_resid;

@@ -93,6 +93,7 @@ struct DecodeTcArgs {
     const CUtensorMap* tmap_dn64 = nullptr;   // down blocks [E][H][I/2] bytes in boxes of 256 rows x 64 bytes (64-byte
                                               // swizzle): enables the row-job kernel
     int plan = 0;                 // 0: the row-job kernel where it applies, else stream-K; 1: stream-K only
+    const uint8_t* dn_img = nullptr;   // the row-job kernel's pre-packed down stages (launch_pack_down_jobs), or null
 };
 // Launches the row-job kernel (decode_rows.cu) when a.tmap_dn64 is set, a.plan == 0 and decode_rows_ok holds, else
 // the stream-K kernel (decode_tc.cu).
@@ -104,6 +105,12 @@ void launch_moe_decode_tc(const DecodeTcArgs& a, cudaStream_t s);
 int decode_rows_jobs(int k, int I);
 bool decode_rows_ok(int k, int H, int I, int E_router);
 void launch_moe_decode_rows(const DecodeTcArgs& a, cudaStream_t s);
+// The row-job kernel's down weights pre-packed per (expert, job, stage): each stage's two 256-row x 64-byte boxes in
+// their 64-byte-swizzled shared-memory image and their scale chunks (from the layer's repacked down scales), so one
+// contiguous bulk copy brings a stage. down_jobs_bytes(E, H, I) bytes.
+size_t down_jobs_bytes(int E, int H, int I);
+void launch_pack_down_jobs(const uint8_t* dn_blocks, const uint8_t* sf_dn_repacked, uint8_t* out, int E, int H, int I,
+                           cudaStream_t s);
 
 // Batched (prefill) MoE on tensor cores (prefill_tc.cu). Workspace layout for T tokens.
 struct PrefillLayout {

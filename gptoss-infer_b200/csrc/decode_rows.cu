@@ -62,6 +62,12 @@ constexpr unsigned kLogitPollNs = GPTOSS_LOGIT_POLL_NS;   // pause between two p
 // Where x's terms are made: 0 in phase 0 from the registers that hold h (each CTA its blocks), counted after phase 0;
 // 1 right after phase 0 by one epilogue warp from h recomputed from global memory; 2 the same after the expert ids.
 constexpr int kXPlan = GPTOSS_X_PLAN;
+#ifndef GPTOSS_STAGE_COUNTS
+#define GPTOSS_STAGE_COUNTS 0
+#endif
+// 1: the partial sums are counted per down stage (reductions of early rows start before the last stage is done);
+// 0: one count after the whole down phase.
+constexpr bool kStageCounts = GPTOSS_STAGE_COUNTS != 0;
 constexpr uint32_t kColGu = 0;                // gate/up accumulator: 2 halves x 8 columns
 constexpr uint32_t kColDn = 16;               // down accumulators: row box d, half h at 16 d + 8 h
 
@@ -95,7 +101,8 @@ struct Job {
     uint8_t* xq_img;                          // x's terms [SPS][NT*128]
     uint8_t* xq_sf;                           // their scales [KT_gu][128]
     float* x_resid;
-    unsigned* gbar;                           // [5]: partial vectors done, exits, -, x blocks written, last epoch
+    unsigned* gbar;                           // [16]: -, exits, -, x blocks written, last epoch, -, -, -, then per down
+                                              // stage p at [8 + p] the CTAs whose partial sums of its rows are stored
     unsigned long long* logit_words;          // [32][2] router logit e as (epoch << 32) | high and low 32 bits
     int* err;
     long long* trace;                         // optional [grid][kTraceSlots] clock64 stamps
@@ -180,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
     uint64_t* accF = fullS + 1;               // gate/up accumulator complete
     uint64_t* dReady = accF + 1;              // down's operand written (128 arrivals)
     uint64_t* accD = dReady + 1;              // [NP] down stage p's accumulators complete
+    uint64_t* pDone = accD + kMaxPairs;       // [NP] down stage p's partial sums stored (128 arrivals)
     uint32_t* holder = reinterpret_cast<uint32_t*>(smem + j.L.misc);
     double* red = reinterpret_cast<double*>(holder + 8);     // [8] router sums
     int* ids_s = reinterpret_cast<int*>(red + 8);            // [8]
@@ -225,7 +233,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         tc::mbar_init(fullS, 1);
         tc::mbar_init(accF, 1);
         tc::mbar_init(dReady, 128);
-        for (int p = 0; p < j.NP; ++p) tc::mbar_init(&accD[p], 1);
+        for (int p = 0; p < j.NP; ++p) {
+            tc::mbar_init(&accD[p], 1);
+            tc::mbar_init(&pDone[p], 128);
+        }
         tc::fence_barrier_init();
     }
     if (warp == 1) {
@@ -397,6 +408,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
             }
             __syncwarp();
         }
+        // Then, per down stage p, once the epilogue warps have stored this CTA's partial sums of its rows: one
+        // release of gbar[8 + p] (the CTAs that reduce those rows wait for the count to reach G). The epilogue warps
+        // arrive on pDone[p] also when a wait gave up, so this never blocks them.
+        // (The mbarrier wait acquires the epilogue threads' stores at CTA scope; the GPU-scope release that follows
+        // is cumulative, so a CTA that acquires the count sees them.)
+        if constexpr (kStageCounts) {
+            for (int p = 0; p < j.NP; ++p) {
+                __all_sync(kFull, tc::mbar_wait(&pDone[p], 0, j.err, 15));
+                if (lane == 0) red_add_release(&j.gbar[8 + p], 1u);
+                __syncwarp();
+            }
+        }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer (one lane of warp 1)
         // One thread issues every tcgen05 operation; its cost per operation bounds the stage rate (the tensor pipe
@@ -557,6 +580,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         if constexpr (kXPlan == 2) x_exchange();
         const int e = ids_s[s_job];
         const float gate = w_s[s_job];
+        // the first row group's weighted down biases and residual for the final reduction, read early
+        float pre_b = 0.f, pre_x = 0.f;
+        if (et < 32 && c * 32 + et < j.H) {
+            const int row = c * 32 + et;
+            for (int s2 = 0; s2 < j.k; ++s2) pre_b = fmaf(w_s[s2], __ldg(j.dn_bias + size_t(ids_s[s2]) * j.H + row), pre_b);
+            pre_x = j.x_resid[row];
+        }
         // gate/up: this thread's rows of the job's tile are r_h = 128 h + 32 quad + lane (h = 0, 1); an even row is a
         // glu row, the odd row after it (the next lane) its linear row.
         float bias[2];
@@ -603,48 +633,47 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
             float* prow = j.part + size_t(c) * j.H;
             for (int p = 0; p < j.NP; ++p) {
                 ok = __all_sync(kFull, ok && tc::mbar_wait(&accD[p], 0, j.err, 14));
-                if (!ok) continue;
-                tc::tc_fence_after();
-                uint32_t v[32];
-                tc::tmem_ld_32x32b_x32(lane_base + kColDn + 32u * p, v);
-                tc::tmem_ld_wait();
+                if (ok) {
+                    tc::tc_fence_after();
+                    uint32_t v[32];
+                    tc::tmem_ld_32x32b_x32(lane_base + kColDn + 32u * p, v);
+                    tc::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int d = 2 * p + i / 2, r0 = d * kRows + 128 * (i & 1) + 32 * quad;   // warp-uniform
-                    if (d < j.RD && r0 < j.H) prow[r0 + lane] = term_sum(v + 8 * i);
+                    for (int i = 0; i < 4; ++i) {
+                        const int d = 2 * p + i / 2, r0 = d * kRows + 128 * (i & 1) + 32 * quad;   // warp-uniform
+                        if (d < j.RD && r0 < j.H) prow[r0 + lane] = term_sum(v + 8 * i);
+                    }
                 }
+                if constexpr (kStageCounts) tc::mbar_arrive(&pDone[p]);   // the stores above precede warp 0's count
                 if (et == 0 && p < 8) stamp<kTrace>(j, 140 + p);
             }
         }
         ok = epi_all(ok);
-        // the first row group's weighted down biases and residual, read before the grid-wide count is awaited
-        float pre_b = 0.f, pre_x = 0.f;
-        if (et < 32 && c * 32 + et < j.H) {
-            const int row = c * 32 + et;
-            for (int s2 = 0; s2 < j.k; ++s2) pre_b = fmaf(w_s[s2], __ldg(j.dn_bias + size_t(ids_s[s2]) * j.H + row), pre_b);
-            pre_x = j.x_resid[row];
-        }
         tc::tc_fence_before();
-        epi_sync();                                  // every thread's partial-vector stores precede the release
-        if (et == 0) {
-            stamp<kTrace>(j, 133);
-            red_add_release(&j.gbar[0], 1u);
-            bool done = false;
-            for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
-                done = ld_acquire(&j.gbar[0]) >= unsigned(nc);
-                if (!done) __nanosleep(32);
-            }
-            if (!done) atomicCAS(j.err, 0, 8);
-            *flag_s = done ? 1 : 0;
-            stamp<kTrace>(j, 81);
+        if (et == 0) stamp<kTrace>(j, 133);
+        if constexpr (!kStageCounts) {               // one count of the CTAs whose partial vectors are complete
+            epi_sync();
+            if (et == 0) red_add_release(&j.gbar[8], 1u);
         }
-        epi_sync();
-        if (*flag_s && ok) {
-            // 32-row group g (g = c, c + G, ...): thread et reads rows 32 g + 4 (et % 8) .. + 3 (one 16-byte load per
-            // job) of jobs et / 8, et / 8 + 16, ..., all loads issued before any addition; the 16 job-lane sums
-            // are then added in job-lane order with the weighted biases and the residual.
+        if (ok) {
+            // 32-row group g (g = c, c + G, ...), in down stage g / 16: once every CTA has stored its partial sums of
+            // that stage (gbar[8 + g / 16] = G), thread et reads rows 32 g + 4 (et % 8) .. + 3 (one 16-byte load per
+            // job) of jobs et / 8, et / 8 + 16, ..., all loads issued before any addition; the 16 job-lane sums are
+            // then added in job-lane order with the weighted biases and the residual.
             const int rq = et & 7, jl = et >> 3;
             for (int g = c; g * 32 < j.H; g += nc) {
+                if (et == 0) {
+                    bool done = false;
+                    for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
+                        done = ld_acquire(&j.gbar[kStageCounts ? 8 + g / 16 : 8]) >= unsigned(nc);
+                        if (!done) __nanosleep(32);
+                    }
+                    if (!done) atomicCAS(j.err, 0, 8);
+                    *flag_s = done ? 1 : 0;
+                    if (g == c) stamp<kTrace>(j, 81);
+                }
+                epi_sync();
+                if (!*flag_s) break;                 // (uniform) gave up: the error word says so
                 const int row4 = g * 32 + 4 * rq;
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (row4 < j.H) {
@@ -691,8 +720,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         stamp<kTrace>(j, 82);
         __threadfence();
         if (atomicAdd(&j.gbar[1], 1u) == unsigned(nc - 1)) {   // last CTA out resets the counters
-            j.gbar[0] = 0;
             j.gbar[3] = 0;
+            for (int p = 0; p < j.NP; ++p) j.gbar[8 + p] = 0;
             j.gbar[4] = ep;                                  // the next launch's epoch is this + 1
             j.gbar[1] = 0;
         }
@@ -718,7 +747,7 @@ Layout make_layout(int NS, int SPS, int KT_gu, int RD) {
     L.dSF = o; o += kSF8;
     L.act = o; o += 128 * 4;
     L.red4 = o; o += 16 * 32 * 4;
-    L.bars = o; o += (2 * NS + 3 + kMaxPairs) * 8;
+    L.bars = o; o += (2 * NS + 3 + 2 * kMaxPairs) * 8;
     o = (o + 15) & ~15;
     L.misc = o; o += 32 + 8 * 8 + 2 * kMaxK * 4 + 8 * 4 + 16;
     L.bytes = 1024 + o;

@@ -68,6 +68,12 @@ constexpr int kXPlan = GPTOSS_X_PLAN;
 // 1: the partial sums are counted per down stage (reductions of early rows start before the last stage is done);
 // 0: one count after the whole down phase.
 constexpr bool kStageCounts = GPTOSS_STAGE_COUNTS != 0;
+#ifndef GPTOSS_TAGGED_PARTIALS
+#define GPTOSS_TAGGED_PARTIALS 1
+#endif
+// 1: partial sums travel as 64-bit words (launch epoch << 32) | fp32 bits, which the reducing CTAs poll directly (no
+// count, no release fence); 0: fp32 words behind one grid-wide count.
+constexpr bool kTagged = GPTOSS_TAGGED_PARTIALS != 0;
 constexpr uint32_t kColGu = 0;                // gate/up accumulator: 2 halves x 8 columns
 constexpr uint32_t kColDn = 16;               // down accumulators: row box d, half h at 16 d + 8 h
 
@@ -96,7 +102,7 @@ struct Job {
     const float* gu_bias;                     // [E][2I]
     const float* dn_bias;                     // [E][H]
     float alpha, limit;
-    float* part;                              // [G][H] partial output vectors
+    float* part;                              // [G][H] partial output vectors (fp32, or 64-bit tagged words)
     const uint8_t* dn_img;                    // pre-packed down stages [E][RT][NP][kSlot], or null (TMA boxes)
     uint8_t* xq_img;                          // x's terms [SPS][NT*128]
     uint8_t* xq_sf;                           // their scales [KT_gu][128]
@@ -330,6 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
 
     if (warp == 0) {
         // ---------------------------------------------------------------- expert ids, then the TMA producer
+        int sel_id = 0;
+        double sel_logit = 0.0;
         if (j.router_w) {
             unsigned long long w0 = 0, w1 = 0;
             bool done = false;
@@ -344,30 +352,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
             if (!done && lane == 0) atomicCAS(j.err, 0, 10);
             const double v = __longlong_as_double(static_cast<long long>((w0 << 32) | (w1 & 0xFFFFFFFFull)));
             if (lane == 0) stamp<kTrace>(j, 120);
-            int sel_id = 0;
-            double sel_logit = 0.0;
             warp_topk_logits(v, lane < j.E, j.k, sel_id, sel_logit);
             if (lane == 0) stamp<kTrace>(j, 121);
-            const float gate = warp_pick_softmax(sel_logit, j.k);
-            if (lane == 0) stamp<kTrace>(j, 122);
-            if (lane < j.k) {
-                ids_s[lane] = sel_id;
-                w_s[lane] = gate;
-                if (j.ids_out && c == 0) { j.ids_out[lane] = sel_id; j.w_out[lane] = gate; }
-            }
-        } else if (lane < j.k) {
-            ids_s[lane] = j.ids_in[lane];
-            w_s[lane] = j.w_in[lane];
         }
-        __syncwarp();
-        asm volatile("bar.arrive 3, 160;" ::: "memory");   // ids known: release the epilogue warps
-        if (lane == 0) stamp<kTrace>(j, 88);
+        // The job's expert is known: the loads start now; the gate weights (the softmax over the k picks), which
+        // only the epilogue needs, are computed after the ring's first loads are issued (publish below).
+        const int e = j.router_w ? __shfl_sync(kFull, sel_id, s_job) : __ldg(j.ids_in + s_job);
+        bool published = false;
+        auto publish = [&]() {
+            if (j.router_w) {
+                const float gate = warp_pick_softmax(sel_logit, j.k);
+                if (lane == 0) stamp<kTrace>(j, 122);
+                if (lane < j.k) {
+                    ids_s[lane] = sel_id;
+                    w_s[lane] = gate;
+                    if (j.ids_out && c == 0) { j.ids_out[lane] = sel_id; j.w_out[lane] = gate; }
+                }
+            } else if (lane < j.k) {
+                ids_s[lane] = j.ids_in[lane];
+                w_s[lane] = j.w_in[lane];
+            }
+            __syncwarp();
+            asm volatile("bar.arrive 3, 160;" ::: "memory");   // ids and gate weights known: release the epilogue
+            if (lane == 0) stamp<kTrace>(j, 88);
+            published = true;
+        };
         if (tc::elect_one()) {
             tc::prefetch_tmap(&tm_gu);
             tc::prefetch_tmap(&tm_dn);
         }
         __syncwarp();
-        const int e = ids_s[s_job];
         const int mat = j.sf_by_slot ? s_job : e;
         int slot = 0;
         uint32_t ph = 0;
@@ -381,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         const int nst = j.SPS + j.NP;
         for (int it = 0; it < nst && ok; ++it, next_slot()) {
             if (it >= NS) ok = __all_sync(kFull, tc::mbar_wait(&emptyB[slot], ph ^ 1u, j.err, 1));
+            __syncwarp();
             if (ok && tc::elect_one()) {
                 if (it < 32) stamp<kTrace>(j, 2 + it);
                 uint8_t* dst = ring + slot * kSlot;
@@ -407,7 +422,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
                 }
             }
             __syncwarp();
+            if (!published) publish();               // after the first stage's loads (measured best)
         }
+        if (!published) publish();                   // no stage issued: the epilogue warps are released all the same
         // Then, per down stage p, once the epilogue warps have stored this CTA's partial sums of its rows: one
         // release of gbar[8 + p] (the CTAs that reduce those rows wait for the count to reach G). The epilogue warps
         // arrive on pDone[p] also when a wait gave up, so this never blocks them.
@@ -630,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         // Stage p's four accumulators (row boxes 2p, 2p + 1) are read out as soon as its MMAs complete.
         {
             const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
-            float* prow = j.part + size_t(c) * j.H;
+            float* prow = j.part + size_t(c) * j.H * (kTagged ? 2 : 1);
             for (int p = 0; p < j.NP; ++p) {
                 ok = __all_sync(kFull, ok && tc::mbar_wait(&accD[p], 0, j.err, 14));
                 if (ok) {
@@ -641,7 +658,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int d = 2 * p + i / 2, r0 = d * kRows + 128 * (i & 1) + 32 * quad;   // warp-uniform
-                        if (d < j.RD && r0 < j.H) prow[r0 + lane] = term_sum(v + 8 * i);
+                        if (d < j.RD && r0 < j.H) {
+                            if constexpr (kTagged)
+                                st_relaxed64(reinterpret_cast<unsigned long long*>(prow) + r0 + lane,
+                                             (static_cast<unsigned long long>(ep) << 32) |
+                                                 __float_as_uint(term_sum(v + 8 * i)));
+                            else
+                                prow[r0 + lane] = term_sum(v + 8 * i);
+                        }
                     }
                 }
                 if constexpr (kStageCounts) tc::mbar_arrive(&pDone[p]);   // the stores above precede warp 0's count
@@ -651,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
         ok = epi_all(ok);
         tc::tc_fence_before();
         if (et == 0) stamp<kTrace>(j, 133);
-        if constexpr (!kStageCounts) {               // one count of the CTAs whose partial vectors are complete
+        if constexpr (!kStageCounts && !kTagged) {   // one count of the CTAs whose partial vectors are complete
             epi_sync();
             if (et == 0) red_add_release(&j.gbar[8], 1u);
         }
@@ -662,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
             // then added in job-lane order with the weighted biases and the residual.
             const int rq = et & 7, jl = et >> 3;
             for (int g = c; g * 32 < j.H; g += nc) {
-                if (et == 0) {
+                if (!kTagged && et == 0) {
                     bool done = false;
                     for (uint32_t w = 0; w < tc::kSpinLimit && !done; ++w) {
                         done = ld_acquire(&j.gbar[kStageCounts ? 8 + g / 16 : 8]) >= unsigned(nc);
@@ -672,6 +696,52 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
                     *flag_s = done ? 1 : 0;
                     if (g == c) stamp<kTrace>(j, 81);
                 }
+                if constexpr (kTagged) {
+                    // the 4 rows of this thread from jobs jl, jl + 16, ...: every word is loaded, then the ones not
+                    // yet tagged with this launch's epoch are loaded again (bounded) until all are current
+                    const int row4 = g * 32 + 4 * rq;
+                    constexpr int kMaxLoads = (160 + 15) / 16;
+                    unsigned long long w[kMaxLoads][4];
+                    const unsigned long long* base = reinterpret_cast<const unsigned long long*>(j.part) + row4;
+                    const unsigned long long cur = static_cast<unsigned long long>(ep);
+#pragma unroll
+                    for (int i = 0; i < kMaxLoads; ++i)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int jb = jl + 16 * i;
+                            w[i][q] = (jb < nc && row4 < j.H) ? ld_relaxed64(base + size_t(jb) * j.H + q) : (cur << 32);
+                        }
+                    bool done = false;
+                    for (uint32_t t = 0; t < tc::kSpinLimit; ++t) {
+                        done = true;
+#pragma unroll
+                        for (int i = 0; i < kMaxLoads; ++i)
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) done = done && (w[i][q] >> 32) == cur;
+                        if (done) break;
+                        __nanosleep(32);
+#pragma unroll
+                        for (int i = 0; i < kMaxLoads; ++i)
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                if ((w[i][q] >> 32) != cur) w[i][q] = ld_relaxed64(base + size_t(jl + 16 * i) * j.H + q);
+                    }
+                    done = epi_all(done);
+                    if (!done) {
+                        if (et == 0) atomicCAS(j.err, 0, 8);
+                        break;                       // (uniform) gave up: the error word says so
+                    }
+                    if (et == 0 && g == c) stamp<kTrace>(j, 81);
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < kMaxLoads; ++i) {
+                        acc.x += __uint_as_float(unsigned(w[i][0]));
+                        acc.y += __uint_as_float(unsigned(w[i][1]));
+                        acc.z += __uint_as_float(unsigned(w[i][2]));
+                        acc.w += __uint_as_float(unsigned(w[i][3]));
+                    }
+                    *reinterpret_cast<float4*>(red16 + jl * 32 + 4 * rq) = acc;
+                } else {
                 epi_sync();
                 if (!*flag_s) break;                 // (uniform) gave up: the error word says so
                 const int row4 = g * 32 + 4 * rq;
@@ -694,6 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_rows_kernel(const __grid_cons
                     }
                 }
                 *reinterpret_cast<float4*>(red16 + jl * 32 + 4 * rq) = acc;
+                }
                 epi_sync();
                 if (et == 0 && g == c) stamp<kTrace>(j, 134);
                 const int row = g * 32 + et;
@@ -886,7 +957,7 @@ void launch_moe_decode_rows(const DecodeTcArgs& a, cudaStream_t s) {
     j.gbar = reinterpret_cast<unsigned*>(ws + W.off_err + 256);
     j.logit_words = reinterpret_cast<unsigned long long*>(ws + W.off_logits);
     j.trace = a.trace;
-    require(j.RT == W.RT_gu && size_t(j.G) * a.H * 4 <= W.rows_bytes, "moe (rows): workspace layout mismatch");
+    require(j.RT == W.RT_gu && size_t(j.G) * a.H * 8 <= W.rows_bytes, "moe (rows): workspace layout mismatch");
     int NS = 6;
     Layout L = make_layout(NS, j.SPS, j.KT_gu, j.RD);
     while (L.bytes > 227 * 1024 && NS > 2) L = make_layout(--NS, j.SPS, j.KT_gu, j.RD);

@@ -888,7 +888,7 @@ DecodeTcLayout decode_tc_layout(int k, int H, int I) {
     L.off_sfa_dn = o; o += al(sf_repacked_bytes(k, H, I / 32, TR));
     L.off_misc = o; o += al(size_t(H) * 4 + 256);
     L.off_rows = o;
-    L.rows_bytes = size_t(k) * L.RT_gu * H * 4;
+    L.rows_bytes = size_t(k) * L.RT_gu * H * 8;
     o += al(L.rows_bytes);
     L.bytes = o;
     L.zero_bytes_from = L.off_part_gu;                        // tagged partial sums and logits, error word, barrier

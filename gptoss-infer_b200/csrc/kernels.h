@@ -63,7 +63,7 @@ struct DecodeTcLayout {
     int SPS_gu, KT_gu, SPS_dn, KT_dn, RT_gu, RT_dn;
     size_t off_logits, off_xq_img, off_xq_sf, off_aq_img, off_aq_sf, off_part_gu, off_part_dn, off_err;
     size_t off_sfa_gu, off_sfa_dn, off_misc, bytes, zero_bytes_from, zero_bytes_to;
-    size_t off_rows, rows_bytes;   // the row-job kernel's partial output vectors [k * RT_gu][H] fp32
+    size_t off_rows, rows_bytes;   // the row-job kernel's partial output vectors [k * RT_gu][H] (64-bit words)
 };
 DecodeTcLayout decode_tc_layout(int k, int H, int I);
 

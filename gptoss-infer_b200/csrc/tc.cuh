@@ -128,6 +128,17 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, in
         : "memory");
 }
 
+// L2 prefetches (no shared memory, no completion): a 3-D tensor box, and a contiguous range (16-byte aligned, size a
+// multiple of 16).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap), "r"(x), "r"(y),
+                 "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -7,8 +7,8 @@ real 20b layer shape:
   * bit-identical to gptoss_kernel_moe on the CUDA-core path (the same kernels, only the scratch differs);
   * against the float64 oracle (oracle/moe.py kernel_moe_f64, applied twice): rtol 1e-4 / atol 1e-3 (the
     reference's runtime/tests/test_kernels.py:174 bound) and max-abs <= 2e-5 * max|x_resid|;
-  * the tensor-core path of gptoss_kernel_moe against the same oracle and bound, and the two paths against each
-    other within the sum of their bounds.
+  * the tensor-core path of gptoss_kernel_moe against the same oracle and bound (its absolute part scaled with the
+    output above 1e3), and the two paths against each other within the sum of their bounds.
 Shapes past the fixed scratch (k * I > 8 * 3072) must fail with -1 and a message. This file is collected last, so a
 run that stops at the first failure has run every other test before it.
 """
@@ -91,9 +91,13 @@ def test_static_scratch_matches_tensor_core_path(case):
     finally:
         lib.gptoss_set_moe_impl(prev)
     want = oracle_twice(case)
-    np.testing.assert_allclose(tc, want, rtol=1e-4, atol=1e-3)
+    # The tensor-core path sums 4 x 23 partial output vectors in fp32 (one per 256-row job), so its absolute error
+    # follows the output's scale: this case's outputs reach ~3.5e3 (scales up to 2^-1, against the reference test's
+    # 2^-4), where atol 1e-3 is 4 fp32 spacings. The absolute bound grows with max|want| / 1e3 above that scale.
+    atol = 1e-3 * max(1.0, np.abs(want).max() / 1e3)
+    np.testing.assert_allclose(tc, want, rtol=1e-4, atol=atol)
     assert np.abs(tc - want).max() <= 2e-5 * np.abs(want).max()
-    np.testing.assert_allclose(got, tc, rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(got, tc, rtol=2e-4, atol=1e-3 + atol)
     assert np.abs(got - tc).max() <= 4e-5 * np.abs(tc).max()
 
 

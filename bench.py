@@ -327,8 +327,10 @@ def run_decode(args, ctx, lib):
         raise RuntimeError(lib.gptoss_last_error().decode())
     layers, t0 = make_layers(args.layers, dev)
     impl = args.moe_impl if args.moe_impl is not None else 1
+    # the prepared layer's tensor-core kernel: impl 1 the row-job kernel (default), impl 2 the stream-K kernel
+    kname = "moe_fused_kernel" if impl == 2 else "moe_rows_kernel"
     handles = []
-    if impl == 1:
+    if impl in (1, 2):
         for L in layers:
             hdl = lib.gptoss_moe_layer_create(P(L["ln"]), 1e-5, P(L["W"]), P(L["b"]), *(P(e) for e in L["ex"]), E,
                                               K_TOP, H, I, 1.702, 7.0)
@@ -411,10 +413,9 @@ def run_decode(args, ctx, lib):
         # the timed region launches nothing but the fused kernel (one per layer) and one 11.5 KB copy per step, so
         # its average launch duration is the timed region's time over its launches (an upper bound: it includes the
         # gaps between launches); the event-bracketed figure is kept beside it
-        kernel_us = {"moe_fused_kernel": ms / args.steps / args.layers * 1e3,
-                     "moe_fused_kernel_event_bracketed": part_us[2]}
+        kernel_us = {kname: ms / args.steps / args.layers * 1e3, kname + "_event_bracketed": part_us[2]}
         top_us, top_name, top_bytes = (ms / args.steps / args.layers * 1e3,
-                                       "moe_fused_kernel (RMSNorm + router + gate/up + down)", LAYER_BYTES)
+                                       kname + " (RMSNorm + router + gate/up + down)", LAYER_BYTES)
     else:
         kernel_us = {"router+rmsnorm": part_us[0], "gate_up": part_us[1], "down+combine": part_us[2]}
         top_us, top_name, top_bytes = part_us[1], "gateup_simt_kernel", GATEUP_BYTES
@@ -458,7 +459,7 @@ def run_decode(args, ctx, lib):
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("moe_fused_kernel" if handles else "gateup_simt_kernel")
+        traffic = json.loads(tf.read_text()).get(kname if handles else "gateup_simt_kernel")
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",

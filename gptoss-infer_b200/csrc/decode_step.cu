@@ -31,16 +31,33 @@ __device__ __forceinline__ float bf16_hi_f(uint32_t w) { return __uint_as_float(
 // Every CTA stages x' (fp32) in shared memory (computing the norm itself when g is given: one read of x from L2).
 // A warp takes kRows rows at a time; lane l reads the rows' 16-byte chunks l, l + 32, ... with streaming loads (all
 // loads of a row group issued before the FMAs) and accumulates in packed fp32 pairs; warp_sum ends each row.
+// The weights do not depend on the previous kernel, so before the dependency wait every warp asks L2 for its first
+// pf_groups row groups (one bulk prefetch per row) and the next kernel's launch is released: a CTA that is resident
+// while the previous kernel still runs (programmatic dependent launch) streams its rows into L2 meanwhile.
 constexpr int kGemvThreads = 256, kRows = 2, kChunksInFlight = 8;
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ W,
                                                                     const float* __restrict__ x,
                                                                     const float* __restrict__ g, float eps,
                                                                     const float* __restrict__ bias,
-                                                                    const float* resid, float* y, int N, int K) {
+                                                                    const float* resid, float* y, int N, int K,
+                                                                    int pf_groups) {
     extern __shared__ float xs[];                               // [K]
     __shared__ float part[kGemvThreads / 32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gw = blockIdx.x * (kGemvThreads / 32) + warp, nw = gridDim.x * (kGemvThreads / 32);
+    {
+        // K % 8 == 0: every row starts on a 16-byte boundary and is a multiple of 16 bytes long
+        int g = 0;
+        for (int row0 = gw * kRows; row0 < N && g < pf_groups; row0 += nw * kRows, ++g)
+            if (lane < kRows && row0 + lane < N)
+                prefetch_l2_bulk(W + size_t(row0 + lane) * K, uint32_t(K) * 2u);
+    }
+    pdl_launch_dependents();
     pdl_wait();                                                 // x comes from the previous kernel
     if (g) {
         float ss = 0.f;
@@ -65,10 +82,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_b
             *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
     }
     __syncthreads();
-    pdl_launch_dependents();
     const int K8 = K >> 3;
     const uint4* Wv = reinterpret_cast<const uint4*>(W);
-    const int gw = blockIdx.x * (kGemvThreads / 32) + warp, nw = gridDim.x * (kGemvThreads / 32);
     for (int row0 = gw * kRows; row0 < N; row0 += nw * kRows) {
         float2 acc[kRows];
 #pragma unroll
@@ -370,72 +385,255 @@ __device__ __forceinline__ float2 rotate_pair(float x1, float x2, float c, float
     return make_float2(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)), __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
 }
 
-// The attention of one decode step in one launch (the engine's path): CTA (h, s) rotates its 8 query heads from the
-// raw QKV output itself; the CTA whose key range holds the new position also rotates that position's key, rounds key
-// and value to fp16, stores them into the cache and uses those values for the position (the cache is read through
-// the non-coherent path, which need not see this kernel's own stores). The last CTA of each key/value head to finish
-// (a per-head counter, reset by that CTA) merges the head's partials with the sinks.
-__global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const float* __restrict__ qkv,
-                                                                      const float* __restrict__ cos_t,
-                                                                      const float* __restrict__ sin_t,
-                                                                      __half* kc, __half* vc,
-                                                                      const float* __restrict__ sinks,
-                                                                      const int* d_pos, int window,
-                                                                      float* part, unsigned* counters, float* out) {
-    __shared__ AttnShared sh;
-    __shared__ __align__(16) __half newk[kHeadDim], newv[kHeadDim];
+// The attention of one decode step in one launch (the engine's path), grid (8 key/value heads, nsplit):
+//   * before the dependency wait (the cache of older positions and the device position were written by kernels that
+//     completed before this one was launched: every kernel of the step waits for its predecessor before it ends),
+//     CTA (h, s) computes its range of visible keys and starts asynchronous copies of their keys and values into
+//     shared memory (up to kStepCap keys per pass), then releases the next kernel's launch;
+//   * after the wait it rotates its 8 query heads from the raw QKV output (query in registers, 8 dims of the 8 heads
+//     per lane); the CTA whose range holds the new position rotates that position's key, rounds key and value to
+//     fp16, appends them to the cache and uses those values for the position;
+//   * scores (an 8-lane group per key), the running softmax per query head (warp) and p·v (a lane per 2 dims);
+//   * the last CTA of each key/value head to finish (a per-head counter, reset by that CTA) merges the head's
+//     partials with the sinks.
+// nsplit (<= kStepMaxSplits) is chosen per launch: many splits for a full-context layer, few for a window layer.
+constexpr int kStepCap = 144, kStepMaxSplits = 32;
+
+struct StepShared {
+    __align__(16) uint8_t ks[kStepCap * 128];                   // keys of the pass, 128 bytes (64 fp16) each
+    __align__(16) uint8_t vs[kStepCap * 128];
+    __align__(16) float ps[kGroup][kStepCap];                   // scores, then exp(score - m_new)
+    __align__(16) __half newkv[2][kHeadDim];                    // the new position's key and value (fp16)
+    float cm[kGroup], cl[kGroup], scale_old[kGroup];
+};
+
+// m, l at [(h * kStepMaxSplits + s) * 8 + g] (two arrays), acc [.. * 64] after them; counters after the partials
+struct StepPartials {
+    float* base;
+    __device__ __forceinline__ size_t idx(int h, int s) const { return (size_t(h) * kStepMaxSplits + s) * kGroup; }
+    __device__ __forceinline__ float* m() const { return base; }
+    __device__ __forceinline__ float* l() const { return base + kKvHeads * kStepMaxSplits * kGroup; }
+    __device__ __forceinline__ float* acc() const { return base + 2 * kKvHeads * kStepMaxSplits * kGroup; }
+};
+
+__device__ __forceinline__ void cp_async16_cg(void* smem_dst, const void* gsrc) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_step_kernel(const float* __restrict__ qkv,
+                                                                         const float* __restrict__ cos_t,
+                                                                         const float* __restrict__ sin_t,
+                                                                         __half* kc, __half* vc,
+                                                                         const float* __restrict__ sinks,
+                                                                         const int* d_pos, int window, int nsplit,
+                                                                         float* part, unsigned* counters,
+                                                                         float* out) {
+    __shared__ StepShared sh;
     __shared__ bool last;
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, qh = warp, sub = lane & 7;
     const int h = blockIdx.x, sp = blockIdx.y;
-    pdl_wait();
-    pdl_launch_dependents();
     const int pos = *d_pos;
-    int first, n, k0, k1;
-    visible_range(pos, window, sp, first, n, k0, k1);
+    const int n = window > 0 ? min(pos + 1, window) : pos + 1, first = pos + 1 - n;
+    const int L = (n + nsplit - 1) / nsplit, k0 = min(n, sp * L), k1 = min(n, k0 + L);
     const bool holds_new = k0 <= n - 1 && n - 1 < k1;
+    const uint8_t* kcb = reinterpret_cast<const uint8_t*>(kc);
+    const uint8_t* vcb = reinterpret_cast<const uint8_t*>(vc);
+    // keys [c0, c0 + len) of the range into shared memory (all but the new position's), asynchronously
+    auto stage = [&](int c0, int len) {
+        for (int i = tid; i < len * 8; i += kAttnThreads) {
+            const int kk = i >> 3, part16 = i & 7;
+            if (c0 + kk == n - 1) continue;
+            const int p = first + c0 + kk;
+            const size_t slot = window > 0 ? size_t(p % window) : size_t(p);
+            const size_t off = (slot * kKvHeads + h) * kHeadDim * 2 + part16 * 16;
+            cp_async16_cg(sh.ks + kk * 128 + part16 * 16, kcb + off);
+            cp_async16_cg(sh.vs + kk * 128 + part16 * 16, vcb + off);
+        }
+    };
+    stage(k0, min(kStepCap, k1 - k0));
+    if (tid < kGroup) {
+        sh.cm[tid] = -INFINITY;
+        sh.cl[tid] = 0.f;
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    // query heads: lane (sub = lane % 8) keeps dims 8 sub .. 8 sub + 7 of all 8 heads; warp j rotates head j's pairs
+    // into the score buffer first (as a staging area), the new key / value go to newkv
+    float qr[kGroup][8];
     {
-        const int j = tid >> 5, i = lane;                        // query head h*8 + j, rotary pair i
-        const float c = cos_t[size_t(pos) * kPairs + i], sn = sin_t[size_t(pos) * kPairs + i];
-        const float* base = qkv + (h * kGroup + j) * kHeadDim;
-        const float2 r = rotate_pair(base[i], base[i + kPairs], c, sn);
-        sh.qs[j][i] = r.x;
-        sh.qs[j][i + kPairs] = r.y;
-        if (holds_new && j == 0) {
+        const float c = cos_t[size_t(pos) * kPairs + lane], sn = sin_t[size_t(pos) * kPairs + lane];
+        const float* base = qkv + (h * kGroup + warp) * kHeadDim;
+        const float2 r = rotate_pair(base[lane], base[lane + kPairs], c, sn);
+        sh.ps[warp][lane] = r.x;
+        sh.ps[warp][lane + kPairs] = r.y;
+        if (holds_new && warp == 0) {
             const float* kb = qkv + (kHeads + h) * kHeadDim;
-            const float2 rk = rotate_pair(kb[i], kb[i + kPairs], c, sn);
-            newk[i] = __float2half_rn(rk.x);
-            newk[i + kPairs] = __float2half_rn(rk.y);
-        } else if (holds_new && j == 1) {
+            const float2 rk = rotate_pair(kb[lane], kb[lane + kPairs], c, sn);
+            sh.newkv[0][lane] = __float2half_rn(rk.x);
+            sh.newkv[0][lane + kPairs] = __float2half_rn(rk.y);
+        } else if (holds_new && warp == 1) {
             const float* vb = qkv + (kHeads + kKvHeads + h) * kHeadDim;
-            newv[i] = __float2half_rn(vb[i]);
-            newv[i + kPairs] = __float2half_rn(vb[i + kPairs]);
+            sh.newkv[1][lane] = __float2half_rn(vb[lane]);
+            sh.newkv[1][lane + kPairs] = __float2half_rn(vb[lane + kPairs]);
         }
     }
     __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qr[g][e] = sh.ps[g][sub * 8 + e];
     if (holds_new && tid < 16) {                                // the new position's key and value into the cache
         const size_t slot = window > 0 ? size_t(pos % window) : size_t(pos);
-        const size_t off = (slot * kKvHeads + h) * kHeadDim * 2;
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(tid < 8 ? newk : newv) + (tid & 7) * 16;
-        uint8_t* dst = reinterpret_cast<uint8_t*>(tid < 8 ? kc : vc) + off + (tid & 7) * 16;
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        const size_t off = (slot * kKvHeads + h) * kHeadDim * 2 + (tid & 7) * 16;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(tid < 8 ? kc : vc) + off;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const uint8_t*>(sh.newkv[tid >> 3]) + (tid & 7) * 16);
     }
-    const float2 acc = attend_keys(sh, k0, k1, [&](int kk, int part16, uint4& kw, uint4& vw) {
-        if (kk == n - 1) {
-            kw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(newk) + part16 * 16);
-            vw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(newv) + part16 * 16);
-        } else {
-            load_cache_kv(kc, vc, h, first + kk, window, part16, kw, vw);
+    float2 acc = make_float2(0.f, 0.f);
+    for (int c0 = k0; c0 < k1; c0 += kStepCap) {
+        const int len = min(kStepCap, k1 - c0);
+        if (c0 != k0) stage(c0, len);
+        cp_async_commit_wait_all();
+        __syncthreads();                                        // every copy landed; qr read before ps is reused
+        if (c0 <= n - 1 && n - 1 < c0 + len && tid < 16)        // the new position from this kernel's own rotation
+            *reinterpret_cast<uint4*>((tid < 8 ? sh.ks : sh.vs) + (n - 1 - c0) * 128 + (tid & 7) * 16) =
+                *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(sh.newkv[tid >> 3]) + (tid & 7) * 16);
+        __syncthreads();
+        // scores: an 8-lane group per key (each lane 8 dims of the 8 heads), 4 keys per warp pass; the group's partial
+        // dots are reduced so that lane j of the group ends with head j's dot
+        for (int kb = warp * 4; kb < len; kb += (kAttnThreads / 32) * 4) {
+            const int kk = kb + (lane >> 3);
+            float d[kGroup];
+            {
+                const uint4 u = kk < len ? *reinterpret_cast<const uint4*>(sh.ks + kk * 128 + sub * 16)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+                float kv[8];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[t]));
+                    kv[2 * t] = f.x;
+                    kv[2 * t + 1] = f.y;
+                }
+#pragma unroll
+                for (int g = 0; g < kGroup; ++g) {
+                    float t = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) t = fmaf(qr[g][e], kv[e], t);
+                    d[g] = t;
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const bool up = sub & 4;
+                const float recv = __shfl_xor_sync(kFull, up ? d[g] : d[g + 4], 4);
+                d[g] = (up ? d[g + 4] : d[g]) + recv;
+            }
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                const bool up = sub & 2;
+                const float recv = __shfl_xor_sync(kFull, up ? d[g] : d[g + 2], 2);
+                d[g] = (up ? d[g + 2] : d[g]) + recv;
+            }
+            {
+                const bool up = sub & 1;
+                const float recv = __shfl_xor_sync(kFull, up ? d[0] : d[1], 1);
+                d[0] = (up ? d[1] : d[0]) + recv;
+            }
+            if (kk < len) sh.ps[sub][kk] = d[0] * 0.125f;          // scale 1 / sqrt(64)
         }
-    });
-    const AttnPartials P{part, 1};
-    store_partials(sh, P, 0, h, sp, acc);
+        __syncthreads();
+        // per query head (warp qh): chunk max, new running max, exp, chunk sum
+        {
+            float m = -INFINITY;
+            for (int kk = lane; kk < len; kk += 32) m = fmaxf(m, sh.ps[qh][kk]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+            const float m_old = sh.cm[qh], m_new = fmaxf(m_old, m);
+            float ssum = 0.f;
+            for (int kk = lane; kk < len; kk += 32) {
+                const float e = expf(sh.ps[qh][kk] - m_new);
+                sh.ps[qh][kk] = e;
+                ssum += e;
+            }
+            ssum = warp_sum(ssum);
+            const float a = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+            __syncwarp();
+            if (lane == 0) {
+                sh.cl[qh] = sh.cl[qh] * a + ssum;
+                sh.cm[qh] = m_new;
+            }
+            // acc = acc exp(m_old - m_new) + sum_k p v (two accumulator pairs, keys in fours)
+            float2 acc2 = make_float2(0.f, 0.f);
+            acc.x *= a;
+            acc.y *= a;
+            const uint8_t* vrow = sh.vs + lane * 4;
+            int kk = 0;
+            for (; kk + 4 <= len; kk += 4) {
+                const float4 p4 = *reinterpret_cast<const float4*>(&sh.ps[qh][kk]);
+                const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(vrow + (kk + 0) * 128));
+                const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(vrow + (kk + 1) * 128));
+                const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(vrow + (kk + 2) * 128));
+                const float2 v3 = __half22float2(*reinterpret_cast<const __half2*>(vrow + (kk + 3) * 128));
+                acc.x = fmaf(p4.x, v0.x, acc.x);
+                acc.y = fmaf(p4.x, v0.y, acc.y);
+                acc2.x = fmaf(p4.y, v1.x, acc2.x);
+                acc2.y = fmaf(p4.y, v1.y, acc2.y);
+                acc.x = fmaf(p4.z, v2.x, acc.x);
+                acc.y = fmaf(p4.z, v2.y, acc.y);
+                acc2.x = fmaf(p4.w, v3.x, acc2.x);
+                acc2.y = fmaf(p4.w, v3.y, acc2.y);
+            }
+            for (; kk < len; ++kk) {
+                const float p = sh.ps[qh][kk];
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(vrow + kk * 128));
+                acc.x = fmaf(p, v.x, acc.x);
+                acc.y = fmaf(p, v.y, acc.y);
+            }
+            acc.x += acc2.x;
+            acc.y += acc2.y;
+        }
+        __syncthreads();                                        // the pass's buffers are refilled next
+    }
+    const StepPartials P{part};
+    {
+        const size_t b = P.idx(h, sp) + qh;
+        if (lane == 0) {
+            P.m()[b] = sh.cm[qh];
+            P.l()[b] = sh.cl[qh];
+        }
+        *reinterpret_cast<float2*>(P.acc() + b * kHeadDim + 2 * lane) = acc;
+    }
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = atomicAdd(counters + h, 1u) == unsigned(kSplits - 1);
+    if (tid == 0) last = atomicAdd(counters + h, 1u) == unsigned(nsplit - 1);
     __syncthreads();
     if (!last) return;
     __threadfence();
-    merge_partials(P, 0, h, sinks, out);
+    {
+        const int head = h * kGroup + qh;
+        const float sink = sinks[head];
+        float M = sink;
+        for (int s2 = 0; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(P.m() + P.idx(h, s2) + qh));
+        float l = expf(sink - M);
+        float2 o = make_float2(0.f, 0.f);
+        for (int s2 = 0; s2 < nsplit; ++s2) {
+            const size_t b = P.idx(h, s2) + qh;
+            const float m = __ldcg(P.m() + b);
+            if (m == -INFINITY) continue;                       // a range with no keys
+            const float a = expf(m - M);
+            l = fmaf(__ldcg(P.l() + b), a, l);
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(P.acc() + b * kHeadDim + 2 * lane));
+            o.x = fmaf(v.x, a, o.x);
+            o.y = fmaf(v.y, a, o.y);
+        }
+        const float inv = 1.f / l;
+        *reinterpret_cast<float2*>(out + size_t(head) * kHeadDim + 2 * lane) = make_float2(o.x * inv, o.y * inv);
+    }
     if (tid == 0) counters[h] = 0;
 }
 
@@ -707,8 +905,10 @@ void launch_gemv_bf16(const void* W, const float* x, const float* norm_w, float 
     }
     const int warps_needed = (N + ds::kRows - 1) / ds::kRows;
     const int grid = std::max(1, std::min(num_sms() * 2, (warps_needed + 7) / 8));
+    // matrices that fit in a half of L2 are prefetched whole, larger ones (the LM head) one row group per warp
+    const int pf_groups = size_t(N) * K * 2 <= (size_t(64) << 20) ? INT_MAX : 1;
     ds::launch(ds::gemv_bf16_kernel, dim3(grid), dim3(ds::kGemvThreads), smem, s, pdl,
-               static_cast<const __nv_bfloat16*>(W), x, norm_w, eps, bias, resid, y, N, K);
+               static_cast<const __nv_bfloat16*>(W), x, norm_w, eps, bias, resid, y, N, K, pf_groups);
 }
 
 void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, const int* d_pos, int pos, void* k_cache,
@@ -718,9 +918,10 @@ void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, cons
                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), window);
 }
 
-// partials (m, l, acc) of every (head, split), then 8 per-head counters (zero-filled before the first use)
+// partials (m, l, acc) of every (head, split), then 8 per-head counters (zero-filled before the first use); sized
+// for the larger of the step kernel's and the two-kernel attention's split counts
 size_t attention_workspace_floats() {
-    return size_t(ds::kKvHeads) * ds::kSplits * ds::kGroup * (2 + ds::kHeadDim) + 16;
+    return size_t(ds::kKvHeads) * std::max(ds::kSplits, ds::kStepMaxSplits) * ds::kGroup * (2 + ds::kHeadDim) + 16;
 }
 
 void launch_attention_step(const float* qkv, const float* cos_t, const float* sin_t, void* k_cache, void* v_cache,
@@ -728,9 +929,12 @@ void launch_attention_step(const float* qkv, const float* cos_t, const float* si
                            bool pdl) {
     require(window >= 0, "attention: window must be >= 0");
     unsigned* counters = reinterpret_cast<unsigned*>(part + (attention_workspace_floats() - 16));
-    ds::launch(ds::attention_step_kernel, dim3(ds::kKvHeads, ds::kSplits), dim3(ds::kAttnThreads), 0, s, pdl, qkv,
-               cos_t, sin_t, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), sinks, d_pos, window, part,
-               counters, out);
+    // a window layer's keys (<= window) in few ranges, a full layer's in kStepMaxSplits ranges (one pass each up to
+    // kStepMaxSplits * kStepCap = 4608 visible keys)
+    const int nsplit = window > 0 ? std::min(ds::kStepMaxSplits, std::max(1, (window + 31) / 32)) : ds::kStepMaxSplits;
+    ds::launch(ds::attention_step_kernel, dim3(ds::kKvHeads, nsplit), dim3(ds::kAttnThreads), 0, s, pdl, qkv, cos_t,
+               sin_t, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), sinks, d_pos, window, nsplit,
+               part, counters, out);
 }
 
 void launch_attention(const float* q, const void* k_cache, const void* v_cache, const float* sinks, const int* d_pos,

@@ -920,6 +920,14 @@ int gptoss_set_prefill_packing(int mode) {
     return g_prefill_pack.exchange(mode);
 }
 
+int gptoss_set_attention_impl(int impl) {
+    if (impl < 0 || impl > 1) {
+        g_error = "gptoss_set_attention_impl: impl must be 0 (three launches) or 1 (one cooperative launch)";
+        return -1;
+    }
+    return gpt::g_attn_impl.exchange(impl);
+}
+
 int gptoss_set_moe_impl(int impl) {
     if (impl < 0 || impl > 2) {
         g_error = "gptoss_set_moe_impl: impl must be 0 (SIMT), 1 (tensor cores) or 2 (tensor cores, stream-K kernel)";

@@ -9,7 +9,8 @@
 //              x += MoE(RMSNorm(x; ln2))                       (the fused tensor-core decode MoE kernel)
 //   logits = lm_head RMSNorm(x; norm); position += 1
 // This is the layer sequence of openvang/gptoss-infer runtime/src/engine.cu:242-262 (and of the fp32 reference
-// gptoss_ref/model.py:107-125), with RMSNorms fused into their consumers and the MoE in one kernel.
+// gptoss_ref/model.py:107-125), with RMSNorms fused into their consumers and the MoE in one kernel. With
+// gptoss_set_attention_impl(1) the first three lines of a layer run as one cooperative launch (attn_block.cu).
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -356,6 +357,10 @@ Engine::Engine(const std::string& dir, int max_ctx, long long vram_budget) : cfg
         token_ = static_cast<int*>(alloc(4));
         pos_d_ = static_cast<int*>(alloc(4));
         next_token_ = static_cast<int*>(alloc(4));
+        err_ = static_cast<int*>(alloc(16));
+        GPT_CHECK(cudaMemset(err_, 0, 16));
+        ab_work_ = alloc(attn_block_workspace_bytes());
+        GPT_CHECK(cudaMemset(ab_work_, 0, attn_block_workspace_bytes()));
         const size_t ws = moe_layer_workspace_bytes(cfg_.top_k, cfg_.hidden, cfg_.intermediate);
         moe_ws_ = alloc(ws);
         GPT_CHECK(cudaMemset(moe_ws_, 0, ws));
@@ -391,10 +396,14 @@ void Engine::forward(cudaStream_t s, bool pdl) {
     const int H = cfg_.hidden;
     const int QD = cfg_.heads * cfg_.head_dim, KVD = cfg_.kv_heads * cfg_.head_dim;
     launch_embed(embed_, token_, x_, H, s, pdl);
+    const bool fused = g_attn_impl.load() == 1;
     for (const Layer& L : layers_) {
-        launch_gemv_bf16(L.wqkv, x_, L.ln1, cfg_.eps, L.bqkv, nullptr, qkv_, QD + 2 * KVD, H, s, pdl);
-        launch_attention_step(qkv_, cos_, sin_, L.kc, L.vc, L.sinks, pos_d_, L.window, part_, attn_, s, pdl);
-        launch_gemv_bf16(L.wo, attn_, nullptr, 0.f, L.bo, x_, x_, H, QD, s, pdl);
+        if (!fused || !launch_attn_block(x_, L.ln1, cfg_.eps, L.wqkv, L.bqkv, L.wo, L.bo, cos_, sin_, L.kc, L.vc,
+                                         L.sinks, pos_d_, L.window, H, ab_work_, err_, s, pdl)) {
+            launch_gemv_bf16(L.wqkv, x_, L.ln1, cfg_.eps, L.bqkv, nullptr, qkv_, QD + 2 * KVD, H, s, pdl);
+            launch_attention_step(qkv_, cos_, sin_, L.kc, L.vc, L.sinks, pos_d_, L.window, part_, attn_, s, pdl);
+            launch_gemv_bf16(L.wo, attn_, nullptr, 0.f, L.bo, x_, x_, H, QD, s, pdl);
+        }
         moe_layer_forward_ws(L.moe, x_, x_, s, nullptr, moe_ws_);
     }
     launch_gemv_bf16(lm_head_, x_, norm_, cfg_.eps, nullptr, nullptr, logits_, cfg_.vocab, H, s, pdl);
@@ -452,6 +461,20 @@ void Engine::step(int token) {
 void Engine::copy_logits(float* host) {
     GPT_CHECK(cudaMemcpyAsync(host, logits_, size_t(cfg_.vocab) * 4, cudaMemcpyDeviceToHost, stream_));
     GPT_CHECK(cudaStreamSynchronize(stream_));
+    check_device_error();
+}
+
+// The step kernels' error word (a bounded wait that ran out), read after the stream has been synchronized; on an
+// error the attention block's workspace (its barrier word and head counters) is zero-filled again.
+void Engine::check_device_error() {
+    int e = 0;
+    GPT_CHECK(cudaMemcpy(&e, err_, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        GPT_CHECK(cudaMemset(err_, 0, sizeof(int)));
+        GPT_CHECK(cudaMemset(ab_work_, 0, attn_block_workspace_bytes()));
+        throw std::runtime_error("decode step: a bounded wait in the attention block ran out (code " +
+                                 std::to_string(e) + ")");
+    }
 }
 
 void Engine::score(const int* ids, int k, int target, float* lp, int* argmax, float* target_lp, float* lse) {
@@ -602,6 +625,7 @@ void Engine::bench_steps(int token, int n) {
     if (n < 0 || pos_ + n > max_ctx_) throw std::runtime_error("context is full");
     for (int i = 0; i < n; ++i) step(token);
     GPT_CHECK(cudaStreamSynchronize(stream_));
+    check_device_error();
 }
 
 // Greedy decode: the argmax of each step's logits is written to the device token the next step embeds, so steps
@@ -627,6 +651,7 @@ void Engine::greedy(int token, int n, int* out_tokens) {
         GPT_CHECK(cudaMemcpyAsync(pinned_ + i, token_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     }
     GPT_CHECK(cudaStreamSynchronize(stream_));
+    check_device_error();
     if (out_tokens) std::memcpy(out_tokens, pinned_, size_t(n) * sizeof(int));
 }
 

@@ -67,6 +67,7 @@ class Engine {
     void forward(cudaStream_t s, bool pdl);
     void capture();
     void run_step();
+    void check_device_error();
     void* scratch(size_t i, size_t bytes);     // grow-only buffers of the batched prefill, counted in device_bytes
     void project(const void* W, int n_out, int K, const void* hi, const void* lo, int rows, float* out, bool accumulate);
 
@@ -87,6 +88,8 @@ class Engine {
     float* score_f_ = nullptr;                  // [score_cap_] log-probabilities, then target_lp, lse
     int* score_i_ = nullptr;                    // [score_cap_] ids, then argmax
     int *token_ = nullptr, *pos_d_ = nullptr, *next_token_ = nullptr;
+    int* err_ = nullptr;                        // error word of the attention block (bounded waits)
+    void* ab_work_ = nullptr;                   // the attention block's workspace (zero-filled)
     void* moe_ws_ = nullptr;                    // the MoE kernel's workspace, owned by this engine
     cublasHandle_t cublas_ = nullptr;           // the batched prefill's projections (created at its first use)
     std::vector<std::pair<void*, size_t>> pre_; // batched prefill buffers

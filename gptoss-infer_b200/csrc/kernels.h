@@ -1,6 +1,7 @@
 // Host-side launchers of the MoE-path kernels. Every launcher takes the stream to run on and throws
 // std::runtime_error on invalid shapes or launch failure; the C ABI (capi.cu) turns that into -1.
 #pragma once
+#include <atomic>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -197,6 +198,16 @@ void selftest_terms(const float* x, int n, float* out, float* per_term, int whic
 // the previous kernel's memory before reading their inputs). d_pos (device int) overrides pos when not null.
 void launch_gemv_bf16(const void* W, const float* x, const float* norm_w, float eps, const float* bias,
                       const float* resid, float* y, int N, int K, cudaStream_t s, bool pdl);
+// The attention block of a bs=1 decode step in one cooperative launch (attn_block.cu): x += Wo attention(RoPE(Wqkv
+// RMSNorm(x) + bqkv)) + bo, the new position's key and value appended to the fp16 cache. work: attn_block_
+// workspace_bytes(), zero-filled before the first use; err: device error word (bounded waits, codes 41-45). Returns
+// false (nothing launched) when the shape does not fit the kernel's shared-memory ring.
+size_t attn_block_workspace_bytes();
+extern std::atomic<int> g_attn_impl;   // 1: the engine's step uses launch_attn_block, 0: three launches per layer
+bool launch_attn_block(float* x, const float* ln, float eps, const void* wqkv, const float* bqkv, const void* wo,
+                       const float* bo, const float* cos_t, const float* sin_t, void* k_cache, void* v_cache,
+                       const float* sinks, const int* d_pos, int window, int H, void* work, int* err, cudaStream_t s,
+                       bool pdl);
 void launch_rope_append(float* qkv, const float* cos_t, const float* sin_t, const int* d_pos, int pos, void* k_cache,
                         void* v_cache, int window, cudaStream_t s, bool pdl);
 size_t attention_workspace_floats();   // zero-filled before the first use of launch_attention_step

@@ -41,6 +41,7 @@ SIGNATURES = {
     "gptoss_ep_layer_forward": ([P, P, P, P, F32, I32, I32, I32, P, P, I32, I32, P, ctypes.c_uint, P], I32),
     "gptoss_ep_status": ([I32, I32, I32, I32, I32, I32, P], I32),
     "gptoss_set_moe_impl": ([I32], I32),
+    "gptoss_set_attention_impl": ([I32], I32),
     "gptoss_set_prefill_terms": ([I32], I32),
     "gptoss_set_prefill_packing": ([I32], I32),
     "gptoss_test_decode_epoch": ([I32, I32, I32, ctypes.c_uint, P], I32),

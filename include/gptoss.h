@@ -244,6 +244,13 @@ int gptoss_test_decode_epoch(int k, int H, int I, unsigned set_to, unsigned* pre
  * kernel (one CTA per SM); 2 = tensor cores with the stream-K kernel only. Returns the previous setting, or -1. */
 int gptoss_set_moe_impl(int impl);
 
+/* [extension] How an engine's bs=1 decode step runs the attention block (RMSNorm, QKV projection, RoPE and cache
+ * append, attention with sinks and window, O projection and residual): 0 (default) = three launches per layer (QKV
+ * GEMV, attention, O GEMV), 1 = one cooperative launch per layer (three phases separated by grid-wide barriers; the
+ * same logits to the engine's tolerance, measured slower on B200: 623 against 677 tok/s on configs[1]). Read when an
+ * engine captures its step graph (its first step); returns the previous setting, or -1. */
+int gptoss_set_attention_impl(int impl);
+
 /* [extension] Activation terms of the batched (prefill) MoE, for every later batched and expert-parallel call in the
  * process: each 32-value block of the tensor-core operand is the sum of `terms` e2m1 terms under E8M0 scales, the
  * nearest such sum. 8 (the default) is exact to 2^-21 of each block's scale and meets the float64 bound of the

@@ -59,4 +59,9 @@ def test_errors_cross_the_abi_as_minus_one(lib):
     prev = lib.gptoss_set_moe_impl(0)
     assert prev in (0, 1)
     assert lib.gptoss_set_moe_impl(prev) == 0
+    assert lib.gptoss_set_attention_impl(2) == -1
+    assert b"impl" in lib.gptoss_last_error()
+    prev = lib.gptoss_set_attention_impl(0)
+    assert prev in (0, 1)
+    assert lib.gptoss_set_attention_impl(prev) == 0
 

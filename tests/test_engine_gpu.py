@@ -211,6 +211,33 @@ def test_engine_batched_prefill_then_decode(lib, ckpt):
         lib.gptoss_destroy(e)
 
 
+def test_engine_attention_block_impls_agree(lib, ckpt):
+    """The decode step's attention block as three launches per layer (default) and as one cooperative launch: the same
+    logits to the engine's tolerance for two paths, on the first positions and after a 5000-position random context
+    (more keys per range than one pass of the fused kernel stages, window layers wrapped many times)."""
+    d, _ = ckpt
+    runs = {}
+    prev = lib.gptoss_set_attention_impl(0)
+    assert prev in (0, 1)
+    try:
+        for impl in (0, 1):
+            assert lib.gptoss_set_attention_impl(impl) in (0, 1)
+            e = create(lib, d, max_ctx=5100)
+            try:
+                first = engine_logits(lib, e, TOKENS[:4])
+                assert lib.gptoss_kv_fill_random(e, 5000, 7) == 0, lib.gptoss_last_error().decode()
+                late = engine_logits(lib, e, TOKENS[4:8])
+                assert lib.gptoss_position(e) == 5004
+            finally:
+                lib.gptoss_destroy(e)
+            runs[impl] = np.concatenate([first, late])
+    finally:
+        lib.gptoss_set_attention_impl(prev)
+    assert np.isfinite(runs[1]).all()
+    for a, b in zip(runs[1], runs[0]):
+        close_logits(a, b)
+
+
 def test_engine_budget_and_bad_dir(lib, ckpt, tmp_path):
     d, _ = ckpt
     assert not lib.gptoss_create(str(d).encode(), 64, 1 << 20)

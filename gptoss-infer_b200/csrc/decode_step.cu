@@ -34,7 +34,10 @@ __device__ __forceinline__ float bf16_hi_f(uint32_t w) { return __uint_as_float(
 // The weights do not depend on the previous kernel, so before the dependency wait every warp asks L2 for its first
 // pf_groups row groups (one bulk prefetch per row) and the next kernel's launch is released: a CTA that is resident
 // while the previous kernel still runs (programmatic dependent launch) streams its rows into L2 meanwhile.
-constexpr int kGemvThreads = 256, kRows = 2, kChunksInFlight = 8;
+// One row per warp at a time with 8 chunks in flight per lane and 4 CTAs per SM (64 registers): more warps in flight
+// measured faster per configs[1] token than two rows per warp at 2 CTAs per SM (1470 -> 1372 us; 12 chunks at 3 CTAs
+// 1414 us, 6 chunks at 5 CTAs 1371 us, 4 rows per warp 1689 us).
+constexpr int kGemvThreads = 256, kRows = 1, kChunksInFlight = 8, kGemvCtasPerSm = 4;
 // x' in shared memory as two float4 arrays (elements 8c..8c+3 at 4c, elements 8c+4..8c+7 at K/2 + 4c), so that the
 // lanes' reads of consecutive chunks are consecutive 16-byte words (no bank conflict; 1485 -> 1463 us per configs[1]
 // token measured against the plain layout, whose 32-byte lane stride is a two-way conflict)
@@ -46,7 +49,7 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ W,
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ W,
                                                                     const float* __restrict__ x,
                                                                     const float* __restrict__ g, float eps,
                                                                     const float* __restrict__ bias,
@@ -910,7 +913,7 @@ void launch_gemv_bf16(const void* W, const float* x, const float* norm_w, float 
         }
     }
     const int warps_needed = (N + ds::kRows - 1) / ds::kRows;
-    const int grid = std::max(1, std::min(num_sms() * 2, (warps_needed + 7) / 8));
+    const int grid = std::max(1, std::min(num_sms() * ds::kGemvCtasPerSm, (warps_needed + 7) / 8));
     // matrices that fit in a half of L2 are prefetched whole, larger ones (the LM head) one row group per warp
     const int pf_groups = size_t(N) * K * 2 <= (size_t(64) << 20) ? INT_MAX : 1;
     ds::launch(ds::gemv_bf16_kernel, dim3(grid), dim3(ds::kGemvThreads), smem, s, pdl,
